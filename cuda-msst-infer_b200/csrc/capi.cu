@@ -1,0 +1,319 @@
+// capi.cu — the extern "C" boundary of libmsst_b200 (declared in include/msst_b200.h).
+// Every entry point catches exceptions and turns them into status codes; the
+// message is kept per thread for msst_last_error().
+#include <cmath>
+#include <string>
+
+#include "attention.cuh"
+#include "gemm.cuh"
+#include "kernels.cuh"
+#include "model.h"
+#include "runtime.h"
+
+struct msst_model {
+  msst::Model impl;
+};
+
+namespace {
+
+thread_local std::string g_last_error;
+
+template <typename F>
+int guarded(F&& f) {
+  try {
+    f();
+    return MSST_OK;
+  } catch (const msst::Error& e) {
+    g_last_error = e.what();
+    return e.code;
+  } catch (const std::bad_alloc&) {
+    g_last_error = "host out of memory";
+    return MSST_ERR_CUDA;
+  } catch (const std::exception& e) {
+    g_last_error = e.what();
+    return MSST_ERR_INVALID;
+  }
+}
+
+cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+int sm_count() {
+  static thread_local int dev = -1, n = 0;
+  int d = 0;
+  MSST_CUDA(cudaGetDevice(&d));
+  if (d != dev) {
+    dev = d;
+    n = msst::device_sm_count();
+  }
+  return n;
+}
+
+int pick_bn(int n) {
+  if (n % 256 == 0) return 256;
+  if (n % 192 == 0) return 192;
+  return n <= 128 ? 128 : 256;
+}
+
+void run_gemm(const CUtensorMap& ma, const CUtensorMap& mb, msst::GemmParams& p, int epi, int bn, int bf16,
+              cudaStream_t s) {
+  int tiles = 0;
+  for (int i = 0; i < p.num_groups; ++i) {
+    msst::GemmGroup& g = p.groups[i];
+    g.tiles_n = (g.n + bn - 1) / bn;
+    g.tile_begin = tiles;
+    tiles += ((g.m + msst::kGemmBM - 1) / msst::kGemmBM) * g.tiles_n;
+  }
+  p.total_tiles = tiles;
+  MSST_CUDA(msst::launch_gemm(ma, mb, p, epi, bn, bf16, sm_count(), s));
+}
+
+void check_dtype(int dtype) { MSST_REQUIRE(dtype == MSST_F16 || dtype == MSST_BF16, "dtype must be MSST_F16 or MSST_BF16"); }
+
+void check_align(const void* p, const char* what) {
+  MSST_REQUIRE((reinterpret_cast<uintptr_t>(p) & 15) == 0, std::string(what) + " must be 16-byte aligned");
+}
+
+// Op-level entry points run on the device that owns their first operand.
+void use_device_of(const void* p) {
+  cudaPointerAttributes a{};
+  MSST_CUDA(cudaPointerGetAttributes(&a, p));
+  MSST_REQUIRE(a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged, "operand is not device memory");
+  int cur = -1;
+  MSST_CUDA(cudaGetDevice(&cur));
+  if (cur != a.device) MSST_CUDA(cudaSetDevice(a.device));
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* msst_last_error(void) { return g_last_error.c_str(); }
+
+unsigned msst_device_error(int clear) { return msst::device_error(clear != 0); }
+
+int msst_version(void) { return 1; }
+
+int msst_rmsnorm(const float* x, long long rows, int D, const float* gamma, float scale, int dtype, void* out16,
+                 const float* wg, const float* bg, int heads, float* gates, void* stream) {
+  return guarded([&] {
+    check_dtype(dtype);
+    MSST_REQUIRE(x && gamma && out16 && rows >= 0, "null argument");
+    MSST_REQUIRE(D % 128 == 0 && D <= 1024, "D must be a multiple of 128 and <= 1024");
+    MSST_REQUIRE(!wg || (bg && gates && heads > 0 && heads <= 32), "gate projection needs bg, gates, 0<heads<=32");
+    check_align(x, "x");
+    use_device_of(x);
+    msst::RmsNormArgs a{};
+    a.x = const_cast<float*>(x);
+    a.rows = rows;
+    a.D = D;
+    a.gamma = gamma;
+    a.scale = scale;
+    a.out16 = out16;
+    a.wg = wg;
+    a.bg = bg;
+    a.gates = gates;
+    a.heads = heads;
+    MSST_CUDA(msst::launch_rmsnorm(a, dtype, as_stream(stream)));
+  });
+}
+
+int msst_gemm(const void* x, long long rows, int K, long long ldx, const void* w, int N, const float* bias,
+              int epilogue, int act, int dtype, void* out, long long ldo, void* stream) {
+  return guarded([&] {
+    check_dtype(dtype);
+    MSST_REQUIRE(x && w && out, "null argument");
+    MSST_REQUIRE(rows > 0 && rows < (1LL << 31) && N > 0, "bad rows / N");
+    MSST_REQUIRE(K > 0 && K % 64 == 0, "K must be a positive multiple of 64");
+    MSST_REQUIRE(ldx >= K && (ldx * 2) % 16 == 0, "ldx must be >= K and a multiple of 8 elements");
+    MSST_REQUIRE(epilogue >= MSST_EPI_STORE16 && epilogue <= MSST_EPI_GLU32, "bad epilogue");
+    MSST_REQUIRE(act >= MSST_ACT_NONE && act <= MSST_ACT_SIGMOID, "bad activation");
+    MSST_REQUIRE(epilogue != MSST_EPI_GLU32 || N % 2 == 0, "GLU needs an even N");
+    check_align(x, "x");
+    check_align(w, "w");
+    use_device_of(x);
+    const int bn = pick_bn(N);
+    const CUtensorMap ma = msst::map_2d(x, (uint64_t)rows, (uint64_t)K, (uint64_t)ldx, msst::kGemmBM);
+    const CUtensorMap mb = msst::map_2d(w, (uint64_t)N, (uint64_t)K, (uint64_t)K, (uint32_t)bn);
+    msst::GemmParams p{};
+    p.num_groups = 1;
+    p.act = act;
+    msst::GemmGroup& g = p.groups[0];
+    g.m = (int)rows;
+    g.n = N;
+    g.k = K;
+    g.out = out;
+    g.ldo = ldo;
+    g.out_row_mul = 1;
+    g.bias = bias;
+    run_gemm(ma, mb, p, epilogue, bn, dtype, as_stream(stream));
+  });
+}
+
+int msst_gemm_qkv_rope(const void* x, long long rows, int K, const void* w, int heads, const float* cos_tab,
+                       const float* sin_tab, int pos_div, int pos_mod, int dtype, void* qkv16, void* stream) {
+  return guarded([&] {
+    check_dtype(dtype);
+    MSST_REQUIRE(x && w && qkv16 && cos_tab && sin_tab, "null argument");
+    MSST_REQUIRE(K > 0 && K % 64 == 0 && heads > 0 && pos_div > 0 && pos_mod > 0, "bad shape");
+    check_align(x, "x");
+    check_align(w, "w");
+    use_device_of(x);
+    const int N = 3 * heads * 64;
+    const int bn = pick_bn(N);
+    const CUtensorMap ma = msst::map_2d(x, (uint64_t)rows, (uint64_t)K, (uint64_t)K, msst::kGemmBM);
+    const CUtensorMap mb = msst::map_2d(w, (uint64_t)N, (uint64_t)K, (uint64_t)K, (uint32_t)bn);
+    msst::GemmParams p{};
+    p.num_groups = 1;
+    p.pos_div = pos_div;
+    p.pos_mod = pos_mod;
+    p.rope_cols = 2 * heads * 64;
+    p.head_dim = 64;
+    p.rope_cos = cos_tab;
+    p.rope_sin = sin_tab;
+    msst::GemmGroup& g = p.groups[0];
+    g.m = (int)rows;
+    g.n = N;
+    g.k = K;
+    g.out = qkv16;
+    g.ldo = N;
+    g.out_row_mul = 1;
+    run_gemm(ma, mb, p, msst::kEpiQkvRope, bn, dtype, as_stream(stream));
+  });
+}
+
+int msst_attention(const void* qkv16, int B, int T, int F, int heads, int axis, float scale, const float* gates,
+                   int dtype, void* out16, void* stream) {
+  return guarded([&] {
+    check_dtype(dtype);
+    MSST_REQUIRE(qkv16 && out16, "null argument");
+    MSST_REQUIRE(B > 0 && T > 0 && F > 0 && heads > 0, "bad shape");
+    MSST_REQUIRE(axis == MSST_AXIS_TIME || axis == MSST_AXIS_BAND, "bad axis");
+    MSST_REQUIRE(axis == MSST_AXIS_TIME || F <= 128, "band axis supports at most 128 bands");
+    check_align(qkv16, "qkv16");
+    check_align(out16, "out16");
+    use_device_of(qkv16);
+    const long long M = (long long)B * T * F;
+    MSST_REQUIRE(M < (1LL << 31), "too many tokens");
+    const uint64_t C3 = 3ull * heads * 64;
+    msst::AttnParams a{};
+    a.mode = axis;
+    a.B = B;
+    a.T = T;
+    a.F = F;
+    a.heads = heads;
+    a.num_tokens = (int)M;
+    a.scale_log2 = scale * 1.4426950408889634f;
+    a.gates = gates;
+    a.out = out16;
+    CUtensorMap m;
+    if (axis == MSST_AXIS_TIME) {
+      a.seq_len = T;
+      a.q_tiles = (T + 127) / 128;
+      a.total_items = B * F * heads * a.q_tiles;
+      const uint64_t dims[4] = {C3, (uint64_t)F, (uint64_t)T, (uint64_t)B};
+      const uint64_t str[3] = {C3 * 2, C3 * 2 * F, C3 * 2 * F * T};
+      const uint32_t box[4] = {64, 1, 128, 1};
+      m = msst::make_tensor_map(qkv16, 4, dims, str, box);
+    } else {
+      a.seq_len = F;
+      a.seqs_per_tile = 128 / F;
+      a.q_tiles = (int)(((long long)B * T + a.seqs_per_tile - 1) / a.seqs_per_tile);
+      a.total_items = a.q_tiles * heads;
+      const uint64_t dims[4] = {C3, (uint64_t)M, 1, 1};
+      const uint64_t str[3] = {C3 * 2, C3 * 2 * M, C3 * 2 * M};
+      const uint32_t box[4] = {64, 128, 1, 1};
+      m = msst::make_tensor_map(qkv16, 4, dims, str, box);
+    }
+    MSST_CUDA(msst::launch_attention(m, a, dtype, sm_count(), as_stream(stream)));
+  });
+}
+
+int msst_model_load(const char* path, int device, int precision, msst_model** out) {
+  return guarded([&] {
+    MSST_REQUIRE(path && out, "null argument");
+    *out = nullptr;
+    auto* m = new msst_model();
+    try {
+      m->impl.load(path, device, precision);
+    } catch (...) {
+      delete m;
+      throw;
+    }
+    *out = m;
+  });
+}
+
+void msst_model_free(msst_model* m) {
+  if (!m) return;
+  cudaSetDevice(m->impl.device());
+  delete m;
+}
+
+int msst_model_get_info(const msst_model* m, msst_model_info* info) {
+  return guarded([&] {
+    MSST_REQUIRE(m && info, "null argument");
+    *info = m->impl.info();
+  });
+}
+
+int msst_model_forward(msst_model* m, const float* audio, int batch, int channels, long long length, float* out,
+                       void* stream) {
+  return guarded([&] {
+    MSST_REQUIRE(m && audio && out, "null argument");
+    MSST_CUDA(cudaSetDevice(m->impl.device()));
+    m->impl.forward(audio, batch, channels, length, out, as_stream(stream));
+  });
+}
+
+int msst_model_masks(msst_model* m, const float* audio, int batch, int channels, long long length, float* masks,
+                     void* stream) {
+  return guarded([&] {
+    MSST_REQUIRE(m && audio && masks, "null argument");
+    MSST_CUDA(cudaSetDevice(m->impl.device()));
+    m->impl.masks(audio, batch, channels, length, masks, as_stream(stream));
+  });
+}
+
+int msst_model_transformer(msst_model* m, int depth_index, int axis, float* x, int batch, int T, void* stream) {
+  return guarded([&] {
+    MSST_REQUIRE(m && x, "null argument");
+    MSST_CUDA(cudaSetDevice(m->impl.device()));
+    m->impl.transformer(depth_index, axis, x, batch, T, as_stream(stream));
+  });
+}
+
+int msst_model_separate(msst_model* m, const float* track, int channels, long long length, float overlap,
+                        int chunk_batch, int flags, float* out, void* stream) {
+  return guarded([&] {
+    MSST_REQUIRE(m && track && out, "null argument");
+    MSST_CUDA(cudaSetDevice(m->impl.device()));
+    m->impl.separate(track, channels, length, overlap, chunk_batch, flags, out, as_stream(stream));
+  });
+}
+
+int msst_model_separate_host(msst_model* m, const float* track_host, int channels, long long length, float overlap,
+                             int chunk_batch, int flags, float* out_host) {
+  return guarded([&] {
+    MSST_REQUIRE(m && track_host && out_host && channels > 0 && length > 0, "null argument");
+    MSST_CUDA(cudaSetDevice(m->impl.device()));
+    const msst_model_info& I = m->impl.info();
+    const size_t in_bytes = sizeof(float) * (size_t)channels * length;
+    const size_t out_bytes = in_bytes * (size_t)I.num_stems;
+    msst::DeviceBuffer din(in_bytes), dout(out_bytes);
+    cudaStream_t s = nullptr;
+    MSST_CUDA(cudaMemcpyAsync(din.get(), track_host, in_bytes, cudaMemcpyHostToDevice, s));
+    m->impl.separate(din.get<float>(), channels, length, overlap, chunk_batch, flags, dout.get<float>(), s);
+    MSST_CUDA(cudaMemcpyAsync(out_host, dout.get(), out_bytes, cudaMemcpyDeviceToHost, s));
+    MSST_CUDA(cudaStreamSynchronize(s));
+  });
+}
+
+int msst_model_chunk_plan(const msst_model* m, long long length, float overlap, int* chunk_size, int* step,
+                          long long* border, long long* padded_length, int* num_chunks) {
+  return guarded([&] {
+    MSST_REQUIRE(m && chunk_size && step && border && padded_length && num_chunks, "null argument");
+    m->impl.chunk_plan(length, overlap, chunk_size, step, border, padded_length, num_chunks);
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,371 @@
+// gemm.cu — persistent, warp-specialised tcgen05 GEMM for sm_100a with fused
+// epilogues.  Replaces the cuBLAS GEMM + separate bias/activation/residual
+// kernels of the reference (src/ops_linear.cu:150-427, src/ops_fused.cu:203-303,
+// the residual add in src/tensor.cu:1439-1442 and the per-band loops of
+// src/model_mel_band_roformer.cu:676-736).
+//
+// CTA = 192 threads:
+//   warp 0     TMA producer (one lane): A/B k-blocks of 64 into a smem ring
+//   warp 1     MMA issuer (one lane): tcgen05.mma M=128 N=BN K=16, fp32 accumulators
+//              in TMEM, double-buffered so the epilogue of tile i overlaps the
+//              main loop of tile i+1; also owns the TMEM allocation
+//   warps 2-5  epilogue: tcgen05.ld 32 columns at a time, fused bias/activation/
+//              RoPE/GLU/residual, direct global stores (each thread owns one row)
+// Tiles of all groups are walked in one static persistent schedule.
+#include "common.cuh"
+#include "gemm.cuh"
+
+namespace msst {
+
+namespace {
+
+template <int BN>
+struct GemmCfg {
+  static constexpr uint32_t kABytes = kGemmBM * kGemmBK * 2;
+  static constexpr uint32_t kBBytes = BN * kGemmBK * 2;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = (int)((196u * 1024u) / kStageBytes) > 8 ? 8 : (int)((196u * 1024u) / kStageBytes);
+  static constexpr uint32_t kTmemCols = (2 * BN <= 256) ? 256 : 512;
+  static constexpr size_t kSmemBytes =
+      1024 + (size_t)kStages * kStageBytes + 256 + sizeof(GemmGroup) * kGemmMaxGroups;
+};
+
+__device__ __forceinline__ int find_group(const GemmGroup* g, int n, int t) {
+  int i = 0;
+  while (i + 1 < n && g[i + 1].tile_begin <= t) ++i;
+  return i;
+}
+
+__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
+
+template <typename T>
+__device__ __forceinline__ void store16_chunk(T* o, const float (&v)[32], int nvalid) {
+  if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
+    uint4* o4 = reinterpret_cast<uint4*>(o);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 w;
+      w.x = pack2<T>(v[8 * q + 0], v[8 * q + 1]);
+      w.y = pack2<T>(v[8 * q + 2], v[8 * q + 3]);
+      w.z = pack2<T>(v[8 * q + 4], v[8 * q + 5]);
+      w.w = pack2<T>(v[8 * q + 6], v[8 * q + 7]);
+      o4[q] = w;
+    }
+  } else {
+    for (int j = 0; j < nvalid; ++j) {
+      uint32_t pk = pack2<T>(v[j], 0.f);
+      o[j] = *reinterpret_cast<T*>(&pk);
+    }
+  }
+}
+
+template <int EPI, typename T>
+__device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const GemmGroup& g, int row, int col,
+                                               const uint32_t (&r)[32]) {
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+  const int nvalid = min(32, g.n - col);
+  if (g.bias != nullptr) {
+    if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(g.bias + col) & 15) == 0)) {
+      const float4* b4 = reinterpret_cast<const float4*>(g.bias + col);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float4 b = __ldg(b4 + q);
+        v[4 * q] += b.x;
+        v[4 * q + 1] += b.y;
+        v[4 * q + 2] += b.z;
+        v[4 * q + 3] += b.w;
+      }
+    } else {
+      for (int j = 0; j < nvalid; ++j) v[j] += __ldg(g.bias + col + j);
+    }
+  }
+  const long long orow = (long long)row * g.out_row_mul + g.out_row_add;
+  if constexpr (EPI == kEpiStore16 || EPI == kEpiQkvRope) {
+    if constexpr (EPI == kEpiStore16) {
+      if (p.act == kActGelu) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+      } else if (p.act == kActTanh) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = tanhf(v[j]);
+      } else if (p.act == kActSigmoid) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = sigmoidf_(v[j]);
+      }
+    } else {
+      if (col < p.rope_cols) {
+        const int half = p.head_dim >> 1;
+        const int pos = (row / p.pos_div) % p.pos_mod;
+        const int i0 = (col % p.head_dim) >> 1;
+        const float* cs = p.rope_cos + (size_t)pos * half + i0;
+        const float* sn = p.rope_sin + (size_t)pos * half + i0;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float c = __ldg(cs + j), s = __ldg(sn + j);
+          const float x0 = v[2 * j], x1 = v[2 * j + 1];
+          v[2 * j] = x0 * c - x1 * s;
+          v[2 * j + 1] = x0 * s + x1 * c;
+        }
+      }
+    }
+    T* o = reinterpret_cast<T*>(g.out) + orow * g.ldo + g.out_col0 + col;
+    store16_chunk<T>(o, v, nvalid);
+  } else if constexpr (EPI == kEpiResid32 || EPI == kEpiStore32) {
+    float* o = reinterpret_cast<float*>(g.out) + orow * g.ldo + g.out_col0 + col;
+    if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
+      float4* o4 = reinterpret_cast<float4*>(o);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float4 w = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        if constexpr (EPI == kEpiResid32) {
+          const float4 old = o4[q];
+          w.x += old.x;
+          w.y += old.y;
+          w.z += old.z;
+          w.w += old.w;
+        }
+        o4[q] = w;
+      }
+    } else {
+      for (int j = 0; j < nvalid; ++j) {
+        if constexpr (EPI == kEpiResid32)
+          o[j] += v[j];
+        else
+          o[j] = v[j];
+      }
+    }
+  } else {  // kEpiGlu32: adjacent columns (2j, 2j+1) are (value, gate)
+    float* o = reinterpret_cast<float*>(g.out) + orow * g.ldo + g.out_col0 + (col >> 1);
+    float w[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) w[j] = v[2 * j] * sigmoidf_(v[2 * j + 1]);
+    const int nout = nvalid >> 1;
+    if (nout == 16 && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
+      float4* o4 = reinterpret_cast<float4*>(o);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) o4[q] = make_float4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+    } else {
+      for (int j = 0; j < nout; ++j) o[j] = w[j];
+    }
+  }
+}
+
+template <int BN, int EPI, typename T>
+__global__ void __launch_bounds__(192, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                const __grid_constant__ GemmParams p) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int kStages = Cfg::kStages;
+  constexpr uint32_t kIsBf16 = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kStages * Cfg::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + kStages * Cfg::kBBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* tfull = empty + kStages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  GemmGroup* groups = reinterpret_cast<GemmGroup*>(smem + kStages * Cfg::kStageBytes + 256);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  {
+    const int words = p.num_groups * (int)(sizeof(GemmGroup) / 4);
+    const int* src = reinterpret_cast<const int*>(p.groups);
+    int* dst = reinterpret_cast<int*>(groups);
+    for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
+        const GemmGroup& g = groups[find_group(groups, p.num_groups, t)];
+        const int lt = t - g.tile_begin;
+        const int tm = lt / g.tiles_n, tn = lt - tm * g.tiles_n;
+        const int kblocks = g.k / kGemmBK;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&empty[stage], ph ^ 1u, kErrTimeoutSmemEmpty, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+          tma_load_2d(sA + stage * Cfg::kABytes, &map_a, &full[stage], g.a_col0 + kb * kGemmBK,
+                      g.a_row0 + tm * kGemmBM);
+          tma_load_2d(sB + stage * Cfg::kBBytes, &map_b, &full[stage], g.b_col0 + kb * kGemmBK, g.b_row0 + tn * BN);
+          if (++stage == kStages) {
+            stage = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // drain: wait (bounded) for copies already issued into the ring
+        for (int s = 0; s < kStages; ++s) (void)mbar_try_wait(smem_u32(&full[s]), 0);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t ph = 0;
+      int abuf = 0;
+      uint32_t aph = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
+        const GemmGroup& g = groups[find_group(groups, p.num_groups, t)];
+        const int lt = t - g.tile_begin;
+        const int tn = lt % g.tiles_n;
+        const int n_eff = min(BN, g.n - tn * BN);
+        const uint32_t n_mma = (uint32_t)((n_eff + 15) & ~15);
+        const uint32_t idesc = umma_idesc_f16(kIsBf16, n_mma);
+        const int kblocks = g.k / kGemmBK;
+        if (!mbar_wait(&tempty[abuf], aph ^ 1u, kErrTimeoutTmemEmpty, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(abuf * BN);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&full[stage], ph, kErrTimeoutTmaFull, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * Cfg::kABytes);
+          const uint32_t b0 = smem_u32(sB + stage * Cfg::kBBytes);
+#pragma unroll
+          for (int kk = 0; kk < kGemmBK / 16; ++kk) {
+            umma_f16_ss(d_tmem, sw128_desc(a0 + kk * 32, 16, 1024), sw128_desc(b0 + kk * 32, 16, 1024), idesc,
+                        (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == kStages) {
+            stage = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[abuf]);
+        abuf ^= 1;
+        if (abuf == 0) aph ^= 1u;
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int row_in_tile = q * 32 + lane;
+    int abuf = 0;
+    uint32_t aph = 0;
+    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
+      const GemmGroup& g = groups[find_group(groups, p.num_groups, t)];
+      const int lt = t - g.tile_begin;
+      const int tm = lt / g.tiles_n, tn = lt - tm * g.tiles_n;
+      const int n_eff = min(BN, g.n - tn * BN);
+      if (!mbar_wait(&tfull[abuf], aph, kErrTimeoutTmemFull, abort_flag)) break;
+      tc_fence_after();
+      const int row = tm * kGemmBM + row_in_tile;
+      const bool valid = row < g.m;
+      for (int c0 = 0; c0 < n_eff; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(abuf * BN + c0), r);
+        tmem_ld_wait();
+        if (valid) epilogue_chunk<EPI, T>(p, g, row, tn * BN + c0, r);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[abuf]);
+      abuf ^= 1;
+      if (abuf == 0) aph ^= 1u;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+template <int BN, int EPI, typename T>
+cudaError_t launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams& p, int num_sms,
+                       cudaStream_t stream) {
+  using Cfg = GemmCfg<BN>;
+  auto kern = gemm_kernel<BN, EPI, T>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  const int grid = p.total_tiles < num_sms ? p.total_tiles : num_sms;
+  if (grid <= 0) return cudaSuccess;
+  kern<<<grid, 192, Cfg::kSmemBytes, stream>>>(ma, mb, p);
+  return cudaGetLastError();
+}
+
+template <int BN, typename T>
+cudaError_t dispatch_epi(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams& p, int epi, int num_sms,
+                         cudaStream_t s) {
+  switch (epi) {
+    case kEpiStore16: return launch_one<BN, kEpiStore16, T>(ma, mb, p, num_sms, s);
+    case kEpiResid32: return launch_one<BN, kEpiResid32, T>(ma, mb, p, num_sms, s);
+    case kEpiStore32: return launch_one<BN, kEpiStore32, T>(ma, mb, p, num_sms, s);
+    case kEpiGlu32: return launch_one<BN, kEpiGlu32, T>(ma, mb, p, num_sms, s);
+    case kEpiQkvRope: return launch_one<BN, kEpiQkvRope, T>(ma, mb, p, num_sms, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_gemm(const CUtensorMap& map_a, const CUtensorMap& map_b, const GemmParams& p, int epilogue,
+                        int bn, int bf16, int num_sms, cudaStream_t stream) {
+  if (p.num_groups < 1 || p.num_groups > kGemmMaxGroups) return cudaErrorInvalidValue;
+  for (int i = 0; i < p.num_groups; ++i) {
+    const GemmGroup& g = p.groups[i];
+    if (g.k <= 0 || (g.k % kGemmBK) != 0 || g.m < 0 || g.n <= 0) return cudaErrorInvalidValue;
+    if (epilogue == kEpiGlu32 && (g.n % 2) != 0) return cudaErrorInvalidValue;
+  }
+  if (bn == 256)
+    return bf16 ? dispatch_epi<256, __nv_bfloat16>(map_a, map_b, p, epilogue, num_sms, stream)
+                : dispatch_epi<256, __half>(map_a, map_b, p, epilogue, num_sms, stream);
+  if (bn == 128)
+    return bf16 ? dispatch_epi<128, __nv_bfloat16>(map_a, map_b, p, epilogue, num_sms, stream)
+                : dispatch_epi<128, __half>(map_a, map_b, p, epilogue, num_sms, stream);
+  if (bn == 192)
+    return bf16 ? dispatch_epi<192, __nv_bfloat16>(map_a, map_b, p, epilogue, num_sms, stream)
+                : dispatch_epi<192, __half>(map_a, map_b, p, epilogue, num_sms, stream);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace msst
+
+namespace msst {
+MSST_DEFINE_ERROR_ACCESSOR(gemm_device_error)
+}  // namespace msst

@@ -1,0 +1,63 @@
+// gemm.cuh — host-visible description of the grouped tcgen05 GEMM.
+//
+//   out_g = epilogue( A_g[m_g, k_g] . B_g[n_g, k_g]^T (+ bias_g) )   for each group g
+//
+// A and B are 16-bit (fp16 or bf16), K-contiguous ("K-major"), read by TMA
+// from 2-D tensor maps with 128B swizzle.  Groups let one launch cover the
+// per-band MLPs of the Roformer band-split and mask estimator (reference
+// src/model_mel_band_roformer.cu:676-685,712-736), which the reference runs as
+// 60-62 separate cuBLAS calls each.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace msst {
+
+constexpr int kGemmBM = 128;
+constexpr int kGemmBK = 64;
+constexpr int kGemmMaxGroups = 64;
+
+enum GemmEpilogue : int {
+  kEpiStore16 = 0,   // out16 = act(acc + bias)
+  kEpiResid32 = 1,   // out32 += acc + bias            (residual stream update)
+  kEpiStore32 = 2,   // out32  = acc + bias
+  kEpiGlu32 = 3,     // out32[j] = (acc[2j]+b[2j]) * sigmoid(acc[2j+1]+b[2j+1])
+  kEpiQkvRope = 4,   // out16 = acc, interleaved-pair rotary on the first rope_cols columns
+};
+
+enum GemmAct : int { kActNone = 0, kActGelu = 1, kActTanh = 2, kActSigmoid = 3 };
+
+struct GemmGroup {
+  int m, n, k;            // output rows, output columns (before GLU halving), reduction length (k % 64 == 0)
+  int a_row0, a_col0;     // A coordinates of this group's (0, 0)
+  int b_row0, b_col0;     // B coordinates of this group's (0, 0)
+  int tiles_n;            // ceil(n / BN)
+  int tile_begin;         // first tile index of this group in the launch
+  int out_col0;           // first output column (GLU: in halved units)
+  long long ldo;          // output row stride, elements
+  long long out_row_mul;  // output row = row * out_row_mul + out_row_add
+  long long out_row_add;
+  void* out;
+  const float* bias;      // [n] or nullptr
+};
+
+struct GemmParams {
+  int num_groups;
+  int total_tiles;
+  int act;
+  // kEpiQkvRope: position = (row / pos_div) % pos_mod; cos/sin tables [pos_mod, head_dim/2]
+  int pos_div, pos_mod, rope_cols, head_dim;
+  const float* rope_cos;
+  const float* rope_sin;
+  GemmGroup groups[kGemmMaxGroups];
+};
+
+// Launches the GEMM.  `map_a` / `map_b` are 2-D tensor maps (inner dim = K) with
+// box {64, 128} for A and {64, bn} for B, 128B swizzle.  bf16 != 0 selects bf16
+// operands (else fp16).  bn in {128, 192, 256}.  Returns a cudaError_t.
+cudaError_t launch_gemm(const CUtensorMap& map_a, const CUtensorMap& map_b, const GemmParams& p, int epilogue,
+                        int bn, int bf16, int num_sms, cudaStream_t stream);
+
+}  // namespace msst

@@ -1,0 +1,405 @@
+// kernels.cu — coalesced memory-bound kernels of the Roformer path (sm_100a).
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace msst {
+
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ long long reflect_idx(long long i, long long n) {
+  // one reflection without edge repeat, then a clamp (Tensor::pad_reflect, src/tensor.cu:394-403)
+  if (i < 0)
+    i = -i;
+  else if (i >= n)
+    i = 2 * (n - 1) - i;
+  return i < 0 ? 0 : (i >= n ? n - 1 : i);
+}
+
+// ------------------------------------------------------------------ RMSNorm
+template <typename T, int V>
+__global__ void __launch_bounds__(256) rmsnorm_kernel(RmsNormArgs a) {
+  extern __shared__ float s_wg[];  // [heads * D]
+  const int lane = threadIdx.x & 31;
+  const int D = a.D;
+  if (a.wg != nullptr) {
+    for (int i = threadIdx.x; i < a.heads * D; i += blockDim.x) s_wg[i] = a.wg[i];
+    __syncthreads();
+  }
+  const long long warps_total = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < a.rows; r += warps_total) {
+    float4* xr = reinterpret_cast<float4*>(a.x + r * D);
+    float4 v[V];
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      v[k] = xr[lane + 32 * k];
+      ss += v[k].x * v[k].x + v[k].y * v[k].y + v[k].z * v[k].z + v[k].w * v[k].w;
+    }
+    ss = warp_sum(ss);
+    if (a.gamma_pre != nullptr) {
+      const float inv = rsqrtf(ss + 1e-12f);
+      const float4* g4 = reinterpret_cast<const float4*>(a.gamma_pre);
+      ss = 0.f;
+#pragma unroll
+      for (int k = 0; k < V; ++k) {
+        const float4 g = __ldg(g4 + lane + 32 * k);
+        v[k].x = v[k].x * inv * g.x * a.scale_pre;
+        v[k].y = v[k].y * inv * g.y * a.scale_pre;
+        v[k].z = v[k].z * inv * g.z * a.scale_pre;
+        v[k].w = v[k].w * inv * g.w * a.scale_pre;
+        xr[lane + 32 * k] = v[k];
+        ss += v[k].x * v[k].x + v[k].y * v[k].y + v[k].z * v[k].z + v[k].w * v[k].w;
+      }
+      ss = warp_sum(ss);
+    }
+    if (a.gamma == nullptr) continue;
+    const float inv = rsqrtf(ss + 1e-12f);
+    const float4* g4 = reinterpret_cast<const float4*>(a.gamma);
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      const float4 g = __ldg(g4 + lane + 32 * k);
+      v[k].x = v[k].x * inv * g.x * a.scale;
+      v[k].y = v[k].y * inv * g.y * a.scale;
+      v[k].z = v[k].z * inv * g.z * a.scale;
+      v[k].w = v[k].w * inv * g.w * a.scale;
+    }
+    long long orow = r;
+    if (a.band_major) {
+      const long long bt_count = a.rows / a.F;
+      orow = (r % a.F) * bt_count + r / a.F;
+    }
+    uint2* o = reinterpret_cast<uint2*>(reinterpret_cast<T*>(a.out16) + orow * D);
+#pragma unroll
+    for (int k = 0; k < V; ++k) o[lane + 32 * k] = make_uint2(pack2<T>(v[k].x, v[k].y), pack2<T>(v[k].z, v[k].w));
+    if (a.wg != nullptr) {
+      for (int h = 0; h < a.heads; ++h) {
+        const float4* w4 = reinterpret_cast<const float4*>(s_wg + h * D);
+        float d = 0.f;
+#pragma unroll
+        for (int k = 0; k < V; ++k) {
+          const float4 w = w4[lane + 32 * k];
+          d += v[k].x * w.x + v[k].y * w.y + v[k].z * w.z + v[k].w * w.w;
+        }
+        d = warp_sum(d);
+        if (lane == h) a.gates[r * a.heads + h] = 1.0f / (1.0f + __expf(-(d + a.bg[h])));
+      }
+    }
+  }
+}
+
+template <typename T>
+cudaError_t rmsnorm_dispatch(const RmsNormArgs& a, cudaStream_t s) {
+  const int V = a.D / 128;
+  const size_t smem = a.wg ? (size_t)a.heads * a.D * sizeof(float) : 0;
+  const long long warps = a.rows;
+  long long blocks = (warps + 7) / 8;
+  if (blocks > 148LL * 16) blocks = 148LL * 16;
+  if (blocks < 1) return cudaSuccess;
+  switch (V) {
+#define MSST_RMS_CASE(v)                                                                                \
+  case v:                                                                                               \
+    if (smem > 48 * 1024)                                                                               \
+      cudaFuncSetAttribute(rmsnorm_kernel<T, v>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    rmsnorm_kernel<T, v><<<(unsigned)blocks, 256, smem, s>>>(a);                                        \
+    break;
+    MSST_RMS_CASE(1)
+    MSST_RMS_CASE(2)
+    MSST_RMS_CASE(3)
+    MSST_RMS_CASE(4)
+    MSST_RMS_CASE(5)
+    MSST_RMS_CASE(6)
+    MSST_RMS_CASE(8)
+#undef MSST_RMS_CASE
+    default:
+      return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ band input
+template <typename T>
+__global__ void __launch_bounds__(256) band_input_kernel(BandInArgs a) {
+  const int lane = threadIdx.x & 31;
+  const long long items = (long long)a.Bc * a.T * a.num_bands;
+  const long long warps_total = (long long)gridDim.x * (blockDim.x >> 5);
+  const int per_bin = 2 * a.C;
+  for (long long it = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); it < items; it += warps_total) {
+    const int band = (int)(it % a.num_bands);
+    const long long bt = it / a.num_bands;
+    const int b = (int)(bt / a.T), t = (int)(bt - (long long)b * a.T);
+    const int nf = a.nfreq[band];
+    const int dims = nf * per_bin;
+    const int* bins = a.bin_list + a.bin_start[band];
+    auto load = [&](int j) -> float {
+      const int fl = j / per_bin;
+      const int rem = j - fl * per_bin;
+      const int ch = rem >> 1, ri = rem & 1;
+      const float2 z = a.spec[((long long)(b * a.C + ch) * a.T + t) * a.nbins + bins[fl]];
+      return ri ? z.y : z.x;
+    };
+    float ss = 0.f;
+    for (int j = lane; j < dims; j += 32) {
+      const float v = load(j);
+      ss += v * v;
+    }
+    ss = warp_sum(ss);
+    const float inv = rsqrtf(ss + 1e-12f);
+    const float scale = sqrtf((float)dims);
+    const float* g = a.gamma + a.gcol[band];
+    T* o = reinterpret_cast<T*>(a.out) + bt * a.ld + a.kcol[band];
+    const int kp = a.kpad[band];
+    for (int j = lane; j < kp; j += 32) {
+      float y = 0.f;
+      if (j < dims) y = load(j) * inv * __ldg(g + j) * scale;
+      uint32_t pk = pack2<T>(y, 0.f);
+      o[j] = *reinterpret_cast<T*>(&pk);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ mask apply
+__global__ void __launch_bounds__(256) mask_apply_kernel(MaskApplyArgs a) {
+  const long long total = (long long)a.Bc * a.S * a.T * a.nbins;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int f = (int)(i % a.nbins);
+    long long r = i / a.nbins;
+    const int t = (int)(r % a.T);
+    r /= a.T;
+    const int st = (int)(r % a.S);
+    const int b = (int)(r / a.S);
+    const float* mrow = a.mask + st * a.mask_stem_stride + ((long long)b * a.T + t) * a.mask_ld;
+    const int k0 = a.contrib_off[f], k1 = a.contrib_off[f + 1];
+    const float den = a.denom[f];
+    for (int c = 0; c < a.C; ++c) {
+      float mr = 0.f, mi = 0.f;
+      for (int k = k0; k < k1; ++k) {
+        const float2 m = *reinterpret_cast<const float2*>(mrow + a.contrib_col[k] + 2 * c);
+        mr += m.x;
+        mi += m.y;
+      }
+      mr = mr / den;
+      mi = mi / den;
+      const float2 z = a.spec[((long long)(b * a.C + c) * a.T + t) * a.nbins + f];
+      float2 o = make_float2(z.x * mr - z.y * mi, z.x * mi + z.y * mr);
+      if (a.zero_dc && f == 0) o = make_float2(0.f, 0.f);
+      a.out[((((long long)b * a.S + st) * a.C + c) * a.T + t) * a.nbins + f] = o;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ STFT / iSTFT
+__global__ void __launch_bounds__(256)
+    stft_frames_kernel(const float* __restrict__ audio, long long L, int BC, int T, int n_fft, int hop,
+                       const float* __restrict__ win, float* __restrict__ frames) {
+  const long long total = (long long)BC * T * n_fft;
+  const int pad = n_fft / 2;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int n = (int)(i % n_fft);
+    const long long ft = i / n_fft;
+    const int t = (int)(ft % T);
+    const long long bc = ft / T;
+    const long long src = reflect_idx((long long)t * hop + n - pad, L);
+    frames[i] = audio[bc * L + src] * win[n];
+  }
+}
+
+__global__ void __launch_bounds__(256)
+    istft_ola_kernel(const float* __restrict__ frames, int BSC, int T, int n_fft, int hop,
+                     const float* __restrict__ win, const float* __restrict__ wsum, float* __restrict__ out) {
+  const long long Lout = (long long)(T - 1) * hop;
+  const long long total = (long long)BSC * Lout;
+  const int pad = n_fft / 2;
+  const float inv_n = 1.0f / (float)n_fft;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long bsc = i / Lout;
+    const long long p = i - bsc * Lout + pad;
+    long long t_lo = (p - n_fft + hop) / hop;  // ceil((p - n_fft + 1) / hop) for p >= n_fft - 1
+    if (p - n_fft + 1 <= 0) t_lo = 0;
+    long long t_hi = p / hop;
+    if (t_hi > T - 1) t_hi = T - 1;
+    float acc = 0.f;
+    for (long long t = t_lo; t <= t_hi; ++t) {
+      const int n = (int)(p - t * hop);
+      if (n < 0 || n >= n_fft) continue;
+      acc += (frames[((bsc * T) + t) * n_fft + n] * inv_n) * win[n];
+    }
+    const float ws = wsum[p];
+    out[i] = ws > 1e-8f ? acc / ws : acc;
+  }
+}
+
+// ------------------------------------------------------------------ chunking
+__device__ __forceinline__ float padded_track(const ChunkArgs& a, int c, long long p) {
+  // value of the reflect-padded track at channel c, padded index p (0 <= p < total)
+  const long long src = a.border ? reflect_idx(p - a.border, a.L) : p;
+  return a.track[(long long)c * a.L + src];
+}
+
+__global__ void __launch_bounds__(256) chunk_gather_kernel(ChunkArgs a, int first, int count, float* batch) {
+  const long long total = (long long)count * a.C * a.chunk;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int j = (int)(i % a.chunk);
+    const long long kc = i / a.chunk;
+    const int c = (int)(kc % a.C);
+    const int k = first + (int)(kc / a.C);
+    const long long start = (long long)k * a.step;
+    const long long end = min(start + (long long)a.chunk, a.total);
+    const long long n = end - start;
+    float v;
+    if (n >= a.chunk) {
+      v = padded_track(a, c, start + j);
+    } else {
+      // src/inference_app.cpp:144-150: reflect if more than half a chunk remains, else zeros
+      const bool reflect = n > a.chunk / 2;
+      long long sj = j < n ? j : 2 * (n - 1) - j;
+      sj = sj < 0 ? 0 : (sj >= n ? n - 1 : sj);
+      if (!reflect && j >= n) {
+        v = 0.f;
+      } else if (a.ref_compat) {
+        const long long flat = start + (long long)c * n + sj;  // contiguous view of a strided slice
+        v = padded_track(a, (int)(flat / a.total), flat % a.total);
+      } else {
+        v = padded_track(a, c, start + sj);
+      }
+    }
+    batch[i] = v;
+  }
+}
+
+__device__ __forceinline__ float fade_weight(int j, int chunk, bool first_chunk, bool last_chunk) {
+  // src/inference_app.cpp:192-204,267-276
+  const int fs = chunk / 10;
+  if (fs <= 0) return 1.f;
+  if (j < fs) {
+    if (first_chunk) return 1.f;
+    if (fs == 1) return 0.f;
+    return (float)j / (float)(fs - 1);
+  }
+  if (j >= chunk - fs) {
+    if (last_chunk) return 1.f;
+    if (fs == 1) return 0.f;
+    return 1.0f - (float)(j - (chunk - fs)) / (float)(fs - 1);
+  }
+  return 1.f;
+}
+
+__global__ void __launch_bounds__(256) chunk_ola_kernel(ChunkArgs a, int first, int count, int num_chunks,
+                                                        const float* y, float* acc, float* wsum) {
+  const long long g0 = (long long)first * a.step;
+  const long long g1 = min((long long)(first + count - 1) * a.step + a.chunk, a.total);
+  const long long span = g1 - g0;
+  const long long total = (long long)(a.C + 1) * span;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(i / span);  // c == C: weight row
+    const long long p = g0 + i % span;
+    float s = c < a.C ? acc[(long long)c * a.total + p] : wsum[p];
+    for (int kk = 0; kk < count; ++kk) {
+      const int k = first + kk;
+      const long long start = (long long)k * a.step;
+      const long long end = min(start + (long long)a.chunk, a.total);
+      if (p < start || p >= end) continue;
+      const int j = (int)(p - start);
+      const float w = fade_weight(j, a.chunk, k == 0, end >= a.total);
+      if (c < a.C)
+        s += y[((long long)kk * a.C + c) * a.chunk + j] * w;
+      else
+        s += w;
+    }
+    if (c < a.C)
+      acc[(long long)c * a.total + p] = s;
+    else
+      wsum[p] = s;
+  }
+  (void)num_chunks;
+}
+
+__global__ void __launch_bounds__(256) chunk_finish_kernel(ChunkArgs a, const float* acc, const float* wsum,
+                                                           float* out) {
+  const long long total = (long long)a.C * a.L;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(i / a.L);
+    const long long p = i % a.L + a.border;
+    const float w = wsum[p];
+    const float v = acc[(long long)c * a.total + p];
+    out[i] = w > 1e-8f ? v / w : v;
+  }
+}
+
+inline unsigned grid_for(long long n) {
+  long long b = (n + 255) / 256;
+  if (b > 148LL * 32) b = 148LL * 32;
+  return (unsigned)(b < 1 ? 1 : b);
+}
+
+}  // namespace
+
+cudaError_t launch_rmsnorm(const RmsNormArgs& a, int bf16, cudaStream_t s) {
+  if (a.D % 128 != 0 || a.D > 1024 || (a.band_major && a.F <= 0) || (a.wg && a.heads > 32))
+    return cudaErrorInvalidValue;
+  return bf16 ? rmsnorm_dispatch<__nv_bfloat16>(a, s) : rmsnorm_dispatch<__half>(a, s);
+}
+
+cudaError_t launch_band_input(const BandInArgs& a, int bf16, cudaStream_t s) {
+  const long long warps = (long long)a.Bc * a.T * a.num_bands;
+  long long blocks = (warps + 7) / 8;
+  if (blocks > 148LL * 32) blocks = 148LL * 32;
+  if (blocks < 1) return cudaSuccess;
+  if (bf16)
+    band_input_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, s>>>(a);
+  else
+    band_input_kernel<__half><<<(unsigned)blocks, 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_mask_apply(const MaskApplyArgs& a, cudaStream_t s) {
+  mask_apply_kernel<<<grid_for((long long)a.Bc * a.S * a.T * a.nbins), 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_stft_frames(const float* audio, long long L, int BC, int T, int n_fft, int hop, const float* win,
+                               float* frames, cudaStream_t s) {
+  stft_frames_kernel<<<grid_for((long long)BC * T * n_fft), 256, 0, s>>>(audio, L, BC, T, n_fft, hop, win, frames);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_istft_ola(const float* frames, int BSC, int T, int n_fft, int hop, const float* win,
+                             const float* wsum, float* out, cudaStream_t s) {
+  istft_ola_kernel<<<grid_for((long long)BSC * (T - 1) * hop), 256, 0, s>>>(frames, BSC, T, n_fft, hop, win, wsum,
+                                                                           out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_chunk_gather(const ChunkArgs& a, int first, int count, float* batch, cudaStream_t s) {
+  chunk_gather_kernel<<<grid_for((long long)count * a.C * a.chunk), 256, 0, s>>>(a, first, count, batch);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_chunk_ola(const ChunkArgs& a, int first, int count, int num_chunks, const float* y, float* acc,
+                             float* wsum, cudaStream_t s) {
+  const long long g0 = (long long)first * a.step;
+  const long long g1 = std::min((long long)(first + count - 1) * a.step + a.chunk, a.total);
+  chunk_ola_kernel<<<grid_for((long long)(a.C + 1) * (g1 - g0)), 256, 0, s>>>(a, first, count, num_chunks, y, acc,
+                                                                              wsum);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_chunk_finish(const ChunkArgs& a, const float* acc, const float* wsum, float* out, cudaStream_t s) {
+  chunk_finish_kernel<<<grid_for((long long)a.C * a.L), 256, 0, s>>>(a, acc, wsum, out);
+  return cudaGetLastError();
+}
+
+MSST_DEFINE_ERROR_ACCESSOR(kernels_device_error)
+
+}  // namespace msst

@@ -1,0 +1,120 @@
+// kernels.cuh — launchers for the memory-bound kernels of the Roformer path.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cufft.h>
+#include <stdint.h>
+
+namespace msst {
+
+// RMSNorm as the reference defines it (src/ops_norm.cu:85-111):
+//   y = x * rsqrt(sum(x^2) + 1e-12) * gamma * scale
+// One warp per row, D % 128 == 0, D <= 1024.  Optional stages, in order:
+//   gamma_pre: x <- RMSNorm(x; gamma_pre, scale_pre) written back to x (fp32)
+//              (the MelBandRoformer per-transformer final norm, fused into the
+//              next transformer's first pre-norm)
+//   gamma:     y  = RMSNorm(x; gamma, scale) -> out16 (fp16/bf16), row r written at
+//              out row  (r % F) * (rows / F) + r / F  when band_major, else r
+//   wg/bg:     gates[r, h] = sigmoid(y . wg[h] + bg[h])  (the attention gate
+//              projection, src/model_mel_band_roformer.cu:575)
+struct RmsNormArgs {
+  float* x;
+  long long rows;
+  int D;
+  const float* gamma_pre;
+  float scale_pre;
+  const float* gamma;
+  float scale;
+  void* out16;
+  int band_major;
+  int F;
+  const float* wg;
+  const float* bg;
+  float* gates;
+  int heads;
+};
+cudaError_t launch_rmsnorm(const RmsNormArgs& a, int bf16, cudaStream_t s);
+
+// Band gather + per-band RMSNorm + 16-bit cast + zero K-padding: builds the A
+// operand of the grouped band-split GEMM from the STFT (cuFFT R2C layout
+// [Bc*C*T, nbins] complex).  Row bt = b*T + t; band j occupies columns
+// [kcol[j], kcol[j] + kpad[j]) with dims[j] = 2*C*nfreq[j] real values ordered
+// (bin, channel, re/im) as the reference folds them
+// (src/model_mel_band_roformer.cu:808-829, src/model_bs_roformer.cu:465-473).
+struct BandInArgs {
+  const float2* spec;
+  int Bc, C, T, nbins;
+  int num_bands;
+  const int* bin_start;   // [num_bands] into bin_list
+  const int* nfreq;       // [num_bands]
+  const int* bin_list;    // mono bin indices, band-concatenated
+  const int* kcol;        // [num_bands]
+  const int* kpad;        // [num_bands]
+  const int* gcol;        // [num_bands] offset into gamma
+  const float* gamma;     // concatenated band gammas
+  void* out;              // [Bc*T, ld] 16-bit
+  long long ld;
+};
+cudaError_t launch_band_input(const BandInArgs& a, int bf16, cudaStream_t s);
+
+// Mask merge + apply (src/model_mel_band_roformer.cu:926-1015,
+// src/model_bs_roformer.cu:552-590): for every (b, stem, t, bin) the complex mask
+// is the sum of the contributing bands' GLU outputs divided by
+// max(count, 1e-8), multiplied into the STFT, DC zeroed when zero_dc; written in
+// the cuFFT C2R input layout [(b*S + stem)*C + c][t][bin].
+struct MaskApplyArgs {
+  const float2* spec;      // [Bc*C*T, nbins]
+  const float* mask;       // [S][Bc*T][mask_ld]
+  long long mask_stem_stride;
+  int mask_ld;
+  const int* contrib_off;  // [nbins + 1]
+  const int* contrib_col;  // mask column of (bin, channel 0, re) per contribution
+  const float* denom;      // [nbins] clamp(count, 1e-8)
+  float2* out;             // [Bc*S*C*T, nbins]
+  int Bc, S, C, T, nbins;
+  int zero_dc;
+};
+cudaError_t launch_mask_apply(const MaskApplyArgs& a, cudaStream_t s);
+
+// STFT framing (torch.stft center=True, reflect pad; src/ops_stft.cu:286-331):
+// frames[(bc*T + t)*n_fft + n] = audio[bc, reflect(t*hop + n - n_fft/2)] * win[n].
+cudaError_t launch_stft_frames(const float* audio, long long L, int BC, int T, int n_fft, int hop,
+                               const float* win, float* frames, cudaStream_t s);
+
+// iSTFT tail (src/ops_stft.cu:411-482): frames are the raw C2R outputs; each
+// output sample gathers its <= ceil(n_fft/hop) windowed frames, scales by
+// 1/n_fft, divides by the summed squared window where > 1e-8 and drops n_fft/2
+// samples of centre padding.  out [BSC, (T-1)*hop].
+cudaError_t launch_istft_ola(const float* frames, int BSC, int T, int n_fft, int hop, const float* win,
+                             const float* wsum, float* out, cudaStream_t s);
+
+// Chunked inference helpers (src/inference_app.cpp:100-324).
+// Gather `count` chunks starting at chunk index `first` of the reflect-padded
+// track into batch [count, C, chunk].  The padded track is never materialised:
+// padded index p maps to track index reflect(p - border).  The final, short
+// chunk is padded to `chunk` samples; ref_compat reproduces the reference's
+// contiguous-source indexing of that strided slice.
+struct ChunkArgs {
+  const float* track;      // [C, L] on device
+  int C;
+  long long L;
+  long long border;        // reflect-pad size (0 when not padded)
+  long long total;         // padded length
+  int chunk;
+  int step;
+  int ref_compat;
+};
+cudaError_t launch_chunk_gather(const ChunkArgs& a, int first, int count, float* batch, cudaStream_t s);
+
+// Windowed overlap-add of `count` chunk outputs y [count, C, chunk] (chunk
+// indices first..first+count-1) into acc [C, total] and wsum [total], chunks in
+// order (deterministic, no atomics).  Linear fade of chunk/10 samples, dropped at
+// the track's first and last chunk.
+cudaError_t launch_chunk_ola(const ChunkArgs& a, int first, int count, int num_chunks, const float* y, float* acc,
+                             float* wsum, cudaStream_t s);
+
+// out[c, i] = acc[c, border + i] / wsum[border + i] (where wsum > 1e-8), i < L.
+cudaError_t launch_chunk_finish(const ChunkArgs& a, const float* acc, const float* wsum, float* out,
+                                cudaStream_t s);
+
+}  // namespace msst

@@ -1,0 +1,1053 @@
+// model.cu — Roformer model driver: .csm loading, weight packing for the
+// tcgen05 kernels, forward pass and chunked separation.
+#include "model.h"
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <fstream>
+
+#include "attention.cuh"
+#include "kernels.cuh"
+
+namespace msst {
+
+// ===========================================================================
+// Minimal JSON (objects, arrays, numbers, strings, booleans, null) for the
+// config block of a .csm file (the reference parses it with its own
+// JsonValue, src/weights.h:18-78).
+// ===========================================================================
+struct Json {
+  enum Kind { Null, Bool, Num, Str, Arr, Obj } kind = Null;
+  bool b = false;
+  double num = 0;
+  std::string str;
+  std::vector<Json> arr;
+  std::vector<std::pair<std::string, Json>> obj;
+
+  const Json* find(const std::string& k) const {
+    for (auto& kv : obj)
+      if (kv.first == k) return &kv.second;
+    return nullptr;
+  }
+  bool has(const std::string& k) const { return find(k) != nullptr; }
+  int get_int(const std::string& k, int def) const {
+    const Json* v = find(k);
+    return (v && v->kind == Num) ? (int)v->num : def;
+  }
+  bool get_bool(const std::string& k, bool def) const {
+    const Json* v = find(k);
+    if (!v) return def;
+    if (v->kind == Bool) return v->b;
+    if (v->kind == Num) return v->num != 0;
+    return def;
+  }
+  std::string get_str(const std::string& k, const std::string& def) const {
+    const Json* v = find(k);
+    return (v && v->kind == Str) ? v->str : def;
+  }
+};
+
+class JsonParser {
+ public:
+  explicit JsonParser(const std::string& s) : s_(s) {}
+  Json parse() {
+    Json v = value();
+    ws();
+    return v;
+  }
+
+ private:
+  const std::string& s_;
+  size_t i_ = 0;
+  [[noreturn]] void bad() { fail(MSST_ERR_IO, "malformed JSON config at offset " + std::to_string(i_)); }
+  void ws() {
+    while (i_ < s_.size() && std::isspace((unsigned char)s_[i_])) ++i_;
+  }
+  char peek() {
+    ws();
+    return i_ < s_.size() ? s_[i_] : '\0';
+  }
+  void expect(char c) {
+    if (peek() != c) bad();
+    ++i_;
+  }
+  std::string string_lit() {
+    expect('"');
+    std::string out;
+    while (i_ < s_.size() && s_[i_] != '"') {
+      char c = s_[i_++];
+      if (c == '\\') {
+        if (i_ >= s_.size()) bad();
+        char e = s_[i_++];
+        switch (e) {
+          case 'n': out += '\n'; break;
+          case 't': out += '\t'; break;
+          case 'r': out += '\r'; break;
+          case 'b': out += '\b'; break;
+          case 'f': out += '\f'; break;
+          case 'u': {
+            if (i_ + 4 > s_.size()) bad();
+            unsigned cp = std::stoul(s_.substr(i_, 4), nullptr, 16);
+            i_ += 4;
+            if (cp < 0x80) {
+              out += (char)cp;
+            } else if (cp < 0x800) {
+              out += (char)(0xC0 | (cp >> 6));
+              out += (char)(0x80 | (cp & 0x3F));
+            } else {
+              out += (char)(0xE0 | (cp >> 12));
+              out += (char)(0x80 | ((cp >> 6) & 0x3F));
+              out += (char)(0x80 | (cp & 0x3F));
+            }
+            break;
+          }
+          default: out += e;
+        }
+      } else {
+        out += c;
+      }
+    }
+    if (i_ >= s_.size()) bad();
+    ++i_;
+    return out;
+  }
+  Json value() {
+    Json v;
+    char c = peek();
+    if (c == '{') {
+      ++i_;
+      v.kind = Json::Obj;
+      if (peek() == '}') {
+        ++i_;
+        return v;
+      }
+      for (;;) {
+        std::string k = string_lit();
+        expect(':');
+        v.obj.emplace_back(k, value());
+        if (peek() == ',') {
+          ++i_;
+          continue;
+        }
+        expect('}');
+        return v;
+      }
+    }
+    if (c == '[') {
+      ++i_;
+      v.kind = Json::Arr;
+      if (peek() == ']') {
+        ++i_;
+        return v;
+      }
+      for (;;) {
+        v.arr.push_back(value());
+        if (peek() == ',') {
+          ++i_;
+          continue;
+        }
+        expect(']');
+        return v;
+      }
+    }
+    if (c == '"') {
+      v.kind = Json::Str;
+      v.str = string_lit();
+      return v;
+    }
+    if (s_.compare(i_, 4, "true") == 0) {
+      i_ += 4;
+      v.kind = Json::Bool;
+      v.b = true;
+      return v;
+    }
+    if (s_.compare(i_, 5, "false") == 0) {
+      i_ += 5;
+      v.kind = Json::Bool;
+      return v;
+    }
+    if (s_.compare(i_, 4, "null") == 0) {
+      i_ += 4;
+      return v;
+    }
+    size_t end = i_;
+    while (end < s_.size() && (std::isdigit((unsigned char)s_[end]) || std::strchr("+-.eE", s_[end]))) ++end;
+    if (end == i_) bad();
+    v.kind = Json::Num;
+    v.num = std::stod(s_.substr(i_, end - i_));
+    i_ = end;
+    return v;
+  }
+};
+
+// ===========================================================================
+// .csm container (reference src/weights.h:83-96): magic "CSM\0", u32 version 1,
+// u32 config length + JSON, u32 tensor count, then per tensor: u32 name
+// length + name, u32 ndim, i64 shape[ndim], u32 dtype (0 f32, 1 f16, 2 i64),
+// raw row-major data.
+// ===========================================================================
+struct HostTensor {
+  std::vector<int64_t> shape;
+  int dtype = 0;
+  const uint8_t* data = nullptr;
+  size_t numel = 1;
+
+  std::vector<float> f32() const {
+    std::vector<float> out(numel);
+    if (dtype == 0) {
+      std::memcpy(out.data(), data, numel * 4);
+    } else if (dtype == 1) {
+      const __half* h = reinterpret_cast<const __half*>(data);
+      for (size_t i = 0; i < numel; ++i) out[i] = __half2float(h[i]);
+    } else {
+      const int64_t* q = reinterpret_cast<const int64_t*>(data);
+      for (size_t i = 0; i < numel; ++i) out[i] = (float)q[i];
+    }
+    return out;
+  }
+  std::vector<int64_t> i64() const {
+    std::vector<int64_t> out(numel);
+    if (dtype == 2) {
+      std::memcpy(out.data(), data, numel * 8);
+    } else {
+      std::vector<float> f = f32();
+      for (size_t i = 0; i < numel; ++i) out[i] = (int64_t)std::llround(f[i]);
+    }
+    return out;
+  }
+};
+
+struct Csm {
+  std::vector<uint8_t> bytes;
+  Json config;
+  std::unordered_map<std::string, HostTensor> tensors;
+
+  const HostTensor& get(const std::string& name) const {
+    auto it = tensors.find(name);
+    if (it == tensors.end()) fail(MSST_ERR_IO, "tensor not found in .csm: " + name);
+    return it->second;
+  }
+  bool has(const std::string& name) const { return tensors.count(name) > 0; }
+};
+
+static Csm read_csm(const std::string& path) {
+  Csm c;
+  std::ifstream f(path, std::ios::binary | std::ios::ate);
+  if (!f) fail(MSST_ERR_IO, "cannot open " + path);
+  const std::streamsize size = f.tellg();
+  f.seekg(0);
+  c.bytes.resize((size_t)size);
+  if (!f.read(reinterpret_cast<char*>(c.bytes.data()), size)) fail(MSST_ERR_IO, "cannot read " + path);
+  size_t off = 0;
+  auto need = [&](size_t n) {
+    if (off + n > c.bytes.size()) fail(MSST_ERR_IO, "truncated .csm file: " + path);
+  };
+  auto u32 = [&]() {
+    need(4);
+    uint32_t v;
+    std::memcpy(&v, c.bytes.data() + off, 4);
+    off += 4;
+    return v;
+  };
+  need(4);
+  if (std::memcmp(c.bytes.data(), "CSM\0", 4) != 0) fail(MSST_ERR_IO, "invalid magic (expected CSM\\0): " + path);
+  off = 4;
+  const uint32_t version = u32();
+  if (version != 1) fail(MSST_ERR_IO, "unsupported .csm version " + std::to_string(version));
+  const uint32_t clen = u32();
+  need(clen);
+  std::string cj(reinterpret_cast<const char*>(c.bytes.data() + off), clen);
+  off += clen;
+  c.config = JsonParser(cj).parse();
+  const uint32_t n = u32();
+  for (uint32_t t = 0; t < n; ++t) {
+    const uint32_t nl = u32();
+    need(nl);
+    std::string name(reinterpret_cast<const char*>(c.bytes.data() + off), nl);
+    off += nl;
+    HostTensor ht;
+    const uint32_t nd = u32();
+    ht.shape.resize(nd);
+    for (uint32_t d = 0; d < nd; ++d) {
+      need(8);
+      std::memcpy(&ht.shape[d], c.bytes.data() + off, 8);
+      off += 8;
+      ht.numel *= (size_t)ht.shape[d];
+    }
+    ht.dtype = (int)u32();
+    if (ht.dtype < 0 || ht.dtype > 2) fail(MSST_ERR_IO, "unknown dtype for tensor " + name);
+    const size_t esz = ht.dtype == 0 ? 4 : (ht.dtype == 1 ? 2 : 8);
+    need(ht.numel * esz);
+    ht.data = c.bytes.data() + off;
+    off += ht.numel * esz;
+    c.tensors.emplace(std::move(name), std::move(ht));
+  }
+  return c;
+}
+
+// ===========================================================================
+// Upload helpers
+// ===========================================================================
+static DeviceBuffer upload_f32(const std::vector<float>& v) {
+  DeviceBuffer b(v.size() * 4);
+  if (!v.empty()) MSST_CUDA(cudaMemcpy(b.get(), v.data(), v.size() * 4, cudaMemcpyHostToDevice));
+  return b;
+}
+
+static DeviceBuffer upload_i32(const std::vector<int>& v) {
+  DeviceBuffer b(std::max<size_t>(v.size(), 1) * 4);
+  if (!v.empty()) MSST_CUDA(cudaMemcpy(b.get(), v.data(), v.size() * 4, cudaMemcpyHostToDevice));
+  return b;
+}
+
+static void to16(const float* src, size_t n, uint16_t* dst, int bf16) {
+  for (size_t i = 0; i < n; ++i) {
+    if (bf16) {
+      __nv_bfloat16 h = __float2bfloat16_rn(src[i]);
+      std::memcpy(dst + i, &h, 2);
+    } else {
+      __half h = __float2half_rn(src[i]);
+      std::memcpy(dst + i, &h, 2);
+    }
+  }
+}
+
+static DeviceBuffer upload_16(const std::vector<float>& v, int bf16) {
+  std::vector<uint16_t> h(v.size());
+  to16(v.data(), v.size(), h.data(), bf16);
+  DeviceBuffer b(h.size() * 2);
+  MSST_CUDA(cudaMemcpy(b.get(), h.data(), h.size() * 2, cudaMemcpyHostToDevice));
+  return b;
+}
+
+static int pick_bn(int n) {
+  if (n % 256 == 0) return 256;
+  if (n % 192 == 0) return 192;
+  return n <= 128 ? 128 : 256;
+}
+
+// ===========================================================================
+// Workspace for one (batch, T) shape
+// ===========================================================================
+struct Model::Work {
+  int B = 0, T = 0;
+  long long M = 0, BT = 0;
+  DeviceBuffer frames, spec, ispec, abs, x, xn, gates, big1, big2, ao, mask, chunk_in, chunk_out;
+  CUtensorMap m_abs, m_xn, m_ao, m_big1_ffh, m_big2_ffh, m_qkv_time, m_qkv_band, m_h1, m_h2;
+};
+
+Model::Model() = default;
+
+Model::~Model() {
+  for (auto& kv : plans_) cufftDestroy(kv.second);
+}
+
+// ===========================================================================
+// load
+// ===========================================================================
+void Model::load(const std::string& path, int device, int precision) {
+  MSST_REQUIRE(precision == MSST_F16 || precision == MSST_BF16, "precision must be MSST_F16 or MSST_BF16");
+  device_ = device;
+  bf16_ = precision;
+  Csm csm = read_csm(path);
+  MSST_CUDA(cudaSetDevice(device));
+  num_sms_ = device_sm_count();
+  const Json& j = csm.config;
+
+  // model type detection as src/inference_app.cpp:77-98 (Roformers only)
+  const std::string mt = j.get_str("model_type", "");
+  if (mt == "mel_band_roformer" || mt == "MelBandRoformer")
+    mel_ = true;
+  else if (mt == "bs_roformer" || mt == "BSRoformer")
+    mel_ = false;
+  else if (j.has("num_bands") || j.has("mel_scale"))
+    mel_ = true;
+  else if (j.has("freqs_per_bands"))
+    mel_ = false;
+  else
+    fail(MSST_ERR_UNSUPPORTED, "not a MelBandRoformer / BSRoformer model (conv models stay on the reference path)");
+
+  // config with the reference defaults (src/model_mel_band_roformer.cu:185-208, src/model_bs_roformer.cu:26-59)
+  msst_model_info& I = info_;
+  I.model_type = mel_ ? 1 : 2;
+  I.dim = j.get_int("dim", 384);
+  I.depth = j.get_int("depth", mel_ ? 6 : 12);
+  const bool stereo = j.get_bool("stereo", true);
+  I.num_stems = j.get_int("num_stems", 1);
+  const int tdepth = j.get_int("time_transformer_depth", 1);
+  const int fdepth = j.get_int("freq_transformer_depth", 1);
+  I.dim_head = j.get_int("dim_head", 64);
+  I.heads = j.get_int("heads", 8);
+  const int me_depth = j.get_int("mask_estimator_depth", mel_ ? 2 : 1);
+  const int mlp_mult = j.get_int("mlp_expansion_factor", 4);
+  zero_dc_ = j.get_bool("zero_dc", true);
+  I.sample_rate = j.get_int("sample_rate", 44100);
+  I.n_fft = j.get_int("stft_n_fft", 2048);
+  I.hop_length = j.get_int("stft_hop_length", 441);
+  const int win_len = j.get_int("stft_win_length", 2048);
+  I.chunk_size = j.get_int("chunk_size", I.n_fft * 256);
+  I.num_overlap = j.has("num_overlap") ? std::max(1, j.get_int("num_overlap", 2)) : 2;
+  I.precision = precision;
+  if (j.get_bool("stft_normalized", false)) fail(MSST_ERR_UNSUPPORTED, "stft_normalized models are not supported");
+  if (j.get_bool("skip_connection", false)) fail(MSST_ERR_UNSUPPORTED, "skip_connection models are not supported");
+  if (j.get_bool("match_input_audio_length", false))
+    fail(MSST_ERR_UNSUPPORTED, "match_input_audio_length models are not supported");
+  if (I.dim_head != 64) fail(MSST_ERR_UNSUPPORTED, "dim_head must be 64");
+  if (win_len != I.n_fft) fail(MSST_ERR_UNSUPPORTED, "stft_win_length must equal stft_n_fft");
+  if (I.n_fft & (I.n_fft - 1)) fail(MSST_ERR_UNSUPPORTED, "stft_n_fft must be a power of two");
+  if (I.dim % 128 != 0 || I.dim > 1024) fail(MSST_ERR_UNSUPPORTED, "dim must be a multiple of 128 (<= 1024)");
+  C_ = stereo ? 2 : 1;
+  I.channels = C_;
+  nbins_ = I.n_fft / 2 + 1;
+  inner_ = I.heads * I.dim_head;
+  ff_ = I.dim * mlp_mult;
+  hid_ = I.dim * mlp_mult;
+  n_lin_ = mel_ ? me_depth + 1 : me_depth;
+  MSST_REQUIRE(n_lin_ >= 1, "mask_estimator_depth must be >= 1");
+
+  // ---- bands
+  nfreq_.clear();
+  bin_list_.clear();
+  std::vector<float> denom(nbins_, 1.0f);
+  if (mel_) {
+    if (!csm.has("__precomputed__.freq_indices"))
+      fail(MSST_ERR_UNSUPPORTED, "MelBandRoformer .csm without __precomputed__ band tables");
+    const std::vector<int64_t> fi = csm.get("__precomputed__.freq_indices").i64();
+    const std::vector<int64_t> nf = csm.get("__precomputed__.num_freqs_per_band").i64();
+    const std::vector<int64_t> nb = csm.get("__precomputed__.num_bands_per_freq").i64();
+    I.num_bands = j.get_int("num_bands", (int)nf.size());
+    MSST_REQUIRE((int)nf.size() == I.num_bands, "num_freqs_per_band length != num_bands");
+    size_t k = 0;
+    for (int b = 0; b < I.num_bands; ++b) {
+      nfreq_.push_back((int)nf[b]);
+      for (int64_t q = 0; q < nf[b]; ++q, ++k) {
+        MSST_REQUIRE(k * C_ < fi.size(), "freq_indices too short");
+        const int64_t v = fi[k * C_];
+        MSST_REQUIRE(v % C_ == 0 && v / C_ < nbins_, "freq_indices not channel-interleaved");
+        bin_list_.push_back((int)(v / C_));
+      }
+    }
+    MSST_REQUIRE((int)nb.size() == nbins_, "num_bands_per_freq length != n_fft/2+1");
+    for (int f = 0; f < nbins_; ++f) denom[f] = std::max((float)nb[f], 1e-8f);
+  } else {
+    const Json* fpb = j.find("freqs_per_bands");
+    MSST_REQUIRE(fpb && fpb->kind == Json::Arr, "BSRoformer config lacks freqs_per_bands");
+    int start = 0;
+    for (auto& v : fpb->arr) {
+      nfreq_.push_back((int)v.num);
+      for (int q = 0; q < (int)v.num; ++q) bin_list_.push_back(start + q);
+      start += (int)v.num;
+    }
+    I.num_bands = (int)nfreq_.size();
+    MSST_REQUIRE(start == nbins_, "sum(freqs_per_bands) != n_fft/2+1");
+  }
+  const int nb = I.num_bands;
+  MSST_REQUIRE(nb <= kGemmMaxGroups, "too many bands for one grouped GEMM");
+  MSST_REQUIRE(nb <= 128, "band-axis attention supports up to 128 bands");
+  bin_start_.assign(nb, 0);
+  dims_.assign(nb, 0);
+  kpad_.assign(nb, 0);
+  kcol_.assign(nb, 0);
+  dim_off_.assign(nb, 0);
+  out3_off_.assign(nb, 0);
+  ktot_ = sum_dims_ = sum_out3_ = 0;
+  for (int b = 0, s = 0; b < nb; ++b) {
+    bin_start_[b] = s;
+    s += nfreq_[b];
+    dims_[b] = 2 * C_ * nfreq_[b];
+    kpad_[b] = (dims_[b] + 63) / 64 * 64;
+    kcol_[b] = ktot_;
+    ktot_ += kpad_[b];
+    dim_off_[b] = sum_dims_;
+    sum_dims_ += dims_[b];
+    out3_off_[b] = sum_out3_;
+    sum_out3_ += 2 * dims_[b];
+  }
+  I.sum_band_dims = sum_dims_;
+  // contributions of every band to every bin (deterministic gather form of the scatter_add)
+  std::vector<std::vector<int>> contrib(nbins_);
+  for (int b = 0; b < nb; ++b)
+    for (int q = 0; q < nfreq_[b]; ++q) contrib[bin_list_[bin_start_[b] + q]].push_back(dim_off_[b] + q * 2 * C_);
+  std::vector<int> coff(nbins_ + 1, 0), ccol;
+  for (int f = 0; f < nbins_; ++f) {
+    coff[f + 1] = coff[f] + (int)contrib[f].size();
+    ccol.insert(ccol.end(), contrib[f].begin(), contrib[f].end());
+  }
+  d_nfreq_ = upload_i32(nfreq_);
+  d_bin_start_ = upload_i32(bin_start_);
+  d_bin_list_ = upload_i32(bin_list_);
+  d_kpad_ = upload_i32(kpad_);
+  d_kcol_ = upload_i32(kcol_);
+  d_gcol_ = upload_i32(dim_off_);
+  d_contrib_off_ = upload_i32(coff);
+  d_contrib_col_ = upload_i32(ccol);
+  d_denom_ = upload_f32(denom);
+
+  // ---- window (periodic Hann, src/ops_stft.cu:253-259)
+  {
+    std::vector<float> w(I.n_fft);
+    for (int i = 0; i < I.n_fft; ++i) w[i] = 0.5f * (1.0f - std::cos(2.0f * (float)M_PI * (float)i / (float)I.n_fft));
+    window_ = upload_f32(w);
+  }
+
+  const int D = I.dim;
+  auto mat = [&](const std::string& name, int rows, int cols) {
+    const HostTensor& t = csm.get(name);
+    MSST_REQUIRE(t.shape.size() == 2 && t.shape[0] == rows && t.shape[1] == cols, "unexpected shape for " + name);
+    return t.f32();
+  };
+  auto vec = [&](const std::string& name, int n) {
+    const HostTensor& t = csm.get(name);
+    MSST_REQUIRE((int)t.numel == n, "unexpected size for " + name);
+    return t.f32();
+  };
+
+  // ---- band split: all bands in one [D, Ktot] matrix, band b at columns kcol[b] (zero padded)
+  {
+    std::vector<float> W((size_t)D * ktot_, 0.f), bias((size_t)nb * D), gam(sum_dims_);
+    for (int b = 0; b < nb; ++b) {
+      const std::string p = "band_split.to_features." + std::to_string(b);
+      std::vector<float> g = vec(p + ".0.gamma", dims_[b]);
+      std::copy(g.begin(), g.end(), gam.begin() + dim_off_[b]);
+      std::vector<float> w = mat(p + ".1.weight", D, dims_[b]);
+      for (int r = 0; r < D; ++r)
+        std::copy(w.begin() + (size_t)r * dims_[b], w.begin() + (size_t)(r + 1) * dims_[b],
+                  W.begin() + (size_t)r * ktot_ + kcol_[b]);
+      std::vector<float> bb = vec(p + ".1.bias", D);
+      std::copy(bb.begin(), bb.end(), bias.begin() + (size_t)b * D);
+    }
+    w_bs_ = upload_16(W, bf16_);
+    b_bs_ = upload_f32(bias);
+    g_bs_ = upload_f32(gam);
+    m_wbs_ = map_2d(w_bs_.get(), D, ktot_, ktot_, pick_bn(D));
+  }
+
+  // ---- transformers
+  blocks_.clear();
+  blocks_.resize(I.depth);
+  for (int d = 0; d < I.depth; ++d) {
+    for (int axis = 0; axis < 2; ++axis) {
+      TransformerWeights& tw = axis == 0 ? blocks_[d].first : blocks_[d].second;
+      const std::string tp = "layers." + std::to_string(d) + "." + std::to_string(axis);
+      const int nl = axis == 0 ? tdepth : fdepth;
+      tw.layers.resize(nl);
+      for (int l = 0; l < nl; ++l) {
+        LayerWeights& L = tw.layers[l];
+        const std::string ap = tp + ".layers." + std::to_string(l) + ".0";
+        const std::string fp = tp + ".layers." + std::to_string(l) + ".1.net";
+        L.g_attn = upload_f32(vec(ap + ".norm.gamma", D));
+        L.wqkv = upload_16(mat(ap + ".to_qkv.weight", 3 * inner_, D), bf16_);
+        L.wg = upload_f32(mat(ap + ".to_gates.weight", I.heads, D));
+        L.bg = upload_f32(vec(ap + ".to_gates.bias", I.heads));
+        L.wout = upload_16(mat(ap + ".to_out.0.weight", D, inner_), bf16_);
+        L.g_ff = upload_f32(vec(fp + ".0.gamma", D));
+        L.w1 = upload_16(mat(fp + ".1.weight", ff_, D), bf16_);
+        L.b1 = upload_f32(vec(fp + ".1.bias", ff_));
+        L.w2 = upload_16(mat(fp + ".4.weight", D, ff_), bf16_);
+        L.b2 = upload_f32(vec(fp + ".4.bias", D));
+        L.m_wqkv = map_2d(L.wqkv.get(), 3 * inner_, D, D, pick_bn(3 * inner_));
+        L.m_wout = map_2d(L.wout.get(), D, inner_, inner_, pick_bn(D));
+        L.m_w1 = map_2d(L.w1.get(), ff_, D, D, pick_bn(ff_));
+        L.m_w2 = map_2d(L.w2.get(), D, ff_, ff_, pick_bn(D));
+      }
+      if (mel_) tw.g_final = upload_f32(vec(tp + ".norm.gamma", D));
+    }
+  }
+  if (!mel_) final_norm_ = upload_f32(vec("final_norm.gamma", D));
+
+  // ---- mask estimators: layer i of every band stacked along rows; the last
+  // layer's rows interleaved (value_j, gate_j) so the GLU pair is adjacent
+  stems_.clear();
+  stems_.resize(I.num_stems);
+  for (int s = 0; s < I.num_stems; ++s) {
+    StemWeights& sw = stems_[s];
+    for (int i = 0; i < n_lin_; ++i) {
+      const bool last = i == n_lin_ - 1;
+      const int K = i == 0 ? D : hid_;
+      const int rows_total = last ? sum_out3_ : nb * hid_;
+      std::vector<float> W((size_t)rows_total * K), bias(rows_total);
+      for (int b = 0; b < nb; ++b) {
+        const std::string p =
+            "mask_estimators." + std::to_string(s) + ".to_freqs." + std::to_string(b) + ".0." + std::to_string(2 * i);
+        const int n_out = last ? 2 * dims_[b] : hid_;
+        std::vector<float> w = mat(p + ".weight", n_out, K);
+        std::vector<float> bb = vec(p + ".bias", n_out);
+        const size_t row0 = last ? (size_t)out3_off_[b] : (size_t)b * hid_;
+        for (int r = 0; r < n_out; ++r) {
+          // GLU: first half = value, second half = gate (src/ops_elementwise.cu:321-343)
+          const int dst = last ? (r < dims_[b] ? 2 * r : 2 * (r - dims_[b]) + 1) : r;
+          std::copy(w.begin() + (size_t)r * K, w.begin() + (size_t)(r + 1) * K, W.begin() + (row0 + dst) * K);
+          bias[row0 + dst] = bb[r];
+        }
+      }
+      sw.w.push_back(upload_16(W, bf16_));
+      sw.b.push_back(upload_f32(bias));
+      sw.m.push_back(map_2d(sw.w.back().get(), rows_total, K, K, 256));
+    }
+  }
+  MSST_CUDA(cudaDeviceSynchronize());
+}
+
+// ===========================================================================
+// helpers
+// ===========================================================================
+const float* Model::rope_table(int n, bool sine) {
+  auto& tab = sine ? rope_sin_ : rope_cos_;
+  auto it = tab.find(n);
+  if (it != tab.end()) return it->second.get<float>();
+  // src/model_mel_band_roformer.cu:487-513 (fp32 on the host)
+  const int half = info_.dim_head / 2;
+  std::vector<float> c((size_t)n * half), s((size_t)n * half);
+  for (int p = 0; p < n; ++p)
+    for (int i = 0; i < half; ++i) {
+      const float freq = 1.0f / std::pow(10000.0f, (float)(2 * i) / (float)info_.dim_head);
+      const float ang = (float)p * freq;
+      c[(size_t)p * half + i] = std::cos(ang);
+      s[(size_t)p * half + i] = std::sin(ang);
+    }
+  rope_cos_[n] = upload_f32(c);
+  rope_sin_[n] = upload_f32(s);
+  return (sine ? rope_sin_[n] : rope_cos_[n]).get<float>();
+}
+
+const float* Model::istft_wsum(int T) {
+  auto it = wsum_.find(T);
+  if (it != wsum_.end()) return it->second.get<float>();
+  const int n = info_.n_fft, hop = info_.hop_length;
+  const size_t full = (size_t)n + (size_t)(T - 1) * hop;
+  std::vector<float> w(n), ws(full, 0.f);
+  for (int i = 0; i < n; ++i) w[i] = 0.5f * (1.0f - std::cos(2.0f * (float)M_PI * (float)i / (float)n));
+  for (int t = 0; t < T; ++t)
+    for (int i = 0; i < n; ++i) ws[(size_t)t * hop + i] += w[i] * w[i];
+  wsum_[T] = upload_f32(ws);
+  return wsum_[T].get<float>();
+}
+
+cufftHandle Model::fft_plan(cufftType type, int batch, cudaStream_t s) {
+  auto key = std::make_pair((int)type, batch);
+  auto it = plans_.find(key);
+  cufftHandle h;
+  if (it == plans_.end()) {
+    int n = info_.n_fft;
+    cufftResult r;
+    if (type == CUFFT_R2C)
+      r = cufftPlanMany(&h, 1, &n, nullptr, 1, n, nullptr, 1, nbins_, CUFFT_R2C, batch);
+    else
+      r = cufftPlanMany(&h, 1, &n, nullptr, 1, nbins_, nullptr, 1, n, CUFFT_C2R, batch);
+    if (r != CUFFT_SUCCESS) fail(MSST_ERR_CUDA, "cufftPlanMany failed (" + std::to_string((int)r) + ")");
+    plans_[key] = h;
+  } else {
+    h = it->second;
+  }
+  if (cufftSetStream(h, s) != CUFFT_SUCCESS) fail(MSST_ERR_CUDA, "cufftSetStream failed");
+  return h;
+}
+
+void Model::gemm(const CUtensorMap& ma, const CUtensorMap& mb, GemmParams& p, int epi, int bn, cudaStream_t s) {
+  int tiles = 0;
+  for (int i = 0; i < p.num_groups; ++i) {
+    GemmGroup& g = p.groups[i];
+    g.tiles_n = (g.n + bn - 1) / bn;
+    g.tile_begin = tiles;
+    tiles += ((g.m + kGemmBM - 1) / kGemmBM) * g.tiles_n;
+  }
+  p.total_tiles = tiles;
+  MSST_CUDA(launch_gemm(ma, mb, p, epi, bn, bf16_, num_sms_, s));
+}
+
+static GemmGroup group(int m, int n, int k, void* out, long long ldo, const float* bias) {
+  GemmGroup g{};
+  g.m = m;
+  g.n = n;
+  g.k = k;
+  g.out = out;
+  g.ldo = ldo;
+  g.out_row_mul = 1;
+  g.bias = bias;
+  return g;
+}
+
+Model::Work& Model::work(int B, int T) {
+  auto key = std::make_pair(B, T);
+  auto it = work_.find(key);
+  if (it != work_.end()) return *it->second;
+  auto w = std::make_unique<Work>();
+  const msst_model_info& I = info_;
+  const int nb = I.num_bands, D = I.dim, S = I.num_stems;
+  w->B = B;
+  w->T = T;
+  w->BT = (long long)B * T;
+  w->M = w->BT * nb;
+  const long long M = w->M;
+  w->frames.reset(sizeof(float) * (size_t)std::max(B * C_, B * S * C_) * T * I.n_fft);
+  w->spec.reset(sizeof(float2) * (size_t)B * C_ * T * nbins_);
+  w->ispec.reset(sizeof(float2) * (size_t)B * S * C_ * T * nbins_);
+  w->abs.reset(2 * (size_t)w->BT * ktot_);
+  w->x.reset(4 * (size_t)M * D);
+  w->xn.reset(2 * (size_t)M * D);
+  w->gates.reset(4 * (size_t)M * I.heads);
+  const size_t big = std::max({(size_t)M * 3 * inner_, (size_t)M * ff_, (size_t)M * hid_});
+  w->big1.reset(2 * big);
+  w->big2.reset(2 * big);
+  w->ao.reset(2 * (size_t)M * inner_);
+  w->mask.reset(4 * (size_t)S * w->BT * sum_dims_);
+  w->m_abs = map_2d(w->abs.get(), w->BT, ktot_, ktot_, kGemmBM);
+  w->m_xn = map_2d(w->xn.get(), M, D, D, kGemmBM);
+  w->m_ao = map_2d(w->ao.get(), M, inner_, inner_, kGemmBM);
+  w->m_big2_ffh = map_2d(w->big2.get(), M, ff_, ff_, kGemmBM);
+  w->m_h1 = map_2d(w->big1.get(), M, hid_, hid_, kGemmBM);
+  w->m_h2 = map_2d(w->big2.get(), M, hid_, hid_, kGemmBM);
+  {
+    const uint64_t C3 = 3 * (uint64_t)inner_;
+    const uint64_t dims[4] = {C3, (uint64_t)nb, (uint64_t)T, (uint64_t)B};
+    const uint64_t str[3] = {C3 * 2, C3 * 2 * nb, C3 * 2 * nb * T};
+    const uint32_t box[4] = {64, 1, 128, 1};
+    w->m_qkv_time = make_tensor_map(w->big1.get(), 4, dims, str, box);
+    const uint64_t dims2[4] = {C3, (uint64_t)M, 1, 1};
+    const uint64_t str2[3] = {C3 * 2, C3 * 2 * M, C3 * 2 * M};
+    const uint32_t box2[4] = {64, 128, 1, 1};
+    w->m_qkv_band = make_tensor_map(w->big1.get(), 4, dims2, str2, box2);
+  }
+  Work& ref = *w;
+  work_[key] = std::move(w);
+  return ref;
+}
+
+// ===========================================================================
+// forward pieces
+// ===========================================================================
+void Model::run_front(const float* audio, int B, long long L, int T, cudaStream_t s, Work& w) {
+  const msst_model_info& I = info_;
+  // STFT (src/ops_stft.cu:286-365) -> [B*C*T, nbins] complex
+  MSST_CUDA(launch_stft_frames(audio, L, B * C_, T, I.n_fft, I.hop_length, window_.get<float>(), w.frames.get<float>(),
+                               s));
+  if (cufftExecR2C(fft_plan(CUFFT_R2C, B * C_ * T, s), w.frames.get<cufftReal>(), w.spec.get<cufftComplex>()) !=
+      CUFFT_SUCCESS)
+    fail(MSST_ERR_CUDA, "cufftExecR2C failed");
+  // band gather + per-band RMSNorm -> A of the band-split GEMM
+  BandInArgs bi{};
+  bi.spec = w.spec.get<float2>();
+  bi.Bc = B;
+  bi.C = C_;
+  bi.T = T;
+  bi.nbins = nbins_;
+  bi.num_bands = I.num_bands;
+  bi.bin_start = d_bin_start_.get<int>();
+  bi.nfreq = d_nfreq_.get<int>();
+  bi.bin_list = d_bin_list_.get<int>();
+  bi.kcol = d_kcol_.get<int>();
+  bi.kpad = d_kpad_.get<int>();
+  bi.gcol = d_gcol_.get<int>();
+  bi.gamma = g_bs_.get<float>();
+  bi.out = w.abs.get();
+  bi.ld = ktot_;
+  MSST_CUDA(launch_band_input(bi, bf16_, s));
+  // band split: one group per band, output rows (bt*nb + band) of the residual stream
+  GemmParams p{};
+  p.num_groups = I.num_bands;
+  for (int b = 0; b < I.num_bands; ++b) {
+    GemmGroup g = group((int)w.BT, I.dim, kpad_[b], w.x.get(), I.dim, b_bs_.get<float>() + (size_t)b * I.dim);
+    g.a_col0 = kcol_[b];
+    g.b_col0 = kcol_[b];
+    g.out_row_mul = I.num_bands;
+    g.out_row_add = b;
+    p.groups[b] = g;
+  }
+  gemm(w.m_abs, m_wbs_, p, kEpiStore32, pick_bn(I.dim), s);
+}
+
+void Model::run_transformer(int d, int axis, float* x, int B, int T, const float* pending_gamma, cudaStream_t s,
+                            Work& w) {
+  const msst_model_info& I = info_;
+  const int D = I.dim, nb = I.num_bands;
+  const TransformerWeights& tw = axis == 0 ? blocks_[d].first : blocks_[d].second;
+  const long long M = (long long)B * T * nb;
+  const float scale = std::sqrt((float)D);
+  for (size_t l = 0; l < tw.layers.size(); ++l) {
+    const LayerWeights& L = tw.layers[l];
+    // attention pre-norm (+ pending final norm of the previous transformer) + gates
+    RmsNormArgs rn{};
+    rn.x = x;
+    rn.rows = M;
+    rn.D = D;
+    rn.gamma_pre = l == 0 ? pending_gamma : nullptr;
+    rn.scale_pre = scale;
+    rn.gamma = L.g_attn.get<float>();
+    rn.scale = scale;
+    rn.out16 = w.xn.get();
+    rn.wg = L.wg.get<float>();
+    rn.bg = L.bg.get<float>();
+    rn.gates = w.gates.get<float>();
+    rn.heads = I.heads;
+    MSST_CUDA(launch_rmsnorm(rn, bf16_, s));
+    // QKV + RoPE
+    {
+      GemmParams p{};
+      p.num_groups = 1;
+      p.groups[0] = group((int)M, 3 * inner_, D, w.big1.get(), 3 * inner_, nullptr);
+      p.rope_cols = 2 * inner_;
+      p.head_dim = I.dim_head;
+      if (axis == 0) {
+        p.pos_div = nb;
+        p.pos_mod = T;
+      } else {
+        p.pos_div = 1;
+        p.pos_mod = nb;
+      }
+      p.rope_cos = rope_table(p.pos_mod, false);
+      p.rope_sin = rope_table(p.pos_mod, true);
+      gemm(w.m_xn, L.m_wqkv, p, kEpiQkvRope, pick_bn(3 * inner_), s);
+    }
+    // attention (+ gate, head merge)
+    {
+      AttnParams a{};
+      a.mode = axis;
+      a.B = B;
+      a.T = T;
+      a.F = nb;
+      a.heads = I.heads;
+      a.num_tokens = (int)M;
+      a.scale_log2 = (1.0f / std::sqrt((float)I.dim_head)) * 1.4426950408889634f;
+      a.gates = w.gates.get<float>();
+      a.out = w.ao.get();
+      if (axis == 0) {
+        a.seq_len = T;
+        a.q_tiles = (T + 127) / 128;
+        a.total_items = B * nb * I.heads * a.q_tiles;
+      } else {
+        a.seq_len = nb;
+        a.seqs_per_tile = 128 / nb;
+        a.q_tiles = (int)((w.BT + a.seqs_per_tile - 1) / a.seqs_per_tile);
+        a.total_items = a.q_tiles * I.heads;
+      }
+      MSST_CUDA(launch_attention(axis == 0 ? w.m_qkv_time : w.m_qkv_band, a, bf16_, num_sms_, s));
+    }
+    // out projection + residual
+    {
+      GemmParams p{};
+      p.num_groups = 1;
+      p.groups[0] = group((int)M, D, inner_, x, D, nullptr);
+      gemm(w.m_ao, L.m_wout, p, kEpiResid32, pick_bn(D), s);
+    }
+    // feed-forward
+    RmsNormArgs rf{};
+    rf.x = x;
+    rf.rows = M;
+    rf.D = D;
+    rf.gamma = L.g_ff.get<float>();
+    rf.scale = scale;
+    rf.out16 = w.xn.get();
+    MSST_CUDA(launch_rmsnorm(rf, bf16_, s));
+    {
+      GemmParams p{};
+      p.num_groups = 1;
+      p.act = kActGelu;
+      p.groups[0] = group((int)M, ff_, D, w.big2.get(), ff_, L.b1.get<float>());
+      gemm(w.m_xn, L.m_w1, p, kEpiStore16, pick_bn(ff_), s);
+    }
+    {
+      GemmParams p{};
+      p.num_groups = 1;
+      p.groups[0] = group((int)M, D, ff_, x, D, L.b2.get<float>());
+      gemm(w.m_big2_ffh, L.m_w2, p, kEpiResid32, pick_bn(D), s);
+    }
+  }
+}
+
+void Model::run_trunk(int B, int T, cudaStream_t s, Work& w) {
+  const msst_model_info& I = info_;
+  const float* pending = nullptr;
+  for (int d = 0; d < I.depth; ++d) {
+    for (int axis = 0; axis < 2; ++axis) {
+      run_transformer(d, axis, w.x.get<float>(), B, T, pending, s, w);
+      const TransformerWeights& tw = axis == 0 ? blocks_[d].first : blocks_[d].second;
+      pending = mel_ ? tw.g_final.get<float>() : nullptr;
+    }
+  }
+  // final norm (MelBandRoformer: last transformer's norm_output; BSRoformer:
+  // final_norm, src/model_bs_roformer.cu:536-539) -> band-major 16-bit input of
+  // the mask estimators
+  RmsNormArgs rn{};
+  rn.x = w.x.get<float>();
+  rn.rows = w.M;
+  rn.D = I.dim;
+  rn.gamma = mel_ ? pending : final_norm_.get<float>();
+  rn.scale = std::sqrt((float)I.dim);
+  rn.out16 = w.xn.get();
+  rn.band_major = 1;
+  rn.F = I.num_bands;
+  MSST_CUDA(launch_rmsnorm(rn, bf16_, s));
+}
+
+void Model::run_masks(int B, int T, cudaStream_t s, Work& w, float* masks_out) {
+  const msst_model_info& I = info_;
+  const int nb = I.num_bands, D = I.dim;
+  const int BT = (int)w.BT;
+  for (int st = 0; st < I.num_stems; ++st) {
+    const StemWeights& sw = stems_[st];
+    float* mask = masks_out + (size_t)st * w.BT * sum_dims_;
+    for (int i = 0; i < n_lin_; ++i) {
+      const bool last = i == n_lin_ - 1;
+      const CUtensorMap& ma = i == 0 ? w.m_xn : ((i - 1) % 2 == 0 ? w.m_h1 : w.m_h2);
+      void* hout = (i % 2 == 0) ? w.big1.get() : w.big2.get();
+      const int K = i == 0 ? D : hid_;
+      GemmParams p{};
+      p.num_groups = nb;
+      p.act = kActTanh;
+      for (int b = 0; b < nb; ++b) {
+        GemmGroup g;
+        if (last) {
+          g = group(BT, 2 * dims_[b], K, mask, sum_dims_, sw.b[i].get<float>() + out3_off_[b]);
+          g.b_row0 = out3_off_[b];
+          g.out_col0 = dim_off_[b];
+        } else {
+          g = group(BT, hid_, K, hout, hid_, sw.b[i].get<float>() + (size_t)b * hid_);
+          g.b_row0 = b * hid_;
+          g.out_row_add = (long long)b * BT;
+        }
+        g.a_row0 = b * BT;
+        p.groups[b] = g;
+      }
+      gemm(ma, sw.m[i], p, last ? kEpiGlu32 : kEpiStore16, 256, s);
+    }
+  }
+  (void)B;
+  (void)T;
+}
+
+void Model::forward(const float* audio, int B, int C, long long L, float* out, cudaStream_t s) {
+  const msst_model_info& I = info_;
+  MSST_REQUIRE(C == C_, "channel count does not match the model (stereo=" + std::to_string(C_ == 2) + ")");
+  MSST_REQUIRE(B >= 1 && L > I.n_fft / 2, "audio too short");
+  const int T = (int)(L / I.hop_length + 1);
+  Work& w = work(B, T);
+  run_front(audio, B, L, T, s, w);
+  run_trunk(B, T, s, w);
+  run_masks(B, T, s, w, w.mask.get<float>());
+  // mask merge + complex multiply + zero DC -> C2R input
+  MaskApplyArgs ma{};
+  ma.spec = w.spec.get<float2>();
+  ma.mask = w.mask.get<float>();
+  ma.mask_stem_stride = w.BT * sum_dims_;
+  ma.mask_ld = sum_dims_;
+  ma.contrib_off = d_contrib_off_.get<int>();
+  ma.contrib_col = d_contrib_col_.get<int>();
+  ma.denom = d_denom_.get<float>();
+  ma.out = w.ispec.get<float2>();
+  ma.Bc = B;
+  ma.S = I.num_stems;
+  ma.C = C_;
+  ma.T = T;
+  ma.nbins = nbins_;
+  ma.zero_dc = zero_dc_ ? 1 : 0;
+  MSST_CUDA(launch_mask_apply(ma, s));
+  // iSTFT (src/ops_stft.cu:371-489)
+  const int BSC = B * I.num_stems * C_;
+  if (cufftExecC2R(fft_plan(CUFFT_C2R, BSC * T, s), w.ispec.get<cufftComplex>(), w.frames.get<cufftReal>()) !=
+      CUFFT_SUCCESS)
+    fail(MSST_ERR_CUDA, "cufftExecC2R failed");
+  MSST_CUDA(launch_istft_ola(w.frames.get<float>(), BSC, T, I.n_fft, I.hop_length, window_.get<float>(),
+                             istft_wsum(T), out, s));
+}
+
+void Model::masks(const float* audio, int B, int C, long long L, float* masks_out, cudaStream_t s) {
+  const msst_model_info& I = info_;
+  MSST_REQUIRE(C == C_, "channel count does not match the model");
+  const int T = (int)(L / I.hop_length + 1);
+  Work& w = work(B, T);
+  run_front(audio, B, L, T, s, w);
+  run_trunk(B, T, s, w);
+  run_masks(B, T, s, w, masks_out);
+}
+
+void Model::transformer(int d, int axis, float* x, int B, int T, cudaStream_t s) {
+  MSST_REQUIRE(d >= 0 && d < info_.depth && (axis == 0 || axis == 1), "bad depth index or axis");
+  Work& w = work(B, T);
+  run_transformer(d, axis, x, B, T, nullptr, s, w);
+  if (mel_) {
+    const TransformerWeights& tw = axis == 0 ? blocks_[d].first : blocks_[d].second;
+    RmsNormArgs rn{};
+    rn.x = x;
+    rn.rows = (long long)B * T * info_.num_bands;
+    rn.D = info_.dim;
+    rn.gamma_pre = tw.g_final.get<float>();
+    rn.scale_pre = std::sqrt((float)info_.dim);
+    MSST_CUDA(launch_rmsnorm(rn, bf16_, s));
+  }
+}
+
+// ===========================================================================
+// chunked separation (src/inference_app.cpp:59-70,100-324)
+// ===========================================================================
+void Model::chunk_plan(long long L, float overlap, int* chunk, int* step, long long* border, long long* total,
+                       int* num_chunks) const {
+  const int cs = info_.chunk_size;
+  int st;
+  if (overlap > 0.0f && overlap < 1.0f) {
+    st = std::max(1, (int)std::lround(cs * (1.0f - overlap)));
+  } else {
+    int n = info_.num_overlap;
+    if (overlap >= 1.0f) n = std::max(1, (int)std::lround(overlap));
+    st = std::max(1, cs / std::max(1, n));
+  }
+  long long b = cs - st;
+  const bool padded = L > 2 * b && b > 0;
+  if (!padded) b = 0;
+  const long long tot = L + 2 * b;
+  *chunk = cs;
+  *step = st;
+  *border = b;
+  *total = tot;
+  *num_chunks = (int)((tot + st - 1) / st);
+}
+
+void Model::separate(const float* track, int C, long long L, float overlap, int chunk_batch, int flags, float* out,
+                     cudaStream_t s) {
+  const msst_model_info& I = info_;
+  MSST_REQUIRE(C == C_, "channel count does not match the model");
+  const int S = I.num_stems;
+  if (I.chunk_size <= 0 || L <= I.chunk_size) {
+    // short input: one forward over the whole track (src/inference_app.cpp:463-472)
+    MSST_REQUIRE(L % I.hop_length == 0, "whole-track forward needs length % hop_length == 0");
+    forward(track, 1, C, L, out, s);
+    return;
+  }
+  int chunk, step, nchunks;
+  long long border, total;
+  chunk_plan(L, overlap, &chunk, &step, &border, &total, &nchunks);
+  MSST_REQUIRE(chunk % I.hop_length == 0, "chunk_size must be a multiple of hop_length");
+  const int eb = std::max(1, std::min(chunk_batch > 0 ? chunk_batch : 2, nchunks));
+  ChunkArgs ci{};
+  ci.track = track;
+  ci.C = C;
+  ci.L = L;
+  ci.border = border;
+  ci.total = total;
+  ci.chunk = chunk;
+  ci.step = step;
+  ci.ref_compat = (flags & MSST_SEPARATE_FIX_TAIL_PADDING) ? 0 : 1;
+  ChunkArgs co = ci;
+  co.C = S * C;
+  const int T = chunk / I.hop_length + 1;
+  Work& w = work(eb, T);
+  w.chunk_in.ensure(sizeof(float) * (size_t)eb * C * chunk);
+  w.chunk_out.ensure(sizeof(float) * (size_t)eb * S * C * chunk);
+  DeviceBuffer acc(sizeof(float) * (size_t)(S * C + 1) * total);
+  float* d_acc = acc.get<float>();
+  float* d_wsum = d_acc + (size_t)S * C * total;
+  MSST_CUDA(cudaMemsetAsync(d_acc, 0, acc.bytes(), s));
+  for (int g0 = 0; g0 < nchunks; g0 += eb) {
+    const int cnt = std::min(eb, nchunks - g0);
+    MSST_CUDA(launch_chunk_gather(ci, g0, cnt, w.chunk_in.get<float>(), s));
+    forward(w.chunk_in.get<float>(), cnt, C, chunk, w.chunk_out.get<float>(), s);
+    MSST_CUDA(launch_chunk_ola(co, g0, cnt, nchunks, w.chunk_out.get<float>(), d_acc, d_wsum, s));
+  }
+  MSST_CUDA(launch_chunk_finish(co, d_acc, d_wsum, out, s));
+  MSST_CUDA(cudaStreamSynchronize(s));
+}
+
+}  // namespace msst

@@ -1,0 +1,93 @@
+// model.h — the Roformer model driver of libmsst_b200 (host side, C++17).
+//
+// Mirrors the reference drivers' public surface (load / forward, reference
+// src/model_mel_band_roformer.h:36-46, src/model_bs_roformer.h) and the app
+// layer's chunked inference (src/inference_app.cpp:100-324), re-pointed at the
+// sm_100a kernels of this library.
+#pragma once
+
+#include <cufft.h>
+
+#include <map>
+#include <memory>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "gemm.cuh"
+#include "runtime.h"
+
+namespace msst {
+
+struct LayerWeights {
+  DeviceBuffer g_attn, wqkv, wg, bg, wout;   // attention (norm gamma, W_qkv, gate W/b, W_out)
+  DeviceBuffer g_ff, w1, b1, w2, b2;         // feed-forward
+  CUtensorMap m_wqkv, m_wout, m_w1, m_w2;
+};
+
+struct TransformerWeights {
+  std::vector<LayerWeights> layers;
+  DeviceBuffer g_final;  // MelBandRoformer only (norm_output)
+};
+
+struct StemWeights {
+  std::vector<DeviceBuffer> w, b;  // per MLP layer, all bands concatenated along rows
+  std::vector<CUtensorMap> m;
+};
+
+class Model {
+ public:
+  void load(const std::string& path, int device, int precision);
+  const msst_model_info& info() const { return info_; }
+  int device() const { return device_; }
+
+  void forward(const float* audio, int B, int C, long long L, float* out, cudaStream_t s);
+  void masks(const float* audio, int B, int C, long long L, float* masks_out, cudaStream_t s);
+  void transformer(int depth_index, int axis, float* x, int B, int T, cudaStream_t s);
+  void separate(const float* track, int C, long long L, float overlap, int chunk_batch, int flags, float* out,
+                cudaStream_t s);
+  void chunk_plan(long long L, float overlap, int* chunk, int* step, long long* border, long long* total,
+                  int* num_chunks) const;
+
+ private:
+  struct Work;  // per-(B, T) workspace
+  Work& work(int B, int T);
+  void run_trunk(int B, int T, cudaStream_t s, Work& w);
+  void run_front(const float* audio, int B, long long L, int T, cudaStream_t s, Work& w);
+  void run_masks(int B, int T, cudaStream_t s, Work& w, float* masks_out);
+  void run_transformer(int d, int axis, float* x, int B, int T, const float* pending_gamma, cudaStream_t s, Work& w);
+  void gemm(const CUtensorMap& ma, const CUtensorMap& mb, GemmParams& p, int epi, int bn, cudaStream_t s);
+  const float* rope_table(int n, bool sine);
+  const float* istft_wsum(int T);
+  cufftHandle fft_plan(cufftType type, int batch, cudaStream_t s);
+
+  msst_model_info info_{};
+  int device_ = 0;
+  int bf16_ = 0;
+  bool mel_ = true;
+  int C_ = 2, nbins_ = 1025, hid_ = 1536, n_lin_ = 3, inner_ = 512, ff_ = 1536;
+  bool zero_dc_ = true;
+  int num_sms_ = 148;
+
+  std::vector<int> nfreq_, bin_start_, bin_list_, dims_, kpad_, kcol_, dim_off_, out3_off_;
+  int ktot_ = 0, sum_dims_ = 0, sum_out3_ = 0;
+  DeviceBuffer d_nfreq_, d_bin_start_, d_bin_list_, d_kpad_, d_kcol_, d_gcol_;
+  DeviceBuffer d_contrib_off_, d_contrib_col_, d_denom_;
+
+  DeviceBuffer w_bs_, b_bs_, g_bs_;
+  CUtensorMap m_wbs_;
+  std::vector<std::pair<TransformerWeights, TransformerWeights>> blocks_;  // (time, band) per depth
+  DeviceBuffer final_norm_;                                                  // BSRoformer
+  std::vector<StemWeights> stems_;
+  DeviceBuffer window_;
+
+  std::map<int, DeviceBuffer> rope_cos_, rope_sin_, wsum_;
+  std::map<std::pair<int, int>, cufftHandle> plans_;
+  std::map<std::pair<int, int>, std::unique_ptr<Work>> work_;
+
+ public:
+  Model();
+  ~Model();
+};
+
+}  // namespace msst

@@ -1,0 +1,315 @@
+"""msst_b200 — Python host layer over libmsst_b200 (B200 / sm_100a).
+
+Mirrors the reference's Python binding `cudasep.Separator`
+(reference src/python_bindings.cpp:80-217: Separator(model_path, device),
+separate_tensor, separate_file, sample_rate, num_sources, model_type) on top of
+the C ABI declared in include/msst_b200.h, and exposes the op-level entry points
+for torch CUDA tensors.  There is no CPU fallback: everything runs through the
+CUDA library, and importing the bindings fails loudly when it is not built.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import wave
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libmsst_b200.so")
+
+MSST_OK, MSST_ERR_INVALID, MSST_ERR_CUDA, MSST_ERR_IO, MSST_ERR_UNSUPPORTED, MSST_ERR_DEVICE = range(6)
+F16, BF16 = 0, 1
+EPI = {"store16": 0, "resid32": 1, "store32": 2, "glu32": 3}
+ACT = {"none": 0, "gelu": 1, "tanh": 2, "sigmoid": 3}
+AXIS = {"time": 0, "band": 1}
+SEPARATE_FIX_TAIL_PADDING = 1
+
+EXPORTS = [
+    "msst_last_error", "msst_device_error", "msst_version", "msst_rmsnorm", "msst_gemm", "msst_gemm_qkv_rope",
+    "msst_attention", "msst_model_load", "msst_model_free", "msst_model_get_info", "msst_model_forward",
+    "msst_model_masks", "msst_model_transformer", "msst_model_separate", "msst_model_separate_host",
+    "msst_model_chunk_plan",
+]
+
+
+class MsstError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"[msst error {code}] {msg}")
+        self.code = code
+
+
+class ModelInfo(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in (
+        "model_type", "dim", "depth", "heads", "dim_head", "num_bands", "num_stems", "channels", "n_fft",
+        "hop_length", "sample_rate", "chunk_size", "num_overlap", "sum_band_dims", "precision")]
+
+    def as_dict(self):
+        return {n: getattr(self, n) for n, _ in self._fields_}
+
+
+_lib = None
+
+
+def lib():
+    """Load libmsst_b200.so (build it first with cuda-msst-infer_b200/build.py)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is not built; run `python cuda-msst-infer_b200/build.py`")
+    L = ctypes.CDLL(LIB_PATH)
+    vp, i64, c_int, c_float = ctypes.c_void_p, ctypes.c_longlong, ctypes.c_int, ctypes.c_float
+    fp = ctypes.POINTER(ctypes.c_float)
+    L.msst_last_error.restype = ctypes.c_char_p
+    L.msst_device_error.restype = ctypes.c_uint
+    L.msst_device_error.argtypes = [c_int]
+    L.msst_rmsnorm.argtypes = [vp, i64, c_int, vp, c_float, c_int, vp, vp, vp, c_int, vp, vp]
+    L.msst_gemm.argtypes = [vp, i64, c_int, i64, vp, c_int, vp, c_int, c_int, c_int, vp, i64, vp]
+    L.msst_gemm_qkv_rope.argtypes = [vp, i64, c_int, vp, c_int, vp, vp, c_int, c_int, c_int, vp, vp]
+    L.msst_attention.argtypes = [vp, c_int, c_int, c_int, c_int, c_int, c_float, vp, c_int, vp, vp]
+    L.msst_model_load.argtypes = [ctypes.c_char_p, c_int, c_int, ctypes.POINTER(vp)]
+    L.msst_model_free.argtypes = [vp]
+    L.msst_model_free.restype = None
+    L.msst_model_get_info.argtypes = [vp, ctypes.POINTER(ModelInfo)]
+    L.msst_model_forward.argtypes = [vp, vp, c_int, c_int, i64, vp, vp]
+    L.msst_model_masks.argtypes = [vp, vp, c_int, c_int, i64, vp, vp]
+    L.msst_model_transformer.argtypes = [vp, c_int, c_int, vp, c_int, c_int, vp]
+    L.msst_model_separate.argtypes = [vp, vp, c_int, i64, c_float, c_int, c_int, vp, vp]
+    L.msst_model_separate_host.argtypes = [vp, fp, c_int, i64, c_float, c_int, c_int, fp]
+    L.msst_model_chunk_plan.argtypes = [vp, i64, c_float, ctypes.POINTER(c_int), ctypes.POINTER(c_int),
+                                        ctypes.POINTER(i64), ctypes.POINTER(i64), ctypes.POINTER(c_int)]
+    _lib = L
+    return L
+
+
+def check(rc: int) -> None:
+    if rc != MSST_OK:
+        raise MsstError(rc, lib().msst_last_error().decode(errors="replace"))
+
+
+def device_error(clear: bool = True) -> int:
+    return int(lib().msst_device_error(1 if clear else 0))
+
+
+# --------------------------------------------------------------------------- torch helpers
+def _torch():
+    import torch
+    return torch
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _stream(stream=None):
+    torch = _torch()
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def _dtype_code(dt) -> int:
+    torch = _torch()
+    if dt == torch.float16:
+        return F16
+    if dt == torch.bfloat16:
+        return BF16
+    raise ValueError(f"16-bit dtype expected, got {dt}")
+
+
+class ops:
+    """Op-level entry points on torch CUDA tensors (launched on the current stream)."""
+
+    @staticmethod
+    def rmsnorm(x, gamma, scale, dtype=None, wg=None, bg=None):
+        torch = _torch()
+        dtype = dtype or torch.float16
+        x = x.contiguous()
+        D = x.shape[-1]
+        rows = x.numel() // D
+        out = torch.empty(x.shape, dtype=dtype, device=x.device)
+        gates = None
+        heads = 0
+        if wg is not None:
+            heads = wg.shape[0]
+            gates = torch.empty(x.shape[:-1] + (heads,), dtype=torch.float32, device=x.device)
+        check(lib().msst_rmsnorm(_ptr(x), rows, D, _ptr(gamma.contiguous()), float(scale), _dtype_code(dtype),
+                                 _ptr(out), _ptr(wg.contiguous()) if wg is not None else None,
+                                 _ptr(bg.contiguous()) if bg is not None else None, heads, _ptr(gates), _stream()))
+        return out, gates
+
+    @staticmethod
+    def gemm(x, w, bias=None, epilogue="store16", act="none", out=None):
+        torch = _torch()
+        K = x.shape[-1]
+        rows = x.numel() // K
+        N = w.shape[0]
+        epi = EPI[epilogue]
+        if out is None:
+            if epi == EPI["store16"]:
+                out = torch.empty(x.shape[:-1] + (N,), dtype=x.dtype, device=x.device)
+            elif epi == EPI["glu32"]:
+                out = torch.empty(x.shape[:-1] + (N // 2,), dtype=torch.float32, device=x.device)
+            else:
+                out = torch.zeros(x.shape[:-1] + (N,), dtype=torch.float32, device=x.device)
+        ldo = out.shape[-1]
+        check(lib().msst_gemm(_ptr(x), rows, K, x.stride(-2) if x.dim() > 1 else K, _ptr(w.contiguous()), N,
+                              _ptr(bias.contiguous()) if bias is not None else None, epi, ACT[act],
+                              _dtype_code(x.dtype), _ptr(out), ldo, _stream()))
+        return out
+
+    @staticmethod
+    def gemm_qkv_rope(x, w, heads, cos, sin, pos_div, pos_mod):
+        torch = _torch()
+        K = x.shape[-1]
+        rows = x.numel() // K
+        out = torch.empty((rows, 3 * heads * 64), dtype=x.dtype, device=x.device)
+        check(lib().msst_gemm_qkv_rope(_ptr(x.contiguous()), rows, K, _ptr(w.contiguous()), heads,
+                                       _ptr(cos.contiguous()), _ptr(sin.contiguous()), pos_div, pos_mod,
+                                       _dtype_code(x.dtype), _ptr(out), _stream()))
+        return out
+
+    @staticmethod
+    def attention(qkv, B, T, F, heads, axis, scale, gates=None):
+        torch = _torch()
+        out = torch.empty((B * T * F, heads * 64), dtype=qkv.dtype, device=qkv.device)
+        check(lib().msst_attention(_ptr(qkv.contiguous()), B, T, F, heads, AXIS[axis] if isinstance(axis, str) else axis,
+                                   float(scale), _ptr(gates.contiguous()) if gates is not None else None,
+                                   _dtype_code(qkv.dtype), _ptr(out), _stream()))
+        return out
+
+
+class Model:
+    """A loaded Roformer (.csm) on one GPU."""
+
+    def __init__(self, path: str, device: int = 0, precision: str = "fp16"):
+        self._h = ctypes.c_void_p()
+        prec = {"fp16": F16, "bf16": BF16}[precision]
+        check(lib().msst_model_load(os.fsencode(path), device, prec, ctypes.byref(self._h)))
+        info = ModelInfo()
+        check(lib().msst_model_get_info(self._h, ctypes.byref(info)))
+        self.info = info.as_dict()
+        self.device = device
+
+    def close(self):
+        if getattr(self, "_h", None) and self._h.value:
+            lib().msst_model_free(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def out_length(self, length: int) -> int:
+        return (length // self.info["hop_length"]) * self.info["hop_length"]
+
+    def forward(self, audio, stream=None):
+        """audio: torch CUDA fp32 [B, C, L] -> [B, S, C, L'] (S dim squeezed when S == 1)."""
+        torch = _torch()
+        audio = audio.contiguous()
+        B, C, L = audio.shape
+        S = self.info["num_stems"]
+        out = torch.empty((B, S, C, self.out_length(L)), dtype=torch.float32, device=audio.device)
+        check(lib().msst_model_forward(self._h, _ptr(audio), B, C, L, _ptr(out), _stream(stream)))
+        return out[:, 0] if S == 1 else out
+
+    def masks(self, audio, stream=None):
+        torch = _torch()
+        audio = audio.contiguous()
+        B, C, L = audio.shape
+        T = L // self.info["hop_length"] + 1
+        out = torch.empty((B, self.info["num_stems"], T, self.info["sum_band_dims"]), dtype=torch.float32,
+                          device=audio.device)
+        check(lib().msst_model_masks(self._h, _ptr(audio), B, C, L, _ptr(out), _stream(stream)))
+        return out
+
+    def transformer(self, depth_index: int, axis, x, stream=None):
+        """Apply one axial transformer in place to x fp32 [B, T, bands, dim]."""
+        B, T = x.shape[0], x.shape[1]
+        check(lib().msst_model_transformer(self._h, depth_index, AXIS[axis] if isinstance(axis, str) else axis,
+                                           _ptr(x), B, T, _stream(stream)))
+        return x
+
+    def chunk_plan(self, length: int, overlap: float = 0.0):
+        c, s, n = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        b, t = ctypes.c_longlong(), ctypes.c_longlong()
+        check(lib().msst_model_chunk_plan(self._h, length, overlap, ctypes.byref(c), ctypes.byref(s),
+                                          ctypes.byref(b), ctypes.byref(t), ctypes.byref(n)))
+        return dict(chunk_size=c.value, step=s.value, border=b.value, padded_length=t.value, num_chunks=n.value)
+
+    def separate(self, track, overlap: float = 0.0, chunk_batch: int = 0, fix_tail_padding: bool = False,
+                 out=None, stream=None):
+        """Chunked separation of a torch CUDA fp32 [C, L] track -> [S, C, L] (S squeezed when 1)."""
+        torch = _torch()
+        track = track.contiguous()
+        C, L = track.shape
+        S = self.info["num_stems"]
+        if out is None:
+            out = torch.empty((S, C, L), dtype=torch.float32, device=track.device)
+        check(lib().msst_model_separate(self._h, _ptr(track), C, L, overlap, chunk_batch,
+                                        SEPARATE_FIX_TAIL_PADDING if fix_tail_padding else 0, _ptr(out),
+                                        _stream(stream)))
+        return out[0] if S == 1 else out
+
+    def separate_host(self, track: np.ndarray, overlap: float = 0.0, chunk_batch: int = 0,
+                      fix_tail_padding: bool = False, out: np.ndarray | None = None) -> np.ndarray:
+        """Chunked separation of a host float32 [C, L] array (copies included)."""
+        track = np.ascontiguousarray(track, dtype=np.float32)
+        C, L = track.shape
+        S = self.info["num_stems"]
+        if out is None:
+            out = np.empty((S, C, L), np.float32)
+        fp = ctypes.POINTER(ctypes.c_float)
+        check(lib().msst_model_separate_host(self._h, track.ctypes.data_as(fp), C, L, overlap, chunk_batch,
+                                             SEPARATE_FIX_TAIL_PADDING if fix_tail_padding else 0,
+                                             out.ctypes.data_as(fp)))
+        return out[0] if S == 1 else out
+
+
+class Separator:
+    """Drop-in for the reference's `cudasep.Separator` (src/python_bindings.cpp:80-217)."""
+
+    def __init__(self, model_path: str, device: int = 0, precision: str = "fp16"):
+        self._model = Model(model_path, device, precision)
+        self.device = device
+
+    @property
+    def sample_rate(self) -> int:
+        return self._model.info["sample_rate"]
+
+    @property
+    def num_sources(self) -> int:
+        return self._model.info["num_stems"]
+
+    @property
+    def model_type(self) -> str:
+        return {1: "MelBandRoformer", 2: "BSRoformer"}.get(self._model.info["model_type"], "Unknown")
+
+    def separate_tensor(self, audio: np.ndarray, stem: int = -1) -> np.ndarray:
+        """numpy [C, L] -> [S, C, L'] or [C, L'] (one whole-input forward, like the reference)."""
+        torch = _torch()
+        a = np.ascontiguousarray(audio, dtype=np.float32)
+        if a.ndim == 1:
+            a = a[None]
+        x = torch.from_numpy(a).to(f"cuda:{self.device}")[None]
+        y = self._model.forward(x)
+        torch.cuda.synchronize(self.device)
+        y = y.cpu().numpy()[0]
+        if self.num_sources > 1 and 0 <= stem < self.num_sources:
+            return y[stem]
+        return y
+
+    def separate_file(self, audio_path: str, stem: int = -1) -> np.ndarray:
+        """16-bit PCM WAV file -> separated numpy array (whole-input forward)."""
+        with wave.open(audio_path, "rb") as w:
+            ch, width, n = w.getnchannels(), w.getsampwidth(), w.getnframes()
+            if width != 2:
+                raise ValueError("only 16-bit PCM WAV is supported")
+            data = np.frombuffer(w.readframes(n), dtype="<i2").astype(np.float32) / 32768.0
+        return self.separate_tensor(data.reshape(n, ch).T, stem)
+
+
+def load_model(model_path: str, device: int = 0, precision: str = "fp16") -> Separator:
+    return Separator(model_path, device, precision)

@@ -1,0 +1,154 @@
+/*
+ * msst_b200.h — C ABI of libmsst_b200, a B200-native (sm_100a) implementation of
+ * the Roformer transformer stack of HuanLinOTO/CUDA-MSST-Infer
+ * (MelBandRoformer and BS-Roformer: band split, axial time/band transformers,
+ * mask estimators, mask merge).
+ *
+ * Conventions (all entry points):
+ *   - plain pointers and sizes, no C++ types; device pointers unless named *_host
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream)
+ *   - return MSST_OK (0) or an MSST_ERR_* code; msst_last_error() gives the
+ *     message of the calling thread's last failure.  The reference throws
+ *     std::runtime_error for the same conditions (src/tensor.h:28-34); its C++
+ *     call sites get that behaviour back from a thin wrapper that throws on a
+ *     non-zero status.
+ *   - 16-bit operands are fp16 (MSST_F16) or bf16 (MSST_BF16); accumulation is
+ *     fp32; the residual stream and all model inputs/outputs are fp32.
+ *   - K (the reduction length) of every GEMM is a multiple of 64; hidden sizes
+ *     of the Roformer (dim, heads*64, 4*dim) satisfy this, band inputs are padded.
+ *   - head_dim is 64.
+ */
+#ifndef MSST_B200_H
+#define MSST_B200_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MSST_OK 0
+#define MSST_ERR_INVALID 1     /* bad argument or unsupported shape            */
+#define MSST_ERR_CUDA 2        /* CUDA runtime / cuFFT / driver error          */
+#define MSST_ERR_IO 3          /* cannot read or parse a .csm file             */
+#define MSST_ERR_UNSUPPORTED 4 /* model feature outside this implementation    */
+#define MSST_ERR_DEVICE 5      /* a kernel's bounded wait gave up (see msst_device_error) */
+
+#define MSST_F16 0
+#define MSST_BF16 1
+
+/* GEMM epilogues */
+#define MSST_EPI_STORE16 0 /* out16 = act(x W^T + b)                               */
+#define MSST_EPI_RESID32 1 /* out32 += x W^T + b   (residual add)                  */
+#define MSST_EPI_STORE32 2 /* out32  = x W^T + b                                   */
+#define MSST_EPI_GLU32 3   /* out32[j] = y[2j] * sigmoid(y[2j+1]), y = x W^T + b    */
+
+#define MSST_ACT_NONE 0
+#define MSST_ACT_GELU 1    /* erf form, src/ops_fused.cu:21-24 */
+#define MSST_ACT_TANH 2
+#define MSST_ACT_SIGMOID 3
+
+#define MSST_AXIS_TIME 0
+#define MSST_AXIS_BAND 1
+
+/* msst_model_separate flags */
+#define MSST_SEPARATE_FIX_TAIL_PADDING 1 /* pad the final short chunk from each channel's own
+                                            samples instead of reproducing the reference's
+                                            contiguous-source read (src/tensor.cu:377-405) */
+
+typedef struct msst_model msst_model;
+
+typedef struct msst_model_info {
+  int model_type; /* 1 MelBandRoformer, 2 BSRoformer (app::ModelType order) */
+  int dim, depth, heads, dim_head, num_bands, num_stems, channels;
+  int n_fft, hop_length, sample_rate, chunk_size, num_overlap;
+  int sum_band_dims; /* width of one mask row, sum over bands of 2*channels*freqs */
+  int precision;     /* MSST_F16 or MSST_BF16 */
+} msst_model_info;
+
+const char* msst_last_error(void);
+/* Code recorded by a kernel whose bounded wait gave up (0 = none); clear != 0 resets it. */
+unsigned msst_device_error(int clear);
+int msst_version(void);
+
+/* ---------------------------------------------------------------- op level -- */
+
+/* RMSNorm of the reference, y = x * rsqrt(sum(x^2) + 1e-12) * gamma * scale
+ * (replaces ops::rms_norm, src/ops_norm.cu:455-491).  x fp32 [rows, D]
+ * (D % 128 == 0, D <= 1024) -> out16 [rows, D].  If wg != NULL also writes
+ * gates[rows, heads] = sigmoid(y wg^T + bg) (the attention gate projection,
+ * ops::linear_sigmoid at src/model_mel_band_roformer.cu:575). */
+int msst_rmsnorm(const float* x, long long rows, int D, const float* gamma, float scale, int dtype, void* out16,
+                 const float* wg, const float* bg, int heads, float* gates, void* stream);
+
+/* out = epilogue(x W^T + b): x 16-bit [rows, K] (row stride ldx elements),
+ * W 16-bit [N, K], bias fp32 [N] or NULL.  out is 16-bit for MSST_EPI_STORE16,
+ * fp32 otherwise, row stride ldo.  Replaces ops::linear / linear_no_bias /
+ * linear_gelu / linear_sigmoid (src/ops_linear.cu:150,349, src/ops_fused.cu:264,285)
+ * and the residual Tensor::add_ (src/tensor.cu:1439). */
+int msst_gemm(const void* x, long long rows, int K, long long ldx, const void* w, int N, const float* bias,
+              int epilogue, int act, int dtype, void* out, long long ldo, void* stream);
+
+/* QKV projection with the rotary embedding fused into the epilogue: qkv16
+ * [rows, 3*heads*64] = x W^T with interleaved-pair rotation of the q and k
+ * columns at position (row / pos_div) % pos_mod, tables cos/sin [pos_mod, 32]
+ * (replaces linear_no_bias + split_qkv_heads + apply_rotary_emb,
+ * src/model_mel_band_roformer.cu:540-559, src/ops_misc.cu:39-131). */
+int msst_gemm_qkv_rope(const void* x, long long rows, int K, const void* w, int heads, const float* cos_tab,
+                       const float* sin_tab, int pos_div, int pos_mod, int dtype, void* qkv16, void* stream);
+
+/* Axial attention over a fused QKV buffer [B*T*F tokens, 3*heads*64] in
+ * [B, T, F] token order: axis MSST_AXIS_TIME attends over t for every (b, f),
+ * MSST_AXIS_BAND over f for every (b, t).  softmax(scale * q k^T) v, multiplied by
+ * gates[token, head] when gates != NULL, heads merged: out16 [tokens, heads*64].
+ * Replaces ops::scaled_dot_product_attention (src/ops_attention.cu:522-599) and
+ * apply_gates_and_merge_heads (src/model_mel_band_roformer.cu:94-163). */
+int msst_attention(const void* qkv16, int B, int T, int F, int heads, int axis, float scale, const float* gates,
+                   int dtype, void* out16, void* stream);
+
+/* ------------------------------------------------------------- model level -- */
+
+/* Load a .csm model (format: src/weights.h:83-96) onto `device` with 16-bit
+ * operands of type `precision` (replaces app::load_model,
+ * src/inference_app.cpp:363-441, and the drivers' load(),
+ * src/model_mel_band_roformer.cu:319-481, src/model_bs_roformer.cu:94-199). */
+int msst_model_load(const char* path, int device, int precision, msst_model** out);
+void msst_model_free(msst_model* m);
+int msst_model_get_info(const msst_model* m, msst_model_info* info);
+
+/* Whole forward pass on device buffers: audio [batch, channels, length] fp32 ->
+ * out [batch, num_stems, channels, (length/hop)*hop] fp32 (the stem axis is
+ * absent from the reference's shape when num_stems == 1; the memory layout is
+ * the same).  Replaces MelBandRoformer::forward / BSRoformer::forward
+ * (src/model_mel_band_roformer.cu:744, src/model_bs_roformer.cu:420). */
+int msst_model_forward(msst_model* m, const float* audio, int batch, int channels, long long length, float* out,
+                       void* stream);
+
+/* Forward steps up to the mask estimators: fp32 masks
+ * [batch, num_stems, T, sum_band_dims], T = length/hop + 1. */
+int msst_model_masks(msst_model* m, const float* audio, int batch, int channels, long long length, float* masks,
+                     void* stream);
+
+/* One axial transformer (all its layers, plus the MelBandRoformer's final norm)
+ * applied in place to the residual stream x fp32 [batch, T, num_bands, dim]
+ * (replaces apply_transformer, src/model_mel_band_roformer.cu:628-651,
+ * src/model_bs_roformer.cu:310-331, with the permutes of forward() folded away). */
+int msst_model_transformer(msst_model* m, int depth_index, int axis, float* x, int batch, int T, void* stream);
+
+/* Chunked overlap-add separation of one track (replaces app::run_inference /
+ * process_chunked, src/inference_app.cpp:100-324,443-497).  track [channels,
+ * length] -> out [num_stems, channels, length].  overlap: (0,1) = overlap
+ * ratio, >= 1 = num_overlap, 0 = model default.  chunk_batch <= 0 uses the
+ * reference default (2).  *_host variants take host memory (copies included). */
+int msst_model_separate(msst_model* m, const float* track, int channels, long long length, float overlap,
+                        int chunk_batch, int flags, float* out, void* stream);
+int msst_model_separate_host(msst_model* m, const float* track_host, int channels, long long length, float overlap,
+                             int chunk_batch, int flags, float* out_host);
+
+/* Chunk plan of msst_model_separate for a track length (src/inference_app.cpp:119-138). */
+int msst_model_chunk_plan(const msst_model* m, long long length, float overlap, int* chunk_size, int* step,
+                          long long* border, long long* padded_length, int* num_chunks);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MSST_B200_H */

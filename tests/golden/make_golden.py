@@ -1,0 +1,225 @@
+"""Generate the golden fixtures in tests/golden/ from the REFERENCE engine.
+
+The reference (HuanLinOTO/CUDA-MSST-Infer) ships no tests and no golden vectors,
+so its own CUDA build (oracle/build_ref.sh -> oracle/_ref/libcudasep_ref.so) is
+run on a B200 over seeded synthetic inputs and its outputs are stored here.
+Every fixture records the seeds and configs it came from; inputs are
+regenerated from those seeds by msst_b200.synth.
+
+Run on a GPU box from the repository root:
+    python tests/golden/make_golden.py --out <dir>
+It also prints how far the CPU oracle (oracle/oracle.py) is from each fixture,
+which is the evidence that pins the oracle.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+sys.path.insert(0, os.path.join(ROOT, "cuda-msst-infer_b200"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+from msst_b200 import synth  # noqa: E402
+import oracle  # noqa: E402
+
+REF_LIB = os.path.join(ROOT, "oracle", "_ref", "libcudasep_ref.so")
+f32p = ctypes.POINTER(ctypes.c_float)
+
+
+def ref_lib():
+    L = ctypes.CDLL(REF_LIB)
+    L.refh_last_error.restype = ctypes.c_char_p
+    L.refh_load.restype = ctypes.c_void_p
+    L.refh_load.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.c_int]
+    L.refh_free.argtypes = [ctypes.c_void_p]
+    ll = ctypes.c_longlong
+    L.refh_forward.argtypes = [ctypes.c_void_p, f32p, ctypes.c_int, ctypes.c_int, ll, f32p, ll,
+                               ctypes.POINTER(ll)]
+    L.refh_masks.argtypes = L.refh_forward.argtypes
+    L.refh_separate.argtypes = [ctypes.c_void_p, f32p, ctypes.c_int, ll, ctypes.c_float, ctypes.c_int, f32p,
+                                ll, ctypes.POINTER(ll), ctypes.POINTER(ctypes.c_double)]
+    L.refh_sdpa.argtypes = [f32p, f32p, f32p] + [ctypes.c_int] * 4 + [ctypes.c_float, ctypes.c_int, f32p]
+    L.refh_flash.argtypes = [f32p, f32p, f32p] + [ctypes.c_int] * 4 + [ctypes.c_float, f32p]
+    L.refh_rope.argtypes = [f32p, f32p, f32p, f32p] + [ctypes.c_int] * 4
+    L.refh_rmsnorm.argtypes = [f32p, f32p, ctypes.c_int, ctypes.c_int, ctypes.c_float, f32p]
+    L.refh_linear.argtypes = [f32p, f32p, f32p] + [ctypes.c_int] * 5 + [f32p]
+    return L
+
+
+def P(a):
+    return a.ctypes.data_as(f32p)
+
+
+def check(rc, L):
+    if rc != 0:
+        raise RuntimeError(L.refh_last_error().decode())
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def snr_db(est, ref):
+    ref = np.asarray(ref, np.float64)
+    err = np.asarray(est, np.float64) - ref
+    return float(10 * np.log10(np.sum(ref * ref) / max(np.sum(err * err), 1e-30)))
+
+
+# Small but structurally complete models (all 60 mel / 62 linear bands, real
+# n_fft/hop, 8 heads x 64) so fixtures stay a few MB.
+MODELS = {
+    "mbr_small": dict(kind="mbr", cfg=dict(depth=1, dim=128), seed=11),
+    "bsr_small": dict(kind="bsr", cfg=dict(depth=1, dim=128), seed=12),
+}
+
+
+def model_cfg(spec):
+    return (synth.mbr_config if spec["kind"] == "mbr" else synth.bsr_config)(**spec["cfg"])
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--out", required=True)
+    ap.add_argument("--full", action="store_true", help="also pin config 0 at full size (summary only)")
+    args = ap.parse_args()
+    os.makedirs(args.out, exist_ok=True)
+    L = ref_lib()
+    tmp = tempfile.mkdtemp()
+    summary = {}
+    ll = ctypes.c_longlong
+
+    # ---------------- model-level fixtures (fp32 mode and fp16 mode) ----------------
+    n_samp, audio_seed = 22050, 5
+    audio = synth.make_audio(n_samp, 2, audio_seed)[None]
+    for name, spec in MODELS.items():
+        cfg = model_cfg(spec)
+        path = os.path.join(tmp, name + ".csm")
+        sd = synth.make_weights(cfg, spec["seed"])
+        synth.write_csm(path, cfg, sd)
+        om = oracle.Model(cfg, sd)
+        o_masks, st = om.masks(audio)
+        o_out = om.apply_masks(o_masks, st)
+        for fp16 in (0, 1):
+            h = L.refh_load(path.encode(), 0, fp16)
+            if not h:
+                raise RuntimeError(L.refh_last_error().decode())
+            cap = 1 << 26
+            buf = np.zeros(cap, np.float32)
+            n = ll(0)
+            check(L.refh_masks(h, P(audio), 1, 2, n_samp, P(buf), cap, ctypes.byref(n)), L)
+            masks = buf[: n.value].reshape(o_masks.shape).copy()
+            check(L.refh_forward(h, P(audio), 1, 2, n_samp, P(buf), cap, ctypes.byref(n)), L)
+            out = buf[: n.value].reshape(o_out.shape).copy()
+            L.refh_free(h)
+            tag = f"{name}_{'fp16' if fp16 else 'fp32'}"
+            np.savez_compressed(os.path.join(args.out, tag + ".npz"), masks=masks, out=out,
+                                meta=json.dumps(dict(model=name, spec=spec, fp16=fp16, n_samples=n_samp,
+                                                     audio_seed=audio_seed)))
+            summary[tag] = dict(mask_rel_l2_oracle=rel_l2(o_masks, masks), out_snr_db_oracle=snr_db(o_out, out))
+            print(tag, summary[tag], flush=True)
+
+    # ---------------- chunked separation (overlap-add path) ----------------
+    cfg = synth.mbr_config(depth=1, dim=128, chunk_size=22050)
+    path = os.path.join(tmp, "mbr_chunk.csm")
+    sd = synth.make_weights(cfg, 13)
+    synth.write_csm(path, cfg, sd)
+    track = synth.make_audio(3 * 22050 + 777, 2, 6)
+    h = L.refh_load(path.encode(), 0, 0)
+    buf = np.zeros(track.size * 2, np.float32)
+    n = ll(0)
+    ms = ctypes.c_double(0)
+    check(L.refh_separate(h, P(track), 2, track.shape[1], 0.25, 4, P(buf), buf.size, ctypes.byref(n),
+                          ctypes.byref(ms)), L)
+    L.refh_free(h)
+    sep = buf[: n.value].reshape(2, -1).copy()
+    om = oracle.Model(cfg, sd)
+    step = oracle.resolve_step(22050, 0.25, 2)
+    o_sep = oracle.separate(lambda x: om.forward(x), track, 22050, step, batch=4)
+    np.savez_compressed(os.path.join(args.out, "mbr_chunked_fp32.npz"), out=sep,
+                        meta=json.dumps(dict(weights_seed=13, cfg=dict(depth=1, dim=128, chunk_size=22050),
+                                             track_len=track.shape[1], track_seed=6, overlap=0.25,
+                                             chunk_batch=4)))
+    summary["mbr_chunked_fp32"] = dict(out_snr_db_oracle=snr_db(o_sep, sep))
+    print("chunked", summary["mbr_chunked_fp32"], flush=True)
+
+    # ---------------- op-level fixtures ----------------
+    rng = np.random.default_rng(21)
+    ops = {}
+    for (B, H, N, D) in ((2, 2, 129, 64), (3, 2, 60, 64)):
+        q, k, v = (rng.standard_normal((B, H, N, D)).astype(np.float32) for _ in range(3))
+        scale = 0.125
+        for fp16 in (0, 1):
+            o = np.zeros_like(q)
+            check(L.refh_sdpa(P(q), P(k), P(v), B, H, N, D, scale, fp16, P(o)), L)
+            ops[f"sdpa_{N}_{'fp16' if fp16 else 'fp32'}"] = o
+        of = np.zeros_like(q)
+        check(L.refh_flash(P(q), P(k), P(v), B, H, N, D, scale, P(of)), L)
+        ops[f"flash_{N}"] = of
+        ops[f"qkv_{N}"] = np.stack([q, k, v])
+        cs, sn = oracle.rope_tables(N, D)
+        q2, k2 = q.copy(), k.copy()
+        check(L.refh_rope(P(q2), P(k2), P(cs), P(sn), B, H, N, D), L)
+        ops[f"rope_q_{N}"], ops[f"rope_k_{N}"] = q2, k2
+        summary[f"sdpa_{N}"] = dict(fp32=rel_l2(oracle.attention(q, k, v, scale), ops[f"sdpa_{N}_fp32"]),
+                                    flash=rel_l2(oracle.attention(q, k, v, scale), of),
+                                    rope_q=rel_l2(oracle.rope(q, cs, sn), q2))
+    rows, nout = 129, 512
+    x = rng.standard_normal((rows, 384)).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(384)).astype(np.float32)
+    o = np.zeros_like(x)
+    check(L.refh_rmsnorm(P(x), P(g), rows, 384, float(np.sqrt(np.float32(384))), P(o)), L)
+    ops["rms_x"], ops["rms_g"], ops["rms_out"] = x, g, o
+    w = (0.02 * rng.standard_normal((nout, 384))).astype(np.float32)
+    b = (0.02 * rng.standard_normal(nout)).astype(np.float32)
+    for act, nm in ((0, "none"), (1, "gelu"), (2, "sigmoid")):
+        for fp16 in (0, 1):
+            o = np.zeros((rows, nout), np.float32)
+            check(L.refh_linear(P(x), P(w), P(b), rows, 384, nout, act, fp16, P(o)), L)
+            ops[f"lin_{nm}_{'fp16' if fp16 else 'fp32'}"] = o
+    ops["lin_w"], ops["lin_b"] = w, b
+    summary["rmsnorm"] = rel_l2(oracle.rmsnorm(x, g, np.sqrt(np.float32(384))), ops["rms_out"])
+    summary["linear_gelu"] = rel_l2(oracle.linear(x, w, b, "gelu"), ops["lin_gelu_fp32"])
+    np.savez_compressed(os.path.join(args.out, "ops.npz"), **ops)
+
+    # ---------------- full-size config 0 (summary only; arrays are too large) ----------------
+    if args.full:
+        cfg = synth.mbr_config(depth=1)
+        path = os.path.join(tmp, "cfg0.csm")
+        sd = synth.make_weights(cfg, 0)
+        synth.write_csm(path, cfg, sd)
+        a0 = synth.make_audio(352800, 2, 0)[None]
+        t = time.time()
+        om = oracle.Model(cfg, sd)
+        o_masks, st = om.masks(a0)
+        o_out = om.apply_masks(o_masks, st)
+        cpu_s = time.time() - t
+        h = L.refh_load(path.encode(), 0, 0)
+        cap = o_masks.size + 16
+        buf = np.zeros(cap, np.float32)
+        n = ll(0)
+        check(L.refh_masks(h, P(a0), 1, 2, 352800, P(buf), cap, ctypes.byref(n)), L)
+        masks = buf[: n.value].reshape(o_masks.shape).copy()
+        check(L.refh_forward(h, P(a0), 1, 2, 352800, P(buf), cap, ctypes.byref(n)), L)
+        out = buf[: n.value].reshape(o_out.shape)
+        L.refh_free(h)
+        summary["config0_full"] = dict(mask_rel_l2_oracle=rel_l2(o_masks, masks), out_snr_db_oracle=snr_db(o_out, out),
+                                       cpu_oracle_s=cpu_s, oracle_threads=oracle.threads())
+        print("config0", summary["config0_full"], flush=True)
+
+    with open(os.path.join(args.out, "pin_summary.json"), "w") as f:
+        json.dump(summary, f, indent=1)
+    print(json.dumps(summary, indent=1))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,178 @@
+"""GPU parity of the model-level C ABI against the reference engine's outputs
+(tests/golden/*, produced by oracle/_ref on a B200) and the CPU fp32 oracle.
+
+Bars: fp32 masks within the stated relative-L2 tolerance, output waveforms at
+>= 45 dB SNR for fp16 and bf16, chunked separation the
+same through the overlap-add path.
+"""
+from __future__ import annotations
+
+import json
+import os
+
+import numpy as np
+import pytest
+
+from conftest import golden, rel_l2, snr_db
+
+pytestmark = pytest.mark.gpu
+
+MASK_TOL = {"fp16": 4e-3, "bf16": 2.5e-2}
+SNR_MIN = {"fp16": 45.0, "bf16": 45.0}
+
+
+def _model_file(tmp_path_factory, kind, cfg_kw, seed, name):
+    from msst_b200 import synth
+
+    cfg = (synth.mbr_config if kind == "mbr" else synth.bsr_config)(**cfg_kw)
+    path = str(tmp_path_factory.mktemp("models") / f"{name}.csm")
+    sd = synth.make_weights(cfg, seed)
+    synth.write_csm(path, cfg, sd)
+    return path, cfg, sd
+
+
+@pytest.fixture(scope="module")
+def small_models(tmp_path_factory):
+    out = {}
+    for name in ("mbr_small", "bsr_small"):
+        z, meta = golden(f"{name}_fp32.npz")
+        spec = meta["spec"]
+        out[name] = _model_file(tmp_path_factory, spec["kind"], spec["cfg"], spec["seed"], name) + (meta,)
+    return out
+
+
+@pytest.mark.parametrize("prec", ["fp16", "bf16"])
+@pytest.mark.parametrize("name", ["mbr_small", "bsr_small"])
+def test_masks_and_output_vs_reference(cuda, small_models, name, prec):
+    torch = cuda
+    from msst_b200 import Model, synth
+
+    path, cfg, sd, meta = small_models[name]
+    audio = synth.make_audio(meta["n_samples"], 2, meta["audio_seed"])[None]
+    m = Model(path, 0, prec)
+    x = torch.from_numpy(audio).cuda()
+    masks = m.masks(x).cpu().numpy()
+    y = m.forward(x).cpu().numpy()
+    zf, _ = golden(f"{name}_fp32.npz")
+    zh, _ = golden(f"{name}_fp16.npz")
+    assert masks.shape == zf["masks"].shape
+    assert rel_l2(masks, zf["masks"]) < MASK_TOL[prec]
+    assert snr_db(y, zf["out"]) >= SNR_MIN[prec]
+    assert snr_db(y, zh["out"]) >= SNR_MIN[prec]
+    m.close()
+
+
+def test_forward_batch_consistency(cuda, small_models):
+    """Each item of a batched forward matches the single-item forward.  Every kernel of
+    the path is batch-independent; cuFFT chooses batch-size-dependent plans, so the
+    bar is >= 70 dB rather than bit equality."""
+    torch = cuda
+    from msst_b200 import Model, synth
+
+    path, _, _, _ = small_models["mbr_small"]
+    m = Model(path, 0, "fp16")
+    a = np.stack([synth.make_audio(22050, 2, s) for s in (1, 2, 3)])
+    yb = m.forward(torch.from_numpy(a).cuda()).cpu().numpy()
+    for i in range(3):
+        y1 = m.forward(torch.from_numpy(a[i : i + 1]).cuda()).cpu().numpy()
+        assert snr_db(yb[i], y1[0]) >= 70.0
+    m.close()
+
+
+def test_determinism(cuda, small_models):
+    torch = cuda
+    from msst_b200 import Model, synth
+
+    path, _, _, _ = small_models["bsr_small"]
+    m = Model(path, 0, "bf16")
+    x = torch.from_numpy(synth.make_audio(22050, 2, 9)[None]).cuda()
+    y0 = m.forward(x).cpu().numpy()
+    y1 = m.forward(x).cpu().numpy()
+    np.testing.assert_array_equal(y0, y1)
+    m.close()
+
+
+@pytest.mark.parametrize("axis", ["time", "band"])
+def test_transformer_layer_vs_oracle(cuda, small_models, axis):
+    torch = cuda
+    import oracle
+    from msst_b200 import Model
+
+    path, cfg, sd, _ = small_models["mbr_small"]
+    om = oracle.Model(cfg, sd)
+    B, T, nb, D = 1, 40, 60, cfg["dim"]
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((B, T, nb, D)).astype(np.float32)
+    m = Model(path, 0, "fp16")
+    xt = torch.from_numpy(x.copy()).cuda()
+    m.transformer(0, axis, xt)
+    y = xt.cpu().numpy()
+    if axis == "time":
+        xr = np.ascontiguousarray(x.transpose(0, 2, 1, 3)).reshape(B * nb, T, D)
+        r = om.transformer(xr, "layers.0.0", 1).reshape(B, nb, T, D).transpose(0, 2, 1, 3)
+    else:
+        r = om.transformer(x.reshape(B * T, nb, D), "layers.0.1", 1).reshape(B, T, nb, D)
+    assert rel_l2(y, r) < 3e-3
+    m.close()
+
+
+def test_chunked_separation_vs_reference(cuda, tmp_path_factory):
+    torch = cuda
+    from msst_b200 import Model, synth
+
+    z, meta = golden("mbr_chunked_fp32.npz")
+    path, _, _ = _model_file(tmp_path_factory, "mbr", meta["cfg"], meta["weights_seed"], "mbr_chunk")
+    track = synth.make_audio(meta["track_len"], 2, meta["track_seed"])
+    m = Model(path, 0, "fp16")
+    y = m.separate(torch.from_numpy(track).cuda(), overlap=meta["overlap"], chunk_batch=meta["chunk_batch"])
+    assert snr_db(y.cpu().numpy(), z["out"]) >= 45.0
+    yh = m.separate_host(track, overlap=meta["overlap"], chunk_batch=meta["chunk_batch"])
+    np.testing.assert_array_equal(yh, y.cpu().numpy())
+    # chunk batching changes only cuFFT's batch-size-dependent rounding
+    y1 = m.separate(torch.from_numpy(track).cuda(), overlap=meta["overlap"], chunk_batch=1)
+    assert snr_db(y1.cpu().numpy(), y.cpu().numpy()) >= 70.0
+    m.close()
+
+
+def test_chunked_fixed_tail_padding_vs_oracle(cuda, tmp_path_factory):
+    """With the opt-in fix, the final chunk is padded from each channel's own samples."""
+    torch = cuda
+    import oracle
+    from msst_b200 import Model, synth
+
+    cfg_kw = dict(depth=1, dim=128, chunk_size=22050)
+    path, cfg, sd = _model_file(tmp_path_factory, "mbr", cfg_kw, 13, "mbr_fix")
+    track = synth.make_audio(3 * 22050 + 777, 2, 6)
+    m = Model(path, 0, "fp16")
+    y = m.separate(torch.from_numpy(track).cuda(), overlap=0.25, chunk_batch=4, fix_tail_padding=True).cpu().numpy()
+    om = oracle.Model(cfg, sd)
+    r = oracle.separate(lambda a: om.forward(a), track, 22050, oracle.resolve_step(22050, 0.25, 2), 4,
+                        ref_compat=False)
+    assert snr_db(y, r) >= 45.0
+    m.close()
+
+
+def test_config0_full_size_vs_oracle(cuda, tmp_path_factory):
+    """BASELINE config 0 shape (MBR dim 384, one time + one band layer, one 8 s chunk)."""
+    torch = cuda
+    import oracle
+    from msst_b200 import Model, synth
+
+    path, cfg, sd = _model_file(tmp_path_factory, "mbr", dict(depth=1), 0, "cfg0")
+    audio = synth.make_audio(352800, 2, 0)[None]
+    om = oracle.Model(cfg, sd)
+    om_masks, st = om.masks(audio)
+    ref = om.apply_masks(om_masks, st)
+    m = Model(path, 0, "fp16")
+    x = torch.from_numpy(audio).cuda()
+    masks = m.masks(x).cpu().numpy()
+    y = m.forward(x).cpu().numpy()
+    assert rel_l2(masks, om_masks) < MASK_TOL["fp16"]
+    assert snr_db(y, ref) >= 45.0
+    m.close()
+
+
+def test_device_error_flag_clear(cuda):
+    from msst_b200 import device_error
+
+    assert device_error(True) == 0
