@@ -360,6 +360,7 @@ cudaError_t launch_t(const CUtensorMap& m, const AttnParams& p, int num_sms, cud
   }
   const int grid = p.total_items < num_sms ? p.total_items : num_sms;
   if (grid <= 0) return cudaSuccess;
+  note_launch();
   attention_kernel<T><<<grid, 192, kAttnSmem, s>>>(m, p);
   return cudaGetLastError();
 }

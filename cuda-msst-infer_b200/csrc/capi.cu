@@ -1,6 +1,7 @@
 // capi.cu — the extern "C" boundary of libmsst_b200 (declared in include/msst_b200.h).
 // Every entry point catches exceptions and turns them into status codes; the
 // message is kept per thread for msst_last_error().
+#include <atomic>
 #include <cmath>
 #include <string>
 
@@ -13,6 +14,11 @@
 struct msst_model {
   msst::Model impl;
 };
+
+namespace msst {
+static std::atomic<unsigned long long> g_launches{0};
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+}  // namespace msst
 
 namespace {
 
@@ -54,8 +60,8 @@ int pick_bn(int n) {
   return n <= 128 ? 128 : 256;
 }
 
-void run_gemm(const CUtensorMap& ma, const CUtensorMap& mb, msst::GemmParams& p, int epi, int bn, int bf16,
-              cudaStream_t s) {
+void run_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, msst::GemmParams& p, int epi,
+              int bn, int bf16, cudaStream_t s) {
   int tiles = 0;
   for (int i = 0; i < p.num_groups; ++i) {
     msst::GemmGroup& g = p.groups[i];
@@ -64,7 +70,7 @@ void run_gemm(const CUtensorMap& ma, const CUtensorMap& mb, msst::GemmParams& p,
     tiles += ((g.m + msst::kGemmBM - 1) / msst::kGemmBM) * g.tiles_n;
   }
   p.total_tiles = tiles;
-  MSST_CUDA(msst::launch_gemm(ma, mb, p, epi, bn, bf16, sm_count(), s));
+  MSST_CUDA(msst::launch_gemm(ma, mb, mo, p, epi, bn, bf16, sm_count(), s));
 }
 
 void check_dtype(int dtype) { MSST_REQUIRE(dtype == MSST_F16 || dtype == MSST_BF16, "dtype must be MSST_F16 or MSST_BF16"); }
@@ -92,6 +98,10 @@ const char* msst_last_error(void) { return g_last_error.c_str(); }
 unsigned msst_device_error(int clear) { return msst::device_error(clear != 0); }
 
 int msst_version(void) { return 1; }
+
+unsigned long long msst_kernel_launches(int reset) {
+  return reset ? msst::g_launches.exchange(0) : msst::g_launches.load();
+}
 
 int msst_rmsnorm(const float* x, long long rows, int D, const float* gamma, float scale, int dtype, void* out16,
                  const float* wg, const float* bg, int heads, float* gates, void* stream) {
@@ -130,10 +140,17 @@ int msst_gemm(const void* x, long long rows, int K, long long ldx, const void* w
     MSST_REQUIRE(epilogue != MSST_EPI_GLU32 || N % 2 == 0, "GLU needs an even N");
     check_align(x, "x");
     check_align(w, "w");
+    check_align(out, "out");
+    const bool out32 = epilogue != MSST_EPI_STORE16;
+    MSST_REQUIRE(ldo >= (epilogue == MSST_EPI_GLU32 ? N / 2 : N) && (ldo * (out32 ? 4 : 2)) % 16 == 0,
+                 "ldo must cover the output row and be a multiple of 16 bytes");
     use_device_of(x);
     const int bn = pick_bn(N);
     const CUtensorMap ma = msst::map_2d(x, (uint64_t)rows, (uint64_t)K, (uint64_t)ldx, msst::kGemmBM);
     const CUtensorMap mb = msst::map_2d(w, (uint64_t)N, (uint64_t)K, (uint64_t)K, (uint32_t)bn);
+    const CUtensorMap mo = epilogue == MSST_EPI_GLU32
+                               ? ma
+                               : msst::map_out_2d(out, out32, (uint64_t)rows, (uint64_t)N, (uint64_t)ldo);
     msst::GemmParams p{};
     p.num_groups = 1;
     p.act = act;
@@ -144,8 +161,9 @@ int msst_gemm(const void* x, long long rows, int K, long long ldx, const void* w
     g.out = out;
     g.ldo = ldo;
     g.out_row_mul = 1;
+    g.oy_row = 1;
     g.bias = bias;
-    run_gemm(ma, mb, p, epilogue, bn, dtype, as_stream(stream));
+    run_gemm(ma, mb, mo, p, epilogue, bn, dtype, as_stream(stream));
   });
 }
 
@@ -177,7 +195,10 @@ int msst_gemm_qkv_rope(const void* x, long long rows, int K, const void* w, int 
     g.out = qkv16;
     g.ldo = N;
     g.out_row_mul = 1;
-    run_gemm(ma, mb, p, msst::kEpiQkvRope, bn, dtype, as_stream(stream));
+    g.oy_row = 1;
+    check_align(qkv16, "qkv16");
+    const CUtensorMap mo = msst::map_out_2d(qkv16, false, (uint64_t)rows, (uint64_t)N, (uint64_t)N);
+    run_gemm(ma, mb, mo, p, msst::kEpiQkvRope, bn, dtype, as_stream(stream));
   });
 }
 
@@ -296,15 +317,7 @@ int msst_model_separate_host(msst_model* m, const float* track_host, int channel
   return guarded([&] {
     MSST_REQUIRE(m && track_host && out_host && channels > 0 && length > 0, "null argument");
     MSST_CUDA(cudaSetDevice(m->impl.device()));
-    const msst_model_info& I = m->impl.info();
-    const size_t in_bytes = sizeof(float) * (size_t)channels * length;
-    const size_t out_bytes = in_bytes * (size_t)I.num_stems;
-    msst::DeviceBuffer din(in_bytes), dout(out_bytes);
-    cudaStream_t s = nullptr;
-    MSST_CUDA(cudaMemcpyAsync(din.get(), track_host, in_bytes, cudaMemcpyHostToDevice, s));
-    m->impl.separate(din.get<float>(), channels, length, overlap, chunk_batch, flags, dout.get<float>(), s);
-    MSST_CUDA(cudaMemcpyAsync(out_host, dout.get(), out_bytes, cudaMemcpyDeviceToHost, s));
-    MSST_CUDA(cudaStreamSynchronize(s));
+    m->impl.separate_host(track_host, channels, length, overlap, chunk_batch, flags, out_host);
   });
 }
 

@@ -4,13 +4,15 @@
 // the residual add in src/tensor.cu:1439-1442 and the per-band loops of
 // src/model_mel_band_roformer.cu:676-736).
 //
-// CTA = 192 threads:
+// CTA = 320 threads:
 //   warp 0     TMA producer (one lane): A/B k-blocks of 64 into a smem ring
 //   warp 1     MMA issuer (one lane): tcgen05.mma M=128 N=BN K=16, fp32 accumulators
 //              in TMEM, double-buffered so the epilogue of tile i overlaps the
 //              main loop of tile i+1; also owns the TMEM allocation
-//   warps 2-5  epilogue: tcgen05.ld 32 columns at a time, fused bias/activation/
-//              RoPE/GLU/residual, direct global stores (each thread owns one row)
+//   warps 2-9  epilogue: warp w reads TMEM lane quarter w%4 and column half
+//              (w-2)/4, 32 columns at a time; bias/activation/RoPE in fp32; the
+//              32x32 result is staged in swizzled smem and leaves by TMA bulk
+//              store (or bulk reduce-add into the fp32 residual stream).
 // Tiles of all groups are walked in one static persistent schedule.
 #include "common.cuh"
 #include "gemm.cuh"
@@ -19,15 +21,29 @@ namespace msst {
 
 namespace {
 
-template <int BN>
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+
+template <int EPI>
+struct EpiTraits {
+  static constexpr bool kTma = EPI != kEpiGlu32;
+  static constexpr bool k16 = EPI == kEpiStore16 || EPI == kEpiQkvRope;
+  // per-warp staging: 32 rows x 32 columns (64 B rows for 16-bit, 128 B for fp32)
+  static constexpr uint32_t kStageBytes = k16 ? 2048 : 4096;
+};
+
+template <int BN, int EPI>
 struct GemmCfg {
   static constexpr uint32_t kABytes = kGemmBM * kGemmBK * 2;
   static constexpr uint32_t kBBytes = BN * kGemmBK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = (int)((196u * 1024u) / kStageBytes) > 8 ? 8 : (int)((196u * 1024u) / kStageBytes);
+  static constexpr uint32_t kEpiBytes = kEpiWarps * EpiTraits<EPI>::kStageBytes;
+  static constexpr size_t kFixed = 1024 + kEpiBytes + 256 + sizeof(GemmGroup) * kGemmMaxGroups;
+  static constexpr int kStagesRaw = (int)((232448 - kFixed) / kStageBytes);
+  static constexpr int kStages = kStagesRaw > 6 ? 6 : kStagesRaw;
   static constexpr uint32_t kTmemCols = (2 * BN <= 256) ? 256 : 512;
-  static constexpr size_t kSmemBytes =
-      1024 + (size_t)kStages * kStageBytes + 256 + sizeof(GemmGroup) * kGemmMaxGroups;
+  static constexpr size_t kSmemBytes = kFixed + (size_t)kStages * kStageBytes;
+  static_assert(kStages >= 2, "not enough shared memory for a 2-stage ring");
 };
 
 __device__ __forceinline__ int find_group(const GemmGroup* g, int n, int t) {
@@ -39,125 +55,109 @@ __device__ __forceinline__ int find_group(const GemmGroup* g, int n, int t) {
 __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
 
-template <typename T>
-__device__ __forceinline__ void store16_chunk(T* o, const float (&v)[32], int nvalid) {
-  if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
-    uint4* o4 = reinterpret_cast<uint4*>(o);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint4 w;
-      w.x = pack2<T>(v[8 * q + 0], v[8 * q + 1]);
-      w.y = pack2<T>(v[8 * q + 2], v[8 * q + 3]);
-      w.z = pack2<T>(v[8 * q + 4], v[8 * q + 5]);
-      w.w = pack2<T>(v[8 * q + 6], v[8 * q + 7]);
-      o4[q] = w;
-    }
-  } else {
-    for (int j = 0; j < nvalid; ++j) {
-      uint32_t pk = pack2<T>(v[j], 0.f);
-      o[j] = *reinterpret_cast<T*>(&pk);
-    }
-  }
-}
-
-template <int EPI, typename T>
-__device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const GemmGroup& g, int row, int col,
-                                               const uint32_t (&r)[32]) {
-  float v[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+// bias, activation and RoPE on one 32-column chunk of one row (fp32 registers)
+template <int EPI>
+__device__ __forceinline__ void chunk_math(const GemmParams& p, const GemmGroup& g, int row, int col, float (&v)[32]) {
   const int nvalid = min(32, g.n - col);
   if (g.bias != nullptr) {
     if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(g.bias + col) & 15) == 0)) {
       const float4* b4 = reinterpret_cast<const float4*>(g.bias + col);
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        float4 b = __ldg(b4 + q);
+        const float4 b = __ldg(b4 + q);
         v[4 * q] += b.x;
         v[4 * q + 1] += b.y;
         v[4 * q + 2] += b.z;
         v[4 * q + 3] += b.w;
       }
     } else {
-      for (int j = 0; j < nvalid; ++j) v[j] += __ldg(g.bias + col + j);
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < nvalid) v[j] += __ldg(g.bias + col + j);
     }
   }
-  const long long orow = (long long)row * g.out_row_mul + g.out_row_add;
-  if constexpr (EPI == kEpiStore16 || EPI == kEpiQkvRope) {
-    if constexpr (EPI == kEpiStore16) {
-      if (p.act == kActGelu) {
+  if constexpr (EPI == kEpiStore16) {
+    if (p.act == kActGelu) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
-      } else if (p.act == kActTanh) {
+      for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+    } else if (p.act == kActTanh) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = tanhf(v[j]);
-      } else if (p.act == kActSigmoid) {
+      for (int j = 0; j < 32; ++j) v[j] = tanhf(v[j]);
+    } else if (p.act == kActSigmoid) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = sigmoidf_(v[j]);
-      }
-    } else {
-      if (col < p.rope_cols) {
-        const int half = p.head_dim >> 1;
-        const int pos = (row / p.pos_div) % p.pos_mod;
-        const int i0 = (col % p.head_dim) >> 1;
-        const float* cs = p.rope_cos + (size_t)pos * half + i0;
-        const float* sn = p.rope_sin + (size_t)pos * half + i0;
+      for (int j = 0; j < 32; ++j) v[j] = sigmoidf_(v[j]);
+    }
+  } else if constexpr (EPI == kEpiQkvRope) {
+    if (col < p.rope_cols) {
+      const int half = p.head_dim >> 1;
+      const int pos = (row / p.pos_div) % p.pos_mod;
+      const int i0 = (col % p.head_dim) >> 1;
+      const float4* cs = reinterpret_cast<const float4*>(p.rope_cos + (size_t)pos * half + i0);
+      const float4* sn = reinterpret_cast<const float4*>(p.rope_sin + (size_t)pos * half + i0);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const float c = __ldg(cs + j), s = __ldg(sn + j);
+      for (int u = 0; u < 4; ++u) {
+        const float4 c4 = __ldg(cs + u), s4 = __ldg(sn + u);
+        const float c[4] = {c4.x, c4.y, c4.z, c4.w}, s[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int j = 4 * u + k;
           const float x0 = v[2 * j], x1 = v[2 * j + 1];
-          v[2 * j] = x0 * c - x1 * s;
-          v[2 * j + 1] = x0 * s + x1 * c;
+          v[2 * j] = x0 * c[k] - x1 * s[k];
+          v[2 * j + 1] = x0 * s[k] + x1 * c[k];
         }
       }
-    }
-    T* o = reinterpret_cast<T*>(g.out) + orow * g.ldo + g.out_col0 + col;
-    store16_chunk<T>(o, v, nvalid);
-  } else if constexpr (EPI == kEpiResid32 || EPI == kEpiStore32) {
-    float* o = reinterpret_cast<float*>(g.out) + orow * g.ldo + g.out_col0 + col;
-    if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
-      float4* o4 = reinterpret_cast<float4*>(o);
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        float4 w = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-        if constexpr (EPI == kEpiResid32) {
-          const float4 old = o4[q];
-          w.x += old.x;
-          w.y += old.y;
-          w.z += old.z;
-          w.w += old.w;
-        }
-        o4[q] = w;
-      }
-    } else {
-      for (int j = 0; j < nvalid; ++j) {
-        if constexpr (EPI == kEpiResid32)
-          o[j] += v[j];
-        else
-          o[j] = v[j];
-      }
-    }
-  } else {  // kEpiGlu32: adjacent columns (2j, 2j+1) are (value, gate)
-    float* o = reinterpret_cast<float*>(g.out) + orow * g.ldo + g.out_col0 + (col >> 1);
-    float w[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) w[j] = v[2 * j] * sigmoidf_(v[2 * j + 1]);
-    const int nout = nvalid >> 1;
-    if (nout == 16 && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
-      float4* o4 = reinterpret_cast<float4*>(o);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) o4[q] = make_float4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
-    } else {
-      for (int j = 0; j < nout; ++j) o[j] = w[j];
     }
   }
 }
 
+// GLU epilogue with direct stores (value/gate columns interleaved by the weight packing)
+__device__ __forceinline__ void glu_store(const GemmGroup& g, int row, int col, const float (&v)[32]) {
+  const int nvalid = min(32, g.n - col);
+  const long long orow = (long long)row * g.out_row_mul + g.out_row_add;
+  float* o = reinterpret_cast<float*>(g.out) + orow * g.ldo + g.out_col0 + (col >> 1);
+  float w[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) w[j] = v[2 * j] * sigmoidf_(v[2 * j + 1]);
+  const int nout = nvalid >> 1;
+  if (nout == 16 && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
+    float4* o4 = reinterpret_cast<float4*>(o);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) o4[q] = make_float4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (j < nout) o[j] = w[j];
+  }
+}
+
+// Write this lane's row of a 32x32 chunk into the warp's staging tile using the
+// swizzle the output tensor map expects (SW64 for 16-bit rows of 64 B, SW128 for
+// fp32 rows of 128 B); 8 consecutive rows cover all 32 banks.
+template <typename T, bool k16>
+__device__ __forceinline__ void stage_row(uint8_t* stg, int r, const float (&v)[32]) {
+  if constexpr (k16) {
+    uint8_t* rowp = stg + r * 64;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const uint4 w = make_uint4(pack2<T>(v[8 * c], v[8 * c + 1]), pack2<T>(v[8 * c + 2], v[8 * c + 3]),
+                                 pack2<T>(v[8 * c + 4], v[8 * c + 5]), pack2<T>(v[8 * c + 6], v[8 * c + 7]));
+      *reinterpret_cast<uint4*>(rowp + ((c ^ ((r >> 1) & 3)) << 4)) = w;
+    }
+  } else {
+    uint8_t* rowp = stg + r * 128;
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      *reinterpret_cast<float4*>(rowp + ((c ^ (r & 7)) << 4)) =
+          make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+  }
+}
+
 template <int BN, int EPI, typename T>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                const __grid_constant__ GemmParams p) {
-  using Cfg = GemmCfg<BN>;
+                const __grid_constant__ CUtensorMap map_o, const __grid_constant__ GemmParams p) {
+  using Cfg = GemmCfg<BN, EPI>;
+  using Epi = EpiTraits<EPI>;
   constexpr int kStages = Cfg::kStages;
   constexpr uint32_t kIsBf16 = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
 
@@ -165,13 +165,14 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + kStages * Cfg::kABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + kStages * Cfg::kBBytes);
+  uint8_t* sEpi = sB + kStages * Cfg::kBBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + Cfg::kEpiBytes);
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  GemmGroup* groups = reinterpret_cast<GemmGroup*>(smem + kStages * Cfg::kStageBytes + 256);
+  GemmGroup* groups = reinterpret_cast<GemmGroup*>(sEpi + Cfg::kEpiBytes + 256);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   {
@@ -187,7 +188,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);
+      mbar_init(&tempty[b], kEpiWarps);
     }
     *abort_flag = 0;
     mbar_fence_init();
@@ -195,6 +196,7 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&map_a);
     tma_prefetch_desc(&map_b);
+    if constexpr (Epi::kTma) tma_prefetch_desc(&map_o);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
@@ -205,6 +207,7 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       int stage = 0;
       uint32_t ph = 0;
@@ -229,12 +232,9 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
       }
-      if (!ok) {
-        // drain: wait (bounded) for copies already issued into the ring
-        for (int s = 0; s < kStages; ++s) (void)mbar_try_wait(smem_u32(&full[s]), 0);
-      }
     }
   } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       int stage = 0;
       uint32_t ph = 0;
@@ -278,8 +278,12 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else {
+    // ------------------------------------------------------------ epilogue (8 warps)
+    const int ew = warp - 2;
     const int q = warp & 3;
+    const int half = ew >> 2;
     const int row_in_tile = q * 32 + lane;
+    uint8_t* stg = sEpi + ew * Epi::kStageBytes;
     int abuf = 0;
     uint32_t aph = 0;
     for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
@@ -290,18 +294,45 @@ __global__ void __launch_bounds__(192, 1)
       if (!mbar_wait(&tfull[abuf], aph, kErrTimeoutTmemFull, abort_flag)) break;
       tc_fence_after();
       const int row = tm * kGemmBM + row_in_tile;
-      const bool valid = row < g.m;
-      for (int c0 = 0; c0 < n_eff; c0 += 32) {
+      const int c_begin = half * (BN / 2);
+      const int c_end = min(c_begin + BN / 2, n_eff);
+      for (int c0 = c_begin; c0 < c_end; c0 += 32) {
         uint32_t r[32];
         tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(abuf * BN + c0), r);
         tmem_ld_wait();
-        if (valid) epilogue_chunk<EPI, T>(p, g, row, tn * BN + c0, r);
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        const int col = tn * BN + c0;
+        chunk_math<EPI>(p, g, row, col, v);
+        if constexpr (Epi::kTma) {
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
+          stage_row<T, Epi::k16>(stg, lane, v);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            const int row0 = tm * kGemmBM + q * 32;
+            const int x = g.out_col0 + col, y = g.oy0 + g.oy_row * row0, z = g.oz0 + g.oz_row * row0;
+            if constexpr (EPI == kEpiResid32)
+              tma_reduce_add_3d(&map_o, stg, x, y, z);
+            else
+              tma_store_3d(&map_o, stg, x, y, z);
+            bulk_commit();
+          }
+        } else {
+          if (row < g.m) glu_store(g, row, col, v);
+        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[abuf]);
       abuf ^= 1;
       if (abuf == 0) aph ^= 1u;
+    }
+    if constexpr (Epi::kTma) {
+      if (lane == 0) bulk_wait0();
+      __syncwarp();
     }
   }
 
@@ -313,9 +344,9 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 template <int BN, int EPI, typename T>
-cudaError_t launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams& p, int num_sms,
-                       cudaStream_t stream) {
-  using Cfg = GemmCfg<BN>;
+cudaError_t launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const GemmParams& p,
+                       int num_sms, cudaStream_t stream) {
+  using Cfg = GemmCfg<BN, EPI>;
   auto kern = gemm_kernel<BN, EPI, T>;
   static bool configured = false;
   if (!configured) {
@@ -325,47 +356,47 @@ cudaError_t launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const GemmP
   }
   const int grid = p.total_tiles < num_sms ? p.total_tiles : num_sms;
   if (grid <= 0) return cudaSuccess;
-  kern<<<grid, 192, Cfg::kSmemBytes, stream>>>(ma, mb, p);
+  note_launch();
+  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ma, mb, mo, p);
   return cudaGetLastError();
 }
 
 template <int BN, typename T>
-cudaError_t dispatch_epi(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams& p, int epi, int num_sms,
-                         cudaStream_t s) {
+cudaError_t dispatch_epi(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const GemmParams& p,
+                         int epi, int num_sms, cudaStream_t s) {
   switch (epi) {
-    case kEpiStore16: return launch_one<BN, kEpiStore16, T>(ma, mb, p, num_sms, s);
-    case kEpiResid32: return launch_one<BN, kEpiResid32, T>(ma, mb, p, num_sms, s);
-    case kEpiStore32: return launch_one<BN, kEpiStore32, T>(ma, mb, p, num_sms, s);
-    case kEpiGlu32: return launch_one<BN, kEpiGlu32, T>(ma, mb, p, num_sms, s);
-    case kEpiQkvRope: return launch_one<BN, kEpiQkvRope, T>(ma, mb, p, num_sms, s);
+    case kEpiStore16: return launch_one<BN, kEpiStore16, T>(ma, mb, mo, p, num_sms, s);
+    case kEpiResid32: return launch_one<BN, kEpiResid32, T>(ma, mb, mo, p, num_sms, s);
+    case kEpiStore32: return launch_one<BN, kEpiStore32, T>(ma, mb, mo, p, num_sms, s);
+    case kEpiGlu32: return launch_one<BN, kEpiGlu32, T>(ma, mb, mo, p, num_sms, s);
+    case kEpiQkvRope: return launch_one<BN, kEpiQkvRope, T>(ma, mb, mo, p, num_sms, s);
     default: return cudaErrorInvalidValue;
   }
 }
 
 }  // namespace
 
-cudaError_t launch_gemm(const CUtensorMap& map_a, const CUtensorMap& map_b, const GemmParams& p, int epilogue,
-                        int bn, int bf16, int num_sms, cudaStream_t stream) {
+cudaError_t launch_gemm(const CUtensorMap& map_a, const CUtensorMap& map_b, const CUtensorMap& map_out,
+                        const GemmParams& p, int epilogue, int bn, int bf16, int num_sms, cudaStream_t stream) {
   if (p.num_groups < 1 || p.num_groups > kGemmMaxGroups) return cudaErrorInvalidValue;
   for (int i = 0; i < p.num_groups; ++i) {
     const GemmGroup& g = p.groups[i];
     if (g.k <= 0 || (g.k % kGemmBK) != 0 || g.m < 0 || g.n <= 0) return cudaErrorInvalidValue;
     if (epilogue == kEpiGlu32 && (g.n % 2) != 0) return cudaErrorInvalidValue;
   }
+  if (epilogue == kEpiQkvRope && (p.rope_cols % 32 != 0 || p.head_dim % 32 != 0)) return cudaErrorInvalidValue;
   if (bn == 256)
-    return bf16 ? dispatch_epi<256, __nv_bfloat16>(map_a, map_b, p, epilogue, num_sms, stream)
-                : dispatch_epi<256, __half>(map_a, map_b, p, epilogue, num_sms, stream);
+    return bf16 ? dispatch_epi<256, __nv_bfloat16>(map_a, map_b, map_out, p, epilogue, num_sms, stream)
+                : dispatch_epi<256, __half>(map_a, map_b, map_out, p, epilogue, num_sms, stream);
   if (bn == 128)
-    return bf16 ? dispatch_epi<128, __nv_bfloat16>(map_a, map_b, p, epilogue, num_sms, stream)
-                : dispatch_epi<128, __half>(map_a, map_b, p, epilogue, num_sms, stream);
+    return bf16 ? dispatch_epi<128, __nv_bfloat16>(map_a, map_b, map_out, p, epilogue, num_sms, stream)
+                : dispatch_epi<128, __half>(map_a, map_b, map_out, p, epilogue, num_sms, stream);
   if (bn == 192)
-    return bf16 ? dispatch_epi<192, __nv_bfloat16>(map_a, map_b, p, epilogue, num_sms, stream)
-                : dispatch_epi<192, __half>(map_a, map_b, p, epilogue, num_sms, stream);
+    return bf16 ? dispatch_epi<192, __nv_bfloat16>(map_a, map_b, map_out, p, epilogue, num_sms, stream)
+                : dispatch_epi<192, __half>(map_a, map_b, map_out, p, epilogue, num_sms, stream);
   return cudaErrorInvalidValue;
 }
 
-}  // namespace msst
-
-namespace msst {
 MSST_DEFINE_ERROR_ACCESSOR(gemm_device_error)
+
 }  // namespace msst

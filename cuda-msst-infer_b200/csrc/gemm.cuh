@@ -7,6 +7,16 @@
 // per-band MLPs of the Roformer band-split and mask estimator (reference
 // src/model_mel_band_roformer.cu:676-685,712-736), which the reference runs as
 // 60-62 separate cuBLAS calls each.
+//
+// Outputs leave through TMA: each epilogue warp stages a 32x32 sub-tile in
+// swizzled shared memory and issues a bulk tensor store (16-bit or fp32), or a
+// bulk tensor reduce-add for the fp32 residual stream (the addition happens in
+// L2; no thread reads the residual).  The output tensor map is 3-D
+// {cols, Y, Z}; a group's output element (row, col) goes to coordinates
+//   (out_col0 + col, oy0 + oy_row * row, oz0 + oz_row * row)
+// so plain row-major outputs, band-strided rows and per-group row clipping are
+// all one map.  The GLU epilogue (half-width, group-interleaved columns) uses
+// direct stores instead.
 #pragma once
 
 #include <cuda.h>
@@ -20,11 +30,11 @@ constexpr int kGemmBK = 64;
 constexpr int kGemmMaxGroups = 64;
 
 enum GemmEpilogue : int {
-  kEpiStore16 = 0,   // out16 = act(acc + bias)
-  kEpiResid32 = 1,   // out32 += acc + bias            (residual stream update)
-  kEpiStore32 = 2,   // out32  = acc + bias
-  kEpiGlu32 = 3,     // out32[j] = (acc[2j]+b[2j]) * sigmoid(acc[2j+1]+b[2j+1])
-  kEpiQkvRope = 4,   // out16 = acc, interleaved-pair rotary on the first rope_cols columns
+  kEpiStore16 = 0,   // out16 = act(acc + bias)                      (TMA store)
+  kEpiResid32 = 1,   // out32 += acc + bias   residual stream update  (TMA reduce-add)
+  kEpiStore32 = 2,   // out32  = acc + bias                           (TMA store)
+  kEpiGlu32 = 3,     // out32[j] = (acc[2j]+b[2j]) * sigmoid(acc[2j+1]+b[2j+1])  (direct stores)
+  kEpiQkvRope = 4,   // out16 = acc with interleaved-pair rotary on the first rope_cols columns (TMA store)
 };
 
 enum GemmAct : int { kActNone = 0, kActGelu = 1, kActTanh = 2, kActSigmoid = 3 };
@@ -36,10 +46,12 @@ struct GemmGroup {
   int tiles_n;            // ceil(n / BN)
   int tile_begin;         // first tile index of this group in the launch
   int out_col0;           // first output column (GLU: in halved units)
-  long long ldo;          // output row stride, elements
-  long long out_row_mul;  // output row = row * out_row_mul + out_row_add
+  int oy0, oy_row;        // TMA output Y coordinate = oy0 + oy_row * row
+  int oz0, oz_row;        // TMA output Z coordinate = oz0 + oz_row * row
+  long long ldo;          // direct stores: output row stride (elements)
+  long long out_row_mul;  // direct stores: output row = row * out_row_mul + out_row_add
   long long out_row_add;
-  void* out;
+  void* out;              // direct stores: output base
   const float* bias;      // [n] or nullptr
 };
 
@@ -55,9 +67,11 @@ struct GemmParams {
 };
 
 // Launches the GEMM.  `map_a` / `map_b` are 2-D tensor maps (inner dim = K) with
-// box {64, 128} for A and {64, bn} for B, 128B swizzle.  bf16 != 0 selects bf16
-// operands (else fp16).  bn in {128, 192, 256}.  Returns a cudaError_t.
-cudaError_t launch_gemm(const CUtensorMap& map_a, const CUtensorMap& map_b, const GemmParams& p, int epilogue,
-                        int bn, int bf16, int num_sms, cudaStream_t stream);
+// box {64, 128} for A and {64, bn} for B, 128B swizzle.  `map_out` is the 3-D
+// output map (box {32, 32, 1}; 64B swizzle for 16-bit outputs, 128B swizzle for
+// fp32), ignored by kEpiGlu32.  bf16 != 0 selects bf16 operands (else fp16).
+// bn in {128, 192, 256}.  Returns a cudaError_t.
+cudaError_t launch_gemm(const CUtensorMap& map_a, const CUtensorMap& map_b, const CUtensorMap& map_out,
+                        const GemmParams& p, int epilogue, int bn, int bf16, int num_sms, cudaStream_t stream);
 
 }  // namespace msst

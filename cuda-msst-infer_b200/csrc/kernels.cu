@@ -346,12 +346,14 @@ inline unsigned grid_for(long long n) {
 }  // namespace
 
 cudaError_t launch_rmsnorm(const RmsNormArgs& a, int bf16, cudaStream_t s) {
+  note_launch();
   if (a.D % 128 != 0 || a.D > 1024 || (a.band_major && a.F <= 0) || (a.wg && a.heads > 32))
     return cudaErrorInvalidValue;
   return bf16 ? rmsnorm_dispatch<__nv_bfloat16>(a, s) : rmsnorm_dispatch<__half>(a, s);
 }
 
 cudaError_t launch_band_input(const BandInArgs& a, int bf16, cudaStream_t s) {
+  note_launch();
   const long long warps = (long long)a.Bc * a.T * a.num_bands;
   long long blocks = (warps + 7) / 8;
   if (blocks > 148LL * 32) blocks = 148LL * 32;
@@ -364,6 +366,7 @@ cudaError_t launch_band_input(const BandInArgs& a, int bf16, cudaStream_t s) {
 }
 
 cudaError_t launch_mask_apply(const MaskApplyArgs& a, cudaStream_t s) {
+  note_launch();
   mask_apply_kernel<<<grid_for((long long)a.Bc * a.S * a.T * a.nbins), 256, 0, s>>>(a);
   return cudaGetLastError();
 }
@@ -382,6 +385,7 @@ cudaError_t launch_istft_ola(const float* frames, int BSC, int T, int n_fft, int
 }
 
 cudaError_t launch_chunk_gather(const ChunkArgs& a, int first, int count, float* batch, cudaStream_t s) {
+  note_launch();
   chunk_gather_kernel<<<grid_for((long long)count * a.C * a.chunk), 256, 0, s>>>(a, first, count, batch);
   return cudaGetLastError();
 }
@@ -396,6 +400,7 @@ cudaError_t launch_chunk_ola(const ChunkArgs& a, int first, int count, int num_c
 }
 
 cudaError_t launch_chunk_finish(const ChunkArgs& a, const float* acc, const float* wsum, float* out, cudaStream_t s) {
+  note_launch();
   chunk_finish_kernel<<<grid_for((long long)a.C * a.L), 256, 0, s>>>(a, acc, wsum, out);
   return cudaGetLastError();
 }

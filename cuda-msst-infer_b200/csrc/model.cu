@@ -338,12 +338,15 @@ struct Model::Work {
   long long M = 0, BT = 0;
   DeviceBuffer frames, spec, ispec, abs, x, xn, gates, big1, big2, ao, mask, chunk_in, chunk_out;
   CUtensorMap m_abs, m_xn, m_ao, m_big1_ffh, m_big2_ffh, m_qkv_time, m_qkv_band, m_h1, m_h2;
+  // GEMM output maps (TMA stores)
+  CUtensorMap mo_qkv, mo_ffh, mo_bs, mo_h1, mo_h2;
 };
 
 Model::Model() = default;
 
 Model::~Model() {
   for (auto& kv : plans_) cufftDestroy(kv.second);
+  if (host_stream_) cudaStreamDestroy(host_stream_);
 }
 
 // ===========================================================================
@@ -647,7 +650,8 @@ cufftHandle Model::fft_plan(cufftType type, int batch, cudaStream_t s) {
   return h;
 }
 
-void Model::gemm(const CUtensorMap& ma, const CUtensorMap& mb, GemmParams& p, int epi, int bn, cudaStream_t s) {
+void Model::gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, GemmParams& p, int epi, int bn,
+                 cudaStream_t s) {
   int tiles = 0;
   for (int i = 0; i < p.num_groups; ++i) {
     GemmGroup& g = p.groups[i];
@@ -656,7 +660,7 @@ void Model::gemm(const CUtensorMap& ma, const CUtensorMap& mb, GemmParams& p, in
     tiles += ((g.m + kGemmBM - 1) / kGemmBM) * g.tiles_n;
   }
   p.total_tiles = tiles;
-  MSST_CUDA(launch_gemm(ma, mb, p, epi, bn, bf16_, num_sms_, s));
+  MSST_CUDA(launch_gemm(ma, mb, mo, p, epi, bn, bf16_, num_sms_, s));
 }
 
 static GemmGroup group(int m, int n, int k, void* out, long long ldo, const float* bias) {
@@ -667,6 +671,7 @@ static GemmGroup group(int m, int n, int k, void* out, long long ldo, const floa
   g.out = out;
   g.ldo = ldo;
   g.out_row_mul = 1;
+  g.oy_row = 1;
   g.bias = bias;
   return g;
 }
@@ -701,6 +706,13 @@ Model::Work& Model::work(int B, int T) {
   w->m_big2_ffh = map_2d(w->big2.get(), M, ff_, ff_, kGemmBM);
   w->m_h1 = map_2d(w->big1.get(), M, hid_, hid_, kGemmBM);
   w->m_h2 = map_2d(w->big2.get(), M, hid_, hid_, kGemmBM);
+  w->mo_qkv = map_out_2d(w->big1.get(), false, M, 3 * inner_, 3 * inner_);
+  w->mo_ffh = map_out_2d(w->big2.get(), false, M, ff_, ff_);
+  // band split writes row (bt*nb + band) of the residual stream: view x as {D, nb, BT}
+  w->mo_bs = map_out(w->x.get(), true, D, nb, w->BT, D, (uint64_t)nb * D, /*rows_along_z=*/true);
+  // mask-estimator hidden layers: {hid, BT, nb} so every band's rows clip at BT
+  w->mo_h1 = map_out(w->big1.get(), false, hid_, w->BT, nb, hid_, (uint64_t)w->BT * hid_);
+  w->mo_h2 = map_out(w->big2.get(), false, hid_, w->BT, nb, hid_, (uint64_t)w->BT * hid_);
   {
     const uint64_t C3 = 3 * (uint64_t)inner_;
     const uint64_t dims[4] = {C3, (uint64_t)nb, (uint64_t)T, (uint64_t)B};
@@ -753,11 +765,12 @@ void Model::run_front(const float* audio, int B, long long L, int T, cudaStream_
     GemmGroup g = group((int)w.BT, I.dim, kpad_[b], w.x.get(), I.dim, b_bs_.get<float>() + (size_t)b * I.dim);
     g.a_col0 = kcol_[b];
     g.b_col0 = kcol_[b];
-    g.out_row_mul = I.num_bands;
-    g.out_row_add = b;
+    g.oy0 = b;
+    g.oy_row = 0;
+    g.oz_row = 1;
     p.groups[b] = g;
   }
-  gemm(w.m_abs, m_wbs_, p, kEpiStore32, pick_bn(I.dim), s);
+  gemm(w.m_abs, m_wbs_, w.mo_bs, p, kEpiStore32, pick_bn(I.dim), s);
 }
 
 void Model::run_transformer(int d, int axis, float* x, int B, int T, const float* pending_gamma, cudaStream_t s,
@@ -767,6 +780,7 @@ void Model::run_transformer(int d, int axis, float* x, int B, int T, const float
   const TransformerWeights& tw = axis == 0 ? blocks_[d].first : blocks_[d].second;
   const long long M = (long long)B * T * nb;
   const float scale = std::sqrt((float)D);
+  const CUtensorMap mo_x = map_out_2d(x, true, M, D, D);  // residual reduce-add target
   for (size_t l = 0; l < tw.layers.size(); ++l) {
     const LayerWeights& L = tw.layers[l];
     // attention pre-norm (+ pending final norm of the previous transformer) + gates
@@ -800,7 +814,7 @@ void Model::run_transformer(int d, int axis, float* x, int B, int T, const float
       }
       p.rope_cos = rope_table(p.pos_mod, false);
       p.rope_sin = rope_table(p.pos_mod, true);
-      gemm(w.m_xn, L.m_wqkv, p, kEpiQkvRope, pick_bn(3 * inner_), s);
+      gemm(w.m_xn, L.m_wqkv, w.mo_qkv, p, kEpiQkvRope, pick_bn(3 * inner_), s);
     }
     // attention (+ gate, head merge)
     {
@@ -831,7 +845,7 @@ void Model::run_transformer(int d, int axis, float* x, int B, int T, const float
       GemmParams p{};
       p.num_groups = 1;
       p.groups[0] = group((int)M, D, inner_, x, D, nullptr);
-      gemm(w.m_ao, L.m_wout, p, kEpiResid32, pick_bn(D), s);
+      gemm(w.m_ao, L.m_wout, mo_x, p, kEpiResid32, pick_bn(D), s);
     }
     // feed-forward
     RmsNormArgs rf{};
@@ -847,13 +861,13 @@ void Model::run_transformer(int d, int axis, float* x, int B, int T, const float
       p.num_groups = 1;
       p.act = kActGelu;
       p.groups[0] = group((int)M, ff_, D, w.big2.get(), ff_, L.b1.get<float>());
-      gemm(w.m_xn, L.m_w1, p, kEpiStore16, pick_bn(ff_), s);
+      gemm(w.m_xn, L.m_w1, w.mo_ffh, p, kEpiStore16, pick_bn(ff_), s);
     }
     {
       GemmParams p{};
       p.num_groups = 1;
       p.groups[0] = group((int)M, D, ff_, x, D, L.b2.get<float>());
-      gemm(w.m_big2_ffh, L.m_w2, p, kEpiResid32, pick_bn(D), s);
+      gemm(w.m_big2_ffh, L.m_w2, mo_x, p, kEpiResid32, pick_bn(D), s);
     }
   }
 }
@@ -908,11 +922,13 @@ void Model::run_masks(int B, int T, cudaStream_t s, Work& w, float* masks_out) {
           g = group(BT, hid_, K, hout, hid_, sw.b[i].get<float>() + (size_t)b * hid_);
           g.b_row0 = b * hid_;
           g.out_row_add = (long long)b * BT;
+          g.oz0 = b;
         }
         g.a_row0 = b * BT;
         p.groups[b] = g;
       }
-      gemm(ma, sw.m[i], p, last ? kEpiGlu32 : kEpiStore16, 256, s);
+      const CUtensorMap& mo = (i % 2 == 0) ? w.mo_h1 : w.mo_h2;
+      gemm(ma, sw.m[i], mo, p, last ? kEpiGlu32 : kEpiStore16, 256, s);
     }
   }
   (void)B;
@@ -1036,10 +1052,11 @@ void Model::separate(const float* track, int C, long long L, float overlap, int 
   Work& w = work(eb, T);
   w.chunk_in.ensure(sizeof(float) * (size_t)eb * C * chunk);
   w.chunk_out.ensure(sizeof(float) * (size_t)eb * S * C * chunk);
-  DeviceBuffer acc(sizeof(float) * (size_t)(S * C + 1) * total);
-  float* d_acc = acc.get<float>();
+  const size_t acc_bytes = sizeof(float) * (size_t)(S * C + 1) * total;
+  sep_acc_.ensure(acc_bytes);
+  float* d_acc = sep_acc_.get<float>();
   float* d_wsum = d_acc + (size_t)S * C * total;
-  MSST_CUDA(cudaMemsetAsync(d_acc, 0, acc.bytes(), s));
+  MSST_CUDA(cudaMemsetAsync(d_acc, 0, acc_bytes, s));
   for (int g0 = 0; g0 < nchunks; g0 += eb) {
     const int cnt = std::min(eb, nchunks - g0);
     MSST_CUDA(launch_chunk_gather(ci, g0, cnt, w.chunk_in.get<float>(), s));
@@ -1048,6 +1065,19 @@ void Model::separate(const float* track, int C, long long L, float overlap, int 
   }
   MSST_CUDA(launch_chunk_finish(co, d_acc, d_wsum, out, s));
   MSST_CUDA(cudaStreamSynchronize(s));
+}
+
+void Model::separate_host(const float* track_host, int C, long long L, float overlap, int chunk_batch, int flags,
+                          float* out_host) {
+  if (!host_stream_) MSST_CUDA(cudaStreamCreateWithFlags(&host_stream_, cudaStreamNonBlocking));
+  const size_t in_bytes = sizeof(float) * (size_t)C * L;
+  const size_t out_bytes = in_bytes * (size_t)info_.num_stems;
+  host_in_.ensure(in_bytes);
+  host_out_.ensure(out_bytes);
+  MSST_CUDA(cudaMemcpyAsync(host_in_.get(), track_host, in_bytes, cudaMemcpyHostToDevice, host_stream_));
+  separate(host_in_.get<float>(), C, L, overlap, chunk_batch, flags, host_out_.get<float>(), host_stream_);
+  MSST_CUDA(cudaMemcpyAsync(out_host, host_out_.get(), out_bytes, cudaMemcpyDeviceToHost, host_stream_));
+  MSST_CUDA(cudaStreamSynchronize(host_stream_));
 }
 
 }  // namespace msst

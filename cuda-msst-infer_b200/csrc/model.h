@@ -46,6 +46,10 @@ class Model {
   void transformer(int depth_index, int axis, float* x, int B, int T, cudaStream_t s);
   void separate(const float* track, int C, long long L, float overlap, int chunk_batch, int flags, float* out,
                 cudaStream_t s);
+  // Host buffers in and out (staged through model-owned device buffers; pinned
+  // host memory makes the copies asynchronous DMA).
+  void separate_host(const float* track_host, int C, long long L, float overlap, int chunk_batch, int flags,
+                     float* out_host);
   void chunk_plan(long long L, float overlap, int* chunk, int* step, long long* border, long long* total,
                   int* num_chunks) const;
 
@@ -56,7 +60,8 @@ class Model {
   void run_front(const float* audio, int B, long long L, int T, cudaStream_t s, Work& w);
   void run_masks(int B, int T, cudaStream_t s, Work& w, float* masks_out);
   void run_transformer(int d, int axis, float* x, int B, int T, const float* pending_gamma, cudaStream_t s, Work& w);
-  void gemm(const CUtensorMap& ma, const CUtensorMap& mb, GemmParams& p, int epi, int bn, cudaStream_t s);
+  void gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, GemmParams& p, int epi, int bn,
+            cudaStream_t s);
   const float* rope_table(int n, bool sine);
   const float* istft_wsum(int T);
   cufftHandle fft_plan(cufftType type, int batch, cudaStream_t s);
@@ -84,6 +89,9 @@ class Model {
   std::map<int, DeviceBuffer> rope_cos_, rope_sin_, wsum_;
   std::map<std::pair<int, int>, cufftHandle> plans_;
   std::map<std::pair<int, int>, std::unique_ptr<Work>> work_;
+  DeviceBuffer sep_acc_;                 // overlap-add accumulator of separate(), grown on demand
+  DeviceBuffer host_in_, host_out_;      // staging of separate_host()
+  cudaStream_t host_stream_ = nullptr;   // stream of separate_host()
 
  public:
   Model();

@@ -90,10 +90,12 @@ inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// 16-bit tiled tensor map with 128B swizzle.  dims/strides innermost first;
-// strides in bytes for dims 1..rank-1.
+// Tiled tensor map (16-bit elements and 128B swizzle unless told otherwise).
+// dims/strides innermost first; strides in bytes for dims 1..rank-1.
 inline CUtensorMap make_tensor_map(const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
-                                   const uint32_t* box) {
+                                   const uint32_t* box,
+                                   CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_UINT16,
+                                   CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   CUtensorMap m;
   cuuint64_t d[5];
   cuuint64_t s[4];
@@ -104,11 +106,31 @@ inline CUtensorMap make_tensor_map(const void* base, int rank, const uint64_t* d
     e[i] = 1;
   }
   for (int i = 0; i + 1 < rank; ++i) s[i] = strides_bytes[i];
-  CUresult r = tensor_map_encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT16, (cuuint32_t)rank, const_cast<void*>(base), d, s,
-                                    b, e, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = tensor_map_encoder()(&m, dtype, (cuuint32_t)rank, const_cast<void*>(base), d, s, b, e,
+                                    CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) fail(MSST_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
   return m;
+}
+
+// Output map of the GEMM epilogue: 3-D {cols, Y, Z}; a warp's 32 staged rows
+// run along Y (box {32, 32, 1}) or, with rows_along_z, along Z (box {32, 1, 32}).
+// fp32 outputs (stores and residual reduce-adds) use 128B swizzle over 128 B
+// staging rows; 16-bit outputs use 64B swizzle over 64 B rows.
+inline CUtensorMap map_out(const void* base, bool fp32, uint64_t cols, uint64_t Y, uint64_t Z, uint64_t y_stride_elems,
+                           uint64_t z_stride_elems, bool rows_along_z = false) {
+  const uint64_t esz = fp32 ? 4 : 2;
+  const uint64_t dims[3] = {cols, Y, Z};
+  const uint64_t strides[2] = {y_stride_elems * esz, z_stride_elems * esz};
+  const uint32_t box[3] = {32, rows_along_z ? 1u : 32u, rows_along_z ? 32u : 1u};
+  return make_tensor_map(base, 3, dims, strides, box,
+                         fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16,
+                         fp32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+}
+
+// Plain row-major output [rows, cols] with row stride ld.
+inline CUtensorMap map_out_2d(const void* base, bool fp32, uint64_t rows, uint64_t cols, uint64_t ld) {
+  return map_out(base, fp32, cols, rows, 1, ld, ld * rows);
 }
 
 // Row-major 16-bit matrix [rows, cols] (row stride ld elements) read in boxes of

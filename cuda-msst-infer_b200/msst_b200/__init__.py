@@ -26,7 +26,7 @@ AXIS = {"time": 0, "band": 1}
 SEPARATE_FIX_TAIL_PADDING = 1
 
 EXPORTS = [
-    "msst_last_error", "msst_device_error", "msst_version", "msst_rmsnorm", "msst_gemm", "msst_gemm_qkv_rope",
+    "msst_last_error", "msst_device_error", "msst_version", "msst_kernel_launches", "msst_rmsnorm", "msst_gemm", "msst_gemm_qkv_rope",
     "msst_attention", "msst_model_load", "msst_model_free", "msst_model_get_info", "msst_model_forward",
     "msst_model_masks", "msst_model_transformer", "msst_model_separate", "msst_model_separate_host",
     "msst_model_chunk_plan",
@@ -64,6 +64,8 @@ def lib():
     L.msst_last_error.restype = ctypes.c_char_p
     L.msst_device_error.restype = ctypes.c_uint
     L.msst_device_error.argtypes = [c_int]
+    L.msst_kernel_launches.restype = ctypes.c_ulonglong
+    L.msst_kernel_launches.argtypes = [c_int]
     L.msst_rmsnorm.argtypes = [vp, i64, c_int, vp, c_float, c_int, vp, vp, vp, c_int, vp, vp]
     L.msst_gemm.argtypes = [vp, i64, c_int, i64, vp, c_int, vp, c_int, c_int, c_int, vp, i64, vp]
     L.msst_gemm_qkv_rope.argtypes = [vp, i64, c_int, vp, c_int, vp, vp, c_int, c_int, c_int, vp, vp]
@@ -90,6 +92,11 @@ def check(rc: int) -> None:
 
 def device_error(clear: bool = True) -> int:
     return int(lib().msst_device_error(1 if clear else 0))
+
+
+def kernel_launches(reset: bool = False) -> int:
+    """Kernels launched by libmsst_b200 so far in this process."""
+    return int(lib().msst_kernel_launches(1 if reset else 0))
 
 
 # --------------------------------------------------------------------------- torch helpers

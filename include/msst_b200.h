@@ -68,6 +68,8 @@ const char* msst_last_error(void);
 /* Code recorded by a kernel whose bounded wait gave up (0 = none); clear != 0 resets it. */
 unsigned msst_device_error(int clear);
 int msst_version(void);
+/* Number of kernels this library has launched (process-wide); reset != 0 returns and zeroes it. */
+unsigned long long msst_kernel_launches(int reset);
 
 /* ---------------------------------------------------------------- op level -- */
 
