@@ -1,16 +1,26 @@
 // attention.cu — tcgen05 flash attention for the Roformer's axial attention on
 // sm_100a (head_dim 64, non-causal).
 //
-// CTA = 192 threads, persistent over work items (sequence-or-tile, head, q-tile):
-//   warp 0     TMA producer: Q tile (double-buffered), K/V tiles into a 3-stage ring
-//   warp 1     MMA issuer: S = Q K^T (M128 N128 K64) into one of two TMEM S buffers,
-//              O_j = P_j V_j (M128 N64 K128, P from smem) into one of two TMEM O buffers
-//   warps 2-5  softmax: one query row per thread; online max/sum in fp32, P written
-//              as 16-bit into 128B-swizzled smem (the UMMA A operand), O_j folded into
-//              a register accumulator one tile late so PV overlaps the next softmax;
-//              epilogue divides by the row sum, applies the head gate, writes the
+// CTA = 320 threads, persistent over work items; an item is a PAIR of 128-row
+// query tiles (a, b) of one head:
+//   time axis: two consecutive q-tiles of one sequence; both consume the same
+//              K/V tiles, so each K/V tile is loaded once for 256 query rows
+//   band axis: two consecutive packed tiles (several short sequences each, with
+//              a block-diagonal mask); each has its own single K/V tile
+//   warp 0     TMA producer: Q_a/Q_b, K/V tiles through a 3-stage ring
+//   warp 1     MMA issuer: S_w = Q_w K^T (M128 N128 K64) and O_w += P_w V
+//              (M128 N64 K128, P from smem), issued per tile as
+//              PV_a(j), S_a(j+1), PV_b(j), S_b(j+1) so that S_w(j+1)'s completion
+//              also guarantees PV_w(j) has finished reading P_w
+//   warps 2-5  softmax of tile a, warps 6-9 softmax of tile b: one query row per
+//              thread; steady-state tiles take one pass over S in TMEM (exponent
+//              against the running reference max, which moves lazily: O in TMEM
+//              is rescaled only when the max grows by more than 2^8), P
+//              written as 16-bit into 128B-swizzled smem (the UMMA A operand);
+//              fully masked 32-column chunks are skipped per warp.  The epilogue
+//              divides by the row sum, applies the head gate and writes the
 //              merged-head row.
-// TMEM columns: S0 [0,128) S1 [128,256) O0 [256,320) O1 [320,384) (512 allocated).
+// TMEM: S_a [0,128) S_b [128,256) O_a [256,320) O_b [320,384) (512 allocated).
 #include "attention.cuh"
 #include "common.cuh"
 
@@ -19,74 +29,177 @@ namespace msst {
 namespace {
 
 constexpr int kKvStages = 3;
+constexpr int kThreads = 320;
 constexpr uint32_t kTileBytes = 128 * 64 * 2;   // one 128x64 16-bit tile
 constexpr uint32_t kPBytes = 128 * 128 * 2;     // P tile (two 64-column K-blocks)
 constexpr size_t kAttnSmem = 1024 + 2 * kTileBytes + kKvStages * 2 * kTileBytes + 2 * kPBytes + 256;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColO = 256;
+constexpr float kRescaleLog2 = 8.0f;  // lazy rescale threshold (log2 units)
 
-struct ItemGeom {
+struct PairGeom {
   int head;
-  int nkv;       // KV tiles
-  // mode 0
-  int b, f, t0;
-  // mode 1
-  int r0, rows;  // first token of the packed tile, valid rows (seqs_per_tile * F)
+  int steps;        // K/V tiles streamed for this pair
+  bool has_b;       // second query tile present
+  // time axis
+  int b, f, t0a;    // t0 of tile a; tile b starts at t0a + 128
+  // band axis
+  int r0a, rows;    // first token of tile a; valid rows per packed tile
 };
 
-__device__ __forceinline__ ItemGeom item_geom(const AttnParams& p, int item) {
-  ItemGeom g;
+__device__ __forceinline__ PairGeom pair_geom(const AttnParams& p, int item) {
+  PairGeom g;
   if (p.mode == 0) {
-    const int qt = item % p.q_tiles;
-    const int sh = item / p.q_tiles;
+    const int pairs = (p.q_tiles + 1) >> 1;
+    const int qp = item % pairs;
+    const int sh = item / pairs;
     g.head = sh % p.heads;
     const int s = sh / p.heads;
     g.b = s / p.F;
     g.f = s - g.b * p.F;
-    g.t0 = qt * 128;
-    g.nkv = p.q_tiles;
-    g.r0 = 0;
-    g.rows = 0;
+    g.t0a = qp * 256;
+    g.has_b = 2 * qp + 1 < p.q_tiles;
+    g.steps = p.q_tiles;
+    g.r0a = g.rows = 0;
   } else {
     g.head = item % p.heads;
-    const int tile = item / p.heads;
+    const int pr = item / p.heads;
     g.rows = p.seqs_per_tile * p.seq_len;
-    g.r0 = tile * g.rows;
-    g.nkv = 1;
-    g.b = g.f = g.t0 = 0;
+    g.r0a = 2 * pr * g.rows;
+    g.has_b = 2 * pr + 1 < p.q_tiles;
+    g.steps = g.has_b ? 2 : 1;
+    g.b = g.f = g.t0a = 0;
   }
   return g;
 }
 
+// Does query tile w (0 = a, 1 = b) consume K/V step j?
+__device__ __forceinline__ bool uses(const AttnParams& p, int w, int j) { return p.mode == 0 ? true : (j == w); }
+
+// ---------------------------------------------------------------------------
+// One softmax pass over a 128-column S row held in TMEM (4 chunks of 32
+// columns, loads software-pipelined: chunk ch+1 is in flight while ch is
+// processed).  Chunks outside [c_lo, c_hi) are fully masked for the whole warp;
+// chunks below `c_full` need no per-column mask (warp-uniform), the others mask
+// columns outside [klo, khi).
+//   kPass 0: row max of the valid scores -> mx
+//   kPass 1: P = exp2(s*c - mc) into smem, row sum, max of the exponent -> mx
+//   kPass 2: P = exp2(s*c - mc) into smem, row sum
+// ---------------------------------------------------------------------------
+template <typename T, int kPass>
+__device__ __forceinline__ void process_chunk(const uint32_t (&r)[32], int ch, bool in_range, bool unmasked, int klo,
+                                              int khi, float2 c2, float2 nm2, float& mx, float2& sum2, uint8_t* prow,
+                                              int row) {
+  if constexpr (kPass == 0) {
+    if (!in_range) return;
+    float m0 = -INFINITY, m1 = -INFINITY;
+    if (unmasked) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        m0 = fmaxf(m0, __uint_as_float(r[i]));
+        m1 = fmaxf(m1, __uint_as_float(r[i + 1]));
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        const int col = ch * 32 + i;
+        if (col >= klo && col < khi) m0 = fmaxf(m0, __uint_as_float(r[i]));
+        if (col + 1 >= klo && col + 1 < khi) m1 = fmaxf(m1, __uint_as_float(r[i + 1]));
+      }
+    }
+    mx = fmaxf(mx, fmaxf(m0, m1));
+  } else {
+    uint32_t pk[16];
+    if (!in_range) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) pk[i] = 0u;
+    } else if (unmasked) {
+      float a0 = -INFINITY, a1 = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float2 a = __ffma2_rn(make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), c2, nm2);
+        if constexpr (kPass == 1) {
+          a0 = fmaxf(a0, a.x);
+          a1 = fmaxf(a1, a.y);
+        }
+        const float e0 = fast_exp2(a.x), e1 = fast_exp2(a.y);
+        sum2 = __fadd2_rn(sum2, make_float2(e0, e1));
+        pk[i] = pack2<T>(e0, e1);
+      }
+      if constexpr (kPass == 1) mx = fmaxf(mx, fmaxf(a0, a1));
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int col = ch * 32 + 2 * i;
+        const bool v0 = col >= klo && col < khi, v1 = col + 1 >= klo && col + 1 < khi;
+        const float2 a = __ffma2_rn(make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), c2, nm2);
+        if constexpr (kPass == 1) {
+          if (v0) mx = fmaxf(mx, a.x);
+          if (v1) mx = fmaxf(mx, a.y);
+        }
+        const float e0 = v0 ? fast_exp2(a.x) : 0.f, e1 = v1 ? fast_exp2(a.y) : 0.f;
+        sum2 = __fadd2_rn(sum2, make_float2(e0, e1));
+        pk[i] = pack2<T>(e0, e1);
+      }
+    }
+    // P row: 128B swizzle, two 64-column K-blocks of kPBytes/2
+    uint8_t* blk = prow + (ch >> 1) * (kPBytes / 2);
+    const int chunk0 = (ch & 1) * 4;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int cc = (chunk0 + u) ^ (row & 7);
+      *reinterpret_cast<uint4*>(blk + cc * 16) = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+    }
+  }
+}
+
+template <typename T, int kPass>
+__device__ __forceinline__ void row_pass(uint32_t sAddr, int c_lo, int c_hi, int c_full, int klo, int khi, float c,
+                                         float mc, float& mx, float2& sum2, uint8_t* prow, int row) {
+  const float2 c2 = make_float2(c, c), nm2 = make_float2(-mc, -mc);
+  uint32_t ra[32], rb[32];
+  tmem_ld32(sAddr, ra);
+  tmem_ld_wait(ra);
+  tmem_ld32(sAddr + 32, rb);
+  process_chunk<T, kPass>(ra, 0, 0 >= c_lo && 0 < c_hi, 0 < c_full, klo, khi, c2, nm2, mx, sum2, prow, row);
+  tmem_ld_wait(rb);
+  tmem_ld32(sAddr + 64, ra);
+  process_chunk<T, kPass>(rb, 1, 1 >= c_lo && 1 < c_hi, 1 < c_full, klo, khi, c2, nm2, mx, sum2, prow, row);
+  tmem_ld_wait(ra);
+  tmem_ld32(sAddr + 96, rb);
+  process_chunk<T, kPass>(ra, 2, 2 >= c_lo && 2 < c_hi, 2 < c_full, klo, khi, c2, nm2, mx, sum2, prow, row);
+  tmem_ld_wait(rb);
+  process_chunk<T, kPass>(rb, 3, 3 >= c_lo && 3 < c_hi, 3 < c_full, klo, khi, c2, nm2, mx, sum2, prow, row);
+}
+
 template <typename T>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kThreads, 1)
     attention_kernel(const __grid_constant__ CUtensorMap qkv, const __grid_constant__ AttnParams p) {
   constexpr uint32_t kIsBf16 = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;                                  // 2 tiles
-  uint8_t* sKV = sQ + 2 * kTileBytes;                  // stages x (K, V)
-  uint8_t* sP = sKV + kKvStages * 2 * kTileBytes;      // 2 P tiles
+  uint8_t* sQ = smem;                              // Q_a, Q_b
+  uint8_t* sKV = sQ + 2 * kTileBytes;              // stages x (K, V)
+  uint8_t* sP = sKV + kKvStages * 2 * kTileBytes;  // P_a, P_b
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kPBytes);
-  uint64_t* q_full = bars;
-  uint64_t* q_empty = bars + 2;
-  uint64_t* kv_full = bars + 4;
+  uint64_t* q_full = bars + 0;
+  uint64_t* q_empty = bars + 1;
+  uint64_t* kv_full = bars + 2;
   uint64_t* kv_empty = kv_full + kKvStages;
-  uint64_t* s_full = kv_empty + kKvStages;
-  uint64_t* p_full = s_full + 2;
-  uint64_t* o_full = p_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 2);
+  uint64_t* s_full = kv_empty + kKvStages;  // [2]
+  uint64_t* p_full = s_full + 2;            // [2]
+  uint64_t* o_done = p_full + 2;            // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int C = 3 * p.heads * 64;
   if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&q_full[i], 1);
-      mbar_init(&q_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
-      mbar_init(&o_full[i], 1);
+      mbar_init(&o_done[i], 1);
     }
     for (int s = 0; s < kKvStages; ++s) {
       mbar_init(&kv_full[s], 1);
@@ -103,38 +216,41 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const int HD = p.heads * 64;
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      int qcount = 0, kvcount = 0;
+      int pc = 0, kvc = 0;
       bool ok = true;
-      for (int item = blockIdx.x; ok && item < p.total_items; item += gridDim.x, ++qcount) {
-        const ItemGeom g = item_geom(p, item);
-        const int qb = qcount & 1;
-        if (!mbar_wait(&q_empty[qb], ((qcount >> 1) & 1) ^ 1, kErrTimeoutAttnQ, abort_flag)) break;
-        mbar_arrive_expect_tx(&q_full[qb], kTileBytes);
+      for (int item = blockIdx.x; ok && item < p.total_items; item += gridDim.x, ++pc) {
+        const PairGeom g = pair_geom(p, item);
+        if (!mbar_wait(q_empty, (pc & 1) ^ 1, kErrTimeoutAttnQ, abort_flag)) break;
+        mbar_arrive_expect_tx(q_full, (g.has_b ? 2 : 1) * kTileBytes);
         const int xq = g.head * 64;
-        if (p.mode == 0)
-          tma_load_4d(sQ + qb * kTileBytes, &qkv, &q_full[qb], xq, g.f, g.t0, g.b);
-        else
-          tma_load_4d(sQ + qb * kTileBytes, &qkv, &q_full[qb], xq, g.r0, 0, 0);
-        for (int j = 0; j < g.nkv; ++j, ++kvcount) {
-          const int st = kvcount % kKvStages;
-          const uint32_t ph = (kvcount / kKvStages) & 1;
-          if (!mbar_wait(&kv_empty[st], ph ^ 1, kErrTimeoutAttnKV, abort_flag)) {
+        if (p.mode == 0) {
+          tma_load_4d(sQ, &qkv, q_full, xq, g.f, g.t0a, g.b);
+          if (g.has_b) tma_load_4d(sQ + kTileBytes, &qkv, q_full, xq, g.f, g.t0a + 128, g.b);
+        } else {
+          tma_load_4d(sQ, &qkv, q_full, xq, g.r0a, 0, 0);
+          if (g.has_b) tma_load_4d(sQ + kTileBytes, &qkv, q_full, xq, g.r0a + g.rows, 0, 0);
+        }
+        const int xk = HD + g.head * 64, xv = 2 * HD + g.head * 64;
+        for (int j = 0; j < g.steps; ++j, ++kvc) {
+          const int st = kvc % kKvStages;
+          if (!mbar_wait(&kv_empty[st], ((kvc / kKvStages) & 1) ^ 1, kErrTimeoutAttnKV, abort_flag)) {
             ok = false;
             break;
           }
           mbar_arrive_expect_tx(&kv_full[st], 2 * kTileBytes);
           uint8_t* dk = sKV + st * 2 * kTileBytes;
-          const int xk = p.heads * 64 + g.head * 64, xv = 2 * p.heads * 64 + g.head * 64;
           if (p.mode == 0) {
             tma_load_4d(dk, &qkv, &kv_full[st], xk, g.f, j * 128, g.b);
             tma_load_4d(dk + kTileBytes, &qkv, &kv_full[st], xv, g.f, j * 128, g.b);
           } else {
-            tma_load_4d(dk, &qkv, &kv_full[st], xk, g.r0, 0, 0);
-            tma_load_4d(dk + kTileBytes, &qkv, &kv_full[st], xv, g.r0, 0, 0);
+            const int r0 = g.r0a + j * g.rows;
+            tma_load_4d(dk, &qkv, &kv_full[st], xk, r0, 0, 0);
+            tma_load_4d(dk + kTileBytes, &qkv, &kv_full[st], xv, r0, 0, 0);
           }
         }
       }
@@ -144,203 +260,210 @@ __global__ void __launch_bounds__(192, 1)
     if (lane == 0) {
       const uint32_t idesc_s = umma_idesc_f16(kIsBf16, 128, 0);
       const uint32_t idesc_o = umma_idesc_f16(kIsBf16, 64, 1);
-      int qcount = 0, kvcount = 0, scount = 0, pcount = 0;
+      int pc = 0, kvc = 0;
+      uint32_t pcnt[2] = {0, 0};  // P tiles consumed per query tile (phase of p_full)
       bool ok = true;
-      for (int item = blockIdx.x; ok && item < p.total_items; item += gridDim.x, ++qcount) {
-        const ItemGeom g = item_geom(p, item);
-        const int qb = qcount & 1;
-        if (!mbar_wait(&q_full[qb], (qcount >> 1) & 1, kErrTimeoutAttnQ, abort_flag)) break;
+      auto issue_s = [&](int w, int st) {
+        const uint32_t qaddr = smem_u32(sQ + w * kTileBytes);
+        const uint32_t kaddr = smem_u32(sKV + st * 2 * kTileBytes);
+        const uint32_t dS = tmem + kColS + (uint32_t)(w * 128);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_f16_ss(dS, sw128_desc(qaddr + kk * 32, 16, 1024), sw128_desc(kaddr + kk * 32, 16, 1024), idesc_s,
+                      kk > 0 ? 1u : 0u);
+        umma_commit(&s_full[w]);
+      };
+      auto issue_pv = [&](int w, int st, bool first) -> bool {
+        if (!mbar_wait(&p_full[w], pcnt[w] & 1, kErrTimeoutAttnP, abort_flag)) return false;
+        ++pcnt[w];
         tc_fence_after();
-        const uint32_t qaddr = smem_u32(sQ + qb * kTileBytes);
-        int prev_stage = -1;
-        for (int j = 0; j <= g.nkv; ++j) {
-          if (j < g.nkv) {
-            const int st = kvcount % kKvStages;
-            if (!mbar_wait(&kv_full[st], (kvcount / kKvStages) & 1, kErrTimeoutAttnKV, abort_flag)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t kaddr = smem_u32(sKV + st * 2 * kTileBytes);
-            const uint32_t dS = tmem + kColS + (uint32_t)((scount & 1) * 128);
+        const uint32_t paddr = smem_u32(sP + w * kPBytes);
+        const uint32_t vaddr = smem_u32(sKV + st * 2 * kTileBytes + kTileBytes);
+        const uint32_t dO = tmem + kColO + (uint32_t)(w * 64);
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              umma_f16_ss(dS, sw128_desc(qaddr + kk * 32, 16, 1024), sw128_desc(kaddr + kk * 32, 16, 1024), idesc_s,
-                          kk > 0 ? 1u : 0u);
-            umma_commit(&s_full[scount & 1]);
-            ++scount;
-            if (j == g.nkv - 1) umma_commit(&q_empty[qb]);
-          }
-          if (j > 0) {
-            // O_{j-1} = P_{j-1} V_{j-1}
-            const int pb = pcount & 1;
-            if (!mbar_wait(&p_full[pb], (pcount >> 1) & 1, kErrTimeoutAttnP, abort_flag)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t paddr = smem_u32(sP + pb * kPBytes);
-            const uint32_t vaddr = smem_u32(sKV + prev_stage * 2 * kTileBytes + kTileBytes);
-            const uint32_t dO = tmem + kColO + (uint32_t)(pb * 64);
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk)
-              umma_f16_ss(dO, sw128_desc(paddr + (kk >> 2) * (kPBytes / 2) + (kk & 3) * 32, 16, 1024),
-                          sw128_desc(vaddr + kk * 2048, kTileBytes, 1024), idesc_o, kk > 0 ? 1u : 0u);
-            umma_commit(&o_full[pb]);
-            umma_commit(&kv_empty[prev_stage]);
-            ++pcount;
-          }
-          if (j < g.nkv) {
-            prev_stage = kvcount % kKvStages;
-            ++kvcount;
-          }
-        }
-      }
-    }
-  } else {
-    // ------------------------------------------------------------ softmax + epilogue
-    const int q = warp & 3;
-    const int row = q * 32 + lane;
-    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-    const float c = p.scale_log2;
-    int scount = 0, pcount = 0;
-    for (int item = blockIdx.x; item < p.total_items; item += gridDim.x) {
-      const ItemGeom g = item_geom(p, item);
-      float acc[64];
-#pragma unroll
-      for (int i = 0; i < 64; ++i) acc[i] = 0.f;
-      float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
-      // band axis: this row's sequence inside the packed tile
-      const int seq_lo = p.mode == 1 ? (row / p.seq_len) * p.seq_len : 0;
-      const int seq_hi = p.mode == 1 ? min(seq_lo + p.seq_len, g.rows) : 0;
-      bool ok = true;
-      for (int j = 0; j < g.nkv; ++j) {
-        if (!mbar_wait(&s_full[scount & 1], (scount >> 1) & 1, kErrTimeoutAttnS, abort_flag)) {
-          ok = false;
-          break;
-        }
+        for (int kk = 0; kk < 8; ++kk)
+          umma_f16_ss(dO, sw128_desc(paddr + (kk >> 2) * (kPBytes / 2) + (kk & 3) * 32, 16, 1024),
+                      sw128_desc(vaddr + kk * 2048, kTileBytes, 1024), idesc_o, (first && kk == 0) ? 0u : 1u);
+        return true;
+      };
+      for (int item = blockIdx.x; ok && item < p.total_items; item += gridDim.x, ++pc) {
+        const PairGeom g = pair_geom(p, item);
+        const int nw = g.has_b ? 2 : 1;
+        if (!mbar_wait(q_full, pc & 1, kErrTimeoutAttnQ, abort_flag)) break;
         tc_fence_after();
-        const uint32_t sAddr = tmem + lane_off + kColS + (uint32_t)((scount & 1) * 128);
-        ++scount;
-        int lo, hi;  // valid key columns [lo, hi) of this tile for this row
-        if (p.mode == 0) {
-          lo = 0;
-          hi = min(128, p.seq_len - j * 128);
-        } else {
-          lo = seq_lo;
-          hi = seq_hi;
-        }
-        // pass 1: row max
-        float mx = -INFINITY;
-#pragma unroll
-        for (int c0 = 0; c0 < 128; c0 += 32) {
-          uint32_t r[32];
-          tmem_ld32(sAddr + c0, r);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int col = c0 + i;
-            if (col >= lo && col < hi) mx = fmaxf(mx, __uint_as_float(r[i]));
-          }
-        }
-        const float m_new = fmaxf(m, mx);
-        const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-        const float alpha = fast_exp2((m - m_use) * c);
-        const float mc = m_use * c;
-        // pass 2: probabilities -> P smem (128B swizzle, K-major), row sum
-        const int pb = pcount & 1;
-        uint8_t* prow = sP + pb * kPBytes + row * 128;
-        float sum = 0.f;
-#pragma unroll
-        for (int c0 = 0; c0 < 128; c0 += 32) {
-          uint32_t r[32];
-          tmem_ld32(sAddr + c0, r);
-          tmem_ld_wait();
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int col = c0 + 2 * i;
-            const float s0 = (col >= lo && col < hi) ? fast_exp2(fmaf(__uint_as_float(r[2 * i]), c, -mc)) : 0.f;
-            const float s1 =
-                (col + 1 >= lo && col + 1 < hi) ? fast_exp2(fmaf(__uint_as_float(r[2 * i + 1]), c, -mc)) : 0.f;
-            sum += s0 + s1;
-            pk[i] = pack2<T>(s0, s1);
-          }
-          uint8_t* blk = prow + (c0 >> 6) * (kPBytes / 2);
-          const int chunk0 = (c0 & 63) >> 3;
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int ch = (chunk0 + u) ^ (row & 7);
-            *reinterpret_cast<uint4*>(blk + ch * 16) = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
-          }
-        }
-        fence_proxy_async_smem();
-        tc_fence_before();
-        mbar_arrive(&p_full[pb]);
-        ++pcount;
-        l = l * alpha + sum;
-        if (j > 0) {
-          const int ob = (pcount - 2) & 1;
-          if (!mbar_wait(&o_full[ob], ((pcount - 2) >> 1) & 1, kErrTimeoutAttnO, abort_flag)) {
+        int last_used[2] = {-1, -1};  // K/V stage of each tile's previous step
+        int used_count[2] = {0, 0};
+        for (int j = 0; ok && j < g.steps; ++j) {
+          const int st = (kvc + j) % kKvStages;
+          if (!mbar_wait(&kv_full[st], ((kvc + j) / kKvStages) & 1, kErrTimeoutAttnKV, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t oAddr = tmem + lane_off + kColO + (uint32_t)(ob * 64);
-#pragma unroll
-          for (int c0 = 0; c0 < 64; c0 += 32) {
-            uint32_t r[32];
-            tmem_ld32(oAddr + c0, r);
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) acc[c0 + i] = fmaf(acc[c0 + i], alpha_prev, __uint_as_float(r[i]));
+          for (int w = 0; w < nw; ++w) {
+            if (!uses(p, w, j)) continue;
+            if (last_used[w] >= 0) {
+              if (!issue_pv(w, last_used[w], used_count[w] == 1)) {
+                ok = false;
+                break;
+              }
+              // the previous K/V stage is free once the last tile using it has issued its PV
+              if (w == nw - 1 || p.mode == 1) umma_commit(&kv_empty[last_used[w]]);
+            }
+            issue_s(w, st);
+            last_used[w] = st;
+            ++used_count[w];
           }
         }
-        alpha_prev = alpha;
-        m = m_new;
-      }
-      if (!ok) break;
-      {
-        const int ob = (pcount - 1) & 1;
-        if (!mbar_wait(&o_full[ob], ((pcount - 1) >> 1) & 1, kErrTimeoutAttnO, abort_flag)) break;
-        tc_fence_after();
-        const uint32_t oAddr = tmem + lane_off + kColO + (uint32_t)(ob * 64);
-#pragma unroll
-        for (int c0 = 0; c0 < 64; c0 += 32) {
-          uint32_t r[32];
-          tmem_ld32(oAddr + c0, r);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) acc[c0 + i] = fmaf(acc[c0 + i], alpha_prev, __uint_as_float(r[i]));
+        if (!ok) break;
+        umma_commit(q_empty);  // every S of this pair has been issued
+        for (int w = 0; w < nw; ++w) {
+          if (!issue_pv(w, last_used[w], used_count[w] == 1)) {
+            ok = false;
+            break;
+          }
+          if (w == nw - 1 || p.mode == 1) umma_commit(&kv_empty[last_used[w]]);
+          umma_commit(&o_done[w]);
         }
+        kvc += g.steps;
       }
-      // epilogue: normalise, gate, merged-head store
-      long long token;
+    }
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue
+    const int w = (warp - 2) >> 2;  // query tile of this warp group
+    const int q = warp & 3;         // TMEM lane quarter
+    const int row = q * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    const uint32_t sAddr = tmem + lane_off + kColS + (uint32_t)(w * 128);
+    const uint32_t oAddr = tmem + lane_off + kColO + (uint32_t)(w * 64);
+    uint8_t* prow = sP + w * kPBytes + row * 128;
+    const float c = p.scale_log2;
+    uint32_t scnt = 0, ocnt = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; ok && item < p.total_items; item += gridDim.x) {
+      const PairGeom g = pair_geom(p, item);
+      if (w == 1 && !g.has_b) continue;
+      // rows of this thread / warp
       bool valid;
+      long long token;
+      int lo = 0, hi_seq = 0;
       if (p.mode == 0) {
-        const int t = g.t0 + row;
+        const int t = g.t0a + w * 128 + row;
         valid = t < p.T;
         token = ((long long)g.b * p.T + t) * p.F + g.f;
       } else {
-        valid = row < g.rows && g.r0 + row < p.num_tokens;
-        token = (long long)g.r0 + row;
+        const int r0 = g.r0a + w * g.rows;
+        valid = row < g.rows && r0 + row < p.num_tokens;
+        token = (long long)r0 + row;
+        lo = (row / p.seq_len) * p.seq_len;
+        hi_seq = min(lo + p.seq_len, g.rows);
       }
-      if (valid) {
-        float scale = l > 0.f ? 1.f / l : 0.f;
-        if (p.gates != nullptr) scale *= __ldg(p.gates + token * p.heads + g.head);
-        uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.out) + token * (p.heads * 64) + g.head * 64);
+      const bool warp_active = __any_sync(0xffffffffu, valid);
+      float m = -INFINITY, l = 0.f;
+      int used = 0;
+      for (int j = 0; j < g.steps; ++j) {
+        if (!uses(p, w, j)) continue;
+        if (!mbar_wait(&s_full[w], scnt & 1, kErrTimeoutAttnS, abort_flag)) {
+          ok = false;
+          break;
+        }
+        ++scnt;
+        tc_fence_after();
+        // valid key columns [klo, khi) of this tile for this row; warp-uniform chunk range
+        int klo, khi;
+        if (p.mode == 0) {
+          klo = 0;
+          khi = min(128, p.seq_len - j * 128);
+        } else {
+          klo = lo;
+          khi = hi_seq;
+        }
+        int wlo = klo, whi = khi;
+        if (p.mode == 1) {
+          wlo = __reduce_min_sync(0xffffffffu, valid ? klo : 128);
+          whi = __reduce_max_sync(0xffffffffu, valid ? khi : 0);
+        }
+        const int c_lo = wlo >> 5, c_hi = (whi + 31) >> 5;  // chunks holding any valid column
+        if (warp_active) {
+          // chunks needing no per-column mask (time axis: entirely below khi)
+          const int c_full = (p.mode == 0) ? (khi >> 5) : 0;
+          float2 sum2 = make_float2(0.f, 0.f);
+          bool exact = (used == 0) || (p.mode == 1);
+          if (!exact) {
+            // steady state: exponentiate against the current reference max in one pass and
+            // track how far above it the row went
+            float amax = -INFINITY;
+            const float mc = (m == -INFINITY) ? 0.f : m * c;
+            row_pass<T, 1>(sAddr, c_lo, c_hi, c_full, klo, khi, c, mc, amax, sum2, prow, row);
+            if (__any_sync(0xffffffffu, amax > kRescaleLog2)) {
+              exact = true;
+              sum2 = make_float2(0.f, 0.f);
+            }
+          }
+          if (exact) {
+            float mx = -INFINITY;
+            row_pass<T, 0>(sAddr, c_lo, c_hi, c_full, klo, khi, c, 0.f, mx, sum2, prow, row);
+            // lazy rescale: move the reference max only when it grows by > 2^8
+            const bool grow = (mx > m) && ((m == -INFINITY) || (mx - m) * c > kRescaleLog2);
+            if (__any_sync(0xffffffffu, grow)) {
+              const float m_new = grow ? mx : m;
+              const float alpha = (m == -INFINITY) ? 0.f : fast_exp2((m - m_new) * c);
+              if (used > 0) {
+                // O_w holds the previous tiles' P.V (complete: S_w(j) was issued after PV_w(j-1))
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          o[u] = make_uint4(pack2<T>(acc[8 * u] * scale, acc[8 * u + 1] * scale),
-                            pack2<T>(acc[8 * u + 2] * scale, acc[8 * u + 3] * scale),
-                            pack2<T>(acc[8 * u + 4] * scale, acc[8 * u + 5] * scale),
-                            pack2<T>(acc[8 * u + 6] * scale, acc[8 * u + 7] * scale));
+                for (int h = 0; h < 2; ++h) {
+                  uint32_t r[32];
+                  tmem_ld32(oAddr + h * 32, r);
+                  tmem_ld_wait(r);
+#pragma unroll
+                  for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+                  tmem_st32(oAddr + h * 32, r);
+                }
+                tmem_st_wait();
+              }
+              l *= alpha;
+              m = m_new;
+            }
+            const float mc = (m == -INFINITY) ? 0.f : m * c;
+            float unused = 0.f;
+            row_pass<T, 2>(sAddr, c_lo, c_hi, c_full, klo, khi, c, mc, unused, sum2, prow, row);
+          }
+          l += sum2.x + sum2.y;
+          fence_proxy_async_smem();
+        }
+        ++used;
+        tc_fence_before();
+        mbar_arrive(&p_full[w]);
+      }
+      if (!ok) break;
+      // epilogue: O_w complete after the pair's last PV
+      if (!mbar_wait(&o_done[w], ocnt & 1, kErrTimeoutAttnO, abort_flag)) break;
+      ++ocnt;
+      tc_fence_after();
+      if (warp_active) {
+        float scale = l > 0.f ? 1.f / l : 0.f;
+        if (valid && p.gates != nullptr) scale *= __ldg(p.gates + token * p.heads + g.head);
+        uint4* out = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.out) + token * HD + g.head * 64);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t r[32];
+          tmem_ld32(oAddr + h * 32, r);
+          tmem_ld_wait();
+          if (valid) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              float v[8];
+#pragma unroll
+              for (int k = 0; k < 8; ++k) v[k] = __uint_as_float(r[8 * u + k]) * scale;
+              out[4 * h + u] = make_uint4(pack2<T>(v[0], v[1]), pack2<T>(v[2], v[3]), pack2<T>(v[4], v[5]),
+                                          pack2<T>(v[6], v[7]));
+            }
+          }
         }
       }
       tc_fence_before();
     }
   }
-  (void)C;
 
   __syncthreads();
   if (warp == 1) {
@@ -361,7 +484,7 @@ cudaError_t launch_t(const CUtensorMap& m, const AttnParams& p, int num_sms, cud
   const int grid = p.total_items < num_sms ? p.total_items : num_sms;
   if (grid <= 0) return cudaSuccess;
   note_launch();
-  attention_kernel<T><<<grid, 192, kAttnSmem, s>>>(m, p);
+  attention_kernel<T><<<grid, kThreads, kAttnSmem, s>>>(m, p);
   return cudaGetLastError();
 }
 
@@ -370,7 +493,13 @@ cudaError_t launch_t(const CUtensorMap& m, const AttnParams& p, int num_sms, cud
 cudaError_t launch_attention(const CUtensorMap& qkv_map, const AttnParams& p, int bf16, int num_sms,
                              cudaStream_t stream) {
   if (p.mode == 1 && (p.seq_len > 128 || p.seqs_per_tile < 1)) return cudaErrorInvalidValue;
-  return bf16 ? launch_t<__nv_bfloat16>(qkv_map, p, num_sms, stream) : launch_t<__half>(qkv_map, p, num_sms, stream);
+  if (p.q_tiles < 1) return cudaSuccess;
+  AttnParams a = p;
+  const long long pairs = (p.q_tiles + 1) / 2;
+  const long long items = p.mode == 0 ? (long long)p.B * p.F * p.heads * pairs : pairs * p.heads;
+  if (items > 0x7fffffffLL) return cudaErrorInvalidValue;
+  a.total_items = (int)items;
+  return bf16 ? launch_t<__nv_bfloat16>(qkv_map, a, num_sms, stream) : launch_t<__half>(qkv_map, a, num_sms, stream);
 }
 
 MSST_DEFINE_ERROR_ACCESSOR(attention_device_error)

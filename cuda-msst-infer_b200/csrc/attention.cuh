@@ -26,7 +26,7 @@ struct AttnParams {
   int seq_len;        // T (mode 0) or F (mode 1)
   int q_tiles;        // mode 0: ceil(T/128); mode 1: number of 128-row packed tiles
   int seqs_per_tile;  // mode 1: floor(128 / F)
-  int total_items;    // work items = (sequences * H * q_tiles) or (q_tiles * H)
+  int total_items;    // set by launch_attention: pairs of q-tiles x heads (x sequences on the time axis)
   int num_tokens;     // B*T*F
   float scale_log2;   // softmax scale * log2(e)
   const float* gates; // [tokens, heads] (sigmoid already applied) or nullptr
