@@ -303,6 +303,15 @@ int msst_model_transformer(msst_model* m, int depth_index, int axis, float* x, i
   });
 }
 
+int msst_model_transformer_noalloc(msst_model* m, int depth_index, int axis, float* x, int batch, int T,
+                                   void* stream) {
+  return guarded([&] {
+    MSST_REQUIRE(m && x, "null argument");
+    MSST_CUDA(cudaSetDevice(m->impl.device()));
+    m->impl.transformer_noalloc(depth_index, axis, x, batch, T, as_stream(stream));
+  });
+}
+
 int msst_model_separate(msst_model* m, const float* track, int channels, long long length, float overlap,
                         int chunk_batch, int flags, float* out, void* stream) {
   return guarded([&] {

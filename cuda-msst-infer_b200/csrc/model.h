@@ -44,6 +44,9 @@ class Model {
   void forward(const float* audio, int B, int C, long long L, float* out, cudaStream_t s);
   void masks(const float* audio, int B, int C, long long L, float* masks_out, cudaStream_t s);
   void transformer(int depth_index, int axis, float* x, int B, int T, cudaStream_t s);
+  // Same as transformer(), with every intermediate in the library's fixed device
+  // array (noalloc.cu); allocates nothing.
+  void transformer_noalloc(int depth_index, int axis, float* x, int B, int T, cudaStream_t s);
   void separate(const float* track, int C, long long L, float overlap, int chunk_batch, int flags, float* out,
                 cudaStream_t s);
   // Host buffers in and out (staged through model-owned device buffers; pinned

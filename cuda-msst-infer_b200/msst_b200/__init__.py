@@ -28,7 +28,7 @@ SEPARATE_FIX_TAIL_PADDING = 1
 EXPORTS = [
     "msst_last_error", "msst_device_error", "msst_version", "msst_kernel_launches", "msst_rmsnorm", "msst_gemm", "msst_gemm_qkv_rope",
     "msst_attention", "msst_model_load", "msst_model_free", "msst_model_get_info", "msst_model_forward",
-    "msst_model_masks", "msst_model_transformer", "msst_model_separate", "msst_model_separate_host",
+    "msst_model_masks", "msst_model_transformer", "msst_model_transformer_noalloc", "msst_model_separate", "msst_model_separate_host",
     "msst_model_chunk_plan",
 ]
 
@@ -77,6 +77,7 @@ def lib():
     L.msst_model_forward.argtypes = [vp, vp, c_int, c_int, i64, vp, vp]
     L.msst_model_masks.argtypes = [vp, vp, c_int, c_int, i64, vp, vp]
     L.msst_model_transformer.argtypes = [vp, c_int, c_int, vp, c_int, c_int, vp]
+    L.msst_model_transformer_noalloc.argtypes = [vp, c_int, c_int, vp, c_int, c_int, vp]
     L.msst_model_separate.argtypes = [vp, vp, c_int, i64, c_float, c_int, c_int, vp, vp]
     L.msst_model_separate_host.argtypes = [vp, fp, c_int, i64, c_float, c_int, c_int, fp]
     L.msst_model_chunk_plan.argtypes = [vp, i64, c_float, ctypes.POINTER(c_int), ctypes.POINTER(c_int),

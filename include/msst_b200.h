@@ -135,6 +135,21 @@ int msst_model_masks(msst_model* m, const float* audio, int batch, int channels,
  * src/model_bs_roformer.cu:310-331, with the permutes of forward() folded away). */
 int msst_model_transformer(msst_model* m, int depth_index, int axis, float* x, int batch, int T, void* stream);
 
+/* msst_model_transformer for callers that cannot allocate device memory while
+ * they run: real-time audio hosts, whose processing callback has a hard deadline
+ * that a cudaMalloc / cudaFree (which can block and synchronise the device)
+ * would break, and applications that own every device allocation themselves.
+ * There is no counterpart in the reference.  All intermediates live in one
+ * fixed 48 MiB device array inside the library (held on every GPU that loads
+ * it, until exit); nothing is allocated.  A call over batch*T*num_bands tokens
+ * needs about dim*2 + heads*4 + 2*max(3*heads*64, 4*dim) + heads*128 bytes per
+ * token (about 10,000 tokens at dim 384) and larger calls fail with
+ * MSST_ERR_INVALID.  Calls on one device share the array: calls that overlap on
+ * the GPU race.  The first call on a device looks up the array's device address;
+ * make it before any stream capture. */
+int msst_model_transformer_noalloc(msst_model* m, int depth_index, int axis, float* x, int batch, int T,
+                                   void* stream);
+
 /* Chunked overlap-add separation of one track (replaces app::run_inference /
  * process_chunked, src/inference_app.cpp:100-324,443-497).  track [channels,
  * length] -> out [num_stems, channels, length].  overlap: (0,1) = overlap
