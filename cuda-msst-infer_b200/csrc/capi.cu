@@ -330,6 +330,25 @@ int msst_model_separate_host(msst_model* m, const float* track_host, int channel
   });
 }
 
+int msst_model_forward_chunks(msst_model* m, const float* track, int channels, long long length, float overlap,
+                              int first_chunk, int count, int chunk_batch, int flags, float* out, void* stream) {
+  return guarded([&] {
+    MSST_REQUIRE(m && track && (out || count == 0), "null argument");
+    MSST_CUDA(cudaSetDevice(m->impl.device()));
+    m->impl.forward_chunks(track, channels, length, overlap, first_chunk, count, chunk_batch, flags, out,
+                           as_stream(stream));
+  });
+}
+
+int msst_model_stitch(msst_model* m, const float* chunks, int channels, long long length, float overlap, float* out,
+                      void* stream) {
+  return guarded([&] {
+    MSST_REQUIRE(m && chunks && out, "null argument");
+    MSST_CUDA(cudaSetDevice(m->impl.device()));
+    m->impl.stitch(chunks, channels, length, overlap, out, as_stream(stream));
+  });
+}
+
 int msst_model_chunk_plan(const msst_model* m, long long length, float overlap, int* chunk_size, int* step,
                           long long* border, long long* padded_length, int* num_chunks) {
   return guarded([&] {

@@ -1067,6 +1067,65 @@ void Model::separate(const float* track, int C, long long L, float overlap, int 
   MSST_CUDA(cudaStreamSynchronize(s));
 }
 
+void Model::forward_chunks(const float* track, int C, long long L, float overlap, int first, int count,
+                           int chunk_batch, int flags, float* out, cudaStream_t s) {
+  const msst_model_info& I = info_;
+  MSST_REQUIRE(C == C_, "channel count does not match the model");
+  int chunk, step, nchunks;
+  long long border, total;
+  chunk_plan(L, overlap, &chunk, &step, &border, &total, &nchunks);
+  MSST_REQUIRE(chunk % I.hop_length == 0, "chunk_size must be a multiple of hop_length");
+  MSST_REQUIRE(first >= 0 && count >= 0 && first + count <= nchunks, "chunk range outside the track's plan");
+  if (count == 0) return;
+  const int S = I.num_stems;
+  const int eb = std::max(1, std::min(chunk_batch > 0 ? chunk_batch : 2, count));
+  ChunkArgs ci{};
+  ci.track = track;
+  ci.C = C;
+  ci.L = L;
+  ci.border = border;
+  ci.total = total;
+  ci.chunk = chunk;
+  ci.step = step;
+  ci.ref_compat = (flags & MSST_SEPARATE_FIX_TAIL_PADDING) ? 0 : 1;
+  const int T = chunk / I.hop_length + 1;
+  Work& w = work(eb, T);
+  w.chunk_in.ensure(sizeof(float) * (size_t)eb * C * chunk);
+  const size_t per_chunk = (size_t)S * C * chunk;
+  for (int g0 = first; g0 < first + count; g0 += eb) {
+    const int cnt = std::min(eb, first + count - g0);
+    MSST_CUDA(launch_chunk_gather(ci, g0, cnt, w.chunk_in.get<float>(), s));
+    forward(w.chunk_in.get<float>(), cnt, C, chunk, out + (size_t)(g0 - first) * per_chunk, s);
+  }
+}
+
+void Model::stitch(const float* chunks, int C, long long L, float overlap, float* out, cudaStream_t s) {
+  const msst_model_info& I = info_;
+  int chunk, step, nchunks;
+  long long border, total;
+  chunk_plan(L, overlap, &chunk, &step, &border, &total, &nchunks);
+  const int S = I.num_stems;
+  ChunkArgs co{};
+  co.C = S * C;
+  co.L = L;
+  co.border = border;
+  co.total = total;
+  co.chunk = chunk;
+  co.step = step;
+  const size_t acc_bytes = sizeof(float) * (size_t)(S * C + 1) * total;
+  sep_acc_.ensure(acc_bytes);
+  float* d_acc = sep_acc_.get<float>();
+  float* d_wsum = d_acc + (size_t)S * C * total;
+  MSST_CUDA(cudaMemsetAsync(d_acc, 0, acc_bytes, s));
+  const size_t per_chunk = (size_t)S * C * chunk;
+  constexpr int kGroup = 4;  // chunks folded per launch, in chunk order
+  for (int g0 = 0; g0 < nchunks; g0 += kGroup) {
+    const int cnt = std::min(kGroup, nchunks - g0);
+    MSST_CUDA(launch_chunk_ola(co, g0, cnt, nchunks, chunks + (size_t)g0 * per_chunk, d_acc, d_wsum, s));
+  }
+  MSST_CUDA(launch_chunk_finish(co, d_acc, d_wsum, out, s));
+}
+
 void Model::separate_host(const float* track_host, int C, long long L, float overlap, int chunk_batch, int flags,
                           float* out_host) {
   if (!host_stream_) MSST_CUDA(cudaStreamCreateWithFlags(&host_stream_, cudaStreamNonBlocking));

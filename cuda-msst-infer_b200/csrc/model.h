@@ -55,6 +55,11 @@ class Model {
                      float* out_host);
   void chunk_plan(long long L, float overlap, int* chunk, int* step, long long* border, long long* total,
                   int* num_chunks) const;
+  // Sharded separation: forward chunks [first, first + count) of the track's plan
+  // into out [count, stems*C, chunk], and stitch all chunk outputs of a track.
+  void forward_chunks(const float* track, int C, long long L, float overlap, int first, int count, int chunk_batch,
+                      int flags, float* out, cudaStream_t s);
+  void stitch(const float* chunks, int C, long long L, float overlap, float* out, cudaStream_t s);
 
  private:
   struct Work;  // per-(B, T) workspace

@@ -29,7 +29,7 @@ EXPORTS = [
     "msst_last_error", "msst_device_error", "msst_version", "msst_kernel_launches", "msst_rmsnorm", "msst_gemm", "msst_gemm_qkv_rope",
     "msst_attention", "msst_model_load", "msst_model_free", "msst_model_get_info", "msst_model_forward",
     "msst_model_masks", "msst_model_transformer", "msst_model_transformer_noalloc", "msst_model_separate", "msst_model_separate_host",
-    "msst_model_chunk_plan",
+    "msst_model_chunk_plan", "msst_model_forward_chunks", "msst_model_stitch",
 ]
 
 
@@ -82,6 +82,8 @@ def lib():
     L.msst_model_separate_host.argtypes = [vp, fp, c_int, i64, c_float, c_int, c_int, fp]
     L.msst_model_chunk_plan.argtypes = [vp, i64, c_float, ctypes.POINTER(c_int), ctypes.POINTER(c_int),
                                         ctypes.POINTER(i64), ctypes.POINTER(i64), ctypes.POINTER(c_int)]
+    L.msst_model_forward_chunks.argtypes = [vp, vp, c_int, i64, c_float, c_int, c_int, c_int, c_int, vp, vp]
+    L.msst_model_stitch.argtypes = [vp, vp, c_int, i64, c_float, vp, vp]
     _lib = L
     return L
 
@@ -259,6 +261,30 @@ class Model:
         check(lib().msst_model_separate(self._h, _ptr(track), C, L, overlap, chunk_batch,
                                         SEPARATE_FIX_TAIL_PADDING if fix_tail_padding else 0, _ptr(out),
                                         _stream(stream)))
+        return out[0] if S == 1 else out
+
+    def forward_chunks(self, track, overlap: float, first: int, count: int, chunk_batch: int = 0,
+                       fix_tail_padding: bool = False, out=None, stream=None):
+        """Forward chunks [first, first+count) of a CUDA fp32 [C, L] track -> [count, S*C, chunk]."""
+        torch = _torch()
+        track = track.contiguous()
+        C, L = track.shape
+        chunk = self.chunk_plan(L, overlap)["chunk_size"]
+        if out is None:
+            out = torch.empty((count, self.info["num_stems"] * C, chunk), dtype=torch.float32, device=track.device)
+        check(lib().msst_model_forward_chunks(self._h, _ptr(track), C, L, overlap, first, count, chunk_batch,
+                                              SEPARATE_FIX_TAIL_PADDING if fix_tail_padding else 0,
+                                              _ptr(out) if count else None, _stream(stream)))
+        return out
+
+    def stitch(self, chunks, channels: int, length: int, overlap: float, out=None, stream=None):
+        """Overlap-add all chunk outputs [num_chunks, S*C, chunk] of a track -> [S, C, L] (S squeezed when 1)."""
+        torch = _torch()
+        S = self.info["num_stems"]
+        if out is None:
+            out = torch.empty((S, channels, length), dtype=torch.float32, device=chunks.device)
+        check(lib().msst_model_stitch(self._h, _ptr(chunks.contiguous()), channels, length, overlap, _ptr(out),
+                                      _stream(stream)))
         return out[0] if S == 1 else out
 
     def separate_host(self, track: np.ndarray, overlap: float = 0.0, chunk_batch: int = 0,

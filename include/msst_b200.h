@@ -160,6 +160,19 @@ int msst_model_separate(msst_model* m, const float* track, int channels, long lo
 int msst_model_separate_host(msst_model* m, const float* track_host, int channels, long long length, float overlap,
                              int chunk_batch, int flags, float* out_host);
 
+/* Sharded separation of one track across GPUs (the reference is single-GPU;
+ * these split msst_model_separate at its independent unit, the chunk).
+ * msst_model_forward_chunks runs chunks [first_chunk, first_chunk + count) of the
+ * track's chunk plan: track [channels, length] (device) -> out [count,
+ * num_stems*channels, chunk_size] (device).  msst_model_stitch overlap-adds the
+ * outputs of all chunks of the plan, chunks [num_chunks, num_stems*channels,
+ * chunk_size], into out [num_stems, channels, length], in chunk order, so the
+ * result equals msst_model_separate's. */
+int msst_model_forward_chunks(msst_model* m, const float* track, int channels, long long length, float overlap,
+                              int first_chunk, int count, int chunk_batch, int flags, float* out, void* stream);
+int msst_model_stitch(msst_model* m, const float* chunks, int channels, long long length, float overlap, float* out,
+                      void* stream);
+
 /* Chunk plan of msst_model_separate for a track length (src/inference_app.cpp:119-138). */
 int msst_model_chunk_plan(const msst_model* m, long long length, float overlap, int* chunk_size, int* step,
                           long long* border, long long* padded_length, int* num_chunks);

@@ -388,17 +388,12 @@ def tail_chunk(mix: np.ndarray, start: int, chunk_size: int, ref_compat: bool = 
     return out
 
 
-def separate(forward, audio: np.ndarray, chunk_size: int, step: int, batch: int = 1, ref_compat: bool = True):
-    """Chunked overlap-add inference over one [C, L] track (src/inference_app.cpp:100-324).
-
-    `forward` maps [b, C, chunk] -> [b, C, chunk] (single stem).
-    """
+def chunk_inputs(audio: np.ndarray, chunk_size: int, step: int, ref_compat: bool = True):
+    """Chunks of the reflect-padded track (src/inference_app.cpp:119-150) -> list of [C, chunk]."""
     C, L = audio.shape
     border, total, starts = chunk_plan(L, chunk_size, step)
     mix = np.pad(audio, ((0, 0), (border, border)), mode="reflect") if border else audio
     mix = np.ascontiguousarray(mix, dtype=np.float32)
-    out = np.zeros((C, total), np.float64)
-    wsum = np.zeros(total, np.float64)
     chunks = []
     for s in starts:
         e = min(s + chunk_size, total)
@@ -406,17 +401,36 @@ def separate(forward, audio: np.ndarray, chunk_size: int, step: int, batch: int 
             chunks.append(tail_chunk(mix, s, chunk_size, ref_compat))
         else:
             chunks.append(mix[:, s:e].astype(np.float32))
-    for g in range(0, len(starts), batch):
-        ys = forward(np.stack(chunks[g:g + batch]))
-        for j, y in enumerate(ys):
-            s = starts[g + j]
-            e = min(s + chunk_size, total)
-            n = e - s
-            w = fade_window(chunk_size, s == 0, e >= total)[:n]
-            out[:, s:e] += y[:, :n] * w
-            wsum[s:e] += w
+    return chunks
+
+
+def stitch(outputs, length: int, chunk_size: int, step: int) -> np.ndarray:
+    """Windowed overlap-add of every chunk's output [C', chunk] in chunk order, normalised
+    and cropped to the track (src/inference_app.cpp:252-306, src/ops_fused.cu:138-188)."""
+    border, total, starts = chunk_plan(length, chunk_size, step)
+    Cp = outputs[0].shape[0]
+    out = np.zeros((Cp, total), np.float64)
+    wsum = np.zeros(total, np.float64)
+    for s, y in zip(starts, outputs):
+        e = min(s + chunk_size, total)
+        n = e - s
+        w = fade_window(chunk_size, s == 0, e >= total)[:n]
+        out[:, s:e] += y[:, :n] * w
+        wsum[s:e] += w
     # divide only where the summed window is non-negligible (src/ops_fused.cu:173-188)
     nz = wsum > 1e-8
     out[:, nz] /= wsum[nz]
     out = out.astype(np.float32)
-    return out[:, border:border + L] if border else out
+    return out[:, border:border + length] if border else out
+
+
+def separate(forward, audio: np.ndarray, chunk_size: int, step: int, batch: int = 1, ref_compat: bool = True):
+    """Chunked overlap-add inference over one [C, L] track (src/inference_app.cpp:100-324).
+
+    `forward` maps [b, C, chunk] -> [b, C', chunk].
+    """
+    chunks = chunk_inputs(audio, chunk_size, step, ref_compat)
+    outputs = []
+    for g in range(0, len(chunks), batch):
+        outputs.extend(forward(np.stack(chunks[g:g + batch])))
+    return stitch(outputs, audio.shape[1], chunk_size, step)
