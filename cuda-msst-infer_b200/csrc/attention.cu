@@ -7,20 +7,20 @@
 //              K/V tiles, so each K/V tile is loaded once for 256 query rows
 //   band axis: two consecutive packed tiles (several short sequences each, with
 //              a block-diagonal mask); each has its own single K/V tile
-//   warp 0     TMA producer: Q_a/Q_b, K/V tiles through a 3-stage ring
+//   warp 0     TMA producer: Q_a/Q_b, K/V tiles through a 4-stage ring
 //   warp 1     MMA issuer: S_w = Q_w K^T (M128 N128 K64) and O_w += P_w V
-//              (M128 N64 K128, P from smem), issued per tile as
+//              (M128 N64 K128, P read from TMEM), issued per tile as
 //              PV_a(j), S_a(j+1), PV_b(j), S_b(j+1) so that S_w(j+1)'s completion
 //              also guarantees PV_w(j) has finished reading P_w
 //   warps 2-5  softmax of tile a, warps 6-9 softmax of tile b: one query row per
 //              thread; steady-state tiles take one pass over S in TMEM (exponent
 //              against the running reference max, which moves lazily: O in TMEM
 //              is rescaled only when the max grows by more than 2^8), P
-//              written as 16-bit into 128B-swizzled smem (the UMMA A operand);
+//              written as packed 16-bit pairs into TMEM (the MMA's A operand);
 //              fully masked 32-column chunks are skipped per warp.  The epilogue
 //              divides by the row sum, applies the head gate and writes the
 //              merged-head row.
-// TMEM: S_a [0,128) S_b [128,256) O_a [256,320) O_b [320,384) (512 allocated).
+// TMEM: S_a [0,128) S_b [128,256) O_a [256,320) O_b [320,384) P_a [384,448) P_b [448,512).
 #include "attention.cuh"
 #include "common.cuh"
 
@@ -28,13 +28,12 @@ namespace msst {
 
 namespace {
 
-constexpr int kKvStages = 3;
+constexpr int kKvStages = 4;
 constexpr int kThreads = 320;
 constexpr uint32_t kTileBytes = 128 * 64 * 2;   // one 128x64 16-bit tile
-constexpr uint32_t kPBytes = 128 * 128 * 2;     // P tile (two 64-column K-blocks)
-constexpr size_t kAttnSmem = 1024 + 2 * kTileBytes + kKvStages * 2 * kTileBytes + 2 * kPBytes + 256;
+constexpr size_t kAttnSmem = 1024 + 2 * kTileBytes + kKvStages * 2 * kTileBytes + 256;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0, kColO = 256;
+constexpr uint32_t kColS = 0, kColO = 256, kColP = 384;
 constexpr float kRescaleLog2 = 8.0f;  // lazy rescale threshold (log2 units)
 
 struct PairGeom {
@@ -88,8 +87,8 @@ __device__ __forceinline__ bool uses(const AttnParams& p, int w, int j) { return
 // ---------------------------------------------------------------------------
 template <typename T, int kPass>
 __device__ __forceinline__ void process_chunk(const uint32_t (&r)[32], int ch, bool in_range, bool unmasked, int klo,
-                                              int khi, float2 c2, float2 nm2, float& mx, float2& sum2, uint8_t* prow,
-                                              int row) {
+                                              int khi, float2 c2, float2 nm2, float& mx, float2& sum2,
+                                              uint32_t pAddr) {
   if constexpr (kPass == 0) {
     if (!in_range) return;
     float m0 = -INFINITY, m1 = -INFINITY;
@@ -142,34 +141,28 @@ __device__ __forceinline__ void process_chunk(const uint32_t (&r)[32], int ch, b
         pk[i] = pack2<T>(e0, e1);
       }
     }
-    // P row: 128B swizzle, two 64-column K-blocks of kPBytes/2
-    uint8_t* blk = prow + (ch >> 1) * (kPBytes / 2);
-    const int chunk0 = (ch & 1) * 4;
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int cc = (chunk0 + u) ^ (row & 7);
-      *reinterpret_cast<uint4*>(blk + cc * 16) = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
-    }
+    // P row chunk -> TMEM (16 columns of packed 16-bit pairs), the A operand of O += P.V
+    tmem_st16(pAddr + ch * 16, pk);
   }
 }
 
 template <typename T, int kPass>
 __device__ __forceinline__ void row_pass(uint32_t sAddr, int c_lo, int c_hi, int c_full, int klo, int khi, float c,
-                                         float mc, float& mx, float2& sum2, uint8_t* prow, int row) {
+                                         float mc, float& mx, float2& sum2, uint32_t pAddr) {
   const float2 c2 = make_float2(c, c), nm2 = make_float2(-mc, -mc);
   uint32_t ra[32], rb[32];
   tmem_ld32(sAddr, ra);
   tmem_ld_wait(ra);
   tmem_ld32(sAddr + 32, rb);
-  process_chunk<T, kPass>(ra, 0, 0 >= c_lo && 0 < c_hi, 0 < c_full, klo, khi, c2, nm2, mx, sum2, prow, row);
+  process_chunk<T, kPass>(ra, 0, 0 >= c_lo && 0 < c_hi, 0 < c_full, klo, khi, c2, nm2, mx, sum2, pAddr);
   tmem_ld_wait(rb);
   tmem_ld32(sAddr + 64, ra);
-  process_chunk<T, kPass>(rb, 1, 1 >= c_lo && 1 < c_hi, 1 < c_full, klo, khi, c2, nm2, mx, sum2, prow, row);
+  process_chunk<T, kPass>(rb, 1, 1 >= c_lo && 1 < c_hi, 1 < c_full, klo, khi, c2, nm2, mx, sum2, pAddr);
   tmem_ld_wait(ra);
   tmem_ld32(sAddr + 96, rb);
-  process_chunk<T, kPass>(ra, 2, 2 >= c_lo && 2 < c_hi, 2 < c_full, klo, khi, c2, nm2, mx, sum2, prow, row);
+  process_chunk<T, kPass>(ra, 2, 2 >= c_lo && 2 < c_hi, 2 < c_full, klo, khi, c2, nm2, mx, sum2, pAddr);
   tmem_ld_wait(rb);
-  process_chunk<T, kPass>(rb, 3, 3 >= c_lo && 3 < c_hi, 3 < c_full, klo, khi, c2, nm2, mx, sum2, prow, row);
+  process_chunk<T, kPass>(rb, 3, 3 >= c_lo && 3 < c_hi, 3 < c_full, klo, khi, c2, nm2, mx, sum2, pAddr);
 }
 
 template <typename T>
@@ -180,8 +173,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                              // Q_a, Q_b
   uint8_t* sKV = sQ + 2 * kTileBytes;              // stages x (K, V)
-  uint8_t* sP = sKV + kKvStages * 2 * kTileBytes;  // P_a, P_b
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kPBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + kKvStages * 2 * kTileBytes);
   uint64_t* q_full = bars + 0;
   uint64_t* q_empty = bars + 1;
   uint64_t* kv_full = bars + 2;
@@ -277,12 +269,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&p_full[w], pcnt[w] & 1, kErrTimeoutAttnP, abort_flag)) return false;
         ++pcnt[w];
         tc_fence_after();
-        const uint32_t paddr = smem_u32(sP + w * kPBytes);
+        const uint32_t paddr = tmem + kColP + (uint32_t)(w * 64);
         const uint32_t vaddr = smem_u32(sKV + st * 2 * kTileBytes + kTileBytes);
         const uint32_t dO = tmem + kColO + (uint32_t)(w * 64);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          umma_f16_ss(dO, sw128_desc(paddr + (kk >> 2) * (kPBytes / 2) + (kk & 3) * 32, 16, 1024),
+          umma_f16_ts(dO, paddr + (uint32_t)(kk * 8),
                       sw128_desc(vaddr + kk * 2048, kTileBytes, 1024), idesc_o, (first && kk == 0) ? 0u : 1u);
         return true;
       };
@@ -336,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     const uint32_t sAddr = tmem + lane_off + kColS + (uint32_t)(w * 128);
     const uint32_t oAddr = tmem + lane_off + kColO + (uint32_t)(w * 64);
-    uint8_t* prow = sP + w * kPBytes + row * 128;
+    const uint32_t pAddr = tmem + lane_off + kColP + (uint32_t)(w * 64);
     const float c = p.scale_log2;
     uint32_t scnt = 0, ocnt = 0;
     bool ok = true;
@@ -394,7 +386,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // track how far above it the row went
             float amax = -INFINITY;
             const float mc = (m == -INFINITY) ? 0.f : m * c;
-            row_pass<T, 1>(sAddr, c_lo, c_hi, c_full, klo, khi, c, mc, amax, sum2, prow, row);
+            row_pass<T, 1>(sAddr, c_lo, c_hi, c_full, klo, khi, c, mc, amax, sum2, pAddr);
             if (__any_sync(0xffffffffu, amax > kRescaleLog2)) {
               exact = true;
               sum2 = make_float2(0.f, 0.f);
@@ -402,7 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (exact) {
             float mx = -INFINITY;
-            row_pass<T, 0>(sAddr, c_lo, c_hi, c_full, klo, khi, c, 0.f, mx, sum2, prow, row);
+            row_pass<T, 0>(sAddr, c_lo, c_hi, c_full, klo, khi, c, 0.f, mx, sum2, pAddr);
             // lazy rescale: move the reference max only when it grows by > 2^8
             const bool grow = (mx > m) && ((m == -INFINITY) || (mx - m) * c > kRescaleLog2);
             if (__any_sync(0xffffffffu, grow)) {
@@ -426,10 +418,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             const float mc = (m == -INFINITY) ? 0.f : m * c;
             float unused = 0.f;
-            row_pass<T, 2>(sAddr, c_lo, c_hi, c_full, klo, khi, c, mc, unused, sum2, prow, row);
+            row_pass<T, 2>(sAddr, c_lo, c_hi, c_full, klo, khi, c, mc, unused, sum2, pAddr);
           }
           l += sum2.x + sum2.y;
-          fence_proxy_async_smem();
+          tmem_st_wait();
         }
         ++used;
         tc_fence_before();

@@ -52,8 +52,24 @@ __device__ __forceinline__ int find_group(const GemmGroup* g, int n, int t) {
   return i;
 }
 
-__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
-__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
+// erf by Abramowitz & Stegun, Handbook of Mathematical Functions, formula 7.1.26
+// (after Hastings): erf(a) = 1 - t(a1 + t(a2 + t(a3 + t(a4 + t a5)))) e^{-a^2},
+// t = 1/(1 + p a), |error| <= 1.5e-7 for a >= 0; odd extension for a < 0.  Two
+// MUFU operations and six FMAs instead of a general-purpose erff, well below the
+// 16-bit output rounding of the GELU epilogue.
+__device__ __forceinline__ float erf_as7126(float z) {
+  const float a = fabsf(z);
+  const float t = __fdividef(1.0f, fmaf(0.3275911f, a, 1.0f));
+  const float poly =
+      t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, 1.061405429f, -1.453152027f), 1.421413741f), -0.284496736f), 0.254829592f);
+  return copysignf(1.0f - poly * __expf(-a * a), z);
+}
+
+// GELU, erf form (reference src/ops_fused.cu:21-24)
+__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erf_as7126(x * 0.70710678118654752f)); }
+// logistic sigmoid with a fast reciprocal (the reference's --use_fast_math build
+// also turns this division into an approximate one)
+__device__ __forceinline__ float sigmoidf_(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 
 // bias, activation and RoPE on one 32-column chunk of one row (fp32 registers)
 template <int EPI>
