@@ -15,9 +15,16 @@ Arms:
   ours (default)   value: device-resident track, CUDA-event time of K steps
                    (max over ranks); e2e: the same through the host-buffer public
                    API (pinned host memory, H2D + D2H inside the timed region).
-                   At N > 1 the track is N x 68.5 s, its chunks are dealt
-                   round-robin to the ranks and the per-chunk stems are gathered
-                   to rank 0 over NCCL for the stitch (weak scaling).
+                   At N > 1 the track is N x 68.5 s, its chunk plan is split into
+                   contiguous balanced ranges, one per rank, and the per-chunk
+                   stems are gathered to rank 0 over NCCL for the stitch (weak
+                   scaling).
+  roofline         every launch of the library inside the timed region is
+                   bracketed by CUDA events on its stream (msst_kernel_timing);
+                   the kernel with the largest total time is the dominant one and
+                   its achieved rate is its algorithmic FLOPs (or bytes) over its
+                   summed event time, against the sustained GEMM peak (or the
+                   copy bandwidth) of MEASURED_PEAKS.json.
   reference        the reference has no CPU path; its CPU arm is the fp32 oracle
                    port (oracle/) on the host cores, timed on a bounded sample
                    (one depth block of one chunk per step, the band-split/mask
@@ -46,12 +53,14 @@ CHUNK_BATCH = 4
 
 
 def peaks():
+    """(burst TFLOP/s, sustained TFLOP/s, HBM GB/s, source)."""
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        return d.get("bf16_tflops", 1590.0), d.get("hbm_gbs", 6650.0), "measured"
-    return 1590.0, 6650.0, "fallback"
+        return (d.get("bf16_tflops", 1590.0), d.get("bf16_tflops_sustained", 1400.0), d.get("hbm_gbs", 6650.0),
+                "measured")
+    return 1590.0, 1400.0, 6650.0, "fallback"
 
 
 def model_config(which: int):
@@ -133,67 +142,58 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def time_op(torch, fn, iters=10, warm=3):
-    for _ in range(warm):
-        fn()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    s.record()
-    for _ in range(iters):
-        fn()
-    e.record()
-    torch.cuda.synchronize()
-    return s.elapsed_time(e) / iters
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one ncu-captured
+# launch per kernel, with that launch's algorithmic FLOPs (or bytes, for kernels
+# without FLOPs): the capture is scaled to the timed region's average launch by
+# the ratio of algorithmic work.  The captures and their commands are in profiles/.
+NCU_TRAFFIC: dict = {
+    # profiles/dram_traffic_mbr_cfg1_chunk1.md: one 352800-sample chunk (48060 tokens)
+    "attention_time": {"dram_bytes": 149286400 + 23763200, "flop": 78839930880},
+    "attention_band": {"dram_bytes": 149328896 + 20584704, "flop": 5905612800},
+    "gemm_qkv_rope": {"dram_bytes": 38387712 + 90150144, "flop": 56693882880},
+    "gemm_store16_gelu": {"dram_bytes": 38210816 + 90500608, "flop": 56693882880},
+    # one FFN2 (K=1536) and one out-projection (K=512) launch, as they alternate
+    "gemm_resid32": {"dram_bytes": 222728448 + 32885760 + 123456512 + 11998464, "flop": 75591843840},
+}
 
 
-def kernel_rooflines(torch, cfg, Bc, T, dtype, peak_tflops):
-    """Time the contraction kernels alone at the workload's shapes (CUDA events on the
-    launching stream) and return per-kernel achieved TFLOP/s and per-forward time."""
-    from msst_b200 import ops
-
-    nb, D, H = cfg["num_bands"], cfg["dim"], cfg["heads"]
-    inner, ff = H * 64, D * cfg["mlp_expansion_factor"]
-    M = Bc * T * nb
-    dev = "cuda"
-    g = torch.Generator(device=dev).manual_seed(0)
-    x = torch.randn(M, D, device=dev, generator=g).to(dtype)
-    wqkv = (0.02 * torch.randn(3 * inner, D, device=dev, generator=g)).to(dtype)
-    w1 = (0.02 * torch.randn(ff, D, device=dev, generator=g)).to(dtype)
-    b1 = torch.zeros(ff, device=dev)
-    h = torch.randn(M, ff, device=dev, generator=g).to(dtype)
-    w2 = (0.02 * torch.randn(D, ff, device=dev, generator=g)).to(dtype)
-    ao = torch.randn(M, inner, device=dev, generator=g).to(dtype)
-    wout = (0.02 * torch.randn(D, inner, device=dev, generator=g)).to(dtype)
-    resid = torch.zeros(M, D, device=dev)
-    qkv = torch.randn(M, 3 * inner, device=dev, generator=g).to(dtype)
-    cs = torch.ones(max(T, nb), 32, device=dev)
-    sn = torch.zeros(max(T, nb), 32, device=dev)
-    layers = 2 * cfg["depth"]  # time + band transformer per depth
-    kern = {}
-
-    def add(name, ms, flops, per_forward):
-        kern[name] = {"ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, "launches_per_forward": per_forward,
-                      "flop_per_launch": flops}
-
-    add("gemm_qkv_rope", time_op(torch, lambda: ops.gemm_qkv_rope(x, wqkv, H, cs, sn, nb, T)), 2.0 * M * D * 3 * inner,
-        layers)
-    add("gemm_ffn1_gelu", time_op(torch, lambda: ops.gemm(x, w1, b1, "store16", "gelu")), 2.0 * M * D * ff, layers)
-    add("gemm_ffn2_resid", time_op(torch, lambda: ops.gemm(h, w2, None, "resid32", out=resid)), 2.0 * M * ff * D,
-        layers)
-    add("gemm_out_resid", time_op(torch, lambda: ops.gemm(ao, wout, None, "resid32", out=resid)),
-        2.0 * M * inner * D, layers)
-    add("attention_time", time_op(torch, lambda: ops.attention(qkv, Bc, T, nb, H, "time", 0.125)),
-        4.0 * Bc * nb * H * T * T * 64, cfg["depth"])
-    add("attention_band", time_op(torch, lambda: ops.attention(qkv, Bc, T, nb, H, "band", 0.125)),
-        4.0 * Bc * T * H * nb * nb * 64, cfg["depth"])
-    for v in kern.values():
-        v["frac_of_peak"] = v["tflops"] / peak_tflops
-    return kern
+def kernel_table(stats, steps, peak_tf_sustained, peak_hbm):
+    """Per-kernel rows from msst_kernel_timing_report over the timed region."""
+    rows = {}
+    for name, k in stats.items():
+        ms = k["total_ms"]
+        row = {"launches_per_step": k["launches"] / steps, "ms_per_step": ms / steps,
+               "ms_per_launch": ms / max(k["launches"], 1)}
+        if k["flop"] > 0:
+            row["tflops"] = k["flop"] / (ms * 1e-3) / 1e12 if ms > 0 else None
+            row["frac_of_sustained_peak"] = row["tflops"] / peak_tf_sustained if row["tflops"] else None
+        row["gbs"] = k["bytes"] / (ms * 1e-3) / 1e9 if ms > 0 else None
+        row["frac_of_hbm"] = row["gbs"] / peak_hbm if row["gbs"] else None
+        rows[name] = row
+    return rows
 
 
-# Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the
-# dominant kernels from ncu captures; see profiles/ for the commands and scaling.
-NCU_TRAFFIC_BYTES: dict = {}
+def dominant_roofline(stats, peaks_):
+    burst, sustained, hbm, src = peaks_
+    name = max(stats, key=lambda n: stats[n]["total_ms"])
+    k = stats[name]
+    per_launch_s = k["total_ms"] * 1e-3 / k["launches"]
+    flop_l, bytes_l = k["flop"] / k["launches"], k["bytes"] / k["launches"]
+    traffic = None
+    cap = NCU_TRAFFIC.get(name)
+    if cap:
+        unit_l = flop_l if cap.get("flop") else bytes_l
+        traffic = cap["dram_bytes"] * unit_l / (cap.get("flop") or cap["alg_bytes"])
+    if k["flop"] > 0:
+        achieved = flop_l / per_launch_s / 1e12
+        return {"bound": "tensor", "kernel": name, "achieved": achieved, "peak": sustained, "unit": "TFLOP/s",
+                "frac": achieved / sustained, "peak_kind": f"bf16_tflops_sustained ({src})",
+                "frac_of_burst_peak": achieved / burst, "traffic": traffic, "alg_bytes_per_launch": bytes_l,
+                "flop_per_launch": flop_l, "launches": k["launches"], "ms_per_launch": per_launch_s * 1e3}
+    achieved = bytes_l / per_launch_s / 1e9
+    return {"bound": "hbm", "kernel": name, "achieved": achieved, "peak": hbm, "unit": "GB/s",
+            "frac": achieved / hbm, "peak_kind": f"hbm_gbs ({src})", "traffic": traffic,
+            "alg_bytes_per_launch": bytes_l, "launches": k["launches"], "ms_per_launch": per_launch_s * 1e3}
 
 
 def cpu_sample(cfg, which):
@@ -232,6 +232,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", type=int, choices=[1, 2], default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--seconds", type=float, default=TRACK_SECONDS,
+                    help="track length per rank (smaller values make a profiling case)")
+    ap.add_argument("--chunk-batch", type=int, default=CHUNK_BATCH, help="chunks per forward")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -250,12 +253,12 @@ def main():
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
-    from msst_b200 import Model, kernel_launches, synth
+    from msst_b200 import Model, kernel_launches, kernel_timing, kernel_timing_report, synth
 
     cfg, prec, desc = model_config(args.config)
     path = model_file(cfg, args.config, rank, world, dist)
     model = Model(path, local, prec)
-    n_samples = int(round(TRACK_SECONDS * SR)) * world
+    n_samples = int(round(args.seconds * SR)) * world
     track = synth.make_audio(n_samples, 2, 1234)
     plan = model.chunk_plan(n_samples, OVERLAP)
     audio_seconds = n_samples / SR
@@ -263,13 +266,13 @@ def main():
     if world == 1:
         track_dev = torch.from_numpy(track).cuda()
         out_dev = torch.empty((cfg["num_stems"], 2, n_samples), dtype=torch.float32, device="cuda")
-        step = lambda: model.separate(track_dev, OVERLAP, CHUNK_BATCH, out=out_dev)
+        step = lambda: model.separate(track_dev, OVERLAP, args.chunk_batch, out=out_dev)
     else:
         from msst_b200.dist import ShardedSeparator
 
         sharded = ShardedSeparator(model, dist, rank, world)
         track_dev = torch.from_numpy(track).cuda()
-        step = lambda: sharded.separate(track_dev, OVERLAP, CHUNK_BATCH)
+        step = lambda: sharded.separate(track_dev, OVERLAP, args.chunk_batch)
 
     for _ in range(args.warmup):
         step()
@@ -277,6 +280,7 @@ def main():
     if world > 1:
         dist.barrier()
     kernel_launches(reset=True)
+    kernel_timing(True)
     with ClockSampler(local) as clk:
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
@@ -285,7 +289,9 @@ def main():
             step()
         e.record()
         torch.cuda.synchronize()
+    kernel_timing(False)
     launches = kernel_launches(reset=True)
+    stats = kernel_timing_report()
     ms = s.elapsed_time(e) / args.steps
     if world > 1:
         t = torch.tensor([ms], device="cuda")
@@ -301,57 +307,61 @@ def main():
         pin_in = torch.from_numpy(track).pin_memory()
         pin_out = torch.empty((cfg["num_stems"], 2, n_samples), dtype=torch.float32).pin_memory()
         hin, hout = pin_in.numpy(), pin_out.numpy()
-        model.separate_host(hin, OVERLAP, CHUNK_BATCH, out=hout)
+        model.separate_host(hin, OVERLAP, args.chunk_batch, out=hout)
         t0 = time.perf_counter()
         for _ in range(args.steps):
-            model.separate_host(hin, OVERLAP, CHUNK_BATCH, out=hout)
+            model.separate_host(hin, OVERLAP, args.chunk_batch, out=hout)
         e2e_s = (time.perf_counter() - t0) / args.steps
         e2e = {"value": audio_seconds / e2e_s, "unit": "audio-s/s", "h2d_bytes_per_step": int(track.nbytes),
                "d2h_bytes_per_step": int(hout.nbytes), "ms_per_step": e2e_s * 1e3}
     else:
-        # host track in, stitched stems out on rank 0 (the gather is inside the step)
+        # every rank copies the host track in (pinned once, outside the timed
+        # region); rank 0 copies the stitched stems out
+        pin_in = torch.from_numpy(track).pin_memory()
+        tdev = torch.empty(pin_in.shape, dtype=torch.float32, device="cuda")
+        pin_out = torch.empty((cfg["num_stems"], 2, n_samples), dtype=torch.float32).pin_memory()
+
+        def e2e_step():
+            tdev.copy_(pin_in, non_blocking=True)
+            y = sharded.separate(tdev, OVERLAP, args.chunk_batch)
+            if rank == 0:
+                pin_out.view(y.shape).copy_(y, non_blocking=True)
+            torch.cuda.synchronize()
+
+        e2e_step()
+        dist.barrier()
         t0 = time.perf_counter()
         for _ in range(args.steps):
-            tdev = torch.from_numpy(track).pin_memory().cuda(non_blocking=True)
-            y = sharded.separate(tdev, OVERLAP, CHUNK_BATCH)
-            if rank == 0:
-                y.cpu()
-        torch.cuda.synchronize()
+            e2e_step()
         dt = torch.tensor([(time.perf_counter() - t0) / args.steps], device="cuda")
         dist.all_reduce(dt, op=dist.ReduceOp.MAX)
         e2e = {"value": audio_seconds / float(dt.item()), "unit": "audio-s/s",
-               "h2d_bytes_per_step": int(track.nbytes), "d2h_bytes_per_step": int(track.nbytes) * cfg["num_stems"],
-               "ms_per_step": float(dt.item()) * 1e3}
+               "h2d_bytes_per_step": int(track.nbytes) * world,
+               "d2h_bytes_per_step": int(track.nbytes) * cfg["num_stems"], "ms_per_step": float(dt.item()) * 1e3}
 
     result = None
     if rank == 0:
-        peak_tf, peak_hbm, peak_src = peaks()
+        pk = peaks()
         T = CHUNK // cfg["stft_hop_length"] + 1
-        dt16 = torch.float16 if prec == "fp16" else torch.bfloat16
-        kern = kernel_rooflines(torch, cfg, CHUNK_BATCH, T, dt16, peak_tf)
-        forwards = -(-plan["num_chunks"] // CHUNK_BATCH)
-        for v in kern.values():
-            v["ms_per_step"] = v["ms"] * v["launches_per_forward"] * forwards
-        dom_name = max(kern, key=lambda k: kern[k]["ms_per_step"])
-        dom = kern[dom_name]
-        roofline = {"bound": "tensor", "kernel": dom_name, "achieved": dom["tflops"], "peak": peak_tf,
-                    "unit": "TFLOP/s", "frac": dom["tflops"] / peak_tf, "peak_source": peak_src,
-                    "traffic": NCU_TRAFFIC_BYTES.get(dom_name)}
-        flop_track = sum(v["flop_per_launch"] * v["launches_per_forward"] for v in kern.values()) * forwards
+        roofline = dominant_roofline(stats, pk)
+        kern = kernel_table(stats, args.steps, pk[1], pk[2])
+        flop_step = sum(k["flop"] for k in stats.values()) / args.steps
+        kernel_ms = sum(k["total_ms"] for k in stats.values()) / args.steps
         result = {
             "metric": "audio-sec separated/sec", "value": value, "unit": "audio-s/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": prec, "data": "synthetic",
             "config": {"workload": f"{desc}; {audio_seconds:.1f} s stereo track, {plan['num_chunks']} chunks of "
-                                   f"{CHUNK} (overlap {OVERLAP}), {CHUNK_BATCH} chunks per forward",
-                       "model": desc, "global_batch": CHUNK_BATCH, "seq_len": T, "parallelism": f"chunks x{world}",
+                                   f"{CHUNK} (overlap {OVERLAP}), {args.chunk_batch} chunks per forward",
+                       "model": desc, "global_batch": args.chunk_batch, "seq_len": T, "parallelism": f"chunks x{world}",
                        "l2": "working set (weights + activations, GBs) far larger than the 126 MB L2",
                        "baseline_config": args.config},
             "e2e": e2e, "gpu_launches": launches, "gpu_launches_per_step": launches / args.steps,
             "roofline": roofline, "clocks": clocks,
             "kernels": {k: {kk: (round(vv, 5) if isinstance(vv, float) else vv) for kk, vv in v.items()}
-                        for k, v in kern.items()},
-            "contraction_tflop_per_step": flop_track / 1e12,
+                        for k, v in sorted(kern.items(), key=lambda kv: -kv[1]["ms_per_step"])},
+            "library_kernel_ms_per_step": kernel_ms,
+            "contraction_tflop_per_step": flop_step / 1e12,
         }
         if not args.no_cpu_baseline and world == 1:
             c = cpu_sample(cfg, args.config)
@@ -377,7 +387,7 @@ def run_reference(args):
     cfg, prec, desc = model_config(args.config)
     from msst_b200 import synth
 
-    n_samples = int(round(TRACK_SECONDS * SR)) * args.gpus
+    n_samples = int(round(args.seconds * SR)) * args.gpus
     audio_seconds = n_samples / SR
     step_sz = oracle.resolve_step(CHUNK, OVERLAP, 2)
     _, _, starts = oracle.chunk_plan(n_samples, CHUNK, step_sz)
@@ -431,13 +441,13 @@ def reference_gpu(cfg, args, prec):
         h = L.refh_load(path.encode(), 0, 1 if prec == "fp16" else 0)
         if not h:
             return {"unavailable": L.refh_last_error().decode()}
-        n = int(round(TRACK_SECONDS * SR))
+        n = int(round(args.seconds * SR))
         track = synth.make_audio(n, 2, 1234)
         buf = np.zeros(track.size, np.float32)
         cnt, ms = ctypes.c_longlong(0), ctypes.c_double(0)
         times = []
         for i in range(2 + max(1, min(args.steps, 3))):
-            rc = L.refh_separate(h, mg.P(track), 2, n, OVERLAP, CHUNK_BATCH, mg.P(buf), buf.size, ctypes.byref(cnt),
+            rc = L.refh_separate(h, mg.P(track), 2, n, OVERLAP, args.chunk_batch, mg.P(buf), buf.size, ctypes.byref(cnt),
                                  ctypes.byref(ms))
             if rc != 0:
                 return {"unavailable": L.refh_last_error().decode()}

@@ -475,7 +475,12 @@ cudaError_t launch_t(const CUtensorMap& m, const AttnParams& p, int num_sms, cud
   }
   const int grid = p.total_items < num_sms ? p.total_items : num_sms;
   if (grid <= 0) return cudaSuccess;
-  note_launch();
+  // algorithmic cost: QK^T and PV of every sequence (4 L^2 d FLOPs per head), Q/K/V
+  // and the gates read once, the merged heads written once
+  const double seqs = (double)p.num_tokens / p.seq_len;
+  const double flop = 4.0 * seqs * p.heads * (double)p.seq_len * p.seq_len * 64.0;
+  const double bytes = (double)p.num_tokens * p.heads * (4.0 * 64.0 * sizeof(T) + (p.gates ? 4.0 : 0.0));
+  LaunchScope scope(p.mode == 0 ? "attention_time" : "attention_band", flop, bytes, s);
   attention_kernel<T><<<grid, kThreads, kAttnSmem, s>>>(m, p);
   return cudaGetLastError();
 }

@@ -3,6 +3,7 @@
 // message is kept per thread for msst_last_error().
 #include <atomic>
 #include <cmath>
+#include <cstring>
 #include <string>
 
 #include "attention.cuh"
@@ -15,10 +16,6 @@ struct msst_model {
   msst::Model impl;
 };
 
-namespace msst {
-static std::atomic<unsigned long long> g_launches{0};
-void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
-}  // namespace msst
 
 namespace {
 
@@ -99,8 +96,27 @@ unsigned msst_device_error(int clear) { return msst::device_error(clear != 0); }
 
 int msst_version(void) { return 1; }
 
-unsigned long long msst_kernel_launches(int reset) {
-  return reset ? msst::g_launches.exchange(0) : msst::g_launches.load();
+unsigned long long msst_kernel_launches(int reset) { return msst::launch_count(reset != 0); }
+
+int msst_kernel_timing(int enable) {
+  return guarded([&] { msst::set_kernel_timing(enable != 0); });
+}
+
+int msst_kernel_timing_report(msst_kernel_stat* out, int cap, int* count) {
+  return guarded([&] {
+    MSST_REQUIRE(count && (cap == 0 || out) && cap >= 0, "null argument");
+    const auto stats = msst::kernel_timing_report();
+    *count = (int)stats.size();
+    for (int i = 0; i < cap && i < (int)stats.size(); ++i) {
+      msst_kernel_stat& o = out[i];
+      std::memset(o.name, 0, sizeof(o.name));
+      std::strncpy(o.name, stats[i].name.c_str(), sizeof(o.name) - 1);
+      o.launches = stats[i].launches;
+      o.total_ms = stats[i].ms;
+      o.flop = stats[i].flop;
+      o.bytes = stats[i].bytes;
+    }
+  });
 }
 
 int msst_rmsnorm(const float* x, long long rows, int D, const float* gamma, float scale, int dtype, void* out16,

@@ -60,8 +60,22 @@ __device__ __forceinline__ unsigned long long global_timer_ns() {
 
 __device__ __forceinline__ void record_error(unsigned code) { atomicCAS(&g_device_error, 0u, code); }
 
-// Host: counts kernel launches made by this library (msst_kernel_launches()).
-void note_launch();
+// Host: accounting of this library's kernel launches.  Each launcher opens a
+// LaunchScope right before its <<<>>>: the scope counts the launch
+// (msst_kernel_launches) and, while per-kernel timing is on (msst_kernel_timing),
+// brackets it with two CUDA events on the launch stream and records the launch's
+// algorithmic FLOPs and DRAM bytes under the kernel's name.
+class LaunchScope {
+ public:
+  LaunchScope(const char* name, double flop, double bytes, cudaStream_t s);
+  ~LaunchScope();
+  LaunchScope(const LaunchScope&) = delete;
+  LaunchScope& operator=(const LaunchScope&) = delete;
+
+ private:
+  long long slot_;
+  cudaStream_t stream_;
+};
 
 // ---------------------------------------------------------------------------
 // mbarrier
@@ -84,14 +98,18 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// One potentially blocking test of the phase: the thread may be suspended until
+// the phase completes or kSuspendHintNs pass, so a waiting warp does not take
+// issue slots from the warps sharing its SM sub-partition.
+constexpr uint32_t kSuspendHintNs = 100000;
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(bar), "r"(parity)
+      : "r"(bar), "r"(parity), "n"(kSuspendHintNs)
       : "memory");
   return ok != 0;
 }
@@ -106,7 +124,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
   const unsigned long long t0 = global_timer_ns();
   for (uint32_t spins = 1;; ++spins) {
     if (mbar_try_wait(a, parity)) return true;
-    if ((spins & 255u) == 0u) {
+    if ((spins & 15u) == 0u) {
       if (*abort) return false;
       if (global_timer_ns() - t0 > kWaitLimitNs) {
         record_error(code);
@@ -280,13 +298,15 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // 32 lanes x 16 consecutive 32-bit columns.
+// No memory clobber: the data dependency is carried by the register operands,
+// and the store stays ordered with tcgen05.wait::st and the other volatile
+// tcgen05 statements, so independent arithmetic may be scheduled around it.
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
       "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
       "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
-      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
-      : "memory");
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]));
 }
 
 // Make generic-proxy shared-memory writes visible to the async proxy (UMMA / TMA).
@@ -325,6 +345,25 @@ __device__ __forceinline__ float to_f32<__half>(__half v) {
 template <>
 __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
   return __bfloat162float(v);
+}
+
+// Warpgroup register reallocation (every warp of the warpgroup executes it).  The
+// shares of all warpgroups must add up to at most the block's launch allocation
+// (threads x registers per thread at launch), or the increase never completes.
+template <uint32_t N>
+__device__ __forceinline__ void warpgroup_reg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void warpgroup_reg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// three-input maximum (PTX max.f32 with three sources, sm_100+)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 __device__ __forceinline__ float fast_exp2(float x) {

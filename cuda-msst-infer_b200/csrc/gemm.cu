@@ -359,6 +359,35 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// Algorithmic cost of one launch: 2*m*n*k FLOPs per group; bytes = A and B read
+// once, the output written once (the residual epilogue also reads it).
+struct GemmCost {
+  const char* name;
+  double flop, bytes;
+};
+
+GemmCost gemm_cost(const GemmParams& p, int epi, int esize) {
+  static const char* const kStore16[4] = {"gemm_store16", "gemm_store16_gelu", "gemm_store16_tanh",
+                                          "gemm_store16_sigmoid"};  // indexed by kAct*
+  GemmCost c{nullptr, 0.0, 0.0};
+  switch (epi) {
+    case kEpiStore16: c.name = kStore16[(p.act >= 0 && p.act < 4) ? p.act : 0]; break;
+    case kEpiResid32: c.name = "gemm_resid32"; break;
+    case kEpiStore32: c.name = "gemm_store32"; break;
+    case kEpiGlu32: c.name = "gemm_glu32"; break;
+    default: c.name = "gemm_qkv_rope"; break;
+  }
+  const double out_bytes = epi == kEpiStore16 || epi == kEpiQkvRope ? 2.0 : epi == kEpiResid32 ? 8.0
+                           : epi == kEpiGlu32                      ? 2.0  // n/2 fp32 columns
+                                                                   : 4.0;
+  for (int i = 0; i < p.num_groups; ++i) {
+    const GemmGroup& g = p.groups[i];
+    c.flop += 2.0 * g.m * (double)g.n * g.k;
+    c.bytes += ((double)g.m * g.k + (double)g.n * g.k) * esize + (double)g.m * g.n * out_bytes;
+  }
+  return c;
+}
+
 template <int BN, int EPI, typename T>
 cudaError_t launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const GemmParams& p,
                        int num_sms, cudaStream_t stream) {
@@ -372,7 +401,8 @@ cudaError_t launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
   }
   const int grid = p.total_tiles < num_sms ? p.total_tiles : num_sms;
   if (grid <= 0) return cudaSuccess;
-  note_launch();
+  const GemmCost cost = gemm_cost(p, EPI, (int)sizeof(T));
+  LaunchScope scope(cost.name, cost.flop, cost.bytes, stream);
   kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ma, mb, mo, p);
   return cudaGetLastError();
 }

@@ -101,6 +101,11 @@ cudaError_t rmsnorm_dispatch(const RmsNormArgs& a, cudaStream_t s) {
   long long blocks = (warps + 7) / 8;
   if (blocks > 148LL * 16) blocks = 148LL * 16;
   if (blocks < 1) return cudaSuccess;
+  const double rd = (double)a.rows * a.D;
+  LaunchScope scope("rmsnorm", 0.0,
+                    rd * 4.0 + (a.gamma_pre ? rd * 4.0 : 0.0) + (a.gamma ? rd * sizeof(T) : 0.0) +
+                        (a.wg ? (double)a.rows * a.heads * 4.0 : 0.0),
+                    s);
   switch (V) {
 #define MSST_RMS_CASE(v)                                                                                \
   case v:                                                                                               \
@@ -346,18 +351,19 @@ inline unsigned grid_for(long long n) {
 }  // namespace
 
 cudaError_t launch_rmsnorm(const RmsNormArgs& a, int bf16, cudaStream_t s) {
-  note_launch();
   if (a.D % 128 != 0 || a.D > 1024 || (a.band_major && a.F <= 0) || (a.wg && a.heads > 32))
     return cudaErrorInvalidValue;
   return bf16 ? rmsnorm_dispatch<__nv_bfloat16>(a, s) : rmsnorm_dispatch<__half>(a, s);
 }
 
 cudaError_t launch_band_input(const BandInArgs& a, int bf16, cudaStream_t s) {
-  note_launch();
   const long long warps = (long long)a.Bc * a.T * a.num_bands;
   long long blocks = (warps + 7) / 8;
   if (blocks > 148LL * 32) blocks = 148LL * 32;
   if (blocks < 1) return cudaSuccess;
+  // the STFT read once, the packed A operand written once
+  LaunchScope scope("band_input", 0.0,
+                    (double)a.Bc * a.C * a.T * a.nbins * 8.0 + (double)a.Bc * a.T * a.ld * 2.0, s);
   if (bf16)
     band_input_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, s>>>(a);
   else
@@ -366,26 +372,31 @@ cudaError_t launch_band_input(const BandInArgs& a, int bf16, cudaStream_t s) {
 }
 
 cudaError_t launch_mask_apply(const MaskApplyArgs& a, cudaStream_t s) {
-  note_launch();
+  const double tb = (double)a.Bc * a.T * a.nbins;
+  LaunchScope scope("mask_apply", 0.0,
+                    tb * a.C * 8.0 + (double)a.S * a.Bc * a.T * a.mask_ld * 4.0 + tb * a.S * a.C * 8.0, s);
   mask_apply_kernel<<<grid_for((long long)a.Bc * a.S * a.T * a.nbins), 256, 0, s>>>(a);
   return cudaGetLastError();
 }
 
 cudaError_t launch_stft_frames(const float* audio, long long L, int BC, int T, int n_fft, int hop, const float* win,
                                float* frames, cudaStream_t s) {
+  LaunchScope scope("stft_frames", 0.0, (double)BC * L * 4.0 + (double)BC * T * n_fft * 4.0, s);
   stft_frames_kernel<<<grid_for((long long)BC * T * n_fft), 256, 0, s>>>(audio, L, BC, T, n_fft, hop, win, frames);
   return cudaGetLastError();
 }
 
 cudaError_t launch_istft_ola(const float* frames, int BSC, int T, int n_fft, int hop, const float* win,
                              const float* wsum, float* out, cudaStream_t s) {
+  LaunchScope scope("istft_ola", 0.0,
+                    (double)BSC * T * n_fft * 4.0 + (double)BSC * (T - 1) * (double)hop * 4.0, s);
   istft_ola_kernel<<<grid_for((long long)BSC * (T - 1) * hop), 256, 0, s>>>(frames, BSC, T, n_fft, hop, win, wsum,
                                                                            out);
   return cudaGetLastError();
 }
 
 cudaError_t launch_chunk_gather(const ChunkArgs& a, int first, int count, float* batch, cudaStream_t s) {
-  note_launch();
+  LaunchScope scope("chunk_gather", 0.0, 2.0 * count * a.C * (double)a.chunk * 4.0, s);
   chunk_gather_kernel<<<grid_for((long long)count * a.C * a.chunk), 256, 0, s>>>(a, first, count, batch);
   return cudaGetLastError();
 }
@@ -394,13 +405,15 @@ cudaError_t launch_chunk_ola(const ChunkArgs& a, int first, int count, int num_c
                              float* wsum, cudaStream_t s) {
   const long long g0 = (long long)first * a.step;
   const long long g1 = std::min((long long)(first + count - 1) * a.step + a.chunk, a.total);
+  LaunchScope scope("chunk_ola", 0.0,
+                    (double)count * a.C * a.chunk * 4.0 + 2.0 * (a.C + 1) * (double)(g1 - g0) * 4.0, s);
   chunk_ola_kernel<<<grid_for((long long)(a.C + 1) * (g1 - g0)), 256, 0, s>>>(a, first, count, num_chunks, y, acc,
                                                                               wsum);
   return cudaGetLastError();
 }
 
 cudaError_t launch_chunk_finish(const ChunkArgs& a, const float* acc, const float* wsum, float* out, cudaStream_t s) {
-  note_launch();
+  LaunchScope scope("chunk_finish", 0.0, (double)a.L * (2.0 * a.C + 1.0) * 4.0, s);
   chunk_finish_kernel<<<grid_for((long long)a.C * a.L), 256, 0, s>>>(a, acc, wsum, out);
   return cudaGetLastError();
 }

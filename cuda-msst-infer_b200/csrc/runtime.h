@@ -158,4 +158,14 @@ inline unsigned device_error(bool clear) {
   return gemm_device_error(clear) | attention_device_error(clear) | kernels_device_error(clear);
 }
 
+// Launch accounting (launch_stats.cu; see LaunchScope in common.cuh).
+struct KernelStat {
+  std::string name;
+  unsigned long long launches = 0;
+  double ms = 0, flop = 0, bytes = 0;
+};
+unsigned long long launch_count(bool reset);
+void set_kernel_timing(bool on);
+std::vector<KernelStat> kernel_timing_report();
+
 }  // namespace msst

@@ -26,7 +26,8 @@ AXIS = {"time": 0, "band": 1}
 SEPARATE_FIX_TAIL_PADDING = 1
 
 EXPORTS = [
-    "msst_last_error", "msst_device_error", "msst_version", "msst_kernel_launches", "msst_rmsnorm", "msst_gemm", "msst_gemm_qkv_rope",
+    "msst_last_error", "msst_device_error", "msst_version", "msst_kernel_launches", "msst_kernel_timing",
+    "msst_kernel_timing_report", "msst_rmsnorm", "msst_gemm", "msst_gemm_qkv_rope",
     "msst_attention", "msst_model_load", "msst_model_free", "msst_model_get_info", "msst_model_forward",
     "msst_model_masks", "msst_model_transformer", "msst_model_transformer_noalloc", "msst_model_separate", "msst_model_separate_host",
     "msst_model_chunk_plan", "msst_model_forward_chunks", "msst_model_stitch",
@@ -66,6 +67,8 @@ def lib():
     L.msst_device_error.argtypes = [c_int]
     L.msst_kernel_launches.restype = ctypes.c_ulonglong
     L.msst_kernel_launches.argtypes = [c_int]
+    L.msst_kernel_timing.argtypes = [c_int]
+    L.msst_kernel_timing_report.argtypes = [vp, c_int, ctypes.POINTER(c_int)]
     L.msst_rmsnorm.argtypes = [vp, i64, c_int, vp, c_float, c_int, vp, vp, vp, c_int, vp, vp]
     L.msst_gemm.argtypes = [vp, i64, c_int, i64, vp, c_int, vp, c_int, c_int, c_int, vp, i64, vp]
     L.msst_gemm_qkv_rope.argtypes = [vp, i64, c_int, vp, c_int, vp, vp, c_int, c_int, c_int, vp, vp]
@@ -100,6 +103,26 @@ def device_error(clear: bool = True) -> int:
 def kernel_launches(reset: bool = False) -> int:
     """Kernels launched by libmsst_b200 so far in this process."""
     return int(lib().msst_kernel_launches(1 if reset else 0))
+
+
+class KernelStat(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char * 40), ("launches", ctypes.c_ulonglong), ("total_ms", ctypes.c_double),
+                ("flop", ctypes.c_double), ("bytes", ctypes.c_double)]
+
+
+def kernel_timing(enable: bool) -> None:
+    """Start (discarding earlier records) or stop per-kernel CUDA-event timing."""
+    check(lib().msst_kernel_timing(1 if enable else 0))
+
+
+def kernel_timing_report() -> dict:
+    """{kernel name: {launches, total_ms, flop, bytes}} over the recorded launches."""
+    n = ctypes.c_int(0)
+    check(lib().msst_kernel_timing_report(None, 0, ctypes.byref(n)))
+    arr = (KernelStat * max(n.value, 1))()
+    check(lib().msst_kernel_timing_report(arr, n.value, ctypes.byref(n)))
+    return {a.name.decode(): {"launches": int(a.launches), "total_ms": a.total_ms, "flop": a.flop,
+                              "bytes": a.bytes} for a in arr[: n.value]}
 
 
 # --------------------------------------------------------------------------- torch helpers

@@ -71,6 +71,23 @@ int msst_version(void);
 /* Number of kernels this library has launched (process-wide); reset != 0 returns and zeroes it. */
 unsigned long long msst_kernel_launches(int reset);
 
+/* Per-kernel timing of this library's launches, a measurement aid with no
+ * counterpart in the reference.  msst_kernel_timing(1) discards earlier records
+ * and starts recording: each launch is bracketed by two CUDA events on its stream
+ * and tagged with its kernel name and its algorithmic FLOPs and DRAM bytes (the
+ * operands read once and the results written once).  msst_kernel_timing(0) stops
+ * recording.  msst_kernel_timing_report waits for the recorded launches, writes up
+ * to `cap` per-name aggregates to `out` and the number of names to *count. */
+typedef struct msst_kernel_stat {
+  char name[40];
+  unsigned long long launches;
+  double total_ms;
+  double flop;
+  double bytes;
+} msst_kernel_stat;
+int msst_kernel_timing(int enable);
+int msst_kernel_timing_report(msst_kernel_stat* out, int cap, int* count);
+
 /* ---------------------------------------------------------------- op level -- */
 
 /* RMSNorm of the reference, y = x * rsqrt(sum(x^2) + 1e-12) * gamma * scale

@@ -105,3 +105,13 @@ def test_library_has_no_cpu_fallback_symbols():
     """The product library links no oracle code."""
     out = os.popen(f"nm -D {os.path.join(ROOT, 'cuda-msst-infer_b200', 'msst_b200', 'lib', 'libmsst_b200.so')}").read()
     assert "msst_oracle" not in out and "refh_" not in out
+
+
+def test_kernel_timing_api_without_gpu():
+    """Timing on/off and an empty report need no device; the report is keyed by kernel name."""
+    from msst_b200 import kernel_launches, kernel_timing, kernel_timing_report
+
+    kernel_timing(True)
+    kernel_timing(False)
+    assert kernel_timing_report() == {}
+    assert kernel_launches(reset=True) >= 0

@@ -226,3 +226,28 @@ def test_linear_matches_reference_engine(cuda):
         torch.cuda.synchronize()
         assert rel_l2(y.float().cpu().numpy(), z[f"lin_{act}_fp16"]) < 2e-3
         assert rel_l2(y.float().cpu().numpy(), z[f"lin_{act}_fp32"]) < 3e-3
+
+
+def test_kernel_timing_records_launches(cuda):
+    """msst_kernel_timing brackets each launch with events and tags it with its algorithmic cost."""
+    torch = cuda
+    from msst_b200 import kernel_timing, kernel_timing_report, ops
+
+    M, K, N = 4096, 384, 1536
+    x = torch.randn(M, K, device="cuda").half()
+    w = (0.02 * torch.randn(N, K, device="cuda")).half()
+    kernel_timing(True)
+    for _ in range(3):
+        ops.gemm(x, w, None, "store16", "gelu")
+    kernel_timing(False)
+    ops.gemm(x, w, None, "store16", "gelu")  # not recorded
+    rep = kernel_timing_report()
+    assert set(rep) == {"gemm_store16_gelu"}
+    k = rep["gemm_store16_gelu"]
+    assert k["launches"] == 3
+    assert k["flop"] == pytest.approx(3 * 2.0 * M * N * K)
+    assert k["bytes"] == pytest.approx(3 * ((M * K + N * K) * 2.0 + M * N * 2.0))
+    assert 0.0 < k["total_ms"] < 1000.0
+    kernel_timing(True)  # restarting discards the records
+    kernel_timing(False)
+    assert kernel_timing_report() == {}
