@@ -52,24 +52,54 @@ __device__ __forceinline__ int find_group(const GemmGroup* g, int n, int t) {
   return i;
 }
 
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
+__device__ __forceinline__ float2 abs2(float2 v) { return make_float2(fabsf(v.x), fabsf(v.y)); }
+
+// The epilogue activations on pairs of columns: the FMA-pipe arithmetic runs as
+// packed f32x2 operations (half the issue slots), the MUFU work (ex2, rcp) per
+// element.
+//
+// GELU, erf form (reference src/ops_fused.cu:21-24): 0.5 x (1 + erf(x / sqrt 2)),
 // erf by Abramowitz & Stegun, Handbook of Mathematical Functions, formula 7.1.26
 // (after Hastings): erf(a) = 1 - t(a1 + t(a2 + t(a3 + t(a4 + t a5)))) e^{-a^2},
-// t = 1/(1 + p a), |error| <= 1.5e-7 for a >= 0; odd extension for a < 0.  Two
-// MUFU operations and six FMAs instead of a general-purpose erff, well below the
-// 16-bit output rounding of the GELU epilogue.
-__device__ __forceinline__ float erf_as7126(float z) {
-  const float a = fabsf(z);
-  const float t = __fdividef(1.0f, fmaf(0.3275911f, a, 1.0f));
-  const float poly =
-      t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, 1.061405429f, -1.453152027f), 1.421413741f), -0.284496736f), 0.254829592f);
-  return copysignf(1.0f - poly * __expf(-a * a), z);
+// t = 1/(1 + p a), |error| <= 1.5e-7 for a >= 0, odd extension for a < 0 -- two
+// MUFU operations and a handful of FMAs, well below the 16-bit output rounding.
+// The polynomial's signs are folded so that 1 - t poly(t) e^{-a^2} is one FMA.
+__device__ __forceinline__ float2 gelu2(float2 x) {
+  const float2 z = __fmul2_rn(x, f2(0.70710678118654752f));
+  const float2 a = abs2(z);
+  const float2 d = __ffma2_rn(a, f2(0.3275911f), f2(1.0f));
+  const float2 t = make_float2(rcp_approx(d.x), rcp_approx(d.y));
+  float2 q = __ffma2_rn(t, f2(-1.061405429f), f2(1.453152027f));
+  q = __ffma2_rn(t, q, f2(-1.421413741f));
+  q = __ffma2_rn(t, q, f2(0.284496736f));
+  q = __ffma2_rn(t, q, f2(-0.254829592f));
+  const float2 np = __fmul2_rn(t, q);                       // -t*poly(t)
+  const float2 s = __fmul2_rn(__fmul2_rn(a, f2(-1.4426950408889634f)), a);  // -a^2 log2(e)
+  const float2 e = make_float2(fast_exp2(s.x), fast_exp2(s.y));
+  const float2 r = __ffma2_rn(np, e, f2(1.0f));             // erf(|z|)
+  const float2 erf = make_float2(copysignf(r.x, z.x), copysignf(r.y, z.y));
+  const float2 h = __fmul2_rn(x, f2(0.5f));
+  return __ffma2_rn(h, erf, h);
 }
-
-// GELU, erf form (reference src/ops_fused.cu:21-24)
-__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erf_as7126(x * 0.70710678118654752f)); }
-// logistic sigmoid with a fast reciprocal (the reference's --use_fast_math build
-// also turns this division into an approximate one)
-__device__ __forceinline__ float sigmoidf_(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+// tanh(x) = 1 - 2 / (1 + 2^(2x log2 e)); saturates exactly to +-1 at both ends
+__device__ __forceinline__ float2 tanh2(float2 x) {
+  const float2 s = __fmul2_rn(x, f2(2.8853900817779268f));
+  const float2 d = __fadd2_rn(make_float2(fast_exp2(s.x), fast_exp2(s.y)), f2(1.0f));
+  return __ffma2_rn(make_float2(rcp_approx(d.x), rcp_approx(d.y)), f2(-2.0f), f2(1.0f));
+}
+// logistic sigmoid, 1 / (1 + 2^(-x log2 e)) with an approximate reciprocal (the
+// reference's --use_fast_math build also makes this division approximate)
+__device__ __forceinline__ float2 sigmoid2(float2 x) {
+  const float2 s = __fmul2_rn(x, f2(-1.4426950408889634f));
+  const float2 d = __fadd2_rn(make_float2(fast_exp2(s.x), fast_exp2(s.y)), f2(1.0f));
+  return make_float2(rcp_approx(d.x), rcp_approx(d.y));
+}
 
 // bias, activation and RoPE on one 32-column chunk of one row (fp32 registers)
 template <int EPI>
@@ -81,10 +111,12 @@ __device__ __forceinline__ void chunk_math(const GemmParams& p, const GemmGroup&
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         const float4 b = __ldg(b4 + q);
-        v[4 * q] += b.x;
-        v[4 * q + 1] += b.y;
-        v[4 * q + 2] += b.z;
-        v[4 * q + 3] += b.w;
+        const float2 lo = __fadd2_rn(make_float2(v[4 * q], v[4 * q + 1]), make_float2(b.x, b.y));
+        const float2 hi = __fadd2_rn(make_float2(v[4 * q + 2], v[4 * q + 3]), make_float2(b.z, b.w));
+        v[4 * q] = lo.x;
+        v[4 * q + 1] = lo.y;
+        v[4 * q + 2] = hi.x;
+        v[4 * q + 3] = hi.y;
       }
     } else {
 #pragma unroll
@@ -95,13 +127,25 @@ __device__ __forceinline__ void chunk_math(const GemmParams& p, const GemmGroup&
   if constexpr (EPI == kEpiStore16) {
     if (p.act == kActGelu) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+      for (int j = 0; j < 32; j += 2) {
+        const float2 y = gelu2(make_float2(v[j], v[j + 1]));
+        v[j] = y.x;
+        v[j + 1] = y.y;
+      }
     } else if (p.act == kActTanh) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = tanhf(v[j]);
+      for (int j = 0; j < 32; j += 2) {
+        const float2 y = tanh2(make_float2(v[j], v[j + 1]));
+        v[j] = y.x;
+        v[j + 1] = y.y;
+      }
     } else if (p.act == kActSigmoid) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = sigmoidf_(v[j]);
+      for (int j = 0; j < 32; j += 2) {
+        const float2 y = sigmoid2(make_float2(v[j], v[j + 1]));
+        v[j] = y.x;
+        v[j + 1] = y.y;
+      }
     }
   } else if constexpr (EPI == kEpiQkvRope) {
     if (col < p.rope_cols) {
@@ -133,7 +177,12 @@ __device__ __forceinline__ void glu_store(const GemmGroup& g, int row, int col, 
   float* o = reinterpret_cast<float*>(g.out) + orow * g.ldo + g.out_col0 + (col >> 1);
   float w[16];
 #pragma unroll
-  for (int j = 0; j < 16; ++j) w[j] = v[2 * j] * sigmoidf_(v[2 * j + 1]);
+  for (int j = 0; j < 16; j += 2) {
+    const float2 gt = sigmoid2(make_float2(v[2 * j + 1], v[2 * j + 3]));
+    const float2 y = __fmul2_rn(make_float2(v[2 * j], v[2 * j + 2]), gt);
+    w[j] = y.x;
+    w[j + 1] = y.y;
+  }
   const int nout = nvalid >> 1;
   if (nout == 16 && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
     float4* o4 = reinterpret_cast<float4*>(o);
