@@ -93,6 +93,97 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(RmsNormArgs a) {
   }
 }
 
+// RMSNorm + 8 attention-gate projections with the gate weights held in registers
+// (8 heads x 4V columns per lane, loaded once per persistent warp) and the eight
+// partial dot products reduced by a butterfly transpose-reduce: 4 + 2 + 1
+// exchanges halve the set of heads a lane keeps, 2 more finish the sum, so lane
+// group h (lanes 4h..4h+3) ends with head h's full dot product (9 shuffles
+// instead of 8 separate 5-shuffle reductions).  The next row's x is prefetched
+// while the current one is processed.
+template <typename T, int V>
+__global__ void __launch_bounds__(384, 1) rmsnorm_gates8_kernel(RmsNormArgs a) {
+  constexpr int H = 8;
+  const int lane = threadIdx.x & 31;
+  const int D = a.D;
+  float4 wr[H][V];
+#pragma unroll
+  for (int h = 0; h < H; ++h)
+#pragma unroll
+    for (int k = 0; k < V; ++k) wr[h][k] = __ldg(reinterpret_cast<const float4*>(a.wg + h * D) + lane + 32 * k);
+  const float bgl = __ldg(a.bg + ((lane >> 2) & 7));
+  const long long warps_total = (long long)gridDim.x * (blockDim.x >> 5);
+  long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  float4 nxt[V];
+  if (r < a.rows) {
+#pragma unroll
+    for (int k = 0; k < V; ++k) nxt[k] = reinterpret_cast<const float4*>(a.x + r * D)[lane + 32 * k];
+  }
+  for (; r < a.rows; r += warps_total) {
+    float4 v[V];
+#pragma unroll
+    for (int k = 0; k < V; ++k) v[k] = nxt[k];
+    const long long rn = r + warps_total;
+    if (rn < a.rows) {
+#pragma unroll
+      for (int k = 0; k < V; ++k) nxt[k] = reinterpret_cast<const float4*>(a.x + rn * D)[lane + 32 * k];
+    }
+    float4* xr = reinterpret_cast<float4*>(a.x + r * D);
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < V; ++k) ss += v[k].x * v[k].x + v[k].y * v[k].y + v[k].z * v[k].z + v[k].w * v[k].w;
+    ss = warp_sum(ss);
+    if (a.gamma_pre != nullptr) {
+      const float inv = rsqrtf(ss + 1e-12f) * a.scale_pre;
+      const float4* g4 = reinterpret_cast<const float4*>(a.gamma_pre);
+      ss = 0.f;
+#pragma unroll
+      for (int k = 0; k < V; ++k) {
+        const float4 g = __ldg(g4 + lane + 32 * k);
+        v[k].x *= inv * g.x;
+        v[k].y *= inv * g.y;
+        v[k].z *= inv * g.z;
+        v[k].w *= inv * g.w;
+        xr[lane + 32 * k] = v[k];
+        ss += v[k].x * v[k].x + v[k].y * v[k].y + v[k].z * v[k].z + v[k].w * v[k].w;
+      }
+      ss = warp_sum(ss);
+    }
+    const float inv = rsqrtf(ss + 1e-12f) * a.scale;
+    const float4* g4 = reinterpret_cast<const float4*>(a.gamma);
+    float part[H];
+#pragma unroll
+    for (int h = 0; h < H; ++h) part[h] = 0.f;
+    uint2* o = reinterpret_cast<uint2*>(reinterpret_cast<T*>(a.out16) + r * D);
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      const float4 g = __ldg(g4 + lane + 32 * k);
+      const float4 y = make_float4(v[k].x * inv * g.x, v[k].y * inv * g.y, v[k].z * inv * g.z, v[k].w * inv * g.w);
+      o[lane + 32 * k] = make_uint2(pack2<T>(y.x, y.y), pack2<T>(y.z, y.w));
+#pragma unroll
+      for (int h = 0; h < H; ++h)
+        part[h] += y.x * wr[h][k].x + y.y * wr[h][k].y + y.z * wr[h][k].z + y.w * wr[h][k].w;
+    }
+    // butterfly: keep heads 4*b4..+3, then 2*b3.., then b2 (b_i = bit i of the lane)
+    const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+    float q4[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float mine = b4 ? part[4 + i] : part[i], other = b4 ? part[i] : part[4 + i];
+      q4[i] = mine + __shfl_xor_sync(0xffffffffu, other, 16);
+    }
+    float q2[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float mine = b3 ? q4[2 + i] : q4[i], other = b3 ? q4[i] : q4[2 + i];
+      q2[i] = mine + __shfl_xor_sync(0xffffffffu, other, 8);
+    }
+    float d = (b2 ? q2[1] : q2[0]) + __shfl_xor_sync(0xffffffffu, b2 ? q2[0] : q2[1], 4);
+    d += __shfl_xor_sync(0xffffffffu, d, 2);
+    d += __shfl_xor_sync(0xffffffffu, d, 1);
+    if ((lane & 3) == 0) a.gates[r * H + (lane >> 2)] = __fdividef(1.0f, 1.0f + __expf(-(d + bgl)));
+  }
+}
+
 template <typename T>
 cudaError_t rmsnorm_dispatch(const RmsNormArgs& a, cudaStream_t s) {
   const int V = a.D / 128;
@@ -106,6 +197,17 @@ cudaError_t rmsnorm_dispatch(const RmsNormArgs& a, cudaStream_t s) {
                     rd * 4.0 + (a.gamma_pre ? rd * 4.0 : 0.0) + (a.gamma ? rd * sizeof(T) : 0.0) +
                         (a.wg ? (double)a.rows * a.heads * 4.0 : 0.0),
                     s);
+  if (a.wg != nullptr && a.heads == 8 && a.gamma != nullptr && !a.band_major && V <= 3) {
+    // one block of 12 warps per SM (the gate weights take 32 * V registers per lane)
+    long long gb = (a.rows + 11) / 12;
+    if (gb > 148) gb = 148;
+    switch (V) {
+      case 1: rmsnorm_gates8_kernel<T, 1><<<(unsigned)gb, 384, 0, s>>>(a); break;
+      case 2: rmsnorm_gates8_kernel<T, 2><<<(unsigned)gb, 384, 0, s>>>(a); break;
+      default: rmsnorm_gates8_kernel<T, 3><<<(unsigned)gb, 384, 0, s>>>(a); break;
+    }
+    return cudaGetLastError();
+  }
   switch (V) {
 #define MSST_RMS_CASE(v)                                                                                \
   case v:                                                                                               \
