@@ -224,7 +224,22 @@ def cpu_sample(cfg, which):
             "x": x}
 
 
+def claim_stdout():
+    """Route everything written to fd 1 (NCCL banners, library logs) to stderr and
+    return a stream on the original stdout for the single JSON result line."""
+    sys.stdout.flush()
+    out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+    return out
+
+
+def emit(out, result):
+    out.write(json.dumps(result) + "\n")
+    out.flush()
+
+
 def main():
+    out = claim_stdout()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
@@ -243,7 +258,7 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        return run_reference(args)
+        return emit(out, run_reference(args))
 
     import torch
     import torch.distributed as dist
@@ -376,7 +391,7 @@ def main():
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
-        print(json.dumps(result))
+        emit(out, result)
 
 
 def run_reference(args):
@@ -422,14 +437,22 @@ def run_reference(args):
     ref = reference_gpu(cfg, args, prec)
     if ref:
         out["ref_gpu"] = ref
-    print(json.dumps(out))
+    return out
 
 
 def reference_gpu(cfg, args, prec):
-    """The reference engine's own CUDA build (oracle/_ref), same model and track, for context."""
+    """The reference engine's own CUDA build (oracle/_ref), same model and track, for context.
+    Its stdout logging lands on stderr (claim_stdout)."""
     lib_path = os.path.join(ROOT, "oracle", "_ref", "libcudasep_ref.so")
     if not os.path.exists(lib_path) or args.gpus != 1:
         return None
+    try:
+        return _reference_gpu(cfg, args, prec, lib_path)
+    finally:
+        ctypes.CDLL(None).fflush(None)
+
+
+def _reference_gpu(cfg, args, prec, lib_path):
     try:
         from msst_b200 import synth
 
