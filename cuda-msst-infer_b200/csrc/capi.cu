@@ -1,6 +1,7 @@
 // capi.cu — the extern "C" boundary of libmsst_b200 (declared in include/msst_b200.h).
 // Every entry point catches exceptions and turns them into status codes; the
 // message is kept per thread for msst_last_error().
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstring>
@@ -265,6 +266,135 @@ int msst_attention(const void* qkv16, int B, int T, int F, int heads, int axis, 
   });
 }
 
+int msst_grouped_gemm(int num_groups, const msst_gemm_group* groups, const void* x, long long x_rows, long long ldx,
+                      const void* w, long long w_rows, long long ldw, int epilogue, int act, int dtype, void* out,
+                      long long out_rows, long long ldo, void* stream) {
+  return guarded([&] {
+    check_dtype(dtype);
+    MSST_REQUIRE(groups && x && w && out, "null argument");
+    MSST_REQUIRE(num_groups >= 1 && num_groups <= msst::kGemmMaxGroups, "num_groups must be 1..64");
+    MSST_REQUIRE(epilogue >= MSST_EPI_STORE16 && epilogue <= MSST_EPI_GLU32, "bad epilogue");
+    MSST_REQUIRE(act >= MSST_ACT_NONE && act <= MSST_ACT_SIGMOID, "bad activation");
+    MSST_REQUIRE(x_rows > 0 && x_rows < (1LL << 31) && w_rows > 0 && w_rows < (1LL << 31) && out_rows > 0 &&
+                     out_rows < (1LL << 31),
+                 "bad matrix row counts");
+    MSST_REQUIRE(ldx >= 64 && ldx % 8 == 0 && ldw >= 64 && ldw % 8 == 0,
+                 "ldx / ldw must be >= 64 and multiples of 8 elements");
+    const bool out32 = epilogue != MSST_EPI_STORE16;
+    const bool tma_out = epilogue != MSST_EPI_GLU32;
+    const int col_align = out32 ? 4 : 8;  // TMA boxes start on 16 bytes
+    MSST_REQUIRE(ldo > 0 && ldo % col_align == 0, "ldo must be a multiple of 16 bytes");
+    check_align(x, "x");
+    check_align(w, "w");
+    check_align(out, "out");
+    use_device_of(x);
+    msst::GemmParams p{};
+    p.num_groups = num_groups;
+    p.act = act;
+    int nmax = 0;
+    for (int i = 0; i < num_groups; ++i) {
+      const msst_gemm_group& q = groups[i];
+      const std::string gi = "group " + std::to_string(i) + ": ";
+      const long long nout = epilogue == MSST_EPI_GLU32 ? q.n / 2 : q.n;
+      MSST_REQUIRE(q.m > 0 && q.n > 0 && q.k > 0 && q.k % 64 == 0, gi + "needs m, n > 0 and k a positive multiple of 64");
+      MSST_REQUIRE(epilogue != MSST_EPI_GLU32 || q.n % 2 == 0, gi + "GLU needs an even n");
+      MSST_REQUIRE(q.a_col0 % 8 == 0 && q.b_col0 % 8 == 0, gi + "a_col0 and b_col0 must be multiples of 8");
+      MSST_REQUIRE(q.a_row0 >= 0 && q.a_row0 + q.m <= x_rows && q.a_col0 >= 0 && q.a_col0 + q.k <= ldx,
+                   gi + "A slice outside x");
+      MSST_REQUIRE(q.b_row0 >= 0 && q.b_row0 + q.n <= w_rows && q.b_col0 >= 0 && q.b_col0 + q.k <= ldw,
+                   gi + "B slice outside W");
+      MSST_REQUIRE(q.out_row0 >= 0 && q.out_row0 + q.m <= out_rows && q.out_col0 >= 0 && q.out_col0 + nout <= ldo,
+                   gi + "output block outside out");
+      if (tma_out) {
+        MSST_REQUIRE(q.out_col0 % col_align == 0, gi + "out_col0 must start on 16 bytes");
+        MSST_REQUIRE(q.m % 32 == 0 || q.out_row0 + q.m == out_rows,
+                     gi + "m must be a multiple of 32 unless the block ends at out_rows");
+        MSST_REQUIRE(q.n % 32 == 0 || q.out_col0 + q.n == ldo,
+                     gi + "n must be a multiple of 32 unless the block ends at column ldo");
+      }
+      msst::GemmGroup& g = p.groups[i];
+      g.m = (int)q.m;
+      g.n = q.n;
+      g.k = q.k;
+      g.a_row0 = (int)q.a_row0;
+      g.a_col0 = q.a_col0;
+      g.b_row0 = q.b_row0;
+      g.b_col0 = q.b_col0;
+      g.out_col0 = q.out_col0;
+      g.oy0 = (int)q.out_row0;
+      g.oy_row = 1;
+      g.out = out;
+      g.ldo = ldo;
+      g.out_row_mul = 1;
+      g.out_row_add = q.out_row0;
+      g.bias = q.bias;
+      nmax = std::max(nmax, q.n);
+    }
+    const int bn = pick_bn(nmax);
+    const CUtensorMap ma = msst::map_2d(x, (uint64_t)x_rows, (uint64_t)ldx, (uint64_t)ldx, msst::kGemmBM);
+    const CUtensorMap mb = msst::map_2d(w, (uint64_t)w_rows, (uint64_t)ldw, (uint64_t)ldw, (uint32_t)bn);
+    const CUtensorMap mo =
+        tma_out ? msst::map_out_2d(out, out32, (uint64_t)out_rows, (uint64_t)ldo, (uint64_t)ldo) : ma;
+    run_gemm(ma, mb, mo, p, epilogue, bn, dtype, as_stream(stream));
+  });
+}
+
+int msst_band_gather(const float* spec, int B, int T, const msst_band_tables* t, int dtype, void* out16,
+                     long long ldo, void* stream) {
+  return guarded([&] {
+    check_dtype(dtype);
+    MSST_REQUIRE(spec && t && out16 && t->bin_start && t->nfreq && t->bin_list && t->kcol && t->kpad && t->gcol &&
+                     t->gamma,
+                 "null argument");
+    MSST_REQUIRE(B > 0 && T > 0 && t->num_bands > 0 && t->nbins > 0 && t->channels > 0, "bad shape");
+    MSST_REQUIRE(ldo >= t->sum_kpad && ldo % 8 == 0, "ldo must cover sum_kpad and be a multiple of 8");
+    check_align(out16, "out16");
+    use_device_of(spec);
+    msst::BandInArgs bi{};
+    bi.spec = reinterpret_cast<const float2*>(spec);
+    bi.Bc = B;
+    bi.C = t->channels;
+    bi.T = T;
+    bi.nbins = t->nbins;
+    bi.num_bands = t->num_bands;
+    bi.bin_start = t->bin_start;
+    bi.nfreq = t->nfreq;
+    bi.bin_list = t->bin_list;
+    bi.kcol = t->kcol;
+    bi.kpad = t->kpad;
+    bi.gcol = t->gcol;
+    bi.gamma = t->gamma;
+    bi.out = out16;
+    bi.ld = ldo;
+    MSST_CUDA(msst::launch_band_input(bi, dtype, as_stream(stream)));
+  });
+}
+
+int msst_mask_apply(const float* spec, const float* masks, int B, int S, int T, const msst_band_tables* t, int zero_dc,
+                    float* out, void* stream) {
+  return guarded([&] {
+    MSST_REQUIRE(spec && masks && t && out && t->contrib_off && t->contrib_col && t->denom, "null argument");
+    MSST_REQUIRE(B > 0 && S > 0 && T > 0 && t->nbins > 0 && t->channels > 0 && t->sum_dims > 0, "bad shape");
+    use_device_of(spec);
+    msst::MaskApplyArgs ma{};
+    ma.spec = reinterpret_cast<const float2*>(spec);
+    ma.mask = masks;
+    ma.mask_stem_stride = (long long)B * T * t->sum_dims;
+    ma.mask_ld = t->sum_dims;
+    ma.contrib_off = t->contrib_off;
+    ma.contrib_col = t->contrib_col;
+    ma.denom = t->denom;
+    ma.out = reinterpret_cast<float2*>(out);
+    ma.Bc = B;
+    ma.S = S;
+    ma.C = t->channels;
+    ma.T = T;
+    ma.nbins = t->nbins;
+    ma.zero_dc = zero_dc ? 1 : 0;
+    MSST_CUDA(msst::launch_mask_apply(ma, as_stream(stream)));
+  });
+}
+
 int msst_model_load(const char* path, int device, int precision, msst_model** out) {
   return guarded([&] {
     MSST_REQUIRE(path && out, "null argument");
@@ -316,6 +446,31 @@ int msst_model_transformer(msst_model* m, int depth_index, int axis, float* x, i
     MSST_REQUIRE(m && x, "null argument");
     MSST_CUDA(cudaSetDevice(m->impl.device()));
     m->impl.transformer(depth_index, axis, x, batch, T, as_stream(stream));
+  });
+}
+
+int msst_roformer_attn_block(msst_model* m, int depth_index, int axis, int layer, float* x, int batch, int T,
+                             void* stream) {
+  return guarded([&] {
+    MSST_REQUIRE(m && x, "null argument");
+    MSST_CUDA(cudaSetDevice(m->impl.device()));
+    m->impl.attn_block(depth_index, axis, layer, x, batch, T, as_stream(stream));
+  });
+}
+
+int msst_roformer_ffn_block(msst_model* m, int depth_index, int axis, int layer, float* x, int batch, int T,
+                            void* stream) {
+  return guarded([&] {
+    MSST_REQUIRE(m && x, "null argument");
+    MSST_CUDA(cudaSetDevice(m->impl.device()));
+    m->impl.ffn_block(depth_index, axis, layer, x, batch, T, as_stream(stream));
+  });
+}
+
+int msst_model_band_tables(const msst_model* m, msst_band_tables* tables) {
+  return guarded([&] {
+    MSST_REQUIRE(m && tables, "null argument");
+    m->impl.band_tables(tables);
   });
 }
 

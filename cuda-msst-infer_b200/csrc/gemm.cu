@@ -376,8 +376,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           stage_row<T, Epi::k16>(stg, lane, v);
           fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0) {
-            const int row0 = tm * kGemmBM + q * 32;
+          // boxes starting past the group's last row stay unwritten (they would hold
+          // products of the next group's A rows)
+          const int row0 = tm * kGemmBM + q * 32;
+          if (lane == 0 && row0 < g.m) {
             const int x = g.out_col0 + col, y = g.oy0 + g.oy_row * row0, z = g.oz0 + g.oz_row * row0;
             if constexpr (EPI == kEpiResid32)
               tma_reduce_add_3d(&map_o, stg, x, y, z);

@@ -775,100 +775,118 @@ void Model::run_front(const float* audio, int B, long long L, int T, cudaStream_
 
 void Model::run_transformer(int d, int axis, float* x, int B, int T, const float* pending_gamma, cudaStream_t s,
                             Work& w) {
+  const TransformerWeights& tw = axis == 0 ? blocks_[d].first : blocks_[d].second;
+  for (int l = 0; l < (int)tw.layers.size(); ++l) {
+    run_attn_block(d, axis, l, x, B, T, l == 0 ? pending_gamma : nullptr, s, w);
+    run_ffn_block(d, axis, l, x, B, T, s, w);
+  }
+}
+
+// src/model_mel_band_roformer.cu:519-591 (apply_attention) + residual
+void Model::run_attn_block(int d, int axis, int l, float* x, int B, int T, const float* pending_gamma, cudaStream_t s,
+                           Work& w) {
   const msst_model_info& I = info_;
   const int D = I.dim, nb = I.num_bands;
   const TransformerWeights& tw = axis == 0 ? blocks_[d].first : blocks_[d].second;
+  const LayerWeights& L = tw.layers[l];
   const long long M = (long long)B * T * nb;
   const float scale = std::sqrt((float)D);
   const CUtensorMap mo_x = map_out_2d(x, true, M, D, D);  // residual reduce-add target
-  for (size_t l = 0; l < tw.layers.size(); ++l) {
-    const LayerWeights& L = tw.layers[l];
-    // attention pre-norm (+ pending final norm of the previous transformer) + gates
-    RmsNormArgs rn{};
-    rn.x = x;
-    rn.rows = M;
-    rn.D = D;
-    rn.gamma_pre = l == 0 ? pending_gamma : nullptr;
-    rn.scale_pre = scale;
-    rn.gamma = L.g_attn.get<float>();
-    rn.scale = scale;
-    rn.out16 = w.xn.get();
-    rn.wg = L.wg.get<float>();
-    rn.bg = L.bg.get<float>();
-    rn.gates = w.gates.get<float>();
-    rn.heads = I.heads;
-    MSST_CUDA(launch_rmsnorm(rn, bf16_, s));
-    // QKV + RoPE
-    {
-      GemmParams p{};
-      p.num_groups = 1;
-      p.groups[0] = group((int)M, 3 * inner_, D, w.big1.get(), 3 * inner_, nullptr);
-      p.rope_cols = 2 * inner_;
-      p.head_dim = I.dim_head;
-      if (axis == 0) {
-        p.pos_div = nb;
-        p.pos_mod = T;
-      } else {
-        p.pos_div = 1;
-        p.pos_mod = nb;
-      }
-      p.rope_cos = rope_table(p.pos_mod, false);
-      p.rope_sin = rope_table(p.pos_mod, true);
-      gemm(w.m_xn, L.m_wqkv, w.mo_qkv, p, kEpiQkvRope, pick_bn(3 * inner_), s);
+  // attention pre-norm (+ pending final norm of the previous transformer) + gates
+  RmsNormArgs rn{};
+  rn.x = x;
+  rn.rows = M;
+  rn.D = D;
+  rn.gamma_pre = pending_gamma;
+  rn.scale_pre = scale;
+  rn.gamma = L.g_attn.get<float>();
+  rn.scale = scale;
+  rn.out16 = w.xn.get();
+  rn.wg = L.wg.get<float>();
+  rn.bg = L.bg.get<float>();
+  rn.gates = w.gates.get<float>();
+  rn.heads = I.heads;
+  MSST_CUDA(launch_rmsnorm(rn, bf16_, s));
+  // QKV + RoPE
+  {
+    GemmParams p{};
+    p.num_groups = 1;
+    p.groups[0] = group((int)M, 3 * inner_, D, w.big1.get(), 3 * inner_, nullptr);
+    p.rope_cols = 2 * inner_;
+    p.head_dim = I.dim_head;
+    if (axis == 0) {
+      p.pos_div = nb;
+      p.pos_mod = T;
+    } else {
+      p.pos_div = 1;
+      p.pos_mod = nb;
     }
-    // attention (+ gate, head merge)
-    {
-      AttnParams a{};
-      a.mode = axis;
-      a.B = B;
-      a.T = T;
-      a.F = nb;
-      a.heads = I.heads;
-      a.num_tokens = (int)M;
-      a.scale_log2 = (1.0f / std::sqrt((float)I.dim_head)) * 1.4426950408889634f;
-      a.gates = w.gates.get<float>();
-      a.out = w.ao.get();
-      if (axis == 0) {
-        a.seq_len = T;
-        a.q_tiles = (T + 127) / 128;
-        a.total_items = B * nb * I.heads * a.q_tiles;
-      } else {
-        a.seq_len = nb;
-        a.seqs_per_tile = 128 / nb;
-        a.q_tiles = (int)((w.BT + a.seqs_per_tile - 1) / a.seqs_per_tile);
-        a.total_items = a.q_tiles * I.heads;
-      }
-      MSST_CUDA(launch_attention(axis == 0 ? w.m_qkv_time : w.m_qkv_band, a, bf16_, num_sms_, s));
+    p.rope_cos = rope_table(p.pos_mod, false);
+    p.rope_sin = rope_table(p.pos_mod, true);
+    gemm(w.m_xn, L.m_wqkv, w.mo_qkv, p, kEpiQkvRope, pick_bn(3 * inner_), s);
+  }
+  // attention (+ gate, head merge)
+  {
+    AttnParams a{};
+    a.mode = axis;
+    a.B = B;
+    a.T = T;
+    a.F = nb;
+    a.heads = I.heads;
+    a.num_tokens = (int)M;
+    a.scale_log2 = (1.0f / std::sqrt((float)I.dim_head)) * 1.4426950408889634f;
+    a.gates = w.gates.get<float>();
+    a.out = w.ao.get();
+    if (axis == 0) {
+      a.seq_len = T;
+      a.q_tiles = (T + 127) / 128;
+      a.total_items = B * nb * I.heads * a.q_tiles;
+    } else {
+      a.seq_len = nb;
+      a.seqs_per_tile = 128 / nb;
+      a.q_tiles = (int)((w.BT + a.seqs_per_tile - 1) / a.seqs_per_tile);
+      a.total_items = a.q_tiles * I.heads;
     }
-    // out projection + residual
-    {
-      GemmParams p{};
-      p.num_groups = 1;
-      p.groups[0] = group((int)M, D, inner_, x, D, nullptr);
-      gemm(w.m_ao, L.m_wout, mo_x, p, kEpiResid32, pick_bn(D), s);
-    }
-    // feed-forward
-    RmsNormArgs rf{};
-    rf.x = x;
-    rf.rows = M;
-    rf.D = D;
-    rf.gamma = L.g_ff.get<float>();
-    rf.scale = scale;
-    rf.out16 = w.xn.get();
-    MSST_CUDA(launch_rmsnorm(rf, bf16_, s));
-    {
-      GemmParams p{};
-      p.num_groups = 1;
-      p.act = kActGelu;
-      p.groups[0] = group((int)M, ff_, D, w.big2.get(), ff_, L.b1.get<float>());
-      gemm(w.m_xn, L.m_w1, w.mo_ffh, p, kEpiStore16, pick_bn(ff_), s);
-    }
-    {
-      GemmParams p{};
-      p.num_groups = 1;
-      p.groups[0] = group((int)M, D, ff_, x, D, L.b2.get<float>());
-      gemm(w.m_big2_ffh, L.m_w2, mo_x, p, kEpiResid32, pick_bn(D), s);
-    }
+    MSST_CUDA(launch_attention(axis == 0 ? w.m_qkv_time : w.m_qkv_band, a, bf16_, num_sms_, s));
+  }
+  // out projection + residual
+  {
+    GemmParams p{};
+    p.num_groups = 1;
+    p.groups[0] = group((int)M, D, inner_, x, D, nullptr);
+    gemm(w.m_ao, L.m_wout, mo_x, p, kEpiResid32, pick_bn(D), s);
+  }
+}
+
+// src/model_mel_band_roformer.cu:597-622 (apply_feedforward) + residual
+void Model::run_ffn_block(int d, int axis, int l, float* x, int B, int T, cudaStream_t s, Work& w) {
+  const msst_model_info& I = info_;
+  const int D = I.dim, nb = I.num_bands;
+  const TransformerWeights& tw = axis == 0 ? blocks_[d].first : blocks_[d].second;
+  const LayerWeights& L = tw.layers[l];
+  const long long M = (long long)B * T * nb;
+  const CUtensorMap mo_x = map_out_2d(x, true, M, D, D);  // residual reduce-add target
+  // feed-forward
+  RmsNormArgs rf{};
+  rf.x = x;
+  rf.rows = M;
+  rf.D = D;
+  rf.gamma = L.g_ff.get<float>();
+  rf.scale = std::sqrt((float)D);
+  rf.out16 = w.xn.get();
+  MSST_CUDA(launch_rmsnorm(rf, bf16_, s));
+  {
+    GemmParams p{};
+    p.num_groups = 1;
+    p.act = kActGelu;
+    p.groups[0] = group((int)M, ff_, D, w.big2.get(), ff_, L.b1.get<float>());
+    gemm(w.m_xn, L.m_w1, w.mo_ffh, p, kEpiStore16, pick_bn(ff_), s);
+  }
+  {
+    GemmParams p{};
+    p.num_groups = 1;
+    p.groups[0] = group((int)M, D, ff_, x, D, L.b2.get<float>());
+    gemm(w.m_big2_ffh, L.m_w2, mo_x, p, kEpiResid32, pick_bn(D), s);
   }
 }
 
@@ -978,6 +996,40 @@ void Model::masks(const float* audio, int B, int C, long long L, float* masks_ou
   run_front(audio, B, L, T, s, w);
   run_trunk(B, T, s, w);
   run_masks(B, T, s, w, masks_out);
+}
+
+void Model::attn_block(int d, int axis, int layer, float* x, int B, int T, cudaStream_t s) {
+  MSST_REQUIRE(d >= 0 && d < info_.depth && (axis == 0 || axis == 1), "bad depth index or axis");
+  const TransformerWeights& tw = axis == 0 ? blocks_[d].first : blocks_[d].second;
+  MSST_REQUIRE(layer >= 0 && layer < (int)tw.layers.size(), "bad layer index");
+  Work& w = work(B, T);
+  run_attn_block(d, axis, layer, x, B, T, nullptr, s, w);
+}
+
+void Model::ffn_block(int d, int axis, int layer, float* x, int B, int T, cudaStream_t s) {
+  MSST_REQUIRE(d >= 0 && d < info_.depth && (axis == 0 || axis == 1), "bad depth index or axis");
+  const TransformerWeights& tw = axis == 0 ? blocks_[d].first : blocks_[d].second;
+  MSST_REQUIRE(layer >= 0 && layer < (int)tw.layers.size(), "bad layer index");
+  Work& w = work(B, T);
+  run_ffn_block(d, axis, layer, x, B, T, s, w);
+}
+
+void Model::band_tables(msst_band_tables* t) const {
+  t->num_bands = info_.num_bands;
+  t->nbins = nbins_;
+  t->channels = C_;
+  t->sum_kpad = ktot_;
+  t->sum_dims = sum_dims_;
+  t->bin_start = d_bin_start_.get<int>();
+  t->nfreq = d_nfreq_.get<int>();
+  t->bin_list = d_bin_list_.get<int>();
+  t->kcol = d_kcol_.get<int>();
+  t->kpad = d_kpad_.get<int>();
+  t->gcol = d_gcol_.get<int>();
+  t->gamma = g_bs_.get<float>();
+  t->contrib_off = d_contrib_off_.get<int>();
+  t->contrib_col = d_contrib_col_.get<int>();
+  t->denom = d_denom_.get<float>();
 }
 
 void Model::transformer(int d, int axis, float* x, int B, int T, cudaStream_t s) {

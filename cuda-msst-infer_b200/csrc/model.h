@@ -44,6 +44,13 @@ class Model {
   void forward(const float* audio, int B, int C, long long L, float* out, cudaStream_t s);
   void masks(const float* audio, int B, int C, long long L, float* masks_out, cudaStream_t s);
   void transformer(int depth_index, int axis, float* x, int B, int T, cudaStream_t s);
+  // One layer's attention block (RMSNorm + gates, QKV + RoPE, attention, out
+  // projection, residual) or feed-forward block (RMSNorm, GELU MLP, residual),
+  // in place on x [B*T*num_bands, dim] fp32.
+  void attn_block(int depth_index, int axis, int layer, float* x, int B, int T, cudaStream_t s);
+  void ffn_block(int depth_index, int axis, int layer, float* x, int B, int T, cudaStream_t s);
+  // Device tables of the band gather and mask merge (read-only, owned by the model).
+  void band_tables(msst_band_tables* t) const;
   // Same as transformer(), with every intermediate in the library's fixed device
   // array (noalloc.cu); allocates nothing.
   void transformer_noalloc(int depth_index, int axis, float* x, int B, int T, cudaStream_t s);
@@ -68,6 +75,9 @@ class Model {
   void run_front(const float* audio, int B, long long L, int T, cudaStream_t s, Work& w);
   void run_masks(int B, int T, cudaStream_t s, Work& w, float* masks_out);
   void run_transformer(int d, int axis, float* x, int B, int T, const float* pending_gamma, cudaStream_t s, Work& w);
+  void run_attn_block(int d, int axis, int l, float* x, int B, int T, const float* pending_gamma, cudaStream_t s,
+                      Work& w);
+  void run_ffn_block(int d, int axis, int l, float* x, int B, int T, cudaStream_t s, Work& w);
   void gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, GemmParams& p, int epi, int bn,
             cudaStream_t s);
   const float* rope_table(int n, bool sine);

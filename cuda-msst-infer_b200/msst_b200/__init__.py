@@ -28,7 +28,8 @@ SEPARATE_FIX_TAIL_PADDING = 1
 EXPORTS = [
     "msst_last_error", "msst_device_error", "msst_version", "msst_kernel_launches", "msst_kernel_timing",
     "msst_kernel_timing_report", "msst_rmsnorm", "msst_gemm", "msst_gemm_qkv_rope",
-    "msst_attention", "msst_model_load", "msst_model_free", "msst_model_get_info", "msst_model_forward",
+    "msst_attention", "msst_grouped_gemm", "msst_band_gather", "msst_mask_apply", "msst_model_band_tables",
+    "msst_roformer_attn_block", "msst_roformer_ffn_block", "msst_model_load", "msst_model_free", "msst_model_get_info", "msst_model_forward",
     "msst_model_masks", "msst_model_transformer", "msst_model_transformer_noalloc", "msst_model_separate", "msst_model_separate_host",
     "msst_model_chunk_plan", "msst_model_forward_chunks", "msst_model_stitch",
 ]
@@ -38,6 +39,20 @@ class MsstError(RuntimeError):
     def __init__(self, code: int, msg: str):
         super().__init__(f"[msst error {code}] {msg}")
         self.code = code
+
+
+class GemmGroupC(ctypes.Structure):
+    """msst_gemm_group."""
+    _fields_ = [("m", ctypes.c_longlong), ("a_row0", ctypes.c_longlong), ("out_row0", ctypes.c_longlong),
+                ("n", ctypes.c_int), ("k", ctypes.c_int), ("a_col0", ctypes.c_int), ("b_row0", ctypes.c_int),
+                ("b_col0", ctypes.c_int), ("out_col0", ctypes.c_int), ("bias", ctypes.c_void_p)]
+
+
+class BandTables(ctypes.Structure):
+    """msst_band_tables (device pointers owned by the model)."""
+    _fields_ = [(n, ctypes.c_int) for n in ("num_bands", "nbins", "channels", "sum_kpad", "sum_dims")] + [
+        (n, ctypes.c_void_p) for n in ("bin_start", "nfreq", "bin_list", "kcol", "kpad", "gcol", "gamma",
+                                       "contrib_off", "contrib_col", "denom")]
 
 
 class ModelInfo(ctypes.Structure):
@@ -73,6 +88,13 @@ def lib():
     L.msst_gemm.argtypes = [vp, i64, c_int, i64, vp, c_int, vp, c_int, c_int, c_int, vp, i64, vp]
     L.msst_gemm_qkv_rope.argtypes = [vp, i64, c_int, vp, c_int, vp, vp, c_int, c_int, c_int, vp, vp]
     L.msst_attention.argtypes = [vp, c_int, c_int, c_int, c_int, c_int, c_float, vp, c_int, vp, vp]
+    L.msst_grouped_gemm.argtypes = [c_int, ctypes.POINTER(GemmGroupC), vp, i64, i64, vp, i64, i64, c_int, c_int,
+                                    c_int, vp, i64, i64, vp]
+    L.msst_band_gather.argtypes = [vp, c_int, c_int, ctypes.POINTER(BandTables), c_int, vp, i64, vp]
+    L.msst_mask_apply.argtypes = [vp, vp, c_int, c_int, c_int, ctypes.POINTER(BandTables), c_int, vp, vp]
+    L.msst_model_band_tables.argtypes = [vp, ctypes.POINTER(BandTables)]
+    L.msst_roformer_attn_block.argtypes = [vp, c_int, c_int, c_int, vp, c_int, c_int, vp]
+    L.msst_roformer_ffn_block.argtypes = [vp, c_int, c_int, c_int, vp, c_int, c_int, vp]
     L.msst_model_load.argtypes = [ctypes.c_char_p, c_int, c_int, ctypes.POINTER(vp)]
     L.msst_model_free.argtypes = [vp]
     L.msst_model_free.restype = None
@@ -212,6 +234,39 @@ class ops:
         return out
 
 
+    @staticmethod
+    def grouped_gemm(x, w, groups, out, epilogue="store16", act="none", stream=None):
+        """Independent GEMMs over one packed x [rows, ldx] and W [n_rows, ldw] into out (2-D);
+        groups: dicts with m, n, k and optionally a_row0, a_col0, b_row0, b_col0, out_row0,
+        out_col0, bias."""
+        arr = (GemmGroupC * len(groups))()
+        for i, g in enumerate(groups):
+            arr[i] = GemmGroupC(g["m"], g.get("a_row0", 0), g.get("out_row0", 0), g["n"], g["k"], g.get("a_col0", 0),
+                                g.get("b_row0", 0), g.get("b_col0", 0), g.get("out_col0", 0),
+                                g["bias"].data_ptr() if g.get("bias") is not None else None)
+        check(lib().msst_grouped_gemm(len(groups), arr, _ptr(x), x.shape[0], x.shape[1], _ptr(w), w.shape[0],
+                                      w.shape[1], EPI[epilogue], ACT[act], _dtype_code(x.dtype), _ptr(out),
+                                      out.shape[0], out.shape[1], _stream(stream)))
+        return out
+
+    @staticmethod
+    def band_gather(spec, B, T, tables, dtype, stream=None):
+        """spec complex STFT [B*C*T, nbins] (float32 [.., nbins, 2]) -> [B*T, sum_kpad] 16-bit."""
+        torch = _torch()
+        out = torch.empty((B * T, tables.sum_kpad), dtype=dtype, device=spec.device)
+        check(lib().msst_band_gather(_ptr(spec.contiguous()), B, T, ctypes.byref(tables), _dtype_code(dtype),
+                                     _ptr(out), tables.sum_kpad, _stream(stream)))
+        return out
+
+    @staticmethod
+    def mask_apply(spec, masks, B, S, T, tables, zero_dc=True, stream=None):
+        """masks fp32 [S, B*T, sum_dims] -> complex [B*S*C, T, nbins] (float32 [.., 2])."""
+        torch = _torch()
+        out = torch.empty((B * S * tables.channels, T, tables.nbins, 2), dtype=torch.float32, device=spec.device)
+        check(lib().msst_mask_apply(_ptr(spec.contiguous()), _ptr(masks.contiguous()), B, S, T, ctypes.byref(tables),
+                                    1 if zero_dc else 0, _ptr(out), _stream(stream)))
+        return out
+
 class Model:
     """A loaded Roformer (.csm) on one GPU."""
 
@@ -257,6 +312,26 @@ class Model:
                           device=audio.device)
         check(lib().msst_model_masks(self._h, _ptr(audio), B, C, L, _ptr(out), _stream(stream)))
         return out
+
+    def attn_block(self, depth_index: int, axis, layer: int, x, stream=None):
+        """Layer `layer`'s attention block, in place on x fp32 [B, T, bands, dim]."""
+        B, T = x.shape[0], x.shape[1]
+        check(lib().msst_roformer_attn_block(self._h, depth_index, AXIS[axis] if isinstance(axis, str) else axis,
+                                             layer, _ptr(x), B, T, _stream(stream)))
+        return x
+
+    def ffn_block(self, depth_index: int, axis, layer: int, x, stream=None):
+        """Layer `layer`'s feed-forward block, in place on x fp32 [B, T, bands, dim]."""
+        B, T = x.shape[0], x.shape[1]
+        check(lib().msst_roformer_ffn_block(self._h, depth_index, AXIS[axis] if isinstance(axis, str) else axis,
+                                            layer, _ptr(x), B, T, _stream(stream)))
+        return x
+
+    def band_tables(self) -> "BandTables":
+        """The model's band gather / mask merge tables (device pointers owned by the model)."""
+        t = BandTables()
+        check(lib().msst_model_band_tables(self._h, ctypes.byref(t)))
+        return t
 
     def transformer(self, depth_index: int, axis, x, stream=None):
         """Apply one axial transformer in place to x fp32 [B, T, bands, dim]."""

@@ -123,6 +123,72 @@ int msst_gemm_qkv_rope(const void* x, long long rows, int K, const void* w, int 
 int msst_attention(const void* qkv16, int B, int T, int F, int heads, int axis, float scale, const float* gates,
                    int dtype, void* out16, void* stream);
 
+/* One problem of msst_grouped_gemm: rows [a_row0, a_row0 + m) and columns
+ * [a_col0, a_col0 + k) of x times rows [b_row0, b_row0 + n) (same k columns from
+ * b_col0) of W, written to out rows out_row0.. and columns out_col0.. (for
+ * MSST_EPI_GLU32 out_col0 counts output columns, n/2 per row); bias [n] or NULL. */
+typedef struct msst_gemm_group {
+  long long m, a_row0, out_row0;
+  int n, k, a_col0, b_row0, b_col0, out_col0;
+  const float* bias;
+} msst_gemm_group;
+
+/* Up to 64 independent GEMMs in one launch over one packed 16-bit x [x_rows, ldx]
+ * and one packed 16-bit W [w_rows, ldw], all with the same epilogue (as
+ * msst_gemm) into one output matrix out [out_rows, ldo].  Per group: k is a
+ * multiple of 64 (pad K slices with zero columns); a_col0 and b_col0 are
+ * multiples of 8 and out_col0 starts on 16 bytes (multiple of 8 for 16-bit, 4
+ * for fp32 output).  The store / reduce epilogues write 32x32 blocks, so a
+ * group's m (n) is a multiple of 32 unless its block ends at out_rows (ldo).
+ * Replaces the reference's per-band GEMM loops of the band split and the mask
+ * estimators (apply_band_split, apply_mask_estimator,
+ * src/model_mel_band_roformer.cu:657-738, src/model_bs_roformer.cu:337-414),
+ * which launch one cuBLAS GEMM per band. */
+int msst_grouped_gemm(int num_groups, const msst_gemm_group* groups, const void* x, long long x_rows, long long ldx,
+                      const void* w, long long w_rows, long long ldw, int epilogue, int act, int dtype, void* out,
+                      long long out_rows, long long ldo, void* stream);
+
+/* Device tables of a model's band gather and mask merge (read-only, owned by the
+ * model; valid until msst_model_free).  Band b gathers nfreq[b] STFT bins
+ * bin_list[bin_start[b] ..] into columns [kcol[b], kcol[b] + kpad[b]) of the
+ * band-split input (2 * channels * nfreq[b] values, zero padding after), scaled
+ * by gamma[gcol[b] ..].  Bin i of the mask merge sums the mask columns
+ * contrib_col[contrib_off[i] .. contrib_off[i+1]) and divides by denom[i]. */
+typedef struct msst_band_tables {
+  int num_bands, nbins, channels, sum_kpad, sum_dims;
+  const int* bin_start;
+  const int* nfreq;
+  const int* bin_list;
+  const int* kcol;
+  const int* kpad;
+  const int* gcol;
+  const float* gamma;
+  const int* contrib_off;
+  const int* contrib_col;
+  const float* denom;
+} msst_band_tables;
+int msst_model_band_tables(const msst_model* m, msst_band_tables* tables);
+
+/* Band gather + per-band RMSNorm (scale sqrt(band dims)) + 16-bit cast: spec is
+ * the complex STFT in cuFFT R2C layout [B*C*T, nbins] (interleaved re/im fp32);
+ * out16 [B*T, ldo] gets band b at columns [kcol[b], kcol[b] + kpad[b]) in the
+ * reference's (bin, channel, re/im) order.  Replaces the per-band slice +
+ * contiguous copy + rms_norm of apply_band_split and the mel-bin gather of
+ * forward (src/model_mel_band_roformer.cu:657-690,808-829,
+ * src/model_bs_roformer.cu:337-369,465-473). */
+int msst_band_gather(const float* spec, int B, int T, const msst_band_tables* tables, int dtype, void* out16,
+                     long long ldo, void* stream);
+
+/* Mask merge: masks fp32 [S][B*T][sum_dims] (band-concatenated estimator output)
+ * are averaged into bins (sum of the contributing bands / denom), multiplied
+ * into the STFT spec [B*C*T, nbins] complex and written to out [(b*S + s)*C + c]
+ * [T][nbins] complex (the iSTFT input), bin 0 zeroed when zero_dc != 0.
+ * Replaces the scatter_add + average + complex multiply + zero-DC sequence of
+ * forward (src/model_mel_band_roformer.cu:926-1015,
+ * src/model_bs_roformer.cu:552-590). */
+int msst_mask_apply(const float* spec, const float* masks, int B, int S, int T, const msst_band_tables* tables,
+                    int zero_dc, float* out, void* stream);
+
 /* ------------------------------------------------------------- model level -- */
 
 /* Load a .csm model (format: src/weights.h:83-96) onto `device` with 16-bit
@@ -151,6 +217,21 @@ int msst_model_masks(msst_model* m, const float* audio, int batch, int channels,
  * (replaces apply_transformer, src/model_mel_band_roformer.cu:628-651,
  * src/model_bs_roformer.cu:310-331, with the permutes of forward() folded away). */
 int msst_model_transformer(msst_model* m, int depth_index, int axis, float* x, int batch, int T, void* stream);
+
+/* Block level, in place on the residual stream x fp32 [batch, T, num_bands, dim]:
+ * layer `layer` of the transformer (depth_index, axis).  The attention block is
+ * RMSNorm + gate projection, QKV + RoPE, attention with gates and head merge, out
+ * projection and residual add (replaces apply_attention + the residual add of
+ * apply_transformer, src/model_mel_band_roformer.cu:519-591,628-651,
+ * src/model_bs_roformer.cu:236-284,310-331); the feed-forward block is RMSNorm,
+ * Linear + GELU, Linear and residual add (apply_feedforward,
+ * src/model_mel_band_roformer.cu:597-622, src/model_bs_roformer.cu:290-304).
+ * Neither applies the MelBandRoformer's per-transformer final norm
+ * (msst_model_transformer does). */
+int msst_roformer_attn_block(msst_model* m, int depth_index, int axis, int layer, float* x, int batch, int T,
+                             void* stream);
+int msst_roformer_ffn_block(msst_model* m, int depth_index, int axis, int layer, float* x, int batch, int T,
+                            void* stream);
 
 /* msst_model_transformer for callers that cannot allocate device memory while
  * they run: real-time audio hosts, whose processing callback has a hard deadline
