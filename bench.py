@@ -250,7 +250,13 @@ def main():
     ap.add_argument("--seconds", type=float, default=TRACK_SECONDS,
                     help="track length per rank (smaller values make a profiling case)")
     ap.add_argument("--chunk-batch", type=int, default=CHUNK_BATCH, help="chunks per forward")
+    ap.add_argument("--micro", choices=["attention"], default=None,
+                    help="BASELINE config 3 instead of the separation bench (1 GPU)")
     args = ap.parse_args()
+    if args.micro == "attention":
+        if int(os.environ.get("RANK", "0")) == 0:
+            emit(out, run_micro_attention(args))
+        return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -392,6 +398,83 @@ def main():
         dist.destroy_process_group()
     if rank == 0:
         emit(out, result)
+
+
+def run_micro_attention(args):
+    """BASELINE config 3: axial attention alone, bf16, q/k/v ~ N(0, 1), scale 1/8, non-causal;
+    time axis B' = 4 x 62 sequences of 801, band axis B' = 4 x 801 sequences of 62 (8 heads x 64).
+    Ours: msst_attention on one fused QKV buffer (RoPE lives in the QKV GEMM epilogue, not in
+    this kernel).  Reference: its ops::scaled_dot_product_attention (oracle/_ref) on the same
+    shapes in fp32 (TF32 GEMMs) and fp16-value mode, device time per call."""
+    import torch
+    from msst_b200 import ops
+
+    torch.cuda.set_device(0)
+    B, T, F, H = 4, 801, 62, 8
+    M = B * T * F
+    g = torch.Generator(device="cuda").manual_seed(0)
+    qkv = torch.randn(M, 3 * H * 64, device="cuda", generator=g).to(torch.bfloat16)
+    res = {}
+    for axis, nseq, n in (("time", B * F, T), ("band", B * T, F)):
+        fn = lambda: ops.attention(qkv, B, T, F, H, axis, 0.125)
+        for _ in range(max(3, args.warmup)):
+            fn()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        s.record()
+        iters = max(5, args.steps)
+        for _ in range(iters):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(e) / iters
+        flop = 4.0 * nseq * H * n * n * 64
+        res[axis] = {"sequences": nseq, "seq_len": n, "gflop": flop / 1e9, "ms": ms,
+                     "tflops": flop / (ms * 1e-3) / 1e12}
+    burst, sustained, hbm, src = peaks()
+    out = {"metric": "attention TFLOP/s (BASELINE config 3)", "value": res["time"]["tflops"], "unit": "TFLOP/s",
+           "higher_is_better": True, "n_gpus": 1, "dtype": "bf16", "data": "synthetic",
+           "config": {"workload": "axial attention, B=4 chunks, T=801, F=62, 8 heads x 64, scale 1/8",
+                      "l2": "QKV 950 MB, larger than L2"},
+           "ours": res, "peak_tflops": burst, "peak_source": src,
+           "frac_of_burst_peak": {k: v["tflops"] / burst for k, v in res.items()}}
+    out["reference_sdpa"] = reference_sdpa(res)
+    return out
+
+
+def reference_sdpa(res):
+    """Device time of the reference's ops::scaled_dot_product_attention on the same shapes."""
+    lib_path = os.path.join(ROOT, "oracle", "_ref", "libcudasep_ref.so")
+    if not os.path.exists(lib_path):
+        return {"unavailable": "oracle/_ref not built"}
+    try:
+        f32p = ctypes.POINTER(ctypes.c_float)
+        L = ctypes.CDLL(lib_path)
+        L.refh_last_error.restype = ctypes.c_char_p
+        L.refh_sdpa_bench.argtypes = [f32p, f32p, f32p] + [ctypes.c_int] * 4 + [ctypes.c_float] + \
+            [ctypes.c_int] * 3 + [f32p]
+        rng = np.random.default_rng(0)
+        out = {}
+        for axis, r in res.items():
+            shape = (r["sequences"], 8, r["seq_len"], 64)
+            q, k, v = (rng.standard_normal(shape, dtype=np.float32) for _ in range(3))
+            P = lambda a: a.ctypes.data_as(f32p)
+            for mode, fp16 in (("fp32", 0), ("fp16", 1)):
+                ms = ctypes.c_float(0)
+                rc = L.refh_sdpa_bench(P(q), P(k), P(v), shape[0], 8, shape[2], 64, 0.125, fp16, 2, 5,
+                                       ctypes.byref(ms))
+                if rc != 0:
+                    out[f"{axis}_{mode}"] = {"unavailable": L.refh_last_error().decode()}
+                    continue
+                flop = r["gflop"] * 1e9
+                out[f"{axis}_{mode}"] = {"ms": ms.value, "tflops": flop / (ms.value * 1e-3) / 1e12,
+                                         "ours_speedup": ms.value / r["ms"]}
+            del q, k, v
+        return out
+    except Exception as e:  # informative leg only
+        return {"unavailable": str(e)}
+    finally:
+        ctypes.CDLL(None).fflush(None)
 
 
 def run_reference(args):

@@ -204,6 +204,39 @@ int refh_sdpa(const float* q, const float* k, const float* v, int B, int H, int 
   }
 }
 
+// Device time of ops::scaled_dot_product_attention (ops_attention.cu:522) on q,k,v
+// [B,H,N,D] uploaded once: `warmup` untimed calls, then `iters` calls bracketed by
+// CUDA events on the default stream; *ms_per_call gets the mean.
+int refh_sdpa_bench(const float* q, const float* k, const float* v, int B, int H, int N, int D, float scale,
+                    int fp16, int warmup, int iters, float* ms_per_call) {
+  try {
+    bool saved = g_quantize_fp16;
+    g_quantize_fp16 = fp16 != 0;
+    Tensor tq = Tensor::from_cpu_f32(q, {B, H, N, D});
+    Tensor tk = Tensor::from_cpu_f32(k, {B, H, N, D});
+    Tensor tv = Tensor::from_cpu_f32(v, {B, H, N, D});
+    for (int i = 0; i < warmup; ++i) ops::scaled_dot_product_attention(tq, tk, tv, scale);
+    CUDA_CHECK(cudaDeviceSynchronize());
+    cudaEvent_t e0, e1;
+    CUDA_CHECK(cudaEventCreate(&e0));
+    CUDA_CHECK(cudaEventCreate(&e1));
+    CUDA_CHECK(cudaEventRecord(e0, 0));
+    for (int i = 0; i < iters; ++i) ops::scaled_dot_product_attention(tq, tk, tv, scale);
+    CUDA_CHECK(cudaEventRecord(e1, 0));
+    CUDA_CHECK(cudaEventSynchronize(e1));
+    float ms = 0.f;
+    CUDA_CHECK(cudaEventElapsedTime(&ms, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    CUDA_CHECK(cudaDeviceSynchronize());
+    g_quantize_fp16 = saved;
+    *ms_per_call = ms / (float)(iters > 0 ? iters : 1);
+    return 0;
+  } catch (const std::exception& e) {
+    return fail(e);
+  }
+}
+
 // The reference's (unused by its own dispatch) scalar flash kernel,
 // flash_attention.cuh:260, on host q,k,v [B,H,N,D] fp32.
 int refh_flash(const float* q, const float* k, const float* v, int B, int H, int N, int D,
