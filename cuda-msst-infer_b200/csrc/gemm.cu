@@ -4,16 +4,19 @@
 // the residual add in src/tensor.cu:1439-1442 and the per-band loops of
 // src/model_mel_band_roformer.cu:676-736).
 //
-// CTA = 320 threads:
+// CTA = 320 threads (192 with the residual epilogue):
 //   warp 0     TMA producer (one lane): A/B k-blocks of 64 into a smem ring
 //   warp 1     MMA issuer (one lane): tcgen05.mma M=128 N=BN K=16, fp32 accumulators
 //              in TMEM, double-buffered so the epilogue of tile i overlaps the
 //              main loop of tile i+1; also owns the TMEM allocation
-//   warps 2-9  epilogue: warp w reads TMEM lane quarter w%4 and column half
+//   warps 2-9  epilogue (warps 2-5 for the residual epilogue): warp w reads
+//              TMEM lane quarter w%4 and, with 8 epilogue warps, column half
 //              (w-2)/4, 32 columns at a time; bias/activation/RoPE in fp32; the
 //              32x32 result is staged in swizzled smem and leaves by TMA bulk
 //              store (or bulk reduce-add into the fp32 residual stream).
-// Tiles of all groups are walked in one static persistent schedule.
+// Tiles of all groups are walked in one static persistent schedule; the group
+// table is read from the kernel's parameter space, so shared memory holds only
+// the ring (4 stages at BN 256, 5 at BN 192 with the residual epilogue) and staging.
 #include "common.cuh"
 #include "gemm.cuh"
 
@@ -21,15 +24,17 @@ namespace msst {
 
 namespace {
 
-constexpr int kEpiWarps = 8;
-constexpr int kThreads = 64 + 32 * kEpiWarps;
-
 template <int EPI>
 struct EpiTraits {
   static constexpr bool kTma = EPI != kEpiGlu32;
   static constexpr bool k16 = EPI == kEpiStore16 || EPI == kEpiQkvRope;
   // per-warp staging: 32 rows x 32 columns (64 B rows for 16-bit, 128 B for fp32)
   static constexpr uint32_t kStageBytes = k16 ? 2048 : 4096;
+  // epilogue warps: two per TMEM lane quarter, each on half the tile's columns;
+  // the residual reduce-add (long K, light epilogue) uses one, which halves its
+  // staging and leaves room for a 5th ring stage
+  static constexpr int kWarps = EPI == kEpiResid32 ? 4 : 8;
+  static constexpr int kThreads = 64 + 32 * kWarps;
 };
 
 template <int BN, int EPI>
@@ -37,8 +42,8 @@ struct GemmCfg {
   static constexpr uint32_t kABytes = kGemmBM * kGemmBK * 2;
   static constexpr uint32_t kBBytes = BN * kGemmBK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
-  static constexpr uint32_t kEpiBytes = kEpiWarps * EpiTraits<EPI>::kStageBytes;
-  static constexpr size_t kFixed = 1024 + kEpiBytes + 256 + sizeof(GemmGroup) * kGemmMaxGroups;
+  static constexpr uint32_t kEpiBytes = EpiTraits<EPI>::kWarps * EpiTraits<EPI>::kStageBytes;
+  static constexpr size_t kFixed = 1024 + kEpiBytes + 256;
   static constexpr int kStagesRaw = (int)((232448 - kFixed) / kStageBytes);
   static constexpr int kStages = kStagesRaw > 6 ? 6 : kStagesRaw;
   static constexpr uint32_t kTmemCols = (2 * BN <= 256) ? 256 : 512;
@@ -218,7 +223,7 @@ __device__ __forceinline__ void stage_row(uint8_t* stg, int r, const float (&v)[
 }
 
 template <int BN, int EPI, typename T>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(EpiTraits<EPI>::kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                 const __grid_constant__ CUtensorMap map_o, const __grid_constant__ GemmParams p) {
   using Cfg = GemmCfg<BN, EPI>;
@@ -237,15 +242,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  GemmGroup* groups = reinterpret_cast<GemmGroup*>(sEpi + Cfg::kEpiBytes + 256);
+  const GemmGroup* groups = p.groups;  // read from the kernel's parameter space
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  {
-    const int words = p.num_groups * (int)(sizeof(GemmGroup) / 4);
-    const int* src = reinterpret_cast<const int*>(p.groups);
-    int* dst = reinterpret_cast<int*>(groups);
-    for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
-  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
@@ -253,7 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], kEpiWarps);
+      mbar_init(&tempty[b], Epi::kWarps);
     }
     *abort_flag = 0;
     mbar_fence_init();
@@ -359,8 +358,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&tfull[abuf], aph, kErrTimeoutTmemFull, abort_flag)) break;
       tc_fence_after();
       const int row = tm * kGemmBM + row_in_tile;
-      const int c_begin = half * (BN / 2);
-      const int c_end = min(c_begin + BN / 2, n_eff);
+      constexpr int kSplit = Epi::kWarps / 4;  // warps per TMEM lane quarter
+      const int c_begin = half * (BN / kSplit);
+      const int c_end = min(c_begin + BN / kSplit, n_eff);
       for (int c0 = c_begin; c0 < c_end; c0 += 32) {
         uint32_t r[32];
         tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(abuf * BN + c0), r);
@@ -454,7 +454,7 @@ cudaError_t launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
   if (grid <= 0) return cudaSuccess;
   const GemmCost cost = gemm_cost(p, EPI, (int)sizeof(T));
   LaunchScope scope(cost.name, cost.flop, cost.bytes, stream);
-  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ma, mb, mo, p);
+  kern<<<grid, EpiTraits<EPI>::kThreads, Cfg::kSmemBytes, stream>>>(ma, mb, mo, p);
   return cudaGetLastError();
 }
 
