@@ -35,6 +35,13 @@ constexpr size_t kAttnSmem = 1024 + 2 * kTileBytes + kKvStages * 2 * kTileBytes 
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColO = 256, kColP = 384;
 constexpr float kRescaleLog2 = 8.0f;  // lazy rescale threshold (log2 units)
+// Of every 4 column pairs of an unmasked 32-column chunk, this many take their
+// exponentials from the FMA-pipe polynomial (poly_exp2x2) and the rest from the
+// MUFU unit, which is the busiest pipe of the softmax.
+#ifndef MSST_ATTN_POLY_PAIRS
+#define MSST_ATTN_POLY_PAIRS 1
+#endif
+constexpr int kPolyPairsPerQuad = MSST_ATTN_POLY_PAIRS;
 
 struct PairGeom {
   int head;
@@ -121,9 +128,15 @@ __device__ __forceinline__ void process_chunk(const uint32_t (&r)[32], int ch, b
           a0 = fmaxf(a0, a.x);
           a1 = fmaxf(a1, a.y);
         }
-        const float e0 = fast_exp2(a.x), e1 = fast_exp2(a.y);
-        sum2 = __fadd2_rn(sum2, make_float2(e0, e1));
-        pk[i] = pack2<T>(e0, e1);
+        float2 e;
+        if ((i & 3) < kPolyPairsPerQuad) {
+          e = poly_exp2x2(a);
+        } else {
+          e.x = fast_exp2(a.x);
+          e.y = fast_exp2(a.y);
+        }
+        sum2 = __fadd2_rn(sum2, e);
+        pk[i] = pack2<T>(e.x, e.y);
       }
       if constexpr (kPass == 1) mx = fmaxf(mx, fmaxf(a0, a1));
     } else {

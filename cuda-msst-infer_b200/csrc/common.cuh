@@ -372,4 +372,27 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// 2^a for two lanes on the FMA and integer pipes instead of the MUFU unit, for
+// a <= 2^21.  Range reduction: adding 1.5 * 2^23 rounds a to the integer n in the
+// low mantissa bits of t, f = a - n lies in [-1/2, 1/2]; 2^f is a degree-3
+// polynomial (relative-error minimax on [-1/2, 1/2] by Remez exchange, max
+// relative error 7.5e-5, below half an fp16 ulp), and n is added to its
+// exponent field by an integer shift-add (t's bits << 23 leave n * 2^23 modulo
+// 2^32).  a is clamped at -125 so the exponent stays in the normal range;
+// results there (< 2^-124) are far below the 16-bit P they feed.
+__device__ __forceinline__ float2 poly_exp2x2(float2 a) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  a.x = fmaxf(a.x, -125.0f);
+  a.y = fmaxf(a.y, -125.0f);
+  const float2 mg = make_float2(kMagic, kMagic);
+  const float2 t = __fadd2_rn(a, mg);
+  const float2 neg_n = __ffma2_rn(t, make_float2(-1.0f, -1.0f), mg);
+  const float2 f = __fadd2_rn(a, neg_n);
+  float2 p = __ffma2_rn(make_float2(0.0551716685f, 0.0551716685f), f, make_float2(0.242611125f, 0.242611125f));
+  p = __ffma2_rn(p, f, make_float2(0.693260968f, 0.693260968f));
+  p = __ffma2_rn(p, f, make_float2(0.999928057f, 0.999928057f));
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
+}
+
 }  // namespace msst

@@ -184,6 +184,130 @@ __global__ void __launch_bounds__(384, 1) rmsnorm_gates8_kernel(RmsNormArgs a) {
   }
 }
 
+// RMSNorm + 8 gate projections for widths whose gate weights do not fit in
+// registers (dim 512): the weights sit in shared memory ([8][D] fp32) and each
+// warp normalises two rows at once, so every shared-memory weight load feeds two
+// rows' dot products (8 KB of shared-memory reads per row instead of 16).  The
+// 16 partial sums (2 rows x 8 heads) are reduced by a butterfly transpose-reduce
+// (8 + 4 + 2 + 1 exchanges, then 1 to finish), leaving lane pair 2i, 2i+1 with
+// value i = row * 8 + head.  The next pair of rows is prefetched.
+template <typename T, int V>
+__global__ void __launch_bounds__(256, 2) rmsnorm_gates8x2_kernel(RmsNormArgs a) {
+  constexpr int H = 8;
+  extern __shared__ float4 s_w4[];  // [H][D/4]
+  const int lane = threadIdx.x & 31;
+  const int D = a.D;
+  for (int i = threadIdx.x; i < H * D / 4; i += blockDim.x) s_w4[i] = __ldg(reinterpret_cast<const float4*>(a.wg) + i);
+  __syncthreads();
+  const float bgl = __ldg(a.bg + ((lane >> 1) & 7));
+  const long long warps_total = (long long)gridDim.x * (blockDim.x >> 5);
+  const long long pairs = (a.rows + 1) / 2;
+  long long p = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  float4 nxt[2][V];
+  auto load_pair = [&](long long pp, float4 (&dst)[2][V]) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const long long r = 2 * pp + j;
+#pragma unroll
+      for (int k = 0; k < V; ++k)
+        dst[j][k] = r < a.rows ? reinterpret_cast<const float4*>(a.x + r * D)[lane + 32 * k] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  if (p < pairs) load_pair(p, nxt);
+  for (; p < pairs; p += warps_total) {
+    float4 v[2][V];
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int k = 0; k < V; ++k) v[j][k] = nxt[j][k];
+    if (p + warps_total < pairs) load_pair(p + warps_total, nxt);
+    float inv[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      float ss = 0.f;
+#pragma unroll
+      for (int k = 0; k < V; ++k) ss += v[j][k].x * v[j][k].x + v[j][k].y * v[j][k].y + v[j][k].z * v[j][k].z + v[j][k].w * v[j][k].w;
+      inv[j] = warp_sum(ss);
+    }
+    if (a.gamma_pre != nullptr) {
+      const float4* g4 = reinterpret_cast<const float4*>(a.gamma_pre);
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const long long r = 2 * p + j;
+        const float s0 = rsqrtf(inv[j] + 1e-12f) * a.scale_pre;
+        float ss = 0.f;
+#pragma unroll
+        for (int k = 0; k < V; ++k) {
+          const float4 g = __ldg(g4 + lane + 32 * k);
+          v[j][k].x *= s0 * g.x;
+          v[j][k].y *= s0 * g.y;
+          v[j][k].z *= s0 * g.z;
+          v[j][k].w *= s0 * g.w;
+          if (r < a.rows) reinterpret_cast<float4*>(a.x + r * D)[lane + 32 * k] = v[j][k];
+          ss += v[j][k].x * v[j][k].x + v[j][k].y * v[j][k].y + v[j][k].z * v[j][k].z + v[j][k].w * v[j][k].w;
+        }
+        inv[j] = warp_sum(ss);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) inv[j] = rsqrtf(inv[j] + 1e-12f) * a.scale;
+    const float4* g4 = reinterpret_cast<const float4*>(a.gamma);
+    float part[2 * H];
+#pragma unroll
+    for (int i = 0; i < 2 * H; ++i) part[i] = 0.f;
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      const float4 g = __ldg(g4 + lane + 32 * k);
+      float4 y[2];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        y[j] = make_float4(v[j][k].x * inv[j] * g.x, v[j][k].y * inv[j] * g.y, v[j][k].z * inv[j] * g.z,
+                           v[j][k].w * inv[j] * g.w);
+        const long long r = 2 * p + j;
+        if (r < a.rows)
+          reinterpret_cast<uint2*>(reinterpret_cast<T*>(a.out16) + r * D)[lane + 32 * k] =
+              make_uint2(pack2<T>(y[j].x, y[j].y), pack2<T>(y[j].z, y[j].w));
+      }
+#pragma unroll
+      for (int h = 0; h < H; ++h) {
+        const float4 w = s_w4[h * (D / 4) + lane + 32 * k];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) part[j * H + h] += y[j].x * w.x + y[j].y * w.y + y[j].z * w.z + y[j].w * w.w;
+      }
+    }
+    // butterfly over 16 values: lane bit 4 picks the upper/lower 8, bit 3 the
+    // upper/lower 4 of those, and so on down to bit 1; bit 0 finishes the sum
+    float q8[8];
+    {
+      const bool b = lane & 16;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        q8[i] = (b ? part[8 + i] : part[i]) + __shfl_xor_sync(0xffffffffu, b ? part[i] : part[8 + i], 16);
+    }
+    float q4[4];
+    {
+      const bool b = lane & 8;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        q4[i] = (b ? q8[4 + i] : q8[i]) + __shfl_xor_sync(0xffffffffu, b ? q8[i] : q8[4 + i], 8);
+    }
+    float q2[2];
+    {
+      const bool b = lane & 4;
+#pragma unroll
+      for (int i = 0; i < 2; ++i)
+        q2[i] = (b ? q4[2 + i] : q4[i]) + __shfl_xor_sync(0xffffffffu, b ? q4[i] : q4[2 + i], 4);
+    }
+    const bool b1 = lane & 2;
+    float d = (b1 ? q2[1] : q2[0]) + __shfl_xor_sync(0xffffffffu, b1 ? q2[0] : q2[1], 2);
+    d += __shfl_xor_sync(0xffffffffu, d, 1);
+    // value index i = 8*b4 + 4*b3 + 2*b2 + b1 = lane >> 1: row i >> 3, head i & 7
+    const long long r = 2 * p + (lane >> 4);
+    if ((lane & 1) == 0 && r < a.rows)
+      a.gates[r * H + ((lane >> 1) & 7)] = __fdividef(1.0f, 1.0f + __expf(-(d + bgl)));
+  }
+}
+
 template <typename T>
 cudaError_t rmsnorm_dispatch(const RmsNormArgs& a, cudaStream_t s) {
   const int V = a.D / 128;
@@ -208,8 +332,15 @@ cudaError_t rmsnorm_dispatch(const RmsNormArgs& a, cudaStream_t s) {
     }
     return cudaGetLastError();
   }
+  if (a.wg != nullptr && a.heads == 8 && a.gamma != nullptr && !a.band_major && V == 4) {
+    // two persistent blocks of 8 warps per SM, each warp two rows at a time
+    long long gb = ((a.rows + 1) / 2 + 7) / 8;
+    if (gb > 2 * 148) gb = 2 * 148;
+    rmsnorm_gates8x2_kernel<T, 4><<<(unsigned)gb, 256, smem, s>>>(a);
+    return cudaGetLastError();
+  }
   switch (V) {
-#define MSST_RMS_CASE(v)                                                                                \
+#define MSST_RMS_CASE(v)                                                                               \
   case v:                                                                                               \
     if (smem > 48 * 1024)                                                                               \
       cudaFuncSetAttribute(rmsnorm_kernel<T, v>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \

@@ -28,7 +28,7 @@ def oracle_mod():
 
 
 @pytest.mark.parametrize("prec", ["fp16", "bf16"])
-@pytest.mark.parametrize("rows,D", [(1000, 384), (20000, 384), (333, 512), (8, 128), (1, 256)])
+@pytest.mark.parametrize("rows,D", [(1000, 384), (20000, 384), (333, 512), (20001, 512), (1, 512), (8, 128), (1, 256)])
 def test_rmsnorm_and_gates(cuda, prec, rows, D):
     torch = cuda
     from msst_b200 import ops
