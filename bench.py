@@ -250,12 +250,13 @@ def main():
     ap.add_argument("--seconds", type=float, default=TRACK_SECONDS,
                     help="track length per rank (smaller values make a profiling case)")
     ap.add_argument("--chunk-batch", type=int, default=CHUNK_BATCH, help="chunks per forward")
-    ap.add_argument("--micro", choices=["attention"], default=None,
-                    help="BASELINE config 3 instead of the separation bench (1 GPU)")
+    ap.add_argument("--micro", choices=["attention", "gemm"], default=None,
+                    help="attention: BASELINE config 3; gemm: the transformer GEMMs at config 1's "
+                         "forward-batch shape (instead of the separation bench, 1 GPU)")
     args = ap.parse_args()
-    if args.micro == "attention":
+    if args.micro is not None:
         if int(os.environ.get("RANK", "0")) == 0:
-            emit(out, run_micro_attention(args))
+            emit(out, run_micro_attention(args) if args.micro == "attention" else run_micro_gemm(args))
         return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -440,6 +441,67 @@ def run_micro_attention(args):
            "frac_of_burst_peak": {k: v["tflops"] / burst for k, v in res.items()}}
     out["reference_sdpa"] = reference_sdpa(res)
     return out
+
+
+def run_micro_gemm(args):
+    """The transformer's four GEMMs alone at BASELINE config 1's forward-batch shape
+    (MBR dim 384, 4 chunks x 801 frames x 60 bands = 192240 rows, fp16): QKV + RoPE,
+    FFN1 + GELU, attention out-projection and FFN2 with the residual reduce-add.
+    Device time per launch with CUDA events; operands (>= 150 MB each) exceed L2."""
+    import torch
+    from msst_b200 import ops
+
+    torch.cuda.set_device(0)
+    B, T, F, D, H = 4, 801, 60, 384, 8
+    M = B * T * F
+    dt = torch.float16
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(M, D, device="cuda", generator=g).to(dt)
+    h = torch.randn(M, 4 * D, device="cuda", generator=g).to(dt)
+    ao = torch.randn(M, H * 64, device="cuda", generator=g).to(dt)
+    wqkv = (0.02 * torch.randn(3 * H * 64, D, device="cuda", generator=g)).to(dt)
+    w1 = (0.02 * torch.randn(4 * D, D, device="cuda", generator=g)).to(dt)
+    b1 = 0.02 * torch.randn(4 * D, device="cuda", generator=g)
+    wo = (0.02 * torch.randn(D, H * 64, device="cuda", generator=g)).to(dt)
+    w2 = (0.02 * torch.randn(D, 4 * D, device="cuda", generator=g)).to(dt)
+    b2 = 0.02 * torch.randn(D, device="cuda", generator=g)
+    resid = torch.zeros(M, D, device="cuda")
+    inv = 10000.0 ** (-np.arange(0, 64, 2, dtype=np.float64) / 64)
+    ang = np.arange(T, dtype=np.float64)[:, None] * inv[None, :]
+    cos = torch.from_numpy(np.cos(ang).astype(np.float32)).cuda()
+    sin = torch.from_numpy(np.sin(ang).astype(np.float32)).cuda()
+    qkv_out = torch.empty(M, 3 * H * 64, device="cuda", dtype=dt)
+    cases = {
+        "qkv_rope": (lambda: ops.gemm_qkv_rope(x, wqkv, H, cos, sin, F, T, out=qkv_out), D, 3 * H * 64),
+        "ffn1_gelu": (lambda: ops.gemm(x, w1, b1, "store16", "gelu", out=h), D, 4 * D),
+        "out_proj_resid": (lambda: ops.gemm(ao, wo, None, "resid32", out=resid), H * 64, D),
+        "ffn2_resid": (lambda: ops.gemm(h, w2, b2, "resid32", out=resid), 4 * D, D),
+    }
+    res = {}
+    for name, (fn, K, N) in cases.items():
+        for _ in range(max(3, args.warmup)):
+            fn()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        s.record()
+        iters = max(5, args.steps)
+        for _ in range(iters):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(e) / iters
+        flop = 2.0 * M * N * K
+        res[name] = {"M": M, "K": K, "N": N, "ms": ms, "tflops": flop / (ms * 1e-3) / 1e12}
+    burst, sustained, hbm, src = peaks()
+    tot_flop = sum(2.0 * M * r["N"] * r["K"] for r in res.values())
+    tot_ms = sum(r["ms"] for r in res.values())
+    return {"metric": "transformer GEMM TFLOP/s (BASELINE config 1 forward-batch shapes)",
+            "value": tot_flop / (tot_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "higher_is_better": True,
+            "n_gpus": 1, "dtype": "fp16", "data": "synthetic",
+            "config": {"workload": "QKV+RoPE, FFN1+GELU, out-proj+residual, FFN2+residual; M=192240, D=384",
+                       "l2": "operands larger than L2"},
+            "ours": res, "peak_tflops": burst, "peak_source": src,
+            "frac_of_burst_peak": {k: v["tflops"] / burst for k, v in res.items()}}
 
 
 def reference_sdpa(res):

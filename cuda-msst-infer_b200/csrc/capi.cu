@@ -164,7 +164,7 @@ int msst_gemm(const void* x, long long rows, int K, long long ldx, const void* w
     use_device_of(x);
     const int bn = pick_bn(N);
     const CUtensorMap ma = msst::map_2d(x, (uint64_t)rows, (uint64_t)K, (uint64_t)ldx, msst::kGemmBM);
-    const CUtensorMap mb = msst::map_2d(w, (uint64_t)N, (uint64_t)K, (uint64_t)K, (uint32_t)bn);
+    const CUtensorMap mb = msst::map_gemm_b(w, (uint64_t)N, (uint64_t)K, (uint64_t)K, bn);
     const CUtensorMap mo = epilogue == MSST_EPI_GLU32
                                ? ma
                                : msst::map_out_2d(out, out32, (uint64_t)rows, (uint64_t)N, (uint64_t)ldo);
@@ -196,7 +196,7 @@ int msst_gemm_qkv_rope(const void* x, long long rows, int K, const void* w, int 
     const int N = 3 * heads * 64;
     const int bn = pick_bn(N);
     const CUtensorMap ma = msst::map_2d(x, (uint64_t)rows, (uint64_t)K, (uint64_t)K, msst::kGemmBM);
-    const CUtensorMap mb = msst::map_2d(w, (uint64_t)N, (uint64_t)K, (uint64_t)K, (uint32_t)bn);
+    const CUtensorMap mb = msst::map_gemm_b(w, (uint64_t)N, (uint64_t)K, (uint64_t)K, bn);
     msst::GemmParams p{};
     p.num_groups = 1;
     p.pos_div = pos_div;
@@ -332,7 +332,7 @@ int msst_grouped_gemm(int num_groups, const msst_gemm_group* groups, const void*
     }
     const int bn = pick_bn(nmax);
     const CUtensorMap ma = msst::map_2d(x, (uint64_t)x_rows, (uint64_t)ldx, (uint64_t)ldx, msst::kGemmBM);
-    const CUtensorMap mb = msst::map_2d(w, (uint64_t)w_rows, (uint64_t)ldw, (uint64_t)ldw, (uint32_t)bn);
+    const CUtensorMap mb = msst::map_gemm_b(w, (uint64_t)w_rows, (uint64_t)ldw, (uint64_t)ldw, bn);
     const CUtensorMap mo =
         tma_out ? msst::map_out_2d(out, out32, (uint64_t)out_rows, (uint64_t)ldo, (uint64_t)ldo) : ma;
     run_gemm(ma, mb, mo, p, epilogue, bn, dtype, as_stream(stream));

@@ -174,6 +174,8 @@ __device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const 
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // The shared-memory sources of all committed bulk groups have been read.
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// All but the most recent committed bulk group have been read.
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 // All committed bulk groups have completed (writes performed).
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
@@ -200,15 +202,17 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_byte
 }
 
 // Instruction descriptor, kind::f16: fp32 accumulate, A/B fp16 (0) or bf16 (1),
-// dense, M = 128.  b_mn_major = 1 when B's N dimension is contiguous.
-__host__ __device__ constexpr uint32_t umma_idesc_f16(uint32_t ab_bf16, uint32_t n, uint32_t b_mn_major = 0) {
+// dense, M = 128 (256 for a CTA-pair MMA).  b_mn_major = 1 when B's N dimension
+// is contiguous.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(uint32_t ab_bf16, uint32_t n, uint32_t b_mn_major = 0,
+                                                      uint32_t m = 128) {
   return (1u << 4)                 // D format f32
          | (ab_bf16 << 7)          // A format
          | (ab_bf16 << 10)         // B format
          | (0u << 15)              // A K-major
          | (b_mn_major << 16)      // B major
          | ((n >> 3) << 17)        // N >> 3
-         | ((128u >> 4) << 24);    // M >> 4
+         | ((m >> 4) << 24);       // M >> 4
 }
 
 __device__ __forceinline__ void umma_f16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
@@ -241,6 +245,76 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// ---------------------------------------------------------------- CTA pairs
+// A cluster of two CTAs on neighbouring SMs runs one M = 256 MMA as a pair
+// (tcgen05 cta_group::2): rank 0 issues the MMAs, each CTA supplies half of the A
+// rows and half of the B rows from its own shared memory (same offsets in both)
+// and receives its 128 accumulator rows in its own TMEM.
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t d;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(addr), "r"(rank));
+  return d;
+}
+
+// All threads of both CTAs: barrier across the cluster (release/acquire).
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Arrive on an mbarrier given by its cluster address (possibly the peer CTA's).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// TMA load into this CTA's shared memory whose completion is counted on the
+// pair leader's mbarrier (bar = its cluster address).  No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_f16_ss_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Completion of the pair's MMAs issued so far, signalled on the mbarrier at the
+// same offset in every CTA of cta_mask.
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(cta_mask)
+      : "memory");
+}
+
+// Pair TMEM allocation: one warp of each CTA (same warp index, same dst offset).
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
 
 // Warp-wide TMEM allocation; the base address is written to *dst (shared memory).
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {

@@ -17,6 +17,9 @@
 // Tiles of all groups are walked in one static persistent schedule; the group
 // table is read from the kernel's parameter space, so shared memory holds only
 // the ring (4 stages at BN 256, 5 at BN 192 with the residual epilogue) and staging.
+// Large launches run the CTA-pair variant (gemm_pair_kernel, below).
+#include <cstdlib>
+
 #include "common.cuh"
 #include "gemm.cuh"
 
@@ -35,6 +38,11 @@ struct EpiTraits {
   // staging and leaves room for a 5th ring stage
   static constexpr int kWarps = EPI == kEpiResid32 ? 4 : 8;
   static constexpr int kThreads = 64 + 32 * kWarps;
+  // staging buffers per warp (a second one, letting a chunk be staged while the
+  // previous chunk's bulk store still reads its buffer, measured no faster: the
+  // stores are bound by the output's DRAM writes, not by the wait)
+  static constexpr int kStgBufs = 1;
+  static constexpr uint32_t kWarpStgBytes = kStageBytes * kStgBufs;
 };
 
 template <int BN, int EPI>
@@ -42,7 +50,7 @@ struct GemmCfg {
   static constexpr uint32_t kABytes = kGemmBM * kGemmBK * 2;
   static constexpr uint32_t kBBytes = BN * kGemmBK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
-  static constexpr uint32_t kEpiBytes = EpiTraits<EPI>::kWarps * EpiTraits<EPI>::kStageBytes;
+  static constexpr uint32_t kEpiBytes = EpiTraits<EPI>::kWarps * EpiTraits<EPI>::kWarpStgBytes;
   static constexpr size_t kFixed = 1024 + kEpiBytes + 256;
   static constexpr int kStagesRaw = (int)((232448 - kFixed) / kStageBytes);
   static constexpr int kStages = kStagesRaw > 6 ? 6 : kStagesRaw;
@@ -106,12 +114,39 @@ __device__ __forceinline__ float2 sigmoid2(float2 x) {
   return make_float2(rcp_approx(d.x), rcp_approx(d.y));
 }
 
+// RoPE table entries of one chunk (cos[4] then sin[4]), fetched before the
+// accumulator wait / TMEM load so the global loads overlap them.  (Fetching the
+// bias the same way measured slower for the GELU epilogue, which needs the
+// registers; the bias is read at use.)
+struct ChunkOps {
+  float4 a[8];
+};
+
+template <int EPI>
+__device__ __forceinline__ void chunk_prefetch(const GemmParams& p, const GemmGroup& g, int row, int col,
+                                               ChunkOps& o) {
+  if constexpr (EPI == kEpiQkvRope) {
+    if (col < p.rope_cols) {
+      const int half = p.head_dim >> 1;
+      const int pos = (row / p.pos_div) % p.pos_mod;
+      const int i0 = (col % p.head_dim) >> 1;
+      const float4* cs = reinterpret_cast<const float4*>(p.rope_cos + (size_t)pos * half + i0);
+      const float4* sn = reinterpret_cast<const float4*>(p.rope_sin + (size_t)pos * half + i0);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        o.a[u] = __ldg(cs + u);
+        o.a[4 + u] = __ldg(sn + u);
+      }
+    }
+  }
+}
+
 // bias, activation and RoPE on one 32-column chunk of one row (fp32 registers)
 template <int EPI>
-__device__ __forceinline__ void chunk_math(const GemmParams& p, const GemmGroup& g, int row, int col, float (&v)[32]) {
-  const int nvalid = min(32, g.n - col);
-  if (g.bias != nullptr) {
-    if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(g.bias + col) & 15) == 0)) {
+__device__ __forceinline__ void chunk_math(const GemmParams& p, const GemmGroup& g, int row, int col, float (&v)[32],
+                                           const ChunkOps& o) {
+  if constexpr (EPI != kEpiQkvRope) {
+    if (g.bias != nullptr && g.n - col >= 32 && ((reinterpret_cast<uintptr_t>(g.bias + col) & 15) == 0)) {
       const float4* b4 = reinterpret_cast<const float4*>(g.bias + col);
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
@@ -123,7 +158,8 @@ __device__ __forceinline__ void chunk_math(const GemmParams& p, const GemmGroup&
         v[4 * q + 2] = hi.x;
         v[4 * q + 3] = hi.y;
       }
-    } else {
+    } else if (g.bias != nullptr) {
+      const int nvalid = min(32, g.n - col);
 #pragma unroll
       for (int j = 0; j < 32; ++j)
         if (j < nvalid) v[j] += __ldg(g.bias + col + j);
@@ -154,21 +190,16 @@ __device__ __forceinline__ void chunk_math(const GemmParams& p, const GemmGroup&
     }
   } else if constexpr (EPI == kEpiQkvRope) {
     if (col < p.rope_cols) {
-      const int half = p.head_dim >> 1;
-      const int pos = (row / p.pos_div) % p.pos_mod;
-      const int i0 = (col % p.head_dim) >> 1;
-      const float4* cs = reinterpret_cast<const float4*>(p.rope_cos + (size_t)pos * half + i0);
-      const float4* sn = reinterpret_cast<const float4*>(p.rope_sin + (size_t)pos * half + i0);
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const float4 c4 = __ldg(cs + u), s4 = __ldg(sn + u);
-        const float c[4] = {c4.x, c4.y, c4.z, c4.w}, s[4] = {s4.x, s4.y, s4.z, s4.w};
+        const float4 c4 = o.a[u], s4 = o.a[4 + u];
+        const float c[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const int j = 4 * u + k;
           const float x0 = v[2 * j], x1 = v[2 * j + 1];
-          v[2 * j] = x0 * c[k] - x1 * s[k];
-          v[2 * j + 1] = x0 * s[k] + x1 * c[k];
+          v[2 * j] = x0 * c[k] - x1 * sn[k];
+          v[2 * j + 1] = x0 * sn[k] + x1 * c[k];
         }
       }
     }
@@ -220,6 +251,69 @@ __device__ __forceinline__ void stage_row(uint8_t* stg, int r, const float (&v)[
       *reinterpret_cast<float4*>(rowp + ((c ^ (r & 7)) << 4)) =
           make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
   }
+}
+
+// Epilogue of one accumulator tile by epilogue warp `warp` (absolute index >= 2):
+// the warp owns TMEM lane quarter warp % 4 (rows row_base + 32 * (warp % 4) + lane
+// of the group) and, with 8 epilogue warps, one half of the tile's columns,
+// 32 at a time.  acc = TMEM address of the tile's column 0.  wait_acc() waits for
+// the accumulator (false: gave up); the first chunk's operands (bias, RoPE
+// tables) are fetched before it.
+template <int BN, int EPI, typename T, typename WaitAcc>
+__device__ __forceinline__ bool epilogue_tile(const GemmParams& p, const GemmGroup& g, const CUtensorMap* map_o,
+                                              uint32_t acc, int row_base, int tn, int warp, int lane, uint8_t* stg,
+                                              WaitAcc&& wait_acc) {
+  using Epi = EpiTraits<EPI>;
+  const int q = warp & 3;
+  const int half = (warp - 2) >> 2;
+  const int row = row_base + q * 32 + lane;
+  const int n_eff = min(BN, g.n - tn * BN);
+  constexpr int kSplit = Epi::kWarps / 4;  // warps per TMEM lane quarter
+  const int c_begin = half * (BN / kSplit);
+  const int c_end = min(c_begin + BN / kSplit, n_eff);
+  ChunkOps ops;
+  if (c_begin < c_end) chunk_prefetch<EPI>(p, g, row, tn * BN + c_begin, ops);
+  if (!wait_acc()) return false;
+  tc_fence_after();
+  int i = 0;
+  for (int c0 = c_begin; c0 < c_end; c0 += 32, ++i) {
+    const int col = tn * BN + c0;
+    if (c0 != c_begin) chunk_prefetch<EPI>(p, g, row, col, ops);
+    uint32_t r[32];
+    tmem_ld32(acc + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, r);
+    tmem_ld_wait();
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+    chunk_math<EPI>(p, g, row, col, v, ops);
+    if constexpr (Epi::kTma) {
+      uint8_t* buf = stg + (Epi::kStgBufs == 2 ? (i & 1) : 0) * Epi::kStageBytes;
+      if (lane == 0) {
+        if constexpr (Epi::kStgBufs == 2)
+          bulk_wait_read1();
+        else
+          bulk_wait_read0();
+      }
+      __syncwarp();
+      stage_row<T, Epi::k16>(buf, lane, v);
+      fence_proxy_async_smem();
+      __syncwarp();
+      // boxes starting past the group's last row stay unwritten (they would hold
+      // products of the next group's A rows)
+      const int row0 = row_base + q * 32;
+      if (lane == 0 && row0 < g.m) {
+        const int x = g.out_col0 + col, y = g.oy0 + g.oy_row * row0, z = g.oz0 + g.oz_row * row0;
+        if constexpr (EPI == kEpiResid32)
+          tma_reduce_add_3d(map_o, buf, x, y, z);
+        else
+          tma_store_3d(map_o, buf, x, y, z);
+      }
+      if (lane == 0) bulk_commit();
+    } else {
+      if (row < g.m) glu_store(g, row, col, v);
+    }
+  }
+  return true;
 }
 
 template <int BN, int EPI, typename T>
@@ -289,7 +383,10 @@ __global__ void __launch_bounds__(EpiTraits<EPI>::kThreads, 1)
           mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
           tma_load_2d(sA + stage * Cfg::kABytes, &map_a, &full[stage], g.a_col0 + kb * kGemmBK,
                       g.a_row0 + tm * kGemmBM);
+          // B in two boxes of BN/2 rows (the tensor map's box is shared with the pair kernel)
           tma_load_2d(sB + stage * Cfg::kBBytes, &map_b, &full[stage], g.b_col0 + kb * kGemmBK, g.b_row0 + tn * BN);
+          tma_load_2d(sB + stage * Cfg::kBBytes + Cfg::kBBytes / 2, &map_b, &full[stage], g.b_col0 + kb * kGemmBK,
+                      g.b_row0 + tn * BN + BN / 2);
           if (++stage == kStages) {
             stage = 0;
             ph ^= 1u;
@@ -343,54 +440,16 @@ __global__ void __launch_bounds__(EpiTraits<EPI>::kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue (8 warps)
-    const int ew = warp - 2;
-    const int q = warp & 3;
-    const int half = ew >> 2;
-    const int row_in_tile = q * 32 + lane;
-    uint8_t* stg = sEpi + ew * Epi::kStageBytes;
+    uint8_t* stg = sEpi + (warp - 2) * Epi::kWarpStgBytes;
     int abuf = 0;
     uint32_t aph = 0;
     for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
       const GemmGroup& g = groups[find_group(groups, p.num_groups, t)];
       const int lt = t - g.tile_begin;
       const int tm = lt / g.tiles_n, tn = lt - tm * g.tiles_n;
-      const int n_eff = min(BN, g.n - tn * BN);
-      if (!mbar_wait(&tfull[abuf], aph, kErrTimeoutTmemFull, abort_flag)) break;
-      tc_fence_after();
-      const int row = tm * kGemmBM + row_in_tile;
-      constexpr int kSplit = Epi::kWarps / 4;  // warps per TMEM lane quarter
-      const int c_begin = half * (BN / kSplit);
-      const int c_end = min(c_begin + BN / kSplit, n_eff);
-      for (int c0 = c_begin; c0 < c_end; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(abuf * BN + c0), r);
-        tmem_ld_wait();
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-        const int col = tn * BN + c0;
-        chunk_math<EPI>(p, g, row, col, v);
-        if constexpr (Epi::kTma) {
-          if (lane == 0) bulk_wait_read0();
-          __syncwarp();
-          stage_row<T, Epi::k16>(stg, lane, v);
-          fence_proxy_async_smem();
-          __syncwarp();
-          // boxes starting past the group's last row stay unwritten (they would hold
-          // products of the next group's A rows)
-          const int row0 = tm * kGemmBM + q * 32;
-          if (lane == 0 && row0 < g.m) {
-            const int x = g.out_col0 + col, y = g.oy0 + g.oy_row * row0, z = g.oz0 + g.oz_row * row0;
-            if constexpr (EPI == kEpiResid32)
-              tma_reduce_add_3d(&map_o, stg, x, y, z);
-            else
-              tma_store_3d(&map_o, stg, x, y, z);
-            bulk_commit();
-          }
-        } else {
-          if (row < g.m) glu_store(g, row, col, v);
-        }
-      }
+      if (!epilogue_tile<BN, EPI, T>(p, g, &map_o, tmem_base + (uint32_t)(abuf * BN), tm * kGemmBM, tn, warp, lane,
+                                     stg, [&] { return mbar_wait(&tfull[abuf], aph, kErrTimeoutTmemFull, abort_flag); }))
+        break;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[abuf]);
@@ -407,6 +466,189 @@ __global__ void __launch_bounds__(EpiTraits<EPI>::kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// CTA-pair variant: a cluster of two CTAs computes 256 x BN output tiles with
+// M = 256 tcgen05 MMAs (cta_group::2) issued by rank 0.  Each CTA streams its own
+// 128 A rows and BN/2 B rows per k-block, so a CTA moves (128 + BN/2) x 64
+// operand elements per k-block for a 128 x BN slice of the product instead of
+// (128 + BN) x 64 -- a third less shared-memory traffic per FLOP at BN = 256,
+// and a 32 KB stage instead of 48 KB, so more k-blocks are in flight.
+//   full[s]   (rank 0 only) one arrival (rank 0's expect_tx of both CTAs' bytes);
+//             both CTAs' TMA loads complete on it
+//   empty[s]  (each CTA) the pair MMA's commit, multicast to both CTAs
+//   tfull[b]  (each CTA) accumulator b ready, multicast commit
+//   tempty[b] (rank 0 only) both CTAs' epilogue warps arrive (2 x kWarps)
+// Every role falls through to the final cluster barrier, including after a
+// bounded wait gave up, so neither CTA leaves while the other may still touch
+// its shared memory; then both free the pair's TMEM.
+template <int BN, int EPI>
+struct PairCfg {
+  static constexpr uint32_t kABytes = kGemmBM * kGemmBK * 2;
+  static constexpr uint32_t kBBytes = (BN / 2) * kGemmBK * 2;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kEpiBytes = EpiTraits<EPI>::kWarps * EpiTraits<EPI>::kWarpStgBytes;
+  static constexpr size_t kFixed = 1024 + kEpiBytes + 256;
+  static constexpr int kStagesRaw = (int)((232448 - kFixed) / kStageBytes);
+  static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
+  static constexpr uint32_t kTmemCols = (2 * BN <= 256) ? 256 : 512;
+  static constexpr size_t kSmemBytes = kFixed + (size_t)kStages * kStageBytes;
+  static_assert(kStages >= 2, "not enough shared memory for a 2-stage ring");
+};
+
+template <int BN, int EPI, typename T>
+__global__ void __launch_bounds__(EpiTraits<EPI>::kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                     const __grid_constant__ CUtensorMap map_o, const __grid_constant__ GemmParams p) {
+  using Cfg = PairCfg<BN, EPI>;
+  using Epi = EpiTraits<EPI>;
+  constexpr int kStages = Cfg::kStages;
+  constexpr uint32_t kIsBf16 = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+  constexpr int kPairM = 2 * kGemmBM;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kStages * Cfg::kABytes;
+  uint8_t* sEpi = sB + kStages * Cfg::kBBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + Cfg::kEpiBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* tfull = empty + kStages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const GemmGroup* groups = p.groups;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = (int)(blockIdx.x >> 1), num_pairs = (int)(gridDim.x >> 1);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 2 * Epi::kWarps);
+    }
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b);
+    if constexpr (Epi::kTma) tma_prefetch_desc(&map_o);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, Cfg::kTmemCols);
+    tc_fence_before();
+  }
+  // barriers initialised in both CTAs before either signals the other's
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int t = pair; ok && t < p.total_tiles; t += num_pairs) {
+        const GemmGroup& g = groups[find_group(groups, p.num_groups, t)];
+        const int lt = t - g.tile_begin;
+        const int tm = lt / g.tiles_n, tn = lt - tm * g.tiles_n;
+        const int kblocks = g.k / kGemmBK;
+        const int a_row = g.a_row0 + tm * kPairM + (int)rank * kGemmBM;
+        const int b_row = g.b_row0 + tn * BN + (int)rank * (BN / 2);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&empty[stage], ph ^ 1u, kErrTimeoutSmemEmpty, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::kStageBytes);
+          tma_load_2d_pair(sA + stage * Cfg::kABytes, &map_a, bar, g.a_col0 + kb * kGemmBK, a_row);
+          tma_load_2d_pair(sB + stage * Cfg::kBBytes, &map_b, bar, g.b_col0 + kb * kGemmBK, b_row);
+          if (++stage == kStages) {
+            stage = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (rank 0)
+    if (lane == 0 && rank == 0) {
+      int stage = 0;
+      uint32_t ph = 0;
+      int abuf = 0;
+      uint32_t aph = 0;
+      bool ok = true;
+      const uint32_t idesc = umma_idesc_f16(kIsBf16, (uint32_t)BN, 0, (uint32_t)kPairM);
+      for (int t = pair; ok && t < p.total_tiles; t += num_pairs) {
+        const GemmGroup& g = groups[find_group(groups, p.num_groups, t)];
+        const int kblocks = g.k / kGemmBK;
+        if (!mbar_wait(&tempty[abuf], aph ^ 1u, kErrTimeoutTmemEmpty, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(abuf * BN);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&full[stage], ph, kErrTimeoutTmaFull, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * Cfg::kABytes);
+          const uint32_t b0 = smem_u32(sB + stage * Cfg::kBBytes);
+#pragma unroll
+          for (int kk = 0; kk < kGemmBK / 16; ++kk) {
+            umma_f16_ss_pair(d_tmem, sw128_desc(a0 + kk * 32, 16, 1024), sw128_desc(b0 + kk * 32, 16, 1024), idesc,
+                             (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair(&empty[stage], 0x3);
+          if (++stage == kStages) {
+            stage = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(&tfull[abuf], 0x3);
+        abuf ^= 1;
+        if (abuf == 0) aph ^= 1u;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    uint8_t* stg = sEpi + (warp - 2) * Epi::kWarpStgBytes;
+    int abuf = 0;
+    uint32_t aph = 0;
+    for (int t = pair; t < p.total_tiles; t += num_pairs) {
+      const GemmGroup& g = groups[find_group(groups, p.num_groups, t)];
+      const int lt = t - g.tile_begin;
+      const int tm = lt / g.tiles_n, tn = lt - tm * g.tiles_n;
+      if (!epilogue_tile<BN, EPI, T>(p, g, &map_o, tmem_base + (uint32_t)(abuf * BN), tm * kPairM + (int)rank * kGemmBM,
+                                     tn, warp, lane, stg,
+                                     [&] { return mbar_wait(&tfull[abuf], aph, kErrTimeoutTmemFull, abort_flag); }))
+        break;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[abuf]), 0));
+      abuf ^= 1;
+      if (abuf == 0) aph ^= 1u;
+    }
+    if constexpr (Epi::kTma) {
+      if (lane == 0) bulk_wait0();
+      __syncwarp();
+    }
+  }
+
+  __syncthreads();
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
   }
 }
 
@@ -458,9 +700,88 @@ cudaError_t launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
   return cudaGetLastError();
 }
 
+// The pair kernel as a cluster launch of 2 x (co-resident clusters) CTAs at most;
+// `pp` holds the group table re-tiled for 256-row pair tiles.
+template <int BN, int EPI, typename T>
+cudaError_t launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const GemmParams& pp,
+                        cudaStream_t stream) {
+  using Cfg = PairCfg<BN, EPI>;
+  auto kern = gemm_pair_kernel<BN, EPI, T>;
+  static int max_pairs = 0;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(EpiTraits<EPI>::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (max_pairs == 0) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    cfg.gridDim = dim3(2 * 148, 1, 1);
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+    if (e != cudaSuccess) return e;
+    if (n < 1) return cudaErrorInvalidConfiguration;
+    max_pairs = n;
+  }
+  const int pairs = pp.total_tiles < max_pairs ? pp.total_tiles : max_pairs;
+  if (pairs <= 0) return cudaSuccess;
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  const GemmCost cost = gemm_cost(pp, EPI, (int)sizeof(T));
+  LaunchScope scope(cost.name, cost.flop, cost.bytes, stream);
+  return cudaLaunchKernelEx(&cfg, kern, ma, mb, mo, pp);
+}
+
+// Pair tiles for the residual reduce-add when every group's columns are whole BN
+// tiles, K >= 512 and there are at least two pair tiles per co-resident pair.
+// Measured: the residual GEMMs gain 4-10 % (their operand stream dominates);
+// the 16-bit-output GEMMs at K = 384 are bound by their output writes and lose
+// 3-5 % to the pair coupling, so they stay on single CTAs.  MSST_GEMM_PAIR=0
+// turns pairs off, MSST_GEMM_PAIR=2 uses them for every eligible launch.
+bool use_pair(const GemmParams& p, int bn, int epi) {
+  static const int env = [] {
+    const char* e = getenv("MSST_GEMM_PAIR");
+    return e ? atoi(e) : 1;
+  }();
+  if (env == 0) return false;
+  if (env == 1 && epi != kEpiResid32) return false;
+  long long pair_tiles = 0;
+  for (int i = 0; i < p.num_groups; ++i) {
+    const GemmGroup& g = p.groups[i];
+    if (g.n % bn != 0) return false;
+    if (env == 1 && g.k < 512) return false;
+    pair_tiles += (long long)((g.m + 2 * kGemmBM - 1) / (2 * kGemmBM)) * (g.n / bn);
+  }
+  return pair_tiles >= 2 * 74;
+}
+
 template <int BN, typename T>
 cudaError_t dispatch_epi(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const GemmParams& p,
                          int epi, int num_sms, cudaStream_t s) {
+  if (use_pair(p, BN, epi)) {
+    GemmParams pp = p;
+    int tiles = 0;
+    for (int i = 0; i < pp.num_groups; ++i) {
+      GemmGroup& g = pp.groups[i];
+      g.tiles_n = g.n / BN;
+      g.tile_begin = tiles;
+      tiles += ((g.m + 2 * kGemmBM - 1) / (2 * kGemmBM)) * g.tiles_n;
+    }
+    pp.total_tiles = tiles;
+    switch (epi) {
+      case kEpiStore16: return launch_pair<BN, kEpiStore16, T>(ma, mb, mo, pp, s);
+      case kEpiResid32: return launch_pair<BN, kEpiResid32, T>(ma, mb, mo, pp, s);
+      case kEpiStore32: return launch_pair<BN, kEpiStore32, T>(ma, mb, mo, pp, s);
+      case kEpiGlu32: return launch_pair<BN, kEpiGlu32, T>(ma, mb, mo, pp, s);
+      case kEpiQkvRope: return launch_pair<BN, kEpiQkvRope, T>(ma, mb, mo, pp, s);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   switch (epi) {
     case kEpiStore16: return launch_one<BN, kEpiStore16, T>(ma, mb, mo, p, num_sms, s);
     case kEpiResid32: return launch_one<BN, kEpiResid32, T>(ma, mb, mo, p, num_sms, s);

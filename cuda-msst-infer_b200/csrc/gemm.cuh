@@ -67,7 +67,9 @@ struct GemmParams {
 };
 
 // Launches the GEMM.  `map_a` / `map_b` are 2-D tensor maps (inner dim = K) with
-// box {64, 128} for A and {64, bn} for B, 128B swizzle.  `map_out` is the 3-D
+// box {64, 128} for A and {64, bn/2} for B (map_gemm_b), 128B swizzle.  Launches
+// whose groups all have whole bn-column tiles and enough rows run as CTA pairs
+// (256-row tiles, cta_group::2 MMAs; MSST_GEMM_PAIR=0 disables them).  `map_out` is the 3-D
 // output map (box {32, 32, 1}; 64B swizzle for 16-bit outputs, 128B swizzle for
 // fp32), ignored by kEpiGlu32.  bf16 != 0 selects bf16 operands (else fp16).
 // bn in {128, 192, 256}.  Returns a cudaError_t.

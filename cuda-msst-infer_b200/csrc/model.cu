@@ -526,7 +526,7 @@ void Model::load(const std::string& path, int device, int precision) {
     w_bs_ = upload_16(W, bf16_);
     b_bs_ = upload_f32(bias);
     g_bs_ = upload_f32(gam);
-    m_wbs_ = map_2d(w_bs_.get(), D, ktot_, ktot_, pick_bn(D));
+    m_wbs_ = map_gemm_b(w_bs_.get(), D, ktot_, ktot_, pick_bn(D));
   }
 
   // ---- transformers
@@ -552,10 +552,10 @@ void Model::load(const std::string& path, int device, int precision) {
         L.b1 = upload_f32(vec(fp + ".1.bias", ff_));
         L.w2 = upload_16(mat(fp + ".4.weight", D, ff_), bf16_);
         L.b2 = upload_f32(vec(fp + ".4.bias", D));
-        L.m_wqkv = map_2d(L.wqkv.get(), 3 * inner_, D, D, pick_bn(3 * inner_));
-        L.m_wout = map_2d(L.wout.get(), D, inner_, inner_, pick_bn(D));
-        L.m_w1 = map_2d(L.w1.get(), ff_, D, D, pick_bn(ff_));
-        L.m_w2 = map_2d(L.w2.get(), D, ff_, ff_, pick_bn(D));
+        L.m_wqkv = map_gemm_b(L.wqkv.get(), 3 * inner_, D, D, pick_bn(3 * inner_));
+        L.m_wout = map_gemm_b(L.wout.get(), D, inner_, inner_, pick_bn(D));
+        L.m_w1 = map_gemm_b(L.w1.get(), ff_, D, D, pick_bn(ff_));
+        L.m_w2 = map_gemm_b(L.w2.get(), D, ff_, ff_, pick_bn(D));
       }
       if (mel_) tw.g_final = upload_f32(vec(tp + ".norm.gamma", D));
     }
@@ -589,7 +589,7 @@ void Model::load(const std::string& path, int device, int precision) {
       }
       sw.w.push_back(upload_16(W, bf16_));
       sw.b.push_back(upload_f32(bias));
-      sw.m.push_back(map_2d(sw.w.back().get(), rows_total, K, K, 256));
+      sw.m.push_back(map_gemm_b(sw.w.back().get(), rows_total, K, K, 256));
     }
   }
   MSST_CUDA(cudaDeviceSynchronize());

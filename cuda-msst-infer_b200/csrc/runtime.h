@@ -142,6 +142,12 @@ inline CUtensorMap map_2d(const void* base, uint64_t rows, uint64_t cols, uint64
   return make_tensor_map(base, 2, dims, strides, box);
 }
 
+// The B (weight) operand of a GEMM with column tile bn: boxes of 64 columns x
+// bn/2 rows (a CTA pair loads one half each; a single CTA loads both).
+inline CUtensorMap map_gemm_b(const void* base, uint64_t rows, uint64_t cols, uint64_t ld, int bn) {
+  return map_2d(base, rows, cols, ld, (uint32_t)(bn / 2));
+}
+
 inline int device_sm_count() {
   int dev = 0, n = 0;
   MSST_CUDA(cudaGetDevice(&dev));

@@ -214,11 +214,12 @@ class ops:
         return out
 
     @staticmethod
-    def gemm_qkv_rope(x, w, heads, cos, sin, pos_div, pos_mod):
+    def gemm_qkv_rope(x, w, heads, cos, sin, pos_div, pos_mod, out=None):
         torch = _torch()
         K = x.shape[-1]
         rows = x.numel() // K
-        out = torch.empty((rows, 3 * heads * 64), dtype=x.dtype, device=x.device)
+        if out is None:
+            out = torch.empty((rows, 3 * heads * 64), dtype=x.dtype, device=x.device)
         check(lib().msst_gemm_qkv_rope(_ptr(x.contiguous()), rows, K, _ptr(w.contiguous()), heads,
                                        _ptr(cos.contiguous()), _ptr(sin.contiguous()), pos_div, pos_mod,
                                        _dtype_code(x.dtype), _ptr(out), _stream()))

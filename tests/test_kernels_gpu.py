@@ -7,6 +7,8 @@ relative); accumulation is fp32 in both paths.
 """
 from __future__ import annotations
 
+import os
+
 import numpy as np
 import pytest
 
@@ -123,14 +125,96 @@ def test_gemm_glu(cuda, prec, N):
     assert rel_l2(y.cpu().numpy(), r.cpu().numpy()) < 1e-5
 
 
+# CTA-pair GEMM tiles (cta_group::2 MMAs): by default only the residual GEMMs
+# with K >= 512 use them; MSST_GEMM_PAIR=2 (read once per process) routes every
+# launch with at least 148 whole-column 256-row pair tiles through them, so the
+# other epilogues are checked in a child process.  The sizes include a last pair
+# tile whose second CTA's rows lie past M (zero-filled A rows, clipped stores).
+PAIR_CASES = [("store16", 37003, 384, 1536), ("store32", 60000, 1536, 384), ("resid32", 60000, 1536, 384),
+              ("glu32", 40000, 512, 1024), ("resid32", 48060, 512, 512), ("qkv", 48060, 384, 1536)]
+
+
+def pair_case_error(epi, M, K, N, prec):
+    """rel-L2 error of one pair-tile GEMM against an fp32 torch reference."""
+    import torch
+    from msst_b200 import ops
+
+    g = torch.Generator(device="cuda").manual_seed(M + N)
+    dt = _dt(torch, prec)
+    x = torch.randn(M, K, device="cuda", generator=g).to(dt)
+    w = (0.05 * torch.randn(N, K, device="cuda", generator=g)).to(dt)
+    b = 0.05 * torch.randn(N, device="cuda", generator=g)
+    r = _lin_ref(x, w, b)
+    if epi == "store16":
+        y = ops.gemm(x, w, b, "store16", "gelu")
+        r = torch.nn.functional.gelu(r)
+    elif epi == "resid32":
+        base = torch.randn(M, N, device="cuda", generator=g)
+        y = base.clone()
+        ops.gemm(x, w, b, "resid32", out=y)
+        r = r + base
+    elif epi == "glu32":
+        y = ops.gemm(x, w, b, "glu32")
+        r = r[:, 0::2] * torch.sigmoid(r[:, 1::2])
+    elif epi == "qkv":
+        T, F, H = 801, 60, 8
+        inv = 10000.0 ** (-np.arange(0, 64, 2, dtype=np.float64) / 64)
+        ang = np.arange(T, dtype=np.float64)[:, None] * inv[None, :]
+        cs, sn = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+        y = ops.gemm_qkv_rope(x, w, H, torch.from_numpy(cs).cuda(), torch.from_numpy(sn).cuda(), F, T)
+        r = _lin_ref(x, w, None).view(M, 3, H, 32, 2)
+        pos = torch.from_numpy((np.arange(M) // F) % T).cuda()
+        c = torch.from_numpy(cs).cuda()[pos][:, None, :]
+        s_ = torch.from_numpy(sn).cuda()[pos][:, None, :]
+        for part in (0, 1):
+            x0, x1 = r[:, part, :, :, 0].clone(), r[:, part, :, :, 1].clone()
+            r[:, part, :, :, 0] = x0 * c - x1 * s_
+            r[:, part, :, :, 1] = x0 * s_ + x1 * c
+        r = r.view(M, N)
+    else:
+        y = ops.gemm(x, w, b, "store32")
+    torch.cuda.synchronize()
+    return rel_l2(y.float().cpu().numpy(), r.cpu().numpy())
+
+
+def _pair_tol(epi, prec):
+    return TOL16[prec] if epi in ("store16", "qkv") else 1e-5
+
+
 @pytest.mark.parametrize("prec", ["fp16", "bf16"])
-@pytest.mark.parametrize("axis", ["time", "band"])
-def test_qkv_rope(cuda, prec, axis):
+def test_gemm_pair_tiles_default(cuda, prec):
+    """The default policy's pair launches (residual, K >= 512)."""
+    for epi, M, K, N in PAIR_CASES:
+        if epi == "resid32":
+            assert pair_case_error(epi, M, K, N, prec) < _pair_tol(epi, prec), (epi, M, K, N)
+
+
+def test_gemm_pair_tiles_all_epilogues(cuda):
+    import subprocess
+    import sys
+
+    here = os.path.dirname(os.path.abspath(__file__))
+    code = ("import sys; sys.path.insert(0, %r); import conftest, test_kernels_gpu as t\n"
+            "bad = []\n"
+            "for prec in ('fp16', 'bf16'):\n"
+            "    for epi, M, K, N in t.PAIR_CASES:\n"
+            "        e = t.pair_case_error(epi, M, K, N, prec)\n"
+            "        if not e < t._pair_tol(epi, prec): bad.append((epi, M, K, N, prec, e))\n"
+            "print('BAD', bad) if bad else print('OK')\n") % here
+    env = dict(os.environ, MSST_GEMM_PAIR="2")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and r.stdout.strip().endswith("OK"), r.stdout[-2000:] + r.stderr[-2000:]
+
+
+@pytest.mark.parametrize("prec", ["fp16", "bf16"])
+@pytest.mark.parametrize("axis,shape", [("time", (2, 131, 5, 2, 128)), ("band", (2, 131, 5, 2, 128)),
+                                        ("time", (1, 801, 60, 8, 384))])
+def test_qkv_rope(cuda, prec, axis, shape):
     torch = cuda
     from msst_b200 import ops
 
     oracle = oracle_mod()
-    B, T, F, H, D = 2, 131, 5, 2, 128
+    B, T, F, H, D = shape
     M = B * T * F
     g = torch.Generator().manual_seed(3)
     dt = _dt(torch, prec)
