@@ -159,13 +159,24 @@ __device__ __forceinline__ void process_chunk(const uint32_t (&r)[32], int ch, b
   }
 }
 
-template <typename T, int kPass>
+// kFirst (with kPass 1): the reference max is not known yet; it is taken from the
+// first chunk's valid scores (returned in m0), and the pass proceeds as a
+// steady-state pass against it (the caller falls back to the exact two passes if
+// a later chunk exceeds it by more than 2^8).
+template <typename T, int kPass, bool kFirst = false>
 __device__ __forceinline__ void row_pass(uint32_t sAddr, int c_lo, int c_hi, int c_full, int klo, int khi, float c,
-                                         float mc, float& mx, float2& sum2, uint32_t pAddr) {
-  const float2 c2 = make_float2(c, c), nm2 = make_float2(-mc, -mc);
+                                         float mc, float& mx, float2& sum2, uint32_t pAddr, float* m0 = nullptr) {
   uint32_t ra[32], rb[32];
   tmem_ld32(sAddr, ra);
   tmem_ld_wait(ra);
+  if constexpr (kFirst) {
+    float m = -INFINITY;
+    process_chunk<T, 0>(ra, 0, 0 >= c_lo && 0 < c_hi, 0 < c_full, klo, khi, make_float2(0.f, 0.f),
+                        make_float2(0.f, 0.f), m, sum2, pAddr);
+    *m0 = m;
+    mc = (m == -INFINITY) ? 0.f : m * c;
+  }
+  const float2 c2 = make_float2(c, c), nm2 = make_float2(-mc, -mc);
   tmem_ld32(sAddr + 32, rb);
   process_chunk<T, kPass>(ra, 0, 0 >= c_lo && 0 < c_hi, 0 < c_full, klo, khi, c2, nm2, mx, sum2, pAddr);
   tmem_ld_wait(rb);
@@ -230,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int item = blockIdx.x; ok && item < p.total_items; item += gridDim.x, ++pc) {
         const PairGeom g = pair_geom(p, item);
-        if (!mbar_wait(q_empty, (pc & 1) ^ 1, kErrTimeoutAttnQ, abort_flag)) break;
+        if (!mbar_wait<false>(q_empty, (pc & 1) ^ 1, kErrTimeoutAttnQ, abort_flag)) break;
         mbar_arrive_expect_tx(q_full, (g.has_b ? 2 : 1) * kTileBytes);
         const int xq = g.head * 64;
         if (p.mode == 0) {
@@ -243,7 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int xk = HD + g.head * 64, xv = 2 * HD + g.head * 64;
         for (int j = 0; j < g.steps; ++j, ++kvc) {
           const int st = kvc % kKvStages;
-          if (!mbar_wait(&kv_empty[st], ((kvc / kKvStages) & 1) ^ 1, kErrTimeoutAttnKV, abort_flag)) {
+          if (!mbar_wait<false>(&kv_empty[st], ((kvc / kKvStages) & 1) ^ 1, kErrTimeoutAttnKV, abort_flag)) {
             ok = false;
             break;
           }
@@ -279,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(&s_full[w]);
       };
       auto issue_pv = [&](int w, int st, bool first) -> bool {
-        if (!mbar_wait(&p_full[w], pcnt[w] & 1, kErrTimeoutAttnP, abort_flag)) return false;
+        if (!mbar_wait<false>(&p_full[w], pcnt[w] & 1, kErrTimeoutAttnP, abort_flag)) return false;
         ++pcnt[w];
         tc_fence_after();
         const uint32_t paddr = tmem + kColP + (uint32_t)(w * 64);
@@ -294,13 +305,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int item = blockIdx.x; ok && item < p.total_items; item += gridDim.x, ++pc) {
         const PairGeom g = pair_geom(p, item);
         const int nw = g.has_b ? 2 : 1;
-        if (!mbar_wait(q_full, pc & 1, kErrTimeoutAttnQ, abort_flag)) break;
+        if (!mbar_wait<false>(q_full, pc & 1, kErrTimeoutAttnQ, abort_flag)) break;
         tc_fence_after();
         int last_used[2] = {-1, -1};  // K/V stage of each tile's previous step
         int used_count[2] = {0, 0};
         for (int j = 0; ok && j < g.steps; ++j) {
           const int st = (kvc + j) % kKvStages;
-          if (!mbar_wait(&kv_full[st], ((kvc + j) / kKvStages) & 1, kErrTimeoutAttnKV, abort_flag)) {
+          if (!mbar_wait<false>(&kv_full[st], ((kvc + j) / kKvStages) & 1, kErrTimeoutAttnKV, abort_flag)) {
             ok = false;
             break;
           }
@@ -368,7 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int used = 0;
       for (int j = 0; j < g.steps; ++j) {
         if (!uses(p, w, j)) continue;
-        if (!mbar_wait(&s_full[w], scnt & 1, kErrTimeoutAttnS, abort_flag)) {
+        if (!mbar_wait<false>(&s_full[w], scnt & 1, kErrTimeoutAttnS, abort_flag)) {
           ok = false;
           break;
         }
@@ -393,16 +404,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           // chunks needing no per-column mask (time axis: entirely below khi)
           const int c_full = (p.mode == 0) ? (khi >> 5) : 0;
           float2 sum2 = make_float2(0.f, 0.f);
-          bool exact = (used == 0) || (p.mode == 1);
+          bool exact = p.mode == 1;
           if (!exact) {
             // steady state: exponentiate against the current reference max in one pass and
-            // track how far above it the row went
+            // track how far above it the row went; a tile's first step takes its
+            // reference max from the first 32 columns
             float amax = -INFINITY;
-            const float mc = (m == -INFINITY) ? 0.f : m * c;
-            row_pass<T, 1>(sAddr, c_lo, c_hi, c_full, klo, khi, c, mc, amax, sum2, pAddr);
+            if (used == 0) {
+              float m0 = -INFINITY;
+              row_pass<T, 1, true>(sAddr, c_lo, c_hi, c_full, klo, khi, c, 0.f, amax, sum2, pAddr, &m0);
+              m = m0;
+            } else {
+              const float mc = (m == -INFINITY) ? 0.f : m * c;
+              row_pass<T, 1>(sAddr, c_lo, c_hi, c_full, klo, khi, c, mc, amax, sum2, pAddr);
+            }
             if (__any_sync(0xffffffffu, amax > kRescaleLog2)) {
               exact = true;
               sum2 = make_float2(0.f, 0.f);
+              if (used == 0) m = -INFINITY;
             }
           }
           if (exact) {
@@ -442,7 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) break;
       // epilogue: O_w complete after the pair's last PV
-      if (!mbar_wait(&o_done[w], ocnt & 1, kErrTimeoutAttnO, abort_flag)) break;
+      if (!mbar_wait<false>(&o_done[w], ocnt & 1, kErrTimeoutAttnO, abort_flag)) break;
       ++ocnt;
       tc_fence_after();
       if (warp_active) {
