@@ -5,8 +5,8 @@
 // query tiles (a, b) of one head:
 //   time axis: two consecutive q-tiles of one sequence; both consume the same
 //              K/V tiles, so each K/V tile is loaded once for 256 query rows
-//   band axis: two consecutive packed tiles (several short sequences each, with
-//              a block-diagonal mask); each has its own single K/V tile
+//   band axis: two consecutive packed tiles (sequences at aligned 32/64/128-row
+//              slots, block-diagonal mask); each has its own single K/V tile
 //   warp 0     TMA producer: Q_a/Q_b, K/V tiles through a 4-stage ring
 //   warp 1     MMA issuer: S_w = Q_w K^T (M128 N128 K64) and O_w += P_w V
 //              (M128 N64 K128, P read from TMEM), issued per tile as
@@ -50,7 +50,7 @@ struct PairGeom {
   // time axis
   int b, f, t0a;    // t0 of tile a; tile b starts at t0a + 128
   // band axis
-  int r0a, rows;    // first token of tile a; valid rows per packed tile
+  int r0a, rows;    // first sequence of tile a; sequences per packed tile
 };
 
 __device__ __forceinline__ PairGeom pair_geom(const AttnParams& p, int item) {
@@ -70,7 +70,7 @@ __device__ __forceinline__ PairGeom pair_geom(const AttnParams& p, int item) {
   } else {
     g.head = item % p.heads;
     const int pr = item / p.heads;
-    g.rows = p.seqs_per_tile * p.seq_len;
+    g.rows = p.seqs_per_tile;
     g.r0a = 2 * pr * g.rows;
     g.has_b = 2 * pr + 1 < p.q_tiles;
     g.steps = g.has_b ? 2 : 1;
@@ -159,34 +159,51 @@ __device__ __forceinline__ void process_chunk(const uint32_t (&r)[32], int ch, b
   }
 }
 
+// One pass over a 128-column S row held in TMEM (4 chunks of 32 columns, loads
+// software-pipelined: chunk ch+1 is in flight while ch is processed).  Chunks
+// outside [c_lo, c_hi) get P = 0 (they are loaded all the same: predicated TMEM
+// loads keep both register buffers live and spill).
+// Chunks in [c_lo, c_full) need no per-column mask.
 // kFirst (with kPass 1): the reference max is not known yet; it is taken from the
-// first chunk's valid scores (returned in m0), and the pass proceeds as a
+// first loaded chunk's valid scores (returned in m0), and the pass proceeds as a
 // steady-state pass against it (the caller falls back to the exact two passes if
 // a later chunk exceeds it by more than 2^8).
-template <typename T, int kPass, bool kFirst = false>
+// kBand: the row's window may start past chunk 0 (band axis); the time axis always
+// starts at chunk 0, where the first-chunk max is taken unconditionally.
+template <typename T, int kPass, bool kFirst = false, bool kBand = false>
 __device__ __forceinline__ void row_pass(uint32_t sAddr, int c_lo, int c_hi, int c_full, int klo, int khi, float c,
                                          float mc, float& mx, float2& sum2, uint32_t pAddr, float* m0 = nullptr) {
+  float2 c2 = make_float2(c, c), nm2 = make_float2(-mc, -mc);
+  auto first_max = [&](const uint32_t(&r)[32], int ch) {
+    if constexpr (kFirst) {
+      if (kBand ? ch == c_lo : ch == 0) {
+        float m = -INFINITY;
+        process_chunk<T, 0>(r, ch, true, ch < c_full, klo, khi, c2, nm2, m, sum2, pAddr);
+        *m0 = m;
+        const float mcf = (m == -INFINITY) ? 0.f : m * c;
+        nm2 = make_float2(-mcf, -mcf);
+      }
+    }
+  };
+  const bool in0 = c_lo <= 0 && 0 < c_hi, in1 = c_lo <= 1 && 1 < c_hi;
+  const bool in2 = c_lo <= 2 && 2 < c_hi, in3 = c_lo <= 3 && 3 < c_hi;
   uint32_t ra[32], rb[32];
   tmem_ld32(sAddr, ra);
   tmem_ld_wait(ra);
-  if constexpr (kFirst) {
-    float m = -INFINITY;
-    process_chunk<T, 0>(ra, 0, 0 >= c_lo && 0 < c_hi, 0 < c_full, klo, khi, make_float2(0.f, 0.f),
-                        make_float2(0.f, 0.f), m, sum2, pAddr);
-    *m0 = m;
-    mc = (m == -INFINITY) ? 0.f : m * c;
-  }
-  const float2 c2 = make_float2(c, c), nm2 = make_float2(-mc, -mc);
   tmem_ld32(sAddr + 32, rb);
-  process_chunk<T, kPass>(ra, 0, 0 >= c_lo && 0 < c_hi, 0 < c_full, klo, khi, c2, nm2, mx, sum2, pAddr);
+  first_max(ra, 0);
+  process_chunk<T, kPass>(ra, 0, in0, c_lo <= 0 && 0 < c_full, klo, khi, c2, nm2, mx, sum2, pAddr);
   tmem_ld_wait(rb);
   tmem_ld32(sAddr + 64, ra);
-  process_chunk<T, kPass>(rb, 1, 1 >= c_lo && 1 < c_hi, 1 < c_full, klo, khi, c2, nm2, mx, sum2, pAddr);
+  if constexpr (kBand) first_max(rb, 1);
+  process_chunk<T, kPass>(rb, 1, in1, c_lo <= 1 && 1 < c_full, klo, khi, c2, nm2, mx, sum2, pAddr);
   tmem_ld_wait(ra);
   tmem_ld32(sAddr + 96, rb);
-  process_chunk<T, kPass>(ra, 2, 2 >= c_lo && 2 < c_hi, 2 < c_full, klo, khi, c2, nm2, mx, sum2, pAddr);
+  if constexpr (kBand) first_max(ra, 2);
+  process_chunk<T, kPass>(ra, 2, in2, c_lo <= 2 && 2 < c_full, klo, khi, c2, nm2, mx, sum2, pAddr);
   tmem_ld_wait(rb);
-  process_chunk<T, kPass>(rb, 3, 3 >= c_lo && 3 < c_hi, 3 < c_full, klo, khi, c2, nm2, mx, sum2, pAddr);
+  if constexpr (kBand) first_max(rb, 3);
+  process_chunk<T, kPass>(rb, 3, in3, c_lo <= 3 && 3 < c_full, klo, khi, c2, nm2, mx, sum2, pAddr);
 }
 
 template <typename T>
@@ -248,8 +265,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_4d(sQ, &qkv, q_full, xq, g.f, g.t0a, g.b);
           if (g.has_b) tma_load_4d(sQ + kTileBytes, &qkv, q_full, xq, g.f, g.t0a + 128, g.b);
         } else {
-          tma_load_4d(sQ, &qkv, q_full, xq, g.r0a, 0, 0);
-          if (g.has_b) tma_load_4d(sQ + kTileBytes, &qkv, q_full, xq, g.r0a + g.rows, 0, 0);
+          // one box of `slot` rows per sequence, at its aligned slot of the tile
+          const uint32_t slot_bytes = (128u / (uint32_t)g.rows) * 128u;
+          for (int w = 0; w < (g.has_b ? 2 : 1); ++w)
+            for (int k = 0; k < g.rows; ++k)
+              tma_load_4d(sQ + w * kTileBytes + k * slot_bytes, &qkv, q_full, xq,
+                          (g.r0a + w * g.rows + k) * p.seq_len, 0, 0);
         }
         const int xk = HD + g.head * 64, xv = 2 * HD + g.head * 64;
         for (int j = 0; j < g.steps; ++j, ++kvc) {
@@ -264,9 +285,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_4d(dk, &qkv, &kv_full[st], xk, g.f, j * 128, g.b);
             tma_load_4d(dk + kTileBytes, &qkv, &kv_full[st], xv, g.f, j * 128, g.b);
           } else {
-            const int r0 = g.r0a + j * g.rows;
-            tma_load_4d(dk, &qkv, &kv_full[st], xk, r0, 0, 0);
-            tma_load_4d(dk + kTileBytes, &qkv, &kv_full[st], xv, r0, 0, 0);
+            const uint32_t slot_bytes = (128u / (uint32_t)g.rows) * 128u;
+            for (int k = 0; k < g.rows; ++k) {
+              const int r0 = (g.r0a + j * g.rows + k) * p.seq_len;
+              tma_load_4d(dk + k * slot_bytes, &qkv, &kv_full[st], xk, r0, 0, 0);
+              tma_load_4d(dk + kTileBytes + k * slot_bytes, &qkv, &kv_full[st], xv, r0, 0, 0);
+            }
           }
         }
       }
@@ -368,11 +392,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         valid = t < p.T;
         token = ((long long)g.b * p.T + t) * p.F + g.f;
       } else {
-        const int r0 = g.r0a + w * g.rows;
-        valid = row < g.rows && r0 + row < p.num_tokens;
-        token = (long long)r0 + row;
-        lo = (row / p.seq_len) * p.seq_len;
-        hi_seq = min(lo + p.seq_len, g.rows);
+        const int slot = 128 / g.rows;
+        const int k = row / slot, rr = row - k * slot;
+        const int sq = g.r0a + w * g.rows + k;  // sequence of this row
+        valid = rr < p.seq_len && (long long)sq * p.seq_len < p.num_tokens;
+        token = (long long)sq * p.seq_len + rr;
+        lo = k * slot;
+        hi_seq = lo + p.seq_len;
       }
       const bool warp_active = __any_sync(0xffffffffu, valid);
       float m = -INFINITY, l = 0.f;
@@ -394,17 +420,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           klo = lo;
           khi = hi_seq;
         }
-        int wlo = klo, whi = khi;
-        if (p.mode == 1) {
-          wlo = __reduce_min_sync(0xffffffffu, valid ? klo : 128);
-          whi = __reduce_max_sync(0xffffffffu, valid ? khi : 0);
-        }
-        const int c_lo = wlo >> 5, c_hi = (whi + 31) >> 5;  // chunks holding any valid column
+        // klo is warp-uniform and 32-aligned on both axes (band: the slot of the warp's rows)
+        const int c_lo = klo >> 5, c_hi = (khi + 31) >> 5;  // chunks holding any valid column
         if (warp_active) {
-          // chunks needing no per-column mask (time axis: entirely below khi)
-          const int c_full = (p.mode == 0) ? (khi >> 5) : 0;
+          // chunks [c_lo, c_full) need no per-column mask
+          const int c_full = khi >> 5;
           float2 sum2 = make_float2(0.f, 0.f);
-          bool exact = p.mode == 1;
+          bool exact = false;
           if (!exact) {
             // steady state: exponentiate against the current reference max in one pass and
             // track how far above it the row went; a tile's first step takes its
@@ -412,7 +434,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             float amax = -INFINITY;
             if (used == 0) {
               float m0 = -INFINITY;
-              row_pass<T, 1, true>(sAddr, c_lo, c_hi, c_full, klo, khi, c, 0.f, amax, sum2, pAddr, &m0);
+              if (p.mode == 0)
+                row_pass<T, 1, true>(sAddr, c_lo, c_hi, c_full, klo, khi, c, 0.f, amax, sum2, pAddr, &m0);
+              else
+                row_pass<T, 1, true, true>(sAddr, c_lo, c_hi, c_full, klo, khi, c, 0.f, amax, sum2, pAddr, &m0);
               m = m0;
             } else {
               const float mc = (m == -INFINITY) ? 0.f : m * c;
@@ -521,7 +546,8 @@ cudaError_t launch_t(const CUtensorMap& m, const AttnParams& p, int num_sms, cud
 
 cudaError_t launch_attention(const CUtensorMap& qkv_map, const AttnParams& p, int bf16, int num_sms,
                              cudaStream_t stream) {
-  if (p.mode == 1 && (p.seq_len > 128 || p.seqs_per_tile < 1)) return cudaErrorInvalidValue;
+  if (p.mode == 1 && (p.seq_len < 1 || p.seq_len > 128 || p.seqs_per_tile != 128 / attn_band_slot(p.seq_len)))
+    return cudaErrorInvalidValue;
   if (p.q_tiles < 1) return cudaSuccess;
   AttnParams a = p;
   const long long pairs = (p.q_tiles + 1) / 2;

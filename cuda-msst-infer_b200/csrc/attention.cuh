@@ -25,7 +25,7 @@ struct AttnParams {
   int heads;          // H (head_dim fixed at 64)
   int seq_len;        // T (mode 0) or F (mode 1)
   int q_tiles;        // mode 0: ceil(T/128); mode 1: number of 128-row packed tiles
-  int seqs_per_tile;  // mode 1: floor(128 / F)
+  int seqs_per_tile;  // mode 1: 128 / attn_band_slot(F)
   int total_items;    // set by launch_attention: pairs of q-tiles x heads (x sequences on the time axis)
   int num_tokens;     // B*T*F
   float scale_log2;   // softmax scale * log2(e)
@@ -33,9 +33,15 @@ struct AttnParams {
   void* out;          // [tokens, heads*64], 16-bit
 };
 
+// Band axis (mode 1): each sequence of F <= 128 tokens occupies an aligned slot of
+// 32, 64 or 128 rows of a 128-row tile (seqs_per_tile = 128 / slot), so every
+// softmax warp's 32 rows belong to one sequence and its keys span at most
+// slot / 32 column chunks.
+inline int attn_band_slot(int F) { return F <= 32 ? 32 : (F <= 64 ? 64 : 128); }
+
 // `qkv_map` is a 4-D tensor map over the QKV buffer (inner dim = 3*H*64 columns)
-// with box {64, 1, 128, 1} (mode 0: dims {C, F, T, B}) or {64, 128, 1, 1}
-// (mode 1: dims {C, tokens, 1, 1}), 128B swizzle.
+// with box {64, 1, 128, 1} (mode 0: dims {C, F, T, B}) or {64, slot, 1, 1}
+// (mode 1: dims {C, tokens, 1, 1}, slot = attn_band_slot(F)), 128B swizzle.
 cudaError_t launch_attention(const CUtensorMap& qkv_map, const AttnParams& p, int bf16, int num_sms,
                              cudaStream_t stream);
 

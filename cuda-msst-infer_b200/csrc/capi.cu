@@ -254,12 +254,12 @@ int msst_attention(const void* qkv16, int B, int T, int F, int heads, int axis, 
       m = msst::make_tensor_map(qkv16, 4, dims, str, box);
     } else {
       a.seq_len = F;
-      a.seqs_per_tile = 128 / F;
+      a.seqs_per_tile = 128 / msst::attn_band_slot(F);
       a.q_tiles = (int)(((long long)B * T + a.seqs_per_tile - 1) / a.seqs_per_tile);
       a.total_items = a.q_tiles * heads;
       const uint64_t dims[4] = {C3, (uint64_t)M, 1, 1};
       const uint64_t str[3] = {C3 * 2, C3 * 2 * M, C3 * 2 * M};
-      const uint32_t box[4] = {64, 128, 1, 1};
+      const uint32_t box[4] = {64, (uint32_t)msst::attn_band_slot(F), 1, 1};
       m = msst::make_tensor_map(qkv16, 4, dims, str, box);
     }
     MSST_CUDA(msst::launch_attention(m, a, dtype, sm_count(), as_stream(stream)));

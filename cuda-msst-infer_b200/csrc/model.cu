@@ -721,7 +721,7 @@ Model::Work& Model::work(int B, int T) {
     w->m_qkv_time = make_tensor_map(w->big1.get(), 4, dims, str, box);
     const uint64_t dims2[4] = {C3, (uint64_t)M, 1, 1};
     const uint64_t str2[3] = {C3 * 2, C3 * 2 * M, C3 * 2 * M};
-    const uint32_t box2[4] = {64, 128, 1, 1};
+    const uint32_t box2[4] = {64, (uint32_t)attn_band_slot(nb), 1, 1};
     w->m_qkv_band = make_tensor_map(w->big1.get(), 4, dims2, str2, box2);
   }
   Work& ref = *w;
@@ -843,7 +843,7 @@ void Model::run_attn_block(int d, int axis, int l, float* x, int B, int T, const
       a.total_items = B * nb * I.heads * a.q_tiles;
     } else {
       a.seq_len = nb;
-      a.seqs_per_tile = 128 / nb;
+      a.seqs_per_tile = 128 / attn_band_slot(nb);
       a.q_tiles = (int)((w.BT + a.seqs_per_tile - 1) / a.seqs_per_tile);
       a.total_items = a.q_tiles * I.heads;
     }

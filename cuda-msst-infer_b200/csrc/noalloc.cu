@@ -125,7 +125,7 @@ void Model::transformer_noalloc(int d, int axis, float* x, int B, int T, cudaStr
   } else {
     const uint64_t dims[4] = {C3, (uint64_t)M, 1, 1};
     const uint64_t str[3] = {C3 * 2, C3 * 2 * M, C3 * 2 * M};
-    const uint32_t box[4] = {64, 128, 1, 1};
+    const uint32_t box[4] = {64, (uint32_t)attn_band_slot(nb), 1, 1};
     m_qkv = make_tensor_map(big, 4, dims, str, box);
   }
 
@@ -185,7 +185,7 @@ void Model::transformer_noalloc(int d, int axis, float* x, int B, int T, cudaStr
         a.q_tiles = (T + 127) / 128;
       } else {
         a.seq_len = nb;
-        a.seqs_per_tile = 128 / nb;
+        a.seqs_per_tile = 128 / attn_band_slot(nb);
         a.q_tiles = (int)(((long long)B * T + a.seqs_per_tile - 1) / a.seqs_per_tile);
       }
       MSST_CUDA(launch_attention(m_qkv, a, bf16_, num_sms_, s));

@@ -257,7 +257,9 @@ def _attn_ref(qkv, B, T, F, H, axis, scale, gates):
 
 @pytest.mark.parametrize("prec", ["fp16", "bf16"])
 @pytest.mark.parametrize("axis,B,T,F,H", [("time", 2, 801, 3, 2), ("time", 1, 100, 2, 8), ("time", 1, 256, 1, 1),
-                                           ("band", 2, 50, 60, 2), ("band", 1, 33, 62, 8), ("band", 3, 7, 5, 1)])
+                                           ("band", 2, 50, 60, 2), ("band", 1, 33, 62, 8), ("band", 3, 7, 5, 1),
+                                           ("band", 1, 20, 100, 2), ("band", 2, 9, 32, 2), ("band", 1, 11, 33, 1),
+                                           ("band", 1, 5, 128, 1), ("band", 1, 40, 1, 1)])
 def test_attention(cuda, prec, axis, B, T, F, H):
     torch = cuda
     from msst_b200 import ops
