@@ -27,6 +27,9 @@ enum DeviceError : unsigned {
   kErrTimeoutAttnO = 7,
   kErrTimeoutAttnQ = 8,
   kErrTimeoutAttnKV = 9,
+  kErrTimeoutFfnS = 10,
+  kErrTimeoutFfnP = 11,
+  kErrTimeoutFfnO = 12,
 };
 
 // One flag per translation unit; each .cu exposes a host accessor (see

@@ -792,6 +792,316 @@ cudaError_t dispatch_epi(const CUtensorMap& ma, const CUtensorMap& mb, const CUt
   }
 }
 
+// ---------------------------------------------------------------------------
+// Fused feed-forward block (see gemm.cuh).  CTA = 320 threads, persistent over
+// 128-row tiles:
+//   warp 0     TMA: the tile's xn (D/64 swizzled 128x64 atoms, resident for the
+//              tile), then W1 / W2 128x64 blocks through a 16 KB ring in the order
+//              the MMAs consume them
+//   warp 1     MMA issuer: S = xn . W1_j^T (TMEM columns [0, 128)) and
+//              O += P_j . W2_j^T (columns [128, 128 + D)), issued as
+//              S_0, S_1, O_0, S_2, O_1, ..., O_{J-1} so that the GELU of chunk j
+//              overlaps S_{j+1}
+//   warps 2-9  per chunk: S -> registers (64 columns each), bias + GELU, 16-bit P
+//              rows into the K-major swizzled P tile; per tile: O + b2 staged (in
+//              the P tile's shared memory) and bulk-reduce-added into x
+// TMEM holds one S chunk and O, so D + 128 <= 512.
+namespace ffn {
+constexpr int kBM = 128, kBH = 128, kBK = 64;
+constexpr uint32_t kBlock = kBM * kBK * 2;  // one 128x64 16-bit block (16 KB)
+constexpr int kStages = 6;
+constexpr int kMaxD = 384;
+constexpr uint32_t kStgBytes = 4096;  // per epilogue warp: 32 x 32 fp32, inside the P tile
+constexpr size_t kSmem = 1024 + (kMaxD / kBK) * kBlock + 2 * kBlock + kStages * kBlock + 256;
+}  // namespace ffn
+
+template <typename T>
+__global__ void __launch_bounds__(320, 1)
+    ffn_fused_kernel(const __grid_constant__ CUtensorMap map_xn, const __grid_constant__ CUtensorMap map_w1,
+                     const __grid_constant__ CUtensorMap map_w2, const __grid_constant__ CUtensorMap map_x,
+                     const __grid_constant__ FfnParams p) {
+  using namespace ffn;
+  constexpr uint32_t kIsBf16 = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sX = smem;                              // D/64 blocks
+  uint8_t* sP = sX + (kMaxD / kBK) * kBlock;       // 2 blocks (128 rows x 128 hidden)
+  uint8_t* sW = sP + 2 * kBlock;                   // ring
+  // The O epilogue stages through the P tile: it runs after the tile's last O MMAs
+  // (which read the last P) completed and before the same warps write the next P.
+  uint8_t* sEpi = sP;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sW + kStages * kBlock);
+  uint64_t* x_full = bars;
+  uint64_t* x_empty = bars + 1;
+  uint64_t* w_full = bars + 2;
+  uint64_t* w_empty = w_full + kStages;
+  uint64_t* s_full = w_empty + kStages;
+  uint64_t* s_free = s_full + 1;
+  uint64_t* p_full = s_free + 1;
+  uint64_t* p_free = p_full + 1;
+  uint64_t* o_full = p_free + 1;
+  uint64_t* o_free = o_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nkb = p.D / kBK;      // k-blocks of S
+  const int nn = p.D / kBM;       // 128-column pieces of O
+  const int J = p.H / kBH;        // hidden chunks
+  const int ntiles = (p.m + kBM - 1) / kBM;
+  if (threadIdx.x == 0) {
+    mbar_init(x_full, 1);
+    mbar_init(x_empty, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&w_full[s], 1);
+      mbar_init(&w_empty[s], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 8);
+    mbar_init(p_full, 8);
+    mbar_init(p_free, 1);
+    mbar_init(o_full, 1);
+    mbar_init(o_free, 8);
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_xn);
+    tma_prefetch_desc(&map_w1);
+    tma_prefetch_desc(&map_w2);
+    tma_prefetch_desc(&map_x);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int st = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      auto load_w = [&](const CUtensorMap* map, int x, int y) -> bool {
+        if (!mbar_wait(&w_empty[st], ph ^ 1u, kErrTimeoutSmemEmpty, abort_flag)) return false;
+        mbar_arrive_expect_tx(&w_full[st], kBlock);
+        tma_load_2d(sW + st * kBlock, map, &w_full[st], x, y);
+        if (++st == kStages) {
+          st = 0;
+          ph ^= 1u;
+        }
+        return true;
+      };
+      int lt = 0;
+      for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x, ++lt) {
+        if (!mbar_wait(x_empty, (lt & 1) ^ 1u, kErrTimeoutSmemEmpty, abort_flag)) break;
+        mbar_arrive_expect_tx(x_full, nkb * kBlock);
+        for (int kb = 0; kb < nkb; ++kb) tma_load_2d(sX + kb * kBlock, &map_xn, x_full, kb * kBK, t * kBM);
+        // consumption order: S_0, then (S_{j+1}, O_j) for j = 0..J-1
+        for (int kb = 0; ok && kb < nkb; ++kb) ok = load_w(&map_w1, kb * kBK, 0);
+        for (int j = 0; ok && j < J; ++j) {
+          if (j + 1 < J)
+            for (int kb = 0; ok && kb < nkb; ++kb) ok = load_w(&map_w1, kb * kBK, (j + 1) * kBH);
+          for (int kb2 = 0; ok && kb2 < kBH / kBK; ++kb2)
+            for (int n3 = 0; ok && n3 < nn; ++n3) ok = load_w(&map_w2, j * kBH + kb2 * kBK, n3 * kBM);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_f16(kIsBf16, 128, 0);
+      const uint32_t tS = tmem, tO = tmem + 128;
+      int st = 0;
+      uint32_t ph = 0;
+      uint32_t sc = 0, pc = 0;  // S chunks issued, P chunks consumed
+      bool ok = true;
+      auto issue_s = [&]() -> bool {
+        if (!mbar_wait(s_free, (sc & 1) ^ 1u, kErrTimeoutFfnS, abort_flag)) return false;
+        tc_fence_after();
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(&w_full[st], ph, kErrTimeoutTmaFull, abort_flag)) return false;
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sX + kb * kBlock), b0 = smem_u32(sW + st * kBlock);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            umma_f16_ss(tS, sw128_desc(a0 + kk * 32, 16, 1024), sw128_desc(b0 + kk * 32, 16, 1024), idesc,
+                        (kb | kk) != 0 ? 1u : 0u);
+          umma_commit(&w_empty[st]);
+          if (++st == kStages) {
+            st = 0;
+            ph ^= 1u;
+          }
+        }
+        umma_commit(s_full);
+        ++sc;
+        return true;
+      };
+      auto issue_o = [&](bool first) -> bool {
+        if (!mbar_wait(p_full, pc & 1, kErrTimeoutFfnP, abort_flag)) return false;
+        tc_fence_after();
+        for (int kb2 = 0; kb2 < kBH / kBK; ++kb2) {
+          for (int n3 = 0; n3 < nn; ++n3) {
+            if (!mbar_wait(&w_full[st], ph, kErrTimeoutTmaFull, abort_flag)) return false;
+            tc_fence_after();
+            const uint32_t a0 = smem_u32(sP + kb2 * kBlock), b0 = smem_u32(sW + st * kBlock);
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk)
+              umma_f16_ss(tO + (uint32_t)(n3 * kBM), sw128_desc(a0 + kk * 32, 16, 1024),
+                          sw128_desc(b0 + kk * 32, 16, 1024), idesc, (first && kb2 == 0 && kk == 0) ? 0u : 1u);
+            umma_commit(&w_empty[st]);
+            if (++st == kStages) {
+              st = 0;
+              ph ^= 1u;
+            }
+          }
+        }
+        umma_commit(p_free);
+        ++pc;
+        return true;
+      };
+      int lt = 0;
+      for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x, ++lt) {
+        if (!mbar_wait(x_full, lt & 1, kErrTimeoutTmaFull, abort_flag)) break;
+        tc_fence_after();
+        ok = issue_s();
+        for (int j = 0; ok && j < J; ++j) {
+          if (j + 1 < J) {
+            ok = issue_s();
+            if (ok && j + 2 == J) umma_commit(x_empty);  // the tile's last S reads xn
+          } else if (J == 1) {
+            umma_commit(x_empty);
+          }
+          if (!ok) break;
+          if (j == 0) {
+            // O of the previous tile drained by the epilogue
+            if (!mbar_wait(o_free, (lt & 1) ^ 1u, kErrTimeoutFfnO, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+          }
+          ok = issue_o(j == 0);
+        }
+        if (!ok) break;
+        umma_commit(o_full);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ GELU + O epilogue (8 warps)
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int r = q * 32 + lane;  // row within the tile
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    // staging = the 4 KB of the P tile this warp writes (rows q*32.. of block `half`),
+    // so waiting for its own bulk reads is enough before it writes P again
+    uint8_t* stg = sEpi + (half * 4 + q) * kStgBytes;
+    uint32_t sc = 0, pc = 0;
+    int lt = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x, ++lt) {
+      for (int j = 0; j < J; ++j) {
+        if (!mbar_wait(s_full, sc & 1, kErrTimeoutFfnS, abort_flag)) {
+          ok = false;
+          break;
+        }
+        ++sc;
+        tc_fence_after();
+        uint32_t ra[32], rb[32];
+        tmem_ld32(tmem + lane_off + (uint32_t)(half * 64), ra);
+        tmem_ld32(tmem + lane_off + (uint32_t)(half * 64 + 32), rb);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(s_free);
+        // bias + GELU, packed to 16-bit pairs: pk[0..15] columns half*64 + [0, 32), pk[16..31] + [32, 64)
+        uint32_t pk[32];
+        const float* b1 = p.b1 + j * kBH + half * 64;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const uint32_t(&rr)[32] = u == 0 ? ra : rb;
+          const float4* b4 = reinterpret_cast<const float4*>(b1 + 32 * u);
+#pragma unroll
+          for (int q4 = 0; q4 < 8; ++q4) {
+            const float4 b = __ldg(b4 + q4);
+            const float2 lo = gelu2(__fadd2_rn(make_float2(__uint_as_float(rr[4 * q4]), __uint_as_float(rr[4 * q4 + 1])),
+                                               make_float2(b.x, b.y)));
+            const float2 hi = gelu2(__fadd2_rn(
+                make_float2(__uint_as_float(rr[4 * q4 + 2]), __uint_as_float(rr[4 * q4 + 3])), make_float2(b.z, b.w)));
+            pk[16 * u + 2 * q4] = pack2<T>(lo.x, lo.y);
+            pk[16 * u + 2 * q4 + 1] = pack2<T>(hi.x, hi.y);
+          }
+        }
+        // P_{j-1} consumed by its O MMAs
+        if (!mbar_wait(p_free, (pc & 1) ^ 1u, kErrTimeoutFfnP, abort_flag)) {
+          ok = false;
+          break;
+        }
+        // the previous tile's O reduce-adds have read this warp's staging (= its P rows)
+        if (lane == 0) bulk_wait_read0();
+        __syncwarp();
+        // row r of the K-major 128B-swizzled P block `half` (64 hidden columns)
+        uint8_t* prow = sP + half * kBlock + r * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
+              make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full);
+        ++pc;
+      }
+      if (!ok) break;
+      // O epilogue: columns [half * D/2, (half + 1) * D/2) of rows t*128 + r
+      if (!mbar_wait(o_full, lt & 1, kErrTimeoutFfnO, abort_flag)) break;
+      tc_fence_after();
+      const int row0 = t * kBM + q * 32;
+      for (int c0 = half * (p.D / 2); c0 < (half + 1) * (p.D / 2); c0 += 32) {
+        uint32_t rr[32];
+        tmem_ld32(tmem + lane_off + 128u + (uint32_t)c0, rr);
+        tmem_ld_wait();
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(rr[i]);
+        if (p.b2 != nullptr) {
+          const float4* b4 = reinterpret_cast<const float4*>(p.b2 + c0);
+#pragma unroll
+          for (int q4 = 0; q4 < 8; ++q4) {
+            const float4 b = __ldg(b4 + q4);
+            v[4 * q4] += b.x;
+            v[4 * q4 + 1] += b.y;
+            v[4 * q4 + 2] += b.z;
+            v[4 * q4 + 3] += b.w;
+          }
+        }
+        if (lane == 0) bulk_wait_read0();
+        __syncwarp();
+        stage_row<float, false>(stg, lane, v);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && row0 < p.m) {
+          tma_reduce_add_3d(&map_x, stg, c0, row0, 0);
+          bulk_commit();
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(o_free);
+    }
+    if (lane == 0) bulk_wait0();
+    __syncwarp();
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_gemm(const CUtensorMap& map_a, const CUtensorMap& map_b, const CUtensorMap& map_out,
@@ -813,6 +1123,28 @@ cudaError_t launch_gemm(const CUtensorMap& map_a, const CUtensorMap& map_b, cons
     return bf16 ? dispatch_epi<192, __nv_bfloat16>(map_a, map_b, map_out, p, epilogue, num_sms, stream)
                 : dispatch_epi<192, __half>(map_a, map_b, map_out, p, epilogue, num_sms, stream);
   return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_ffn_fused(const CUtensorMap& map_xn, const CUtensorMap& map_w1, const CUtensorMap& map_w2,
+                             const CUtensorMap& map_x, const FfnParams& p, int bf16, int num_sms, cudaStream_t stream) {
+  if (p.m < 0 || p.D % ffn::kBM != 0 || p.D > ffn::kMaxD || p.H % ffn::kBH != 0 || p.H <= 0 || p.b1 == nullptr)
+    return cudaErrorInvalidValue;
+  if (p.m == 0) return cudaSuccess;
+  auto kern = bf16 ? ffn_fused_kernel<__nv_bfloat16> : ffn_fused_kernel<__half>;
+  static bool configured[2] = {false, false};
+  if (!configured[bf16 ? 1 : 0]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ffn::kSmem);
+    if (e != cudaSuccess) return e;
+    configured[bf16 ? 1 : 0] = true;
+  }
+  const int ntiles = (p.m + ffn::kBM - 1) / ffn::kBM;
+  const int grid = ntiles < num_sms ? ntiles : num_sms;
+  // algorithmic cost: both GEMMs; bytes = xn, W1, W2 read once, x read and written once
+  const double flop = 4.0 * p.m * (double)p.D * p.H;
+  const double bytes = (double)p.m * p.D * (2.0 + 8.0) + 2.0 * p.D * (double)p.H * (bf16 ? 2.0 : 2.0);
+  LaunchScope scope("ffn_fused", flop, bytes, stream);
+  kern<<<grid, 320, ffn::kSmem, stream>>>(map_xn, map_w1, map_w2, map_x, p);
+  return cudaGetLastError();
 }
 
 MSST_DEFINE_ERROR_ACCESSOR(gemm_device_error)

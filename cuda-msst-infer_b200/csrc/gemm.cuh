@@ -76,4 +76,20 @@ struct GemmParams {
 cudaError_t launch_gemm(const CUtensorMap& map_a, const CUtensorMap& map_b, const CUtensorMap& map_out,
                         const GemmParams& p, int epilogue, int bn, int bf16, int num_sms, cudaStream_t stream);
 
+// Fused feed-forward block (dim D <= 384, D and H multiples of 128):
+//   x[m, D] += GELU(xn . W1^T + b1) . W2^T + b2
+// xn [m, D] 16-bit (map box {64, 128}), W1 [H, D] (box {64, 128}), W2 [D, H]
+// (box {64, 128}), x fp32 through the residual output map (box {32, 32, 1}).
+// The hidden activation never leaves the SM: per 128-row tile the kernel loops
+// over H/128 hidden chunks, S = xn . W1_j^T into TMEM, bias + GELU into a 16-bit
+// P tile in shared memory, O += P . W2_j^T into TMEM (D columns), then adds O + b2
+// to x by bulk tensor reduce-add.
+struct FfnParams {
+  int m, D, H;
+  const float* b1;  // [H]
+  const float* b2;  // [D] or nullptr
+};
+cudaError_t launch_ffn_fused(const CUtensorMap& map_xn, const CUtensorMap& map_w1, const CUtensorMap& map_w2,
+                             const CUtensorMap& map_x, const FfnParams& p, int bf16, int num_sms, cudaStream_t stream);
+
 }  // namespace msst

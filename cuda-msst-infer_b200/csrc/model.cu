@@ -556,6 +556,8 @@ void Model::load(const std::string& path, int device, int precision) {
         L.m_wout = map_gemm_b(L.wout.get(), D, inner_, inner_, pick_bn(D));
         L.m_w1 = map_gemm_b(L.w1.get(), ff_, D, D, pick_bn(ff_));
         L.m_w2 = map_gemm_b(L.w2.get(), D, ff_, ff_, pick_bn(D));
+        L.m_w1_f = map_2d(L.w1.get(), ff_, D, D, 128);
+        L.m_w2_f = map_2d(L.w2.get(), D, ff_, ff_, 128);
       }
       if (mel_) tw.g_final = upload_f32(vec(tp + ".norm.gamma", D));
     }
@@ -859,6 +861,16 @@ void Model::run_attn_block(int d, int axis, int l, float* x, int B, int T, const
 }
 
 // src/model_mel_band_roformer.cu:597-622 (apply_feedforward) + residual
+// Fused feed-forward when the model's widths allow it (dim a multiple of 128 up to 384,
+// hidden a multiple of 128); MSST_FFN_FUSED=0 selects the two-GEMM path.
+bool Model::ffn_fused_ok() const {
+  static const int env = [] {
+    const char* e = getenv("MSST_FFN_FUSED");
+    return e ? atoi(e) : 1;
+  }();
+  return env != 0 && info_.dim % 128 == 0 && info_.dim <= 384 && ff_ % 128 == 0;
+}
+
 void Model::run_ffn_block(int d, int axis, int l, float* x, int B, int T, cudaStream_t s, Work& w) {
   const msst_model_info& I = info_;
   const int D = I.dim, nb = I.num_bands;
@@ -875,6 +887,17 @@ void Model::run_ffn_block(int d, int axis, int l, float* x, int B, int T, cudaSt
   rf.scale = std::sqrt((float)D);
   rf.out16 = w.xn.get();
   MSST_CUDA(launch_rmsnorm(rf, bf16_, s));
+  if (ffn_fused_ok()) {
+    // the hidden activation stays on chip (dim <= 384: S chunk + O fit TMEM)
+    FfnParams fp{};
+    fp.m = (int)M;
+    fp.D = D;
+    fp.H = ff_;
+    fp.b1 = L.b1.get<float>();
+    fp.b2 = L.b2.get<float>();
+    MSST_CUDA(launch_ffn_fused(w.m_xn, L.m_w1_f, L.m_w2_f, mo_x, fp, bf16_, num_sms_, s));
+    return;
+  }
   {
     GemmParams p{};
     p.num_groups = 1;

@@ -23,6 +23,7 @@ struct LayerWeights {
   DeviceBuffer g_attn, wqkv, wg, bg, wout;   // attention (norm gamma, W_qkv, gate W/b, W_out)
   DeviceBuffer g_ff, w1, b1, w2, b2;         // feed-forward
   CUtensorMap m_wqkv, m_wout, m_w1, m_w2;
+  CUtensorMap m_w1_f, m_w2_f;                // 128-row boxes for the fused feed-forward kernel
 };
 
 struct TransformerWeights {
@@ -77,6 +78,7 @@ class Model {
   void run_transformer(int d, int axis, float* x, int B, int T, const float* pending_gamma, cudaStream_t s, Work& w);
   void run_attn_block(int d, int axis, int l, float* x, int B, int T, const float* pending_gamma, cudaStream_t s,
                       Work& w);
+  bool ffn_fused_ok() const;
   void run_ffn_block(int d, int axis, int l, float* x, int B, int T, cudaStream_t s, Work& w);
   void gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, GemmParams& p, int epi, int bn,
             cudaStream_t s);
