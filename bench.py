@@ -152,8 +152,10 @@ NCU_TRAFFIC: dict = {
     "attention_band": {"dram_bytes": 149328896 + 20584704, "flop": 5905612800},
     "gemm_qkv_rope": {"dram_bytes": 38387712 + 90150144, "flop": 56693882880},
     "gemm_store16_gelu": {"dram_bytes": 38210816 + 90500608, "flop": 56693882880},
-    # one FFN2 (K=1536) and one out-projection (K=512) launch, as they alternate
-    "gemm_resid32": {"dram_bytes": 222728448 + 32885760 + 123456512 + 11998464, "flop": 75591843840},
+    # the out-projection (K=512); at dim <= 384 the FFN2 residual GEMM is part of ffn_fused
+    "gemm_resid32": {"dram_bytes": 123456512 + 11998464, "flop": 18897960960},
+    # profiles/ffn_fused_mbr_cfg1_chunk1.md: the fused feed-forward block, one chunk
+    "ffn_fused": {"dram_bytes": 113149440 + 18041856, "flop": 113387765760},
 }
 
 
