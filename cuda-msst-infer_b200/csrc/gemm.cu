@@ -809,10 +809,11 @@ cudaError_t dispatch_epi(const CUtensorMap& ma, const CUtensorMap& mb, const CUt
 namespace ffn {
 constexpr int kBM = 128, kBH = 128, kBK = 64;
 constexpr uint32_t kBlock = kBM * kBK * 2;  // one 128x64 16-bit block (16 KB)
-constexpr int kStages = 6;
+constexpr uint32_t kStage = 2 * kBlock;      // ring stage: two blocks, 8 MMAs per wait and commit
+constexpr int kStages = 3;
 constexpr int kMaxD = 384;
 constexpr uint32_t kStgBytes = 4096;  // per epilogue warp: 32 x 32 fp32, inside the P tile
-constexpr size_t kSmem = 1024 + (kMaxD / kBK) * kBlock + 2 * kBlock + kStages * kBlock + 256;
+constexpr size_t kSmem = 1024 + (kMaxD / kBK) * kBlock + 2 * kBlock + kStages * kStage + 256;
 }  // namespace ffn
 
 template <typename T>
@@ -830,7 +831,7 @@ __global__ void __launch_bounds__(320, 1)
   // The O epilogue stages through the P tile: it runs after the tile's last O MMAs
   // (which read the last P) completed and before the same warps write the next P.
   uint8_t* sEpi = sP;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sW + kStages * kBlock);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sW + kStages * kStage);
   uint64_t* x_full = bars;
   uint64_t* x_empty = bars + 1;
   uint64_t* w_full = bars + 2;
@@ -885,10 +886,12 @@ __global__ void __launch_bounds__(320, 1)
       int st = 0;
       uint32_t ph = 0;
       bool ok = true;
-      auto load_w = [&](const CUtensorMap* map, int x, int y) -> bool {
+      // one stage = two 128x64 boxes: (x, y) and (x + dx, y + dy)
+      auto load_w = [&](const CUtensorMap* map, int x, int y, int dx, int dy) -> bool {
         if (!mbar_wait(&w_empty[st], ph ^ 1u, kErrTimeoutSmemEmpty, abort_flag)) return false;
-        mbar_arrive_expect_tx(&w_full[st], kBlock);
-        tma_load_2d(sW + st * kBlock, map, &w_full[st], x, y);
+        mbar_arrive_expect_tx(&w_full[st], kStage);
+        tma_load_2d(sW + st * kStage, map, &w_full[st], x, y);
+        tma_load_2d(sW + st * kStage + kBlock, map, &w_full[st], x + dx, y + dy);
         if (++st == kStages) {
           st = 0;
           ph ^= 1u;
@@ -900,13 +903,14 @@ __global__ void __launch_bounds__(320, 1)
         if (!mbar_wait(x_empty, (lt & 1) ^ 1u, kErrTimeoutSmemEmpty, abort_flag)) break;
         mbar_arrive_expect_tx(x_full, nkb * kBlock);
         for (int kb = 0; kb < nkb; ++kb) tma_load_2d(sX + kb * kBlock, &map_xn, x_full, kb * kBK, t * kBM);
-        // consumption order: S_0, then (S_{j+1}, O_j) for j = 0..J-1
-        for (int kb = 0; ok && kb < nkb; ++kb) ok = load_w(&map_w1, kb * kBK, 0);
+        // consumption order: S_0, then (S_{j+1}, O_j) for j = 0..J-1; an S stage holds
+        // k-blocks kb, kb+1 of W1_j, an O stage the chunk's two 64-column halves of W2
+        // rows n3*128..
+        for (int kb = 0; ok && kb < nkb; kb += 2) ok = load_w(&map_w1, kb * kBK, 0, kBK, 0);
         for (int j = 0; ok && j < J; ++j) {
           if (j + 1 < J)
-            for (int kb = 0; ok && kb < nkb; ++kb) ok = load_w(&map_w1, kb * kBK, (j + 1) * kBH);
-          for (int kb2 = 0; ok && kb2 < kBH / kBK; ++kb2)
-            for (int n3 = 0; ok && n3 < nn; ++n3) ok = load_w(&map_w2, j * kBH + kb2 * kBK, n3 * kBM);
+            for (int kb = 0; ok && kb < nkb; kb += 2) ok = load_w(&map_w1, kb * kBK, (j + 1) * kBH, kBK, 0);
+          for (int n3 = 0; ok && n3 < nn; ++n3) ok = load_w(&map_w2, j * kBH, n3 * kBM, kBK, 0);
         }
       }
     }
@@ -922,14 +926,17 @@ __global__ void __launch_bounds__(320, 1)
       auto issue_s = [&]() -> bool {
         if (!mbar_wait(s_free, (sc & 1) ^ 1u, kErrTimeoutFfnS, abort_flag)) return false;
         tc_fence_after();
-        for (int kb = 0; kb < nkb; ++kb) {
+        for (int kb = 0; kb < nkb; kb += 2) {
           if (!mbar_wait(&w_full[st], ph, kErrTimeoutTmaFull, abort_flag)) return false;
           tc_fence_after();
-          const uint32_t a0 = smem_u32(sX + kb * kBlock), b0 = smem_u32(sW + st * kBlock);
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk)
-            umma_f16_ss(tS, sw128_desc(a0 + kk * 32, 16, 1024), sw128_desc(b0 + kk * 32, 16, 1024), idesc,
-                        (kb | kk) != 0 ? 1u : 0u);
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t a0 = smem_u32(sX + (kb + h) * kBlock), b0 = smem_u32(sW + st * kStage + h * kBlock);
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk)
+              umma_f16_ss(tS, sw128_desc(a0 + kk * 32, 16, 1024), sw128_desc(b0 + kk * 32, 16, 1024), idesc,
+                          (kb | h | kk) != 0 ? 1u : 0u);
+          }
           umma_commit(&w_empty[st]);
           if (++st == kStages) {
             st = 0;
@@ -943,20 +950,21 @@ __global__ void __launch_bounds__(320, 1)
       auto issue_o = [&](bool first) -> bool {
         if (!mbar_wait(p_full, pc & 1, kErrTimeoutFfnP, abort_flag)) return false;
         tc_fence_after();
-        for (int kb2 = 0; kb2 < kBH / kBK; ++kb2) {
-          for (int n3 = 0; n3 < nn; ++n3) {
-            if (!mbar_wait(&w_full[st], ph, kErrTimeoutTmaFull, abort_flag)) return false;
-            tc_fence_after();
-            const uint32_t a0 = smem_u32(sP + kb2 * kBlock), b0 = smem_u32(sW + st * kBlock);
+        for (int n3 = 0; n3 < nn; ++n3) {
+          if (!mbar_wait(&w_full[st], ph, kErrTimeoutTmaFull, abort_flag)) return false;
+          tc_fence_after();
+#pragma unroll
+          for (int kb2 = 0; kb2 < kBH / kBK; ++kb2) {
+            const uint32_t a0 = smem_u32(sP + kb2 * kBlock), b0 = smem_u32(sW + st * kStage + kb2 * kBlock);
 #pragma unroll
             for (int kk = 0; kk < kBK / 16; ++kk)
               umma_f16_ss(tO + (uint32_t)(n3 * kBM), sw128_desc(a0 + kk * 32, 16, 1024),
                           sw128_desc(b0 + kk * 32, 16, 1024), idesc, (first && kb2 == 0 && kk == 0) ? 0u : 1u);
-            umma_commit(&w_empty[st]);
-            if (++st == kStages) {
-              st = 0;
-              ph ^= 1u;
-            }
+          }
+          umma_commit(&w_empty[st]);
+          if (++st == kStages) {
+            st = 0;
+            ph ^= 1u;
           }
         }
         umma_commit(p_free);
