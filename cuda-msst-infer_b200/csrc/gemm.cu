@@ -929,14 +929,17 @@ __global__ void __launch_bounds__(320, 1)
         for (int kb = 0; kb < nkb; kb += 2) {
           if (!mbar_wait(&w_full[st], ph, kErrTimeoutTmaFull, abort_flag)) return false;
           tc_fence_after();
+          // descriptors of the stage's first k-step; each further 16-element k-step is
+          // +32 bytes (+2 in the start-address field), the second block +16 KB
+          const uint64_t da = sw128_desc(smem_u32(sX + kb * kBlock), 16, 1024);
+          const uint64_t db = sw128_desc(smem_u32(sW + st * kStage), 16, 1024);
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const uint32_t a0 = smem_u32(sX + (kb + h) * kBlock), b0 = smem_u32(sW + st * kStage + h * kBlock);
+          for (int h = 0; h < 2; ++h)
 #pragma unroll
-            for (int kk = 0; kk < kBK / 16; ++kk)
-              umma_f16_ss(tS, sw128_desc(a0 + kk * 32, 16, 1024), sw128_desc(b0 + kk * 32, 16, 1024), idesc,
-                          (kb | h | kk) != 0 ? 1u : 0u);
-          }
+            for (int kk = 0; kk < kBK / 16; ++kk) {
+              const uint64_t off = (uint64_t)(h * (kBlock >> 4) + kk * 2);
+              umma_f16_ss(tS, da + off, db + off, idesc, (kb | h | kk) != 0 ? 1u : 0u);
+            }
           umma_commit(&w_empty[st]);
           if (++st == kStages) {
             st = 0;
@@ -953,14 +956,16 @@ __global__ void __launch_bounds__(320, 1)
         for (int n3 = 0; n3 < nn; ++n3) {
           if (!mbar_wait(&w_full[st], ph, kErrTimeoutTmaFull, abort_flag)) return false;
           tc_fence_after();
+          const uint64_t da = sw128_desc(smem_u32(sP), 16, 1024);
+          const uint64_t db = sw128_desc(smem_u32(sW + st * kStage), 16, 1024);
+          const uint32_t dO = tO + (uint32_t)(n3 * kBM);
 #pragma unroll
-          for (int kb2 = 0; kb2 < kBH / kBK; ++kb2) {
-            const uint32_t a0 = smem_u32(sP + kb2 * kBlock), b0 = smem_u32(sW + st * kStage + kb2 * kBlock);
+          for (int kb2 = 0; kb2 < kBH / kBK; ++kb2)
 #pragma unroll
-            for (int kk = 0; kk < kBK / 16; ++kk)
-              umma_f16_ss(tO + (uint32_t)(n3 * kBM), sw128_desc(a0 + kk * 32, 16, 1024),
-                          sw128_desc(b0 + kk * 32, 16, 1024), idesc, (first && kb2 == 0 && kk == 0) ? 0u : 1u);
-          }
+            for (int kk = 0; kk < kBK / 16; ++kk) {
+              const uint64_t off = (uint64_t)(kb2 * (kBlock >> 4) + kk * 2);
+              umma_f16_ss(dO, da + off, db + off, idesc, (first && kb2 == 0 && kk == 0) ? 0u : 1u);
+            }
           umma_commit(&w_empty[st]);
           if (++st == kStages) {
             st = 0;
