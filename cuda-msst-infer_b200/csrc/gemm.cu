@@ -847,7 +847,6 @@ __global__ void __launch_bounds__(320, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nkb = p.D / kBK;      // k-blocks of S
-  const int nn = p.D / kBM;       // 128-column pieces of O
   const int J = p.H / kBH;        // hidden chunks
   const int ntiles = (p.m + kBM - 1) / kBM;
   if (threadIdx.x == 0) {
@@ -910,7 +909,11 @@ __global__ void __launch_bounds__(320, 1)
         for (int j = 0; ok && j < J; ++j) {
           if (j + 1 < J)
             for (int kb = 0; ok && kb < nkb; kb += 2) ok = load_w(&map_w1, kb * kBK, (j + 1) * kBH, kBK, 0);
-          for (int n3 = 0; ok && n3 < nn; ++n3) ok = load_w(&map_w2, j * kBH, n3 * kBM, kBK, 0);
+          // O stages: each 256-row piece of W2 per 64-column hidden half (two 128-row
+          // boxes), then a last 128-row piece with both hidden halves
+          for (int r = 0; ok && r < p.D / 256; ++r)
+            for (int kb2 = 0; ok && kb2 < kBH / kBK; ++kb2) ok = load_w(&map_w2, j * kBH + kb2 * kBK, r * 256, 0, kBM);
+          if (ok && p.D % 256 != 0) ok = load_w(&map_w2, j * kBH, (p.D / 256) * 256, kBK, 0);
         }
       }
     }
@@ -918,6 +921,7 @@ __global__ void __launch_bounds__(320, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_f16(kIsBf16, 128, 0);
+      const uint32_t idesc256 = umma_idesc_f16(kIsBf16, 256, 0);
       const uint32_t tS = tmem, tO = tmem + 128;
       int st = 0;
       uint32_t ph = 0;
@@ -953,12 +957,31 @@ __global__ void __launch_bounds__(320, 1)
       auto issue_o = [&](bool first) -> bool {
         if (!mbar_wait(p_full, pc & 1, kErrTimeoutFfnP, abort_flag)) return false;
         tc_fence_after();
-        for (int n3 = 0; n3 < nn; ++n3) {
+        const uint64_t da = sw128_desc(smem_u32(sP), 16, 1024);
+        // 256-row pieces: N = 256 MMAs over one hidden half per stage
+        for (int r = 0; r < p.D / 256; ++r) {
+          for (int kb2 = 0; kb2 < kBH / kBK; ++kb2) {
+            if (!mbar_wait(&w_full[st], ph, kErrTimeoutTmaFull, abort_flag)) return false;
+            tc_fence_after();
+            const uint64_t db = sw128_desc(smem_u32(sW + st * kStage), 16, 1024);
+            const uint32_t dO = tO + (uint32_t)(r * 256);
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk)
+              umma_f16_ss(dO, da + (uint64_t)(kb2 * (kBlock >> 4) + kk * 2), db + (uint64_t)(kk * 2), idesc256,
+                          (first && kb2 == 0 && kk == 0) ? 0u : 1u);
+            umma_commit(&w_empty[st]);
+            if (++st == kStages) {
+              st = 0;
+              ph ^= 1u;
+            }
+          }
+        }
+        // last 128-row piece: N = 128 over both hidden halves in one stage
+        if (p.D % 256 != 0) {
           if (!mbar_wait(&w_full[st], ph, kErrTimeoutTmaFull, abort_flag)) return false;
           tc_fence_after();
-          const uint64_t da = sw128_desc(smem_u32(sP), 16, 1024);
           const uint64_t db = sw128_desc(smem_u32(sW + st * kStage), 16, 1024);
-          const uint32_t dO = tO + (uint32_t)(n3 * kBM);
+          const uint32_t dO = tO + (uint32_t)((p.D / 256) * 256);
 #pragma unroll
           for (int kb2 = 0; kb2 < kBH / kBK; ++kb2)
 #pragma unroll
