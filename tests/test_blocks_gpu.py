@@ -158,6 +158,29 @@ def test_attn_and_ffn_block_vs_oracle(cuda, tmp_path_factory):
     m.close()
 
 
+@pytest.mark.parametrize("dim", [128, 256, 384])
+def test_ffn_block_large_vs_oracle(cuda, tmp_path_factory, dim):
+    """Feed-forward block at M = 801 x 60 = 48060 rows (376 row tiles, several per CTA of
+    the fused kernel at dims <= 384)."""
+    torch = cuda
+    import oracle
+    from msst_b200 import Model
+
+    path, cfg, sd = _model(tmp_path_factory, "mbr", dict(depth=1, dim=dim), 17 + dim)
+    om = oracle.Model(cfg, sd)
+    m = Model(path, 0, "fp16")
+    B, T, nb, D = 1, 801, m.info["num_bands"], m.info["dim"]
+    rng = np.random.default_rng(dim)
+    x = rng.standard_normal((B, T, nb, D)).astype(np.float32)
+    xt = torch.from_numpy(x.copy()).cuda()
+    m.ffn_block(0, "time", 0, xt)
+    y = xt.cpu().numpy()
+    xr = np.ascontiguousarray(x.transpose(0, 2, 1, 3)).reshape(B * nb, T, D)
+    r = (xr + om.ff_block(xr, "layers.0.0.layers.0.1")).reshape(B, nb, T, D).transpose(0, 2, 1, 3)
+    assert rel_l2(y, r) < 3e-3
+    m.close()
+
+
 def _spec_cufft(om, audio):
     """The oracle STFT in the library's cuFFT R2C layout: [B*C*T, nbins, 2]."""
     import oracle
