@@ -523,13 +523,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <typename T>
 cudaError_t launch_t(const CUtensorMap& m, const AttnParams& p, int num_sms, cudaStream_t s) {
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(attention_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)kAttnSmem);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static std::atomic<unsigned long long> configured{0};
+  cudaError_t e = ensure_smem_limit(attention_kernel<T>, (int)kAttnSmem, configured);
+  if (e != cudaSuccess) return e;
+
   const int grid = p.total_items < num_sms ? p.total_items : num_sms;
   if (grid <= 0) return cudaSuccess;
   // algorithmic cost: QK^T and PV of every sequence (4 L^2 d FLOPs per head), Q/K/V

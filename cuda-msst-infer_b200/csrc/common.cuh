@@ -9,6 +9,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 namespace msst {
 
 // ---------------------------------------------------------------------------
@@ -79,6 +81,21 @@ class LaunchScope {
   long long slot_;
   cudaStream_t stream_;
 };
+
+// Host: raise a kernel's dynamic shared-memory limit on the current device.  The
+// attribute is per device, so `done` keeps one bit per device; after the first call
+// on a device this costs a cudaGetDevice and an atomic load.
+template <typename K>
+inline cudaError_t ensure_smem_limit(K kern, int bytes, std::atomic<unsigned long long>& done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
+}
 
 // ---------------------------------------------------------------------------
 // mbarrier

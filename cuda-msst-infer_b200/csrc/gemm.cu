@@ -686,12 +686,9 @@ cudaError_t launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
                        int num_sms, cudaStream_t stream) {
   using Cfg = GemmCfg<BN, EPI>;
   auto kern = gemm_kernel<BN, EPI, T>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::kSmemBytes);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static std::atomic<unsigned long long> configured{0};
+  cudaError_t e = ensure_smem_limit(kern, (int)Cfg::kSmemBytes, configured);
+  if (e != cudaSuccess) return e;
   const int grid = p.total_tiles < num_sms ? p.total_tiles : num_sms;
   if (grid <= 0) return cudaSuccess;
   const GemmCost cost = gemm_cost(p, EPI, (int)sizeof(T));
@@ -707,7 +704,8 @@ cudaError_t launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUte
                         cudaStream_t stream) {
   using Cfg = PairCfg<BN, EPI>;
   auto kern = gemm_pair_kernel<BN, EPI, T>;
-  static int max_pairs = 0;
+  // co-resident pairs: the same for every B200 of the process, so cached once
+  static std::atomic<int> max_pairs{0};
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -719,17 +717,19 @@ cudaError_t launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUte
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (max_pairs == 0) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::kSmemBytes);
-    if (e != cudaSuccess) return e;
+  static std::atomic<unsigned long long> configured{0};
+  cudaError_t e = ensure_smem_limit(kern, (int)Cfg::kSmemBytes, configured);
+  if (e != cudaSuccess) return e;
+  if (max_pairs.load() == 0) {
     cfg.gridDim = dim3(2 * 148, 1, 1);
     int n = 0;
     e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
     if (e != cudaSuccess) return e;
     if (n < 1) return cudaErrorInvalidConfiguration;
-    max_pairs = n;
+    max_pairs.store(n);
   }
-  const int pairs = pp.total_tiles < max_pairs ? pp.total_tiles : max_pairs;
+  const int mp = max_pairs.load();
+  const int pairs = pp.total_tiles < mp ? pp.total_tiles : mp;
   if (pairs <= 0) return cudaSuccess;
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   const GemmCost cost = gemm_cost(pp, EPI, (int)sizeof(T));
@@ -1167,12 +1167,9 @@ cudaError_t launch_ffn_fused(const CUtensorMap& map_xn, const CUtensorMap& map_w
     return cudaErrorInvalidValue;
   if (p.m == 0) return cudaSuccess;
   auto kern = bf16 ? ffn_fused_kernel<__nv_bfloat16> : ffn_fused_kernel<__half>;
-  static bool configured[2] = {false, false};
-  if (!configured[bf16 ? 1 : 0]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ffn::kSmem);
-    if (e != cudaSuccess) return e;
-    configured[bf16 ? 1 : 0] = true;
-  }
+  static std::atomic<unsigned long long> configured[2];
+  cudaError_t e = ensure_smem_limit(kern, (int)ffn::kSmem, configured[bf16 ? 1 : 0]);
+  if (e != cudaSuccess) return e;
   const int ntiles = (p.m + ffn::kBM - 1) / ffn::kBM;
   const int grid = ntiles < num_sms ? ntiles : num_sms;
   // algorithmic cost: both GEMMs; bytes = xn, W1, W2 read once, x read and written once

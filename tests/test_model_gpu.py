@@ -218,6 +218,24 @@ def test_dim512_vs_oracle(cuda, tmp_path_factory, kind, prec):
     m.close()
 
 
+def test_two_devices_one_process(cuda, small_models):
+    """Models on two GPUs of one process: every launcher configures its kernel's
+    shared-memory limit per device, and the two devices give identical outputs."""
+    torch = cuda
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from msst_b200 import Model, synth
+
+    path, _, _, _ = small_models["mbr_small"]
+    audio = synth.make_audio(22050, 2, 4)[None]
+    ys = []
+    for dev in (0, 1):
+        m = Model(path, dev, "bf16")
+        ys.append(m.forward(torch.from_numpy(audio).to(f"cuda:{dev}")).cpu().numpy())
+        m.close()
+    np.testing.assert_array_equal(ys[0], ys[1])
+
+
 def test_device_error_flag_clear(cuda):
     from msst_b200 import device_error
 
