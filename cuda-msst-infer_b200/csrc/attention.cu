@@ -55,7 +55,7 @@ struct PairGeom {
 
 __device__ __forceinline__ PairGeom pair_geom(const AttnParams& p, int item) {
   PairGeom g;
-  if (p.mode == 0) {
+  if (p.mode != 1) {
     const int pairs = (p.q_tiles + 1) >> 1;
     const int qp = item % pairs;
     const int sh = item / pairs;
@@ -65,7 +65,7 @@ __device__ __forceinline__ PairGeom pair_geom(const AttnParams& p, int item) {
     g.f = s - g.b * p.F;
     g.t0a = qp * 256;
     g.has_b = 2 * qp + 1 < p.q_tiles;
-    g.steps = p.q_tiles;
+    g.steps = p.kv_tiles;
     g.r0a = g.rows = 0;
   } else {
     g.head = item % p.heads;
@@ -80,7 +80,7 @@ __device__ __forceinline__ PairGeom pair_geom(const AttnParams& p, int item) {
 }
 
 // Does query tile w (0 = a, 1 = b) consume K/V step j?
-__device__ __forceinline__ bool uses(const AttnParams& p, int w, int j) { return p.mode == 0 ? true : (j == w); }
+__device__ __forceinline__ bool uses(const AttnParams& p, int w, int j) { return p.mode != 1 ? true : (j == w); }
 
 // ---------------------------------------------------------------------------
 // One softmax pass over a 128-column S row held in TMEM (4 chunks of 32
@@ -208,7 +208,8 @@ __device__ __forceinline__ void row_pass(uint32_t sAddr, int c_lo, int c_hi, int
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
-    attention_kernel(const __grid_constant__ CUtensorMap qkv, const __grid_constant__ AttnParams p) {
+    attention_kernel(const __grid_constant__ CUtensorMap qkv, const __grid_constant__ CUtensorMap kmap,
+                     const __grid_constant__ CUtensorMap vmap, const __grid_constant__ AttnParams p) {
   constexpr uint32_t kIsBf16 = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -241,7 +242,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort_flag = 0;
     mbar_fence_init();
   }
-  if (warp == 0 && lane == 0) tma_prefetch_desc(&qkv);
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&qkv);
+    tma_prefetch_desc(&kmap);
+    tma_prefetch_desc(&vmap);
+  }
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
     tc_fence_before();
@@ -249,7 +254,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int HD = p.heads * 64;
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -261,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait<false>(q_empty, (pc & 1) ^ 1, kErrTimeoutAttnQ, abort_flag)) break;
         mbar_arrive_expect_tx(q_full, (g.has_b ? 2 : 1) * kTileBytes);
         const int xq = g.head * 64;
-        if (p.mode == 0) {
+        if (p.mode != 1) {
           tma_load_4d(sQ, &qkv, q_full, xq, g.f, g.t0a, g.b);
           if (g.has_b) tma_load_4d(sQ + kTileBytes, &qkv, q_full, xq, g.f, g.t0a + 128, g.b);
         } else {
@@ -272,7 +276,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_load_4d(sQ + w * kTileBytes + k * slot_bytes, &qkv, q_full, xq,
                           (g.r0a + w * g.rows + k) * p.seq_len, 0, 0);
         }
-        const int xk = HD + g.head * 64, xv = 2 * HD + g.head * 64;
+        const int xk = p.k_col + g.head * 64, xv = p.v_col + g.head * 64;
         for (int j = 0; j < g.steps; ++j, ++kvc) {
           const int st = kvc % kKvStages;
           if (!mbar_wait<false>(&kv_empty[st], ((kvc / kKvStages) & 1) ^ 1, kErrTimeoutAttnKV, abort_flag)) {
@@ -281,15 +285,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           mbar_arrive_expect_tx(&kv_full[st], 2 * kTileBytes);
           uint8_t* dk = sKV + st * 2 * kTileBytes;
-          if (p.mode == 0) {
-            tma_load_4d(dk, &qkv, &kv_full[st], xk, g.f, j * 128, g.b);
-            tma_load_4d(dk + kTileBytes, &qkv, &kv_full[st], xv, g.f, j * 128, g.b);
+          if (p.mode != 1) {
+            tma_load_4d(dk, &kmap, &kv_full[st], xk, g.f, j * 128, g.b);
+            tma_load_4d(dk + kTileBytes, &vmap, &kv_full[st], xv, g.f, j * 128, g.b);
           } else {
             const uint32_t slot_bytes = (128u / (uint32_t)g.rows) * 128u;
             for (int k = 0; k < g.rows; ++k) {
               const int r0 = (g.r0a + j * g.rows + k) * p.seq_len;
-              tma_load_4d(dk + k * slot_bytes, &qkv, &kv_full[st], xk, r0, 0, 0);
-              tma_load_4d(dk + kTileBytes + k * slot_bytes, &qkv, &kv_full[st], xv, r0, 0, 0);
+              tma_load_4d(dk + k * slot_bytes, &kmap, &kv_full[st], xk, r0, 0, 0);
+              tma_load_4d(dk + kTileBytes + k * slot_bytes, &vmap, &kv_full[st], xv, r0, 0, 0);
             }
           }
         }
@@ -387,7 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool valid;
       long long token;
       int lo = 0, hi_seq = 0;
-      if (p.mode == 0) {
+      if (p.mode != 1) {
         const int t = g.t0a + w * 128 + row;
         valid = t < p.T;
         token = ((long long)g.b * p.T + t) * p.F + g.f;
@@ -413,9 +417,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         // valid key columns [klo, khi) of this tile for this row; warp-uniform chunk range
         int klo, khi;
-        if (p.mode == 0) {
+        if (p.mode != 1) {
           klo = 0;
-          khi = min(128, p.seq_len - j * 128);
+          khi = min(128, p.kv_len - j * 128);
         } else {
           klo = lo;
           khi = hi_seq;
@@ -434,7 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             float amax = -INFINITY;
             if (used == 0) {
               float m0 = -INFINITY;
-              if (p.mode == 0)
+              if (p.mode != 1)
                 row_pass<T, 1, true>(sAddr, c_lo, c_hi, c_full, klo, khi, c, 0.f, amax, sum2, pAddr, &m0);
               else
                 row_pass<T, 1, true, true>(sAddr, c_lo, c_hi, c_full, klo, khi, c, 0.f, amax, sum2, pAddr, &m0);
@@ -492,7 +496,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (warp_active) {
         float scale = l > 0.f ? 1.f / l : 0.f;
         if (valid && p.gates != nullptr) scale *= __ldg(p.gates + token * p.heads + g.head);
-        uint4* out = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.out) + token * HD + g.head * 64);
+        uint4* out = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.out) + token * p.out_ld + g.head * 64);
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           uint32_t r[32];
@@ -501,6 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (valid) {
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
+              if (8 * (4 * h + u) >= p.d_out) break;
               float v[8];
 #pragma unroll
               for (int k = 0; k < 8; ++k) v[k] = __uint_as_float(r[8 * u + k]) * scale;
@@ -522,36 +527,69 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <typename T>
-cudaError_t launch_t(const CUtensorMap& m, const AttnParams& p, int num_sms, cudaStream_t s) {
+cudaError_t launch_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const AttnParams& p,
+                     int num_sms, cudaStream_t s) {
   static std::atomic<unsigned long long> configured{0};
   cudaError_t e = ensure_smem_limit(attention_kernel<T>, (int)kAttnSmem, configured);
   if (e != cudaSuccess) return e;
 
   const int grid = p.total_items < num_sms ? p.total_items : num_sms;
   if (grid <= 0) return cudaSuccess;
-  // algorithmic cost: QK^T and PV of every sequence (4 L^2 d FLOPs per head), Q/K/V
-  // and the gates read once, the merged heads written once
-  const double seqs = (double)p.num_tokens / p.seq_len;
-  const double flop = 4.0 * seqs * p.heads * (double)p.seq_len * p.seq_len * 64.0;
-  const double bytes = (double)p.num_tokens * p.heads * (4.0 * 64.0 * sizeof(T) + (p.gates ? 4.0 : 0.0));
-  LaunchScope scope(p.mode == 0 ? "attention_time" : "attention_band", flop, bytes, s);
-  attention_kernel<T><<<grid, kThreads, kAttnSmem, s>>>(m, p);
+  // algorithmic cost: QK^T and PV of every query row against its sequence's keys
+  // (4 Nq Nk d FLOPs per head), Q/K/V and the gates read once, the output written once
+  const double d = p.mode == 2 ? p.d_out : 64.0;
+  const double qrows = (double)p.num_tokens * p.heads;                    // query rows x heads
+  const double krows = qrows / p.seq_len * p.kv_len;                      // key rows x heads
+  const double flop = 4.0 * qrows * p.kv_len * d;
+  const double bytes = (2.0 * qrows + 2.0 * krows) * d * sizeof(T) + (p.gates ? 4.0 * qrows : 0.0);
+  LaunchScope scope(p.mode == 0 ? "attention_time" : (p.mode == 1 ? "attention_band" : "attention_sdpa"), flop,
+                    bytes, s);
+  attention_kernel<T><<<grid, kThreads, kAttnSmem, s>>>(mq, mk, mv, p);
   return cudaGetLastError();
+}
+
+cudaError_t launch_checked(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const AttnParams& a,
+                           int bf16, int num_sms, cudaStream_t stream) {
+  if (a.q_tiles < 1) return cudaSuccess;
+  return bf16 ? launch_t<__nv_bfloat16>(mq, mk, mv, a, num_sms, stream)
+              : launch_t<__half>(mq, mk, mv, a, num_sms, stream);
 }
 
 }  // namespace
 
 cudaError_t launch_attention(const CUtensorMap& qkv_map, const AttnParams& p, int bf16, int num_sms,
                              cudaStream_t stream) {
+  if (p.mode != 0 && p.mode != 1) return cudaErrorInvalidValue;
   if (p.mode == 1 && (p.seq_len < 1 || p.seq_len > 128 || p.seqs_per_tile != 128 / attn_band_slot(p.seq_len)))
     return cudaErrorInvalidValue;
-  if (p.q_tiles < 1) return cudaSuccess;
   AttnParams a = p;
   const long long pairs = (p.q_tiles + 1) / 2;
   const long long items = p.mode == 0 ? (long long)p.B * p.F * p.heads * pairs : pairs * p.heads;
   if (items > 0x7fffffffLL) return cudaErrorInvalidValue;
   a.total_items = (int)items;
-  return bf16 ? launch_t<__nv_bfloat16>(qkv_map, a, num_sms, stream) : launch_t<__half>(qkv_map, a, num_sms, stream);
+  a.kv_len = p.seq_len;
+  a.kv_tiles = p.q_tiles;
+  a.k_col = p.heads * 64;
+  a.v_col = 2 * p.heads * 64;
+  a.out_ld = (long long)p.heads * 64;
+  a.d_out = 64;
+  return launch_checked(qkv_map, qkv_map, qkv_map, a, bf16, num_sms, stream);
+}
+
+cudaError_t launch_sdpa(const CUtensorMap& q_map, const CUtensorMap& k_map, const CUtensorMap& v_map,
+                        const AttnParams& p, int bf16, int num_sms, cudaStream_t stream) {
+  if (p.mode != 2 || p.F != 1 || p.heads != 1 || p.gates != nullptr) return cudaErrorInvalidValue;
+  if (p.B < 1 || p.T < 1 || p.kv_len < 1 || p.seq_len != p.T) return cudaErrorInvalidValue;
+  if (p.d_out < 8 || p.d_out > 64 || p.d_out % 8 != 0 || p.out_ld < p.d_out || p.out_ld % 8 != 0)
+    return cudaErrorInvalidValue;
+  if (p.q_tiles != (p.T + 127) / 128 || p.kv_tiles != (p.kv_len + 127) / 128) return cudaErrorInvalidValue;
+  if ((long long)p.B * p.T != p.num_tokens) return cudaErrorInvalidValue;
+  AttnParams a = p;
+  const long long items = (long long)p.B * ((p.q_tiles + 1) / 2);
+  if (items > 0x7fffffffLL) return cudaErrorInvalidValue;
+  a.total_items = (int)items;
+  a.k_col = a.v_col = 0;
+  return launch_checked(q_map, k_map, v_map, a, bf16, num_sms, stream);
 }
 
 MSST_DEFINE_ERROR_ACCESSOR(attention_device_error)

@@ -266,6 +266,77 @@ int msst_attention(const void* qkv16, int B, int T, int F, int heads, int axis, 
   });
 }
 
+int msst_layernorm(const float* x, long long rows, int D, const float* gamma, const float* beta, float eps,
+                   int out_dtype, void* out, void* stream) {
+  return guarded([&] {
+    MSST_REQUIRE(out_dtype == MSST_F16 || out_dtype == MSST_BF16 || out_dtype == MSST_F32,
+                 "out_dtype must be MSST_F16, MSST_BF16 or MSST_F32");
+    MSST_REQUIRE(x && gamma && beta && out && rows >= 0, "null argument");
+    MSST_REQUIRE(D >= 4 && D % 4 == 0 && D <= 1024, "D must be a multiple of 4 and <= 1024");
+    MSST_REQUIRE(eps >= 0.f, "eps must be >= 0");
+    check_align(x, "x");
+    check_align(gamma, "gamma");
+    check_align(beta, "beta");
+    check_align(out, "out");
+    if (rows == 0) return;
+    use_device_of(x);
+    msst::LayerNormArgs a{};
+    a.x = x;
+    a.rows = rows;
+    a.D = D;
+    a.gamma = gamma;
+    a.beta = beta;
+    a.eps = eps;
+    a.out = out;
+    a.out_kind = out_dtype == MSST_F32 ? 0 : (out_dtype == MSST_F16 ? 1 : 2);
+    MSST_CUDA(msst::launch_layernorm(a, as_stream(stream)));
+  });
+}
+
+int msst_sdpa(const void* q, const void* k, const void* v, int B, int H, int Nq, int Nk, int head_dim, float scale,
+              int dtype, void* out, void* stream) {
+  return guarded([&] {
+    check_dtype(dtype);
+    MSST_REQUIRE(q && k && v && out, "null argument");
+    MSST_REQUIRE(B > 0 && H > 0 && Nq > 0 && Nk > 0, "bad shape");
+    MSST_REQUIRE(head_dim >= 8 && head_dim <= 64 && head_dim % 8 == 0, "head_dim must be a multiple of 8, <= 64");
+    MSST_REQUIRE(std::isfinite(scale), "scale must be finite");
+    const long long BH = (long long)B * H;
+    MSST_REQUIRE(BH * Nq < (1LL << 31) && BH * Nk < (1LL << 31), "too many rows");
+    check_align(q, "q");
+    check_align(k, "k");
+    check_align(v, "v");
+    check_align(out, "out");
+    use_device_of(q);
+    const float s = scale == 0.f ? 1.0f / std::sqrt((float)head_dim) : scale;
+    msst::AttnParams a{};
+    a.mode = 2;
+    a.B = (int)BH;
+    a.T = Nq;
+    a.F = 1;
+    a.heads = 1;
+    a.seq_len = Nq;
+    a.q_tiles = (Nq + 127) / 128;
+    a.num_tokens = (int)(BH * Nq);
+    a.kv_len = Nk;
+    a.kv_tiles = (Nk + 127) / 128;
+    a.out_ld = head_dim;
+    a.d_out = head_dim;
+    a.scale_log2 = s * 1.4426950408889634f;
+    a.gates = nullptr;
+    a.out = out;
+    // {d, 1, N, B*H} with box {64, 1, 128, 1}: columns d..63 and rows past N read as zero
+    auto seq_map = [&](const void* base, int n) {
+      const uint64_t dims[4] = {(uint64_t)head_dim, 1, (uint64_t)n, (uint64_t)BH};
+      const uint64_t str[3] = {(uint64_t)head_dim * 2, (uint64_t)head_dim * 2, (uint64_t)head_dim * 2 * n};
+      const uint32_t box[4] = {64, 1, 128, 1};
+      return msst::make_tensor_map(base, 4, dims, str, box);
+    };
+    const CUtensorMap mq = seq_map(q, Nq), mk = seq_map(k, Nk), mv = seq_map(v, Nk);
+    MSST_CUDA(msst::launch_sdpa(mq, mk, mv, a, dtype, sm_count(), as_stream(stream)));
+  });
+}
+
 int msst_grouped_gemm(int num_groups, const msst_gemm_group* groups, const void* x, long long x_rows, long long ldx,
                       const void* w, long long w_rows, long long ldw, int epilogue, int act, int dtype, void* out,
                       long long out_rows, long long ldo, void* stream) {

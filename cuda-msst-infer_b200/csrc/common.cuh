@@ -10,6 +10,7 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <type_traits>
 
 namespace msst {
 

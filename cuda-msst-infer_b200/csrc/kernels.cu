@@ -93,6 +93,78 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(RmsNormArgs a) {
   }
 }
 
+// ---------------------------------------------------------------- LayerNorm
+// One warp per row (grid-stride over rows); lane l holds columns 4l + 128k, k < V.
+// Mean first, then the variance of the centred values from registers (the
+// reference's two-pass order, src/ops_norm.cu:160-176).
+template <typename OutT, int V>
+__global__ void __launch_bounds__(256) layernorm_kernel(LayerNormArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int D = a.D;
+  const float invD = 1.0f / (float)D;
+  const long long warps_total = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < a.rows; r += warps_total) {
+    const float4* xr = reinterpret_cast<const float4*>(a.x + r * D);
+    float4 v[V];
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      const int c4 = lane + 32 * k;
+      v[k] = c4 * 4 < D ? __ldg(xr + c4) : make_float4(0.f, 0.f, 0.f, 0.f);
+      s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+    }
+    const float mean = warp_sum(s) * invD;
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      if ((lane + 32 * k) * 4 >= D) continue;
+      v[k].x -= mean;
+      v[k].y -= mean;
+      v[k].z -= mean;
+      v[k].w -= mean;
+      ss += (v[k].x * v[k].x + v[k].y * v[k].y) + (v[k].z * v[k].z + v[k].w * v[k].w);
+    }
+    const float inv = rsqrtf(warp_sum(ss) * invD + a.eps);
+    const float4* g4 = reinterpret_cast<const float4*>(a.gamma);
+    const float4* b4 = reinterpret_cast<const float4*>(a.beta);
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      const int c4 = lane + 32 * k;
+      if (c4 * 4 >= D) continue;
+      const float4 g = __ldg(g4 + c4), b = __ldg(b4 + c4);
+      const float4 y = make_float4(v[k].x * inv * g.x + b.x, v[k].y * inv * g.y + b.y, v[k].z * inv * g.z + b.z,
+                                   v[k].w * inv * g.w + b.w);
+      if constexpr (std::is_same<OutT, float>::value) {
+        reinterpret_cast<float4*>(a.out)[r * (D / 4) + c4] = y;
+      } else {
+        reinterpret_cast<uint2*>(a.out)[r * (D / 4) + c4] = make_uint2(pack2<OutT>(y.x, y.y), pack2<OutT>(y.z, y.w));
+      }
+    }
+  }
+}
+
+template <typename OutT>
+cudaError_t layernorm_dispatch(const LayerNormArgs& a, unsigned blocks, cudaStream_t s) {
+  switch ((a.D + 127) / 128) {
+#define MSST_LN_CASE(v) \
+  case v:               \
+    layernorm_kernel<OutT, v><<<blocks, 256, 0, s>>>(a); \
+    break;
+    MSST_LN_CASE(1)
+    MSST_LN_CASE(2)
+    MSST_LN_CASE(3)
+    MSST_LN_CASE(4)
+    MSST_LN_CASE(5)
+    MSST_LN_CASE(6)
+    MSST_LN_CASE(7)
+    MSST_LN_CASE(8)
+#undef MSST_LN_CASE
+    default:
+      return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
 // RMSNorm + 8 attention-gate projections with the gate weights held in registers
 // (8 heads x 4V columns per lane, loaded once per persistent warp) and the eight
 // partial dot products reduced by a butterfly transpose-reduce: 4 + 2 + 1
@@ -587,6 +659,18 @@ cudaError_t launch_rmsnorm(const RmsNormArgs& a, int bf16, cudaStream_t s) {
   if (a.D % 128 != 0 || a.D > 1024 || (a.band_major && a.F <= 0) || (a.wg && a.heads > 32))
     return cudaErrorInvalidValue;
   return bf16 ? rmsnorm_dispatch<__nv_bfloat16>(a, s) : rmsnorm_dispatch<__half>(a, s);
+}
+
+cudaError_t launch_layernorm(const LayerNormArgs& a, cudaStream_t s) {
+  if (a.D < 4 || a.D % 4 != 0 || a.D > 1024 || a.out_kind < 0 || a.out_kind > 2) return cudaErrorInvalidValue;
+  if (a.rows <= 0) return cudaSuccess;
+  long long blocks = (a.rows + 7) / 8;
+  if (blocks > 148LL * 16) blocks = 148LL * 16;
+  const double out_bytes = a.out_kind == 0 ? 4.0 : 2.0;
+  LaunchScope scope("layernorm", 0.0, (double)a.rows * a.D * (4.0 + out_bytes), s);
+  if (a.out_kind == 0) return layernorm_dispatch<float>(a, (unsigned)blocks, s);
+  if (a.out_kind == 1) return layernorm_dispatch<__half>(a, (unsigned)blocks, s);
+  return layernorm_dispatch<__nv_bfloat16>(a, (unsigned)blocks, s);
 }
 
 cudaError_t launch_band_input(const BandInArgs& a, int bf16, cudaStream_t s) {

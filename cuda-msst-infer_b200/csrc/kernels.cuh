@@ -35,6 +35,22 @@ struct RmsNormArgs {
 };
 cudaError_t launch_rmsnorm(const RmsNormArgs& a, int bf16, cudaStream_t s);
 
+// LayerNorm over the last dimension (ops::layer_norm, src/ops_norm.cu:150-182,496-533):
+// y = (x - mean) * rsqrt(var + eps) * gamma + beta, var the biased variance,
+// x fp32 [rows, D] (D % 4 == 0, D <= 1024) -> out [rows, D] as fp32 (out_kind 0),
+// fp16 (1) or bf16 (2).  One warp per row, the row held in registers.
+struct LayerNormArgs {
+  const float* x;
+  long long rows;
+  int D;
+  const float* gamma;
+  const float* beta;
+  float eps;
+  void* out;
+  int out_kind;
+};
+cudaError_t launch_layernorm(const LayerNormArgs& a, cudaStream_t s);
+
 // Band gather + per-band RMSNorm + 16-bit cast + zero K-padding: builds the A
 // operand of the grouped band-split GEMM from the STFT (cuFFT R2C layout
 // [Bc*C*T, nbins] complex).  Row bt = b*T + t; band j occupies columns

@@ -19,7 +19,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "lib", "libmsst_b200.so")
 
 MSST_OK, MSST_ERR_INVALID, MSST_ERR_CUDA, MSST_ERR_IO, MSST_ERR_UNSUPPORTED, MSST_ERR_DEVICE = range(6)
-F16, BF16 = 0, 1
+F16, BF16, F32 = 0, 1, 2
 EPI = {"store16": 0, "resid32": 1, "store32": 2, "glu32": 3}
 ACT = {"none": 0, "gelu": 1, "tanh": 2, "sigmoid": 3}
 AXIS = {"time": 0, "band": 1}
@@ -28,7 +28,7 @@ SEPARATE_FIX_TAIL_PADDING = 1
 EXPORTS = [
     "msst_last_error", "msst_device_error", "msst_version", "msst_kernel_launches", "msst_kernel_timing",
     "msst_kernel_timing_report", "msst_rmsnorm", "msst_gemm", "msst_gemm_qkv_rope",
-    "msst_attention", "msst_grouped_gemm", "msst_band_gather", "msst_mask_apply", "msst_model_band_tables",
+    "msst_attention", "msst_layernorm", "msst_sdpa", "msst_grouped_gemm", "msst_band_gather", "msst_mask_apply", "msst_model_band_tables",
     "msst_roformer_attn_block", "msst_roformer_ffn_block", "msst_model_load", "msst_model_free", "msst_model_get_info", "msst_model_forward",
     "msst_model_masks", "msst_model_transformer", "msst_model_transformer_noalloc", "msst_model_separate", "msst_model_separate_host",
     "msst_model_chunk_plan", "msst_model_forward_chunks", "msst_model_stitch",
@@ -88,6 +88,8 @@ def lib():
     L.msst_gemm.argtypes = [vp, i64, c_int, i64, vp, c_int, vp, c_int, c_int, c_int, vp, i64, vp]
     L.msst_gemm_qkv_rope.argtypes = [vp, i64, c_int, vp, c_int, vp, vp, c_int, c_int, c_int, vp, vp]
     L.msst_attention.argtypes = [vp, c_int, c_int, c_int, c_int, c_int, c_float, vp, c_int, vp, vp]
+    L.msst_layernorm.argtypes = [vp, i64, c_int, vp, vp, c_float, c_int, vp, vp]
+    L.msst_sdpa.argtypes = [vp, vp, vp, c_int, c_int, c_int, c_int, c_int, c_float, c_int, vp, vp]
     L.msst_grouped_gemm.argtypes = [c_int, ctypes.POINTER(GemmGroupC), vp, i64, i64, vp, i64, i64, c_int, c_int,
                                     c_int, vp, i64, i64, vp]
     L.msst_band_gather.argtypes = [vp, c_int, c_int, ctypes.POINTER(BandTables), c_int, vp, i64, vp]
@@ -234,6 +236,35 @@ class ops:
                                    _dtype_code(qkv.dtype), _ptr(out), _stream()))
         return out
 
+    @staticmethod
+    def layer_norm(x, gamma, beta, eps=1e-5, dtype=None):
+        """ops::layer_norm (src/ops_norm.cu:496): x fp32 [..., D] -> [..., D] in `dtype`
+        (torch.float32 by default, as the reference returns; fp16 / bf16 to feed a GEMM)."""
+        torch = _torch()
+        dtype = dtype or torch.float32
+        x = x.contiguous()
+        D = x.shape[-1]
+        out = torch.empty(x.shape, dtype=dtype, device=x.device)
+        code = F32 if dtype == torch.float32 else _dtype_code(dtype)
+        check(lib().msst_layernorm(_ptr(x), x.numel() // D, D, _ptr(gamma.contiguous()), _ptr(beta.contiguous()),
+                                   float(eps), code, _ptr(out), _stream()))
+        return out
+
+    @staticmethod
+    def scaled_dot_product_attention(q, k, v, scale=0.0):
+        """ops::scaled_dot_product_attention (src/ops_attention.cu:522): q [B, H, Nq, d],
+        k / v [B, H, Nk, d], 16-bit, d <= 64; scale 0 -> 1/sqrt(d).  Returns [B, H, Nq, d]."""
+        torch = _torch()
+        B, H, Nq, d = q.shape
+        Nk = k.shape[2]
+        if tuple(k.shape) != (B, H, Nk, d) or tuple(v.shape) != (B, H, Nk, d):
+            raise ValueError("k and v must be [B, H, Nk, d] with q's B, H, d")
+        if k.dtype != q.dtype or v.dtype != q.dtype:
+            raise ValueError("q, k and v must share one 16-bit dtype")
+        out = torch.empty((B, H, Nq, d), dtype=q.dtype, device=q.device)
+        check(lib().msst_sdpa(_ptr(q.contiguous()), _ptr(k.contiguous()), _ptr(v.contiguous()), B, H, Nq, Nk, d,
+                              float(scale), _dtype_code(q.dtype), _ptr(out), _stream()))
+        return out
 
     @staticmethod
     def grouped_gemm(x, w, groups, out, epilogue="store16", act="none", stream=None):

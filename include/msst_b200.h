@@ -16,7 +16,7 @@
  *     fp32; the residual stream and all model inputs/outputs are fp32.
  *   - K (the reduction length) of every GEMM is a multiple of 64; hidden sizes
  *     of the Roformer (dim, heads*64, 4*dim) satisfy this, band inputs are padded.
- *   - head_dim is 64.
+ *   - head_dim is 64 on the Roformer path; msst_sdpa takes head_dim <= 64.
  */
 #ifndef MSST_B200_H
 #define MSST_B200_H
@@ -34,6 +34,7 @@ extern "C" {
 
 #define MSST_F16 0
 #define MSST_BF16 1
+#define MSST_F32 2 /* output type of msst_layernorm only */
 
 /* GEMM epilogues */
 #define MSST_EPI_STORE16 0 /* out16 = act(x W^T + b)                               */
@@ -122,6 +123,23 @@ int msst_gemm_qkv_rope(const void* x, long long rows, int K, const void* w, int 
  * apply_gates_and_merge_heads (src/model_mel_band_roformer.cu:94-163). */
 int msst_attention(const void* qkv16, int B, int T, int F, int heads, int axis, float scale, const float* gates,
                    int dtype, void* out16, void* stream);
+
+/* ---- ops the reference shares with its conv model (HTDemucs' transformer,
+ * src/model_htdemucs.cu:542-659); its linear and linear_gelu calls map to msst_gemm. */
+
+/* LayerNorm over the last dimension, y = (x - mean) * rsqrt(var + eps) * gamma + beta
+ * with the biased variance (replaces ops::layer_norm, src/ops_norm.cu:496-533;
+ * the reference's default eps is 1e-5).  x fp32 [rows, D], D % 4 == 0 and
+ * D <= 1024; out [rows, D] as out_dtype MSST_F32, MSST_F16 or MSST_BF16. */
+int msst_layernorm(const float* x, long long rows, int D, const float* gamma, const float* beta, float eps,
+                   int out_dtype, void* out, void* stream);
+
+/* out = softmax(scale * q k^T) v per (batch, head), non-causal: q [B, H, Nq, d],
+ * k and v [B, H, Nk, d], out [B, H, Nq, d], all 16-bit (dtype), d a multiple of 8
+ * and <= 64; scale 0 selects 1/sqrt(d) (replaces ops::scaled_dot_product_attention,
+ * src/ops_attention.cu:522-599, including its cross-attention form Nq != Nk). */
+int msst_sdpa(const void* q, const void* k, const void* v, int B, int H, int Nq, int Nk, int head_dim, float scale,
+              int dtype, void* out, void* stream);
 
 /* One problem of msst_grouped_gemm: rows [a_row0, a_row0 + m) and columns
  * [a_col0, a_col0 + k) of x times rows [b_row0, b_row0 + n) (same k columns from

@@ -199,33 +199,52 @@ void msst_oracle_rope(float* x, const float* cosv, const float* sinv, int64_t B,
 // Non-causal softmax(scale * Q K^T) V over q,k,v [B,H,N,D] (src/ops_attention.cu:522-599,
 // softmax src/ops_attention.cu:390-452).
 void msst_oracle_attention(const float* q, const float* k, const float* v, float* out, int64_t B,
-                           int64_t H, int64_t N, int64_t D, float scale) {
+                           int64_t H, int64_t N, int64_t Nk, int64_t D, float scale) {
 #pragma omp parallel for schedule(dynamic, 1)
   for (int64_t bh = 0; bh < B * H; ++bh) {
     const float* Q = q + bh * N * D;
-    const float* K = k + bh * N * D;
-    const float* V = v + bh * N * D;
+    const float* K = k + bh * Nk * D;
+    const float* V = v + bh * Nk * D;
     float* O = out + bh * N * D;
-    std::vector<float> s(N);
+    std::vector<float> s(Nk);
     std::vector<double> acc(D);
     for (int64_t i = 0; i < N; ++i) {
       float mx = -INFINITY;
-      for (int64_t j = 0; j < N; ++j) {
+      for (int64_t j = 0; j < Nk; ++j) {
         float d = 0.f;
         for (int64_t c = 0; c < D; ++c) d += Q[i * D + c] * K[j * D + c];
         s[j] = d * scale;
         mx = std::max(mx, s[j]);
       }
       double sum = 0.0;
-      for (int64_t j = 0; j < N; ++j) {
+      for (int64_t j = 0; j < Nk; ++j) {
         s[j] = std::exp(s[j] - mx);
         sum += s[j];
       }
       std::fill(acc.begin(), acc.end(), 0.0);
-      for (int64_t j = 0; j < N; ++j)
+      for (int64_t j = 0; j < Nk; ++j)
         for (int64_t c = 0; c < D; ++c) acc[c] += (double)s[j] * V[j * D + c];
       for (int64_t c = 0; c < D; ++c) O[i * D + c] = (float)(acc[c] / sum);
     }
+  }
+}
+
+// LayerNorm over the last dimension as src/ops_norm.cu:150-182 computes it: mean,
+// then the biased variance of (x - mean), y = (x - mean) * rsqrt(var + eps) * gamma + beta
+// (double accumulation here; the reference sums in fp32).
+void msst_oracle_layernorm(const float* x, const float* gamma, const float* beta, float* out, int64_t rows,
+                           int64_t D, float eps) {
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < rows; ++r) {
+    const float* xr = x + r * D;
+    double s = 0.0;
+    for (int64_t j = 0; j < D; ++j) s += xr[j];
+    const double mean = s / (double)D;
+    double ss = 0.0;
+    for (int64_t j = 0; j < D; ++j) ss += (xr[j] - mean) * (xr[j] - mean);
+    const double inv = 1.0 / std::sqrt(ss / (double)D + (double)eps);
+    float* o = out + r * D;
+    for (int64_t j = 0; j < D; ++j) o[j] = (float)((xr[j] - mean) * inv * gamma[j] + beta[j]);
   }
 }
 

@@ -52,7 +52,8 @@ def lib():
         L.msst_oracle_glu.argtypes = [_f32p, _f32p, i64, i64]
         L.msst_oracle_rope_tables.argtypes = [c_int, c_int, _f32p, _f32p]
         L.msst_oracle_rope.argtypes = [_f32p, _f32p, _f32p, i64, i64, i64, i64]
-        L.msst_oracle_attention.argtypes = [_f32p, _f32p, _f32p, _f32p, i64, i64, i64, i64, c_float]
+        L.msst_oracle_attention.argtypes = [_f32p, _f32p, _f32p, _f32p, i64, i64, i64, i64, i64, c_float]
+        L.msst_oracle_layernorm.argtypes = [_f32p, _f32p, _f32p, _f32p, i64, i64, c_float]
         L.msst_oracle_hann.argtypes = [c_int, _f32p]
         L.msst_oracle_stft.argtypes = [_f32p, i64, i64, c_int, c_int, _f32p, _f32p]
         L.msst_oracle_istft.argtypes = [_f32p, i64, i64, c_int, c_int, _f32p, _f32p]
@@ -127,10 +128,23 @@ def rope(x, cosv, sinv):
 
 
 def attention(q, k, v, scale):
+    """softmax(scale * q k^T) v per (b, h): q [B,H,N,D], k/v [B,H,Nk,D]
+    (ops::scaled_dot_product_attention, src/ops_attention.cu:522-599)."""
     q, k, v = _c(q), _c(k), _c(v)
     B, H, N, D = q.shape
+    Nk = k.shape[2]
+    assert k.shape == (B, H, Nk, D) and v.shape == k.shape
     out = np.empty_like(q)
-    lib().msst_oracle_attention(_p(q), _p(k), _p(v), _p(out), B, H, N, D, float(scale))
+    lib().msst_oracle_attention(_p(q), _p(k), _p(v), _p(out), B, H, N, Nk, D, float(scale))
+    return out
+
+
+def layernorm(x, gamma, beta, eps=1e-5):
+    """ops::layer_norm over the last dimension (src/ops_norm.cu:150-182,496-533)."""
+    x = _c(x)
+    D = x.shape[-1]
+    out = np.empty_like(x)
+    lib().msst_oracle_layernorm(_p(x), _p(_c(gamma)), _p(_c(beta)), _p(out), x.size // D, D, float(eps))
     return out
 
 

@@ -204,6 +204,40 @@ int refh_sdpa(const float* q, const float* k, const float* v, int B, int H, int 
   }
 }
 
+// ops::scaled_dot_product_attention with its own query and key lengths, q [B,H,N,D],
+// k,v [B,H,Nk,D] (the cross-attention form of model_htdemucs.cu:640-650); scale 0
+// selects the op's default 1/sqrt(D) (ops_attention.cu:541-543).
+int refh_sdpa2(const float* q, const float* k, const float* v, int B, int H, int N, int Nk, int D, float scale,
+               int fp16, float* out) {
+  try {
+    bool saved = g_quantize_fp16;
+    g_quantize_fp16 = fp16 != 0;
+    Tensor tq = Tensor::from_cpu_f32(q, {B, H, N, D});
+    Tensor tk = Tensor::from_cpu_f32(k, {B, H, Nk, D});
+    Tensor tv = Tensor::from_cpu_f32(v, {B, H, Nk, D});
+    Tensor o = ops::scaled_dot_product_attention(tq, tk, tv, scale);
+    cudaDeviceSynchronize();
+    g_quantize_fp16 = saved;
+    return copy_out(o, out, (long long)B * H * N * D, nullptr);
+  } catch (const std::exception& e) {
+    return fail(e);
+  }
+}
+
+// ops::layer_norm (ops_norm.cu:496) on host x [rows, D].
+int refh_layer_norm(const float* x, const float* gamma, const float* beta, int rows, int D, float eps, float* out) {
+  try {
+    Tensor tx = Tensor::from_cpu_f32(x, {rows, D});
+    Tensor tg = Tensor::from_cpu_f32(gamma, {D});
+    Tensor tb = Tensor::from_cpu_f32(beta, {D});
+    Tensor o = ops::layer_norm(tx, tg, tb, eps);
+    cudaDeviceSynchronize();
+    return copy_out(o, out, (long long)rows * D, nullptr);
+  } catch (const std::exception& e) {
+    return fail(e);
+  }
+}
+
 // Device time of ops::scaled_dot_product_attention (ops_attention.cu:522) on q,k,v
 // [B,H,N,D] uploaded once: `warmup` untimed calls, then `iters` calls bracketed by
 // CUDA events on the default stream; *ms_per_call gets the mean.

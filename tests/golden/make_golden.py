@@ -26,9 +26,11 @@ import numpy as np
 ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 sys.path.insert(0, os.path.join(ROOT, "cuda-msst-infer_b200"))
 sys.path.insert(0, os.path.join(ROOT, "oracle"))
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 
 from msst_b200 import synth  # noqa: E402
 import oracle  # noqa: E402
+import op_cases  # noqa: E402
 
 REF_LIB = os.path.join(ROOT, "oracle", "_ref", "libcudasep_ref.so")
 f32p = ctypes.POINTER(ctypes.c_float)
@@ -51,6 +53,8 @@ def ref_lib():
     L.refh_rope.argtypes = [f32p, f32p, f32p, f32p] + [ctypes.c_int] * 4
     L.refh_rmsnorm.argtypes = [f32p, f32p, ctypes.c_int, ctypes.c_int, ctypes.c_float, f32p]
     L.refh_linear.argtypes = [f32p, f32p, f32p] + [ctypes.c_int] * 5 + [f32p]
+    L.refh_sdpa2.argtypes = [f32p, f32p, f32p] + [ctypes.c_int] * 5 + [ctypes.c_float, ctypes.c_int, f32p]
+    L.refh_layer_norm.argtypes = [f32p, f32p, f32p, ctypes.c_int, ctypes.c_int, ctypes.c_float, f32p]
     return L
 
 
@@ -87,13 +91,45 @@ def model_cfg(spec):
     return (synth.mbr_config if spec["kind"] == "mbr" else synth.bsr_config)(**spec["cfg"])
 
 
+def htdemucs_ops(L, out_dir):
+    """ops_htdemucs.npz: the reference's ops::scaled_dot_product_attention (fp32 and
+    fp16 value-GEMM modes) and ops::layer_norm on the op_cases shapes."""
+    ops, summary = {}, {}
+    for name, (_, B, H, Nq, Nk, D, _) in op_cases.SDPA_CASES.items():
+        q, k, v, scale = op_cases.sdpa_inputs(name)
+        for fp16 in (0, 1):
+            o = np.zeros_like(q)
+            check(L.refh_sdpa2(P(q), P(k), P(v), B, H, Nq, Nk, D, scale, fp16, P(o)), L)
+            ops[f"sdpa_{name}_{'fp16' if fp16 else 'fp32'}"] = o
+        s = scale if scale != 0.0 else op_cases.default_scale(D)
+        summary[f"sdpa_{name}"] = rel_l2(oracle.attention(q, k, v, s), ops[f"sdpa_{name}_fp32"])
+    for name, (_, rows, D) in op_cases.LN_CASES.items():
+        x, g, b = op_cases.ln_inputs(name)
+        o = np.zeros_like(x)
+        check(L.refh_layer_norm(P(x), P(g), P(b), rows, D, op_cases.LN_EPS, P(o)), L)
+        ops[f"ln_{name}"] = o
+        summary[f"ln_{name}"] = rel_l2(oracle.layernorm(x, g, b, op_cases.LN_EPS), o)
+    np.savez_compressed(os.path.join(out_dir, "ops_htdemucs.npz"), **ops)
+    return summary
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", required=True)
     ap.add_argument("--full", action="store_true", help="also pin config 0 at full size (summary only)")
+    ap.add_argument("--only", choices=["all", "htdemucs-ops"], default="all",
+                    help="htdemucs-ops: write ops_htdemucs.npz only and merge its pin summary")
     args = ap.parse_args()
     os.makedirs(args.out, exist_ok=True)
     L = ref_lib()
+    if args.only == "htdemucs-ops":
+        path = os.path.join(args.out, "pin_summary.json")
+        summary = json.load(open(path)) if os.path.exists(path) else {}
+        summary["htdemucs_ops"] = htdemucs_ops(L, args.out)
+        with open(path, "w") as f:
+            json.dump(summary, f, indent=1)
+        print(json.dumps(summary["htdemucs_ops"], indent=1))
+        return
     tmp = tempfile.mkdtemp()
     summary = {}
     ll = ctypes.c_longlong
@@ -190,6 +226,7 @@ def main():
     summary["rmsnorm"] = rel_l2(oracle.rmsnorm(x, g, np.sqrt(np.float32(384))), ops["rms_out"])
     summary["linear_gelu"] = rel_l2(oracle.linear(x, w, b, "gelu"), ops["lin_gelu_fp32"])
     np.savez_compressed(os.path.join(args.out, "ops.npz"), **ops)
+    summary["htdemucs_ops"] = htdemucs_ops(L, args.out)
 
     # ---------------- full-size config 0 (summary only; arrays are too large) ----------------
     if args.full:

@@ -101,6 +101,24 @@ def test_c_abi_error_paths_without_gpu(tmp_path):
         check(MSST_ERR_IO)
 
 
+def test_shared_op_argument_checks_without_gpu():
+    """msst_sdpa / msst_layernorm reject bad shapes before touching a device."""
+    from msst_b200 import BF16, F16, F32, MSST_ERR_INVALID, lib
+
+    L = lib()
+    p = ctypes.c_void_p(16)  # never dereferenced: validation fails first
+    assert L.msst_sdpa(None, p, p, 1, 1, 4, 4, 64, 0.0, F16, p, None) == MSST_ERR_INVALID
+    assert L.msst_sdpa(p, p, p, 1, 1, 4, 4, 72, 0.0, F16, p, None) == MSST_ERR_INVALID
+    assert b"head_dim" in L.msst_last_error()
+    assert L.msst_sdpa(p, p, p, 1, 1, 4, 4, 20, 0.0, BF16, p, None) == MSST_ERR_INVALID
+    assert L.msst_sdpa(p, p, p, 1, 1, 0, 4, 64, 0.0, F16, p, None) == MSST_ERR_INVALID
+    assert L.msst_sdpa(p, p, p, 1, 1, 4, 4, 64, 0.0, F32, p, None) == MSST_ERR_INVALID
+    assert L.msst_layernorm(p, 4, 6, p, p, 1e-5, F32, p, None) == MSST_ERR_INVALID
+    assert L.msst_layernorm(p, 4, 2048, p, p, 1e-5, F16, p, None) == MSST_ERR_INVALID
+    assert L.msst_layernorm(p, 4, 384, p, p, 1e-5, 7, p, None) == MSST_ERR_INVALID
+    assert L.msst_layernorm(None, 4, 384, p, p, 1e-5, F32, p, None) == MSST_ERR_INVALID
+
+
 def test_library_has_no_cpu_fallback_symbols():
     """The product library links no oracle code."""
     out = os.popen(f"nm -D {os.path.join(ROOT, 'cuda-msst-infer_b200', 'msst_b200', 'lib', 'libmsst_b200.so')}").read()

@@ -100,3 +100,26 @@ def test_chunk_plan_matches_reference_rules():
     assert (border, total, len(starts)) == (88200, 3197250, 13)
     assert o.resolve_step(352800, 0.0, 2) == 176400      # default num_overlap = 2
     assert o.resolve_step(352800, 4.0, 2) == 88200       # overlap >= 1 is num_overlap
+
+
+@pytest.mark.parametrize("name", ["self48", "cross48", "cross64", "self32"])
+def test_sdpa_cross_length_pin(name):
+    """ops::scaled_dot_product_attention at head_dim 48 / 32 and Nq != Nk (the shapes
+    HTDemucs' transformer feeds it), default scale 1/sqrt(d)."""
+    import op_cases
+
+    o = oracle_mod()
+    z, _ = golden("ops_htdemucs.npz")
+    q, k, v, scale = op_cases.sdpa_inputs(name)
+    s = scale if scale != 0.0 else op_cases.default_scale(q.shape[-1])
+    assert rel_l2(o.attention(q, k, v, s), z[f"sdpa_{name}_fp32"]) < 2e-3  # reference QK^T is TF32
+
+
+@pytest.mark.parametrize("name", ["ln384", "ln512", "ln200"])
+def test_layernorm_pin(name):
+    import op_cases
+
+    o = oracle_mod()
+    z, _ = golden("ops_htdemucs.npz")
+    x, g, b = op_cases.ln_inputs(name)
+    assert rel_l2(o.layernorm(x, g, b, op_cases.LN_EPS), z[f"ln_{name}"]) < 1e-6
