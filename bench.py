@@ -252,13 +252,15 @@ def main():
     ap.add_argument("--seconds", type=float, default=TRACK_SECONDS,
                     help="track length per rank (smaller values make a profiling case)")
     ap.add_argument("--chunk-batch", type=int, default=CHUNK_BATCH, help="chunks per forward")
-    ap.add_argument("--micro", choices=["attention", "gemm"], default=None,
+    ap.add_argument("--micro", choices=["attention", "gemm", "sdpa"], default=None,
                     help="attention: BASELINE config 3; gemm: the transformer GEMMs at config 1's "
-                         "forward-batch shape (instead of the separation bench, 1 GPU)")
+                         "forward-batch shape; sdpa: msst_sdpa at HTDemucs' transformer shapes "
+                         "(instead of the separation bench, 1 GPU)")
     args = ap.parse_args()
     if args.micro is not None:
         if int(os.environ.get("RANK", "0")) == 0:
-            emit(out, run_micro_attention(args) if args.micro == "attention" else run_micro_gemm(args))
+            micro = {"attention": run_micro_attention, "gemm": run_micro_gemm, "sdpa": run_micro_sdpa}
+            emit(out, micro[args.micro](args))
         return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -443,6 +445,99 @@ def run_micro_attention(args):
            "frac_of_burst_peak": {k: v["tflops"] / burst for k, v in res.items()}}
     out["reference_sdpa"] = reference_sdpa(res)
     return out
+
+
+# HTDemucs' cross-transformer at the reference's default config (HTDemucsConfig,
+# src/model_htdemucs.h:11-41: segment 11 s at 44.1 kHz, nfft 4096, hop 1024, 4 encoder
+# layers of stride 4, t_heads 8, bottom_channels 512 -> head_dim 64): the frequency
+# branch carries 2048 / 4^4 = 8 bins x 474 frames = 3792 tokens, the time branch
+# about 485100 / 4^4 = 1895; self-attention in each branch and cross-attention both
+# ways.  head_dim 48 is the bottom_channels = 0 variant (dim 384).
+SDPA_CASES = {
+    "freq_self": (3792, 3792, 64),
+    "time_self": (1895, 1895, 64),
+    "freq_to_time": (3792, 1895, 64),
+    "time_to_freq": (1895, 3792, 64),
+    "freq_self_d48": (3792, 3792, 48),
+}
+SDPA_BATCH, SDPA_HEADS = 4, 8
+
+
+def run_micro_sdpa(args):
+    """msst_sdpa (fp16, default scale 1/sqrt(d)) on SDPA_CASES, 4 segments x 8 heads,
+    q/k/v ~ N(0, 1).  Four input sets are rotated so the operands of consecutive
+    launches (>= 190 MB together) do not sit in L2.  Reference: its
+    ops::scaled_dot_product_attention (oracle/_ref) on the same shapes, fp32 (TF32
+    GEMMs) and fp16-value modes."""
+    import torch
+    from msst_b200 import ops
+
+    torch.cuda.set_device(0)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    B, H = SDPA_BATCH, SDPA_HEADS
+    res = {}
+    for name, (nq, nk, d) in SDPA_CASES.items():
+        sets = [tuple(torch.randn(B, H, n, d, device="cuda", generator=g).half() for n in (nq, nk, nk))
+                for _ in range(4)]
+        fn = lambda i: ops.scaled_dot_product_attention(*sets[i % 4])
+        for i in range(max(3, args.warmup)):
+            fn(i)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        s.record()
+        iters = max(8, args.steps)
+        for i in range(iters):
+            fn(i)
+        e.record()
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(e) / iters
+        flop = 4.0 * B * H * nq * nk * d
+        res[name] = {"Nq": nq, "Nk": nk, "head_dim": d, "gflop": flop / 1e9, "ms": ms,
+                     "tflops": flop / (ms * 1e-3) / 1e12}
+        del sets
+    burst, _, _, src = peaks()
+    out = {"metric": "sdpa TFLOP/s (HTDemucs transformer shapes)", "value": res["freq_self"]["tflops"],
+           "unit": "TFLOP/s", "higher_is_better": True, "n_gpus": 1, "dtype": "fp16", "data": "synthetic",
+           "config": {"workload": f"msst_sdpa, B={B} segments x {H} heads, cases {list(SDPA_CASES)}",
+                      "l2": "4 input sets rotated"},
+           "ours": res, "peak_tflops": burst, "peak_source": src,
+           "frac_of_burst_peak": {k: v["tflops"] / burst for k, v in res.items()}}
+    out["reference_sdpa"] = reference_sdpa2(res)
+    return out
+
+
+def reference_sdpa2(res):
+    """Device time of the reference's ops::scaled_dot_product_attention on SDPA_CASES."""
+    lib_path = os.path.join(ROOT, "oracle", "_ref", "libcudasep_ref.so")
+    if not os.path.exists(lib_path):
+        return {"unavailable": "oracle/_ref not built"}
+    try:
+        f32p = ctypes.POINTER(ctypes.c_float)
+        L = ctypes.CDLL(lib_path)
+        L.refh_last_error.restype = ctypes.c_char_p
+        L.refh_sdpa2_bench.argtypes = [f32p, f32p, f32p] + [ctypes.c_int] * 5 + [ctypes.c_float] + \
+            [ctypes.c_int] * 3 + [f32p]
+        rng = np.random.default_rng(0)
+        P = lambda a: a.ctypes.data_as(f32p)
+        out = {}
+        for name, r in res.items():
+            B, H, nq, nk, d = SDPA_BATCH, SDPA_HEADS, r["Nq"], r["Nk"], r["head_dim"]
+            q = rng.standard_normal((B, H, nq, d), dtype=np.float32)
+            k, v = (rng.standard_normal((B, H, nk, d), dtype=np.float32) for _ in range(2))
+            for mode, fp16 in (("fp32", 0), ("fp16", 1)):
+                ms = ctypes.c_float(0)
+                rc = L.refh_sdpa2_bench(P(q), P(k), P(v), B, H, nq, nk, d, 0.0, fp16, 2, 5, ctypes.byref(ms))
+                if rc != 0:
+                    out[f"{name}_{mode}"] = {"unavailable": L.refh_last_error().decode()}
+                    continue
+                flop = r["gflop"] * 1e9
+                out[f"{name}_{mode}"] = {"ms": ms.value, "tflops": flop / (ms.value * 1e-3) / 1e12,
+                                         "ours_speedup": ms.value / r["ms"]}
+        return out
+    except Exception as e:  # informative leg only
+        return {"unavailable": str(e)}
+    finally:
+        ctypes.CDLL(None).fflush(None)
 
 
 def run_micro_gemm(args):

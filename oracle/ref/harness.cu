@@ -271,6 +271,37 @@ int refh_sdpa_bench(const float* q, const float* k, const float* v, int B, int H
   }
 }
 
+// As refh_sdpa_bench with its own key length Nk (k, v [B,H,Nk,D]).
+int refh_sdpa2_bench(const float* q, const float* k, const float* v, int B, int H, int N, int Nk, int D, float scale,
+                    int fp16, int warmup, int iters, float* ms_per_call) {
+  try {
+    bool saved = g_quantize_fp16;
+    g_quantize_fp16 = fp16 != 0;
+    Tensor tq = Tensor::from_cpu_f32(q, {B, H, N, D});
+    Tensor tk = Tensor::from_cpu_f32(k, {B, H, Nk, D});
+    Tensor tv = Tensor::from_cpu_f32(v, {B, H, Nk, D});
+    for (int i = 0; i < warmup; ++i) ops::scaled_dot_product_attention(tq, tk, tv, scale);
+    CUDA_CHECK(cudaDeviceSynchronize());
+    cudaEvent_t e0, e1;
+    CUDA_CHECK(cudaEventCreate(&e0));
+    CUDA_CHECK(cudaEventCreate(&e1));
+    CUDA_CHECK(cudaEventRecord(e0, 0));
+    for (int i = 0; i < iters; ++i) ops::scaled_dot_product_attention(tq, tk, tv, scale);
+    CUDA_CHECK(cudaEventRecord(e1, 0));
+    CUDA_CHECK(cudaEventSynchronize(e1));
+    float ms = 0.f;
+    CUDA_CHECK(cudaEventElapsedTime(&ms, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    CUDA_CHECK(cudaDeviceSynchronize());
+    g_quantize_fp16 = saved;
+    *ms_per_call = ms / (float)(iters > 0 ? iters : 1);
+    return 0;
+  } catch (const std::exception& e) {
+    return fail(e);
+  }
+}
+
 // The reference's (unused by its own dispatch) scalar flash kernel,
 // flash_attention.cuh:260, on host q,k,v [B,H,N,D] fp32.
 int refh_flash(const float* q, const float* k, const float* v, int B, int H, int N, int D,
