@@ -5,6 +5,7 @@
 #include <atomic>
 #include <cmath>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "attention.cuh"
@@ -15,6 +16,11 @@
 
 struct msst_model {
   msst::Model impl;
+  // calls share the model's workspace: see serialized()
+  std::mutex mu;
+  cudaEvent_t done = nullptr;  // recorded at the end of every call
+  cudaStream_t last = nullptr;  // stream of the previous call
+  bool used = false;
 };
 
 
@@ -40,6 +46,31 @@ int guarded(F&& f) {
 }
 
 cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// The model-level calls of one msst_model share its workspace, so they run one
+// host thread at a time, and a call on a different stream than the previous one
+// first makes its stream wait (on the device) for the previous call's work.  The
+// event is recorded even when the call fails part way, since some of its work may
+// already be queued.
+template <typename F>
+void serialized(msst_model* m, cudaStream_t s, F&& f) {
+  std::lock_guard<std::mutex> lock(m->mu);
+  MSST_CUDA(cudaSetDevice(m->impl.device()));
+  if (!m->done) MSST_CUDA(cudaEventCreateWithFlags(&m->done, cudaEventDisableTiming));
+  if (m->used && s != m->last) MSST_CUDA(cudaStreamWaitEvent(s, m->done, 0));
+  try {
+    f();
+  } catch (...) {
+    if (cudaEventRecord(m->done, s) == cudaSuccess) {
+      m->last = s;
+      m->used = true;
+    }
+    throw;
+  }
+  MSST_CUDA(cudaEventRecord(m->done, s));
+  m->last = s;
+  m->used = true;
+}
 
 int sm_count() {
   static thread_local int dev = -1, n = 0;
@@ -484,6 +515,7 @@ int msst_model_load(const char* path, int device, int precision, msst_model** ou
 void msst_model_free(msst_model* m) {
   if (!m) return;
   cudaSetDevice(m->impl.device());
+  if (m->done) cudaEventDestroy(m->done);
   delete m;
 }
 
@@ -498,8 +530,7 @@ int msst_model_forward(msst_model* m, const float* audio, int batch, int channel
                        void* stream) {
   return guarded([&] {
     MSST_REQUIRE(m && audio && out, "null argument");
-    MSST_CUDA(cudaSetDevice(m->impl.device()));
-    m->impl.forward(audio, batch, channels, length, out, as_stream(stream));
+    serialized(m, as_stream(stream), [&] { m->impl.forward(audio, batch, channels, length, out, as_stream(stream)); });
   });
 }
 
@@ -507,16 +538,14 @@ int msst_model_masks(msst_model* m, const float* audio, int batch, int channels,
                      void* stream) {
   return guarded([&] {
     MSST_REQUIRE(m && audio && masks, "null argument");
-    MSST_CUDA(cudaSetDevice(m->impl.device()));
-    m->impl.masks(audio, batch, channels, length, masks, as_stream(stream));
+    serialized(m, as_stream(stream), [&] { m->impl.masks(audio, batch, channels, length, masks, as_stream(stream)); });
   });
 }
 
 int msst_model_transformer(msst_model* m, int depth_index, int axis, float* x, int batch, int T, void* stream) {
   return guarded([&] {
     MSST_REQUIRE(m && x, "null argument");
-    MSST_CUDA(cudaSetDevice(m->impl.device()));
-    m->impl.transformer(depth_index, axis, x, batch, T, as_stream(stream));
+    serialized(m, as_stream(stream), [&] { m->impl.transformer(depth_index, axis, x, batch, T, as_stream(stream)); });
   });
 }
 
@@ -524,8 +553,9 @@ int msst_roformer_attn_block(msst_model* m, int depth_index, int axis, int layer
                              void* stream) {
   return guarded([&] {
     MSST_REQUIRE(m && x, "null argument");
-    MSST_CUDA(cudaSetDevice(m->impl.device()));
-    m->impl.attn_block(depth_index, axis, layer, x, batch, T, as_stream(stream));
+    serialized(m, as_stream(stream), [&] {
+      m->impl.attn_block(depth_index, axis, layer, x, batch, T, as_stream(stream));
+    });
   });
 }
 
@@ -533,8 +563,9 @@ int msst_roformer_ffn_block(msst_model* m, int depth_index, int axis, int layer,
                             void* stream) {
   return guarded([&] {
     MSST_REQUIRE(m && x, "null argument");
-    MSST_CUDA(cudaSetDevice(m->impl.device()));
-    m->impl.ffn_block(depth_index, axis, layer, x, batch, T, as_stream(stream));
+    serialized(m, as_stream(stream), [&] {
+      m->impl.ffn_block(depth_index, axis, layer, x, batch, T, as_stream(stream));
+    });
   });
 }
 
@@ -549,8 +580,9 @@ int msst_model_transformer_noalloc(msst_model* m, int depth_index, int axis, flo
                                    void* stream) {
   return guarded([&] {
     MSST_REQUIRE(m && x, "null argument");
-    MSST_CUDA(cudaSetDevice(m->impl.device()));
-    m->impl.transformer_noalloc(depth_index, axis, x, batch, T, as_stream(stream));
+    serialized(m, as_stream(stream), [&] {
+      m->impl.transformer_noalloc(depth_index, axis, x, batch, T, as_stream(stream));
+    });
   });
 }
 
@@ -558,8 +590,9 @@ int msst_model_separate(msst_model* m, const float* track, int channels, long lo
                         int chunk_batch, int flags, float* out, void* stream) {
   return guarded([&] {
     MSST_REQUIRE(m && track && out, "null argument");
-    MSST_CUDA(cudaSetDevice(m->impl.device()));
-    m->impl.separate(track, channels, length, overlap, chunk_batch, flags, out, as_stream(stream));
+    serialized(m, as_stream(stream), [&] {
+      m->impl.separate(track, channels, length, overlap, chunk_batch, flags, out, as_stream(stream));
+    });
   });
 }
 
@@ -568,7 +601,9 @@ int msst_model_separate_host(msst_model* m, const float* track_host, int channel
   return guarded([&] {
     MSST_REQUIRE(m && track_host && out_host && channels > 0 && length > 0, "null argument");
     MSST_CUDA(cudaSetDevice(m->impl.device()));
-    m->impl.separate_host(track_host, channels, length, overlap, chunk_batch, flags, out_host);
+    serialized(m, m->impl.host_stream(), [&] {
+      m->impl.separate_host(track_host, channels, length, overlap, chunk_batch, flags, out_host);
+    });
   });
 }
 
@@ -576,9 +611,10 @@ int msst_model_forward_chunks(msst_model* m, const float* track, int channels, l
                               int first_chunk, int count, int chunk_batch, int flags, float* out, void* stream) {
   return guarded([&] {
     MSST_REQUIRE(m && track && (out || count == 0), "null argument");
-    MSST_CUDA(cudaSetDevice(m->impl.device()));
-    m->impl.forward_chunks(track, channels, length, overlap, first_chunk, count, chunk_batch, flags, out,
-                           as_stream(stream));
+    serialized(m, as_stream(stream), [&] {
+      m->impl.forward_chunks(track, channels, length, overlap, first_chunk, count, chunk_batch, flags, out,
+                             as_stream(stream));
+    });
   });
 }
 
@@ -586,8 +622,9 @@ int msst_model_stitch(msst_model* m, const float* chunks, int channels, long lon
                       void* stream) {
   return guarded([&] {
     MSST_REQUIRE(m && chunks && out, "null argument");
-    MSST_CUDA(cudaSetDevice(m->impl.device()));
-    m->impl.stitch(chunks, channels, length, overlap, out, as_stream(stream));
+    serialized(m, as_stream(stream), [&] {
+      m->impl.stitch(chunks, channels, length, overlap, out, as_stream(stream));
+    });
   });
 }
 

@@ -1201,9 +1201,14 @@ void Model::stitch(const float* chunks, int C, long long L, float overlap, float
   MSST_CUDA(launch_chunk_finish(co, d_acc, d_wsum, out, s));
 }
 
+cudaStream_t Model::host_stream() {
+  if (!host_stream_) MSST_CUDA(cudaStreamCreateWithFlags(&host_stream_, cudaStreamNonBlocking));
+  return host_stream_;
+}
+
 void Model::separate_host(const float* track_host, int C, long long L, float overlap, int chunk_batch, int flags,
                           float* out_host) {
-  if (!host_stream_) MSST_CUDA(cudaStreamCreateWithFlags(&host_stream_, cudaStreamNonBlocking));
+  host_stream();
   const size_t in_bytes = sizeof(float) * (size_t)C * L;
   const size_t out_bytes = in_bytes * (size_t)info_.num_stems;
   host_in_.ensure(in_bytes);

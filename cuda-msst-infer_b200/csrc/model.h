@@ -61,6 +61,8 @@ class Model {
   // host memory makes the copies asynchronous DMA).
   void separate_host(const float* track_host, int C, long long L, float overlap, int chunk_batch, int flags,
                      float* out_host);
+  // The stream separate_host() runs on (created on first use, on the current device).
+  cudaStream_t host_stream();
   void chunk_plan(long long L, float overlap, int* chunk, int* step, long long* border, long long* total,
                   int* num_chunks) const;
   // Sharded separation: forward chunks [first, first + count) of the track's plan

@@ -218,6 +218,43 @@ def test_dim512_vs_oracle(cuda, tmp_path_factory, kind, prec):
     m.close()
 
 
+def test_one_model_many_threads_and_streams(cuda, small_models):
+    """Calls on one model from several host threads, each on its own stream, give
+    the single-threaded result: the model serialises its calls (mutex + event)."""
+    import threading
+
+    torch = cuda
+    from msst_b200 import Model, synth
+
+    path, _, _, _ = small_models["mbr_small"]
+    m = Model(path, 0, "fp16")
+    inputs = [torch.from_numpy(synth.make_audio(22050, 2, s)[None]).cuda() for s in (11, 12, 13, 14)]
+    ref = [m.forward(x).cpu().numpy() for x in inputs]
+    outs = [[None] * 3 for _ in inputs]
+    errors = []
+
+    def worker(i):
+        try:
+            s = torch.cuda.Stream()
+            with torch.cuda.stream(s):
+                for r in range(3):
+                    y = m.forward(inputs[i], stream=s)
+                    outs[i][r] = y.cpu().numpy()
+        except Exception as e:  # reported below
+            errors.append(e)
+
+    threads = [threading.Thread(target=worker, args=(i,)) for i in range(len(inputs))]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    assert not errors, errors
+    for i in range(len(inputs)):
+        for r in range(3):
+            np.testing.assert_array_equal(outs[i][r], ref[i])
+    m.close()
+
+
 def test_two_devices_one_process(cuda, small_models):
     """Models on two GPUs of one process: every launcher configures its kernel's
     shared-memory limit per device, and the two devices give identical outputs."""
