@@ -256,8 +256,9 @@ __global__ void __launch_bounds__(384, 1) rmsnorm_gates8_kernel(RmsNormArgs a) {
   }
 }
 
-// RMSNorm + 8 gate projections for widths whose gate weights do not fit in
-// registers (dim 512): the weights sit in shared memory ([8][D] fp32) and each
+// RMSNorm + 8 gate projections at dims 384 and 512 (at 512 the gate weights do
+// not fit in registers; at 384 the register form holds too few rows in flight per
+// SM): the weights sit in shared memory ([8][D] fp32) and each
 // warp normalises two rows at once, so every shared-memory weight load feeds two
 // rows' dot products (8 KB of shared-memory reads per row instead of 16).  The
 // 16 partial sums (2 rows x 8 heads) are reduced by a butterfly transpose-reduce
@@ -393,22 +394,26 @@ cudaError_t rmsnorm_dispatch(const RmsNormArgs& a, cudaStream_t s) {
                     rd * 4.0 + (a.gamma_pre ? rd * 4.0 : 0.0) + (a.gamma ? rd * sizeof(T) : 0.0) +
                         (a.wg ? (double)a.rows * a.heads * 4.0 : 0.0),
                     s);
-  if (a.wg != nullptr && a.heads == 8 && a.gamma != nullptr && !a.band_major && V <= 3) {
+  if (a.wg != nullptr && a.heads == 8 && a.gamma != nullptr && !a.band_major && V <= 2) {
     // one block of 12 warps per SM (the gate weights take 32 * V registers per lane)
     long long gb = (a.rows + 11) / 12;
     if (gb > 148) gb = 148;
-    switch (V) {
-      case 1: rmsnorm_gates8_kernel<T, 1><<<(unsigned)gb, 384, 0, s>>>(a); break;
-      case 2: rmsnorm_gates8_kernel<T, 2><<<(unsigned)gb, 384, 0, s>>>(a); break;
-      default: rmsnorm_gates8_kernel<T, 3><<<(unsigned)gb, 384, 0, s>>>(a); break;
-    }
+    if (V == 1)
+      rmsnorm_gates8_kernel<T, 1><<<(unsigned)gb, 384, 0, s>>>(a);
+    else
+      rmsnorm_gates8_kernel<T, 2><<<(unsigned)gb, 384, 0, s>>>(a);
     return cudaGetLastError();
   }
-  if (a.wg != nullptr && a.heads == 8 && a.gamma != nullptr && !a.band_major && V == 4) {
-    // two persistent blocks of 8 warps per SM, each warp two rows at a time
+  if (a.wg != nullptr && a.heads == 8 && a.gamma != nullptr && !a.band_major && (V == 3 || V == 4)) {
+    // two persistent blocks of 8 warps per SM, each warp two rows at a time (four
+    // rows in flight per warp with the prefetch: dim 384 went from 79 % to 87 % of
+    // HBM against the register-weight kernel's one block of 12 warps)
     long long gb = ((a.rows + 1) / 2 + 7) / 8;
     if (gb > 2 * 148) gb = 2 * 148;
-    rmsnorm_gates8x2_kernel<T, 4><<<(unsigned)gb, 256, smem, s>>>(a);
+    if (V == 3)
+      rmsnorm_gates8x2_kernel<T, 3><<<(unsigned)gb, 256, smem, s>>>(a);
+    else
+      rmsnorm_gates8x2_kernel<T, 4><<<(unsigned)gb, 256, smem, s>>>(a);
     return cudaGetLastError();
   }
   switch (V) {
