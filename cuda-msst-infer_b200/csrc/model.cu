@@ -324,12 +324,6 @@ static DeviceBuffer upload_16(const std::vector<float>& v, int bf16) {
   return b;
 }
 
-static int pick_bn(int n) {
-  if (n % 256 == 0) return 256;
-  if (n % 192 == 0) return 192;
-  return n <= 128 ? 128 : 256;
-}
-
 // ===========================================================================
 // Workspace for one (batch, T) shape
 // ===========================================================================
@@ -526,7 +520,7 @@ void Model::load(const std::string& path, int device, int precision) {
     w_bs_ = upload_16(W, bf16_);
     b_bs_ = upload_f32(bias);
     g_bs_ = upload_f32(gam);
-    m_wbs_ = map_gemm_b(w_bs_.get(), D, ktot_, ktot_, pick_bn(D));
+    m_wbs_ = map_gemm_b(w_bs_.get(), D, ktot_, ktot_, gemm_pick_bn(D));
   }
 
   // ---- transformers
@@ -552,10 +546,14 @@ void Model::load(const std::string& path, int device, int precision) {
         L.b1 = upload_f32(vec(fp + ".1.bias", ff_));
         L.w2 = upload_16(mat(fp + ".4.weight", D, ff_), bf16_);
         L.b2 = upload_f32(vec(fp + ".4.bias", D));
-        L.m_wqkv = map_gemm_b(L.wqkv.get(), 3 * inner_, D, D, pick_bn(3 * inner_));
-        L.m_wout = map_gemm_b(L.wout.get(), D, inner_, inner_, pick_bn(D));
-        L.m_w1 = map_gemm_b(L.w1.get(), ff_, D, D, pick_bn(ff_));
-        L.m_w2 = map_gemm_b(L.w2.get(), D, ff_, ff_, pick_bn(D));
+        L.bn_qkv = gemm_pick_bn(3 * inner_);
+        L.bn_out = gemm_pick_bn(D);
+        L.bn_w1 = gemm_pick_bn(ff_);
+        L.bn_w2 = gemm_pick_bn(D);
+        L.m_wqkv = map_gemm_b(L.wqkv.get(), 3 * inner_, D, D, L.bn_qkv);
+        L.m_wout = map_gemm_b(L.wout.get(), D, inner_, inner_, L.bn_out);
+        L.m_w1 = map_gemm_b(L.w1.get(), ff_, D, D, L.bn_w1);
+        L.m_w2 = map_gemm_b(L.w2.get(), D, ff_, ff_, L.bn_w2);
         L.m_w1_f = map_2d(L.w1.get(), ff_, D, D, 128);
         L.m_w2_f = map_2d(L.w2.get(), D, ff_, ff_, 128);
       }
@@ -772,7 +770,7 @@ void Model::run_front(const float* audio, int B, long long L, int T, cudaStream_
     g.oz_row = 1;
     p.groups[b] = g;
   }
-  gemm(w.m_abs, m_wbs_, w.mo_bs, p, kEpiStore32, pick_bn(I.dim), s);
+  gemm(w.m_abs, m_wbs_, w.mo_bs, p, kEpiStore32, gemm_pick_bn(I.dim), s);
 }
 
 void Model::run_transformer(int d, int axis, float* x, int B, int T, const float* pending_gamma, cudaStream_t s,
@@ -825,7 +823,7 @@ void Model::run_attn_block(int d, int axis, int l, float* x, int B, int T, const
     }
     p.rope_cos = rope_table(p.pos_mod, false);
     p.rope_sin = rope_table(p.pos_mod, true);
-    gemm(w.m_xn, L.m_wqkv, w.mo_qkv, p, kEpiQkvRope, pick_bn(3 * inner_), s);
+    gemm(w.m_xn, L.m_wqkv, w.mo_qkv, p, kEpiQkvRope, L.bn_qkv, s);
   }
   // attention (+ gate, head merge)
   {
@@ -856,7 +854,7 @@ void Model::run_attn_block(int d, int axis, int l, float* x, int B, int T, const
     GemmParams p{};
     p.num_groups = 1;
     p.groups[0] = group((int)M, D, inner_, x, D, nullptr);
-    gemm(w.m_ao, L.m_wout, mo_x, p, kEpiResid32, pick_bn(D), s);
+    gemm(w.m_ao, L.m_wout, mo_x, p, kEpiResid32, L.bn_out, s);
   }
 }
 
@@ -903,13 +901,13 @@ void Model::run_ffn_block(int d, int axis, int l, float* x, int B, int T, cudaSt
     p.num_groups = 1;
     p.act = kActGelu;
     p.groups[0] = group((int)M, ff_, D, w.big2.get(), ff_, L.b1.get<float>());
-    gemm(w.m_xn, L.m_w1, w.mo_ffh, p, kEpiStore16, pick_bn(ff_), s);
+    gemm(w.m_xn, L.m_w1, w.mo_ffh, p, kEpiStore16, L.bn_w1, s);
   }
   {
     GemmParams p{};
     p.num_groups = 1;
     p.groups[0] = group((int)M, D, ff_, x, D, L.b2.get<float>());
-    gemm(w.m_big2_ffh, L.m_w2, mo_x, p, kEpiResid32, pick_bn(D), s);
+    gemm(w.m_big2_ffh, L.m_w2, mo_x, p, kEpiResid32, L.bn_w2, s);
   }
 }
 

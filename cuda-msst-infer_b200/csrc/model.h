@@ -23,6 +23,9 @@ struct LayerWeights {
   DeviceBuffer g_attn, wqkv, wg, bg, wout;   // attention (norm gamma, W_qkv, gate W/b, W_out)
   DeviceBuffer g_ff, w1, b1, w2, b2;         // feed-forward
   CUtensorMap m_wqkv, m_wout, m_w1, m_w2;
+  // GEMM column tile each B map above was encoded for (its box holds bn/2 rows):
+  // every launch that reads a map must pass the same bn
+  int bn_qkv = 0, bn_out = 0, bn_w1 = 0, bn_w2 = 0;
   CUtensorMap m_w1_f, m_w2_f;                // 128-row boxes for the fused feed-forward kernel
 };
 

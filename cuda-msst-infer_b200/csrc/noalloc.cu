@@ -22,8 +22,11 @@
 //     race and corrupt each other; every region is fully written before it is
 //     read, so nothing needs clearing between calls;
 //   * the first call on a device resolves the array's device address
-//     (cudaGetSymbolAddress) for that device; make that first call before any
-//     stream capture.
+//     (cudaGetSymbolAddress) for that device, and with CUDA's lazy module
+//     loading that first use is also when the driver loads this file's module
+//     and backs the array with device memory: make one warm-up call per device
+//     at start-up, off the real-time thread and before any stream capture;
+//     later calls allocate nothing.
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -64,6 +67,20 @@ unsigned char* scratch_on_current_device() {
 
 size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
 
+// cos / sin of the interleaved-pair rotary embedding, [npos, 32] each: angle
+// p * 10000^(-2i / head_dim), the values Model::rope_table computes on the host
+// (reference src/model_mel_band_roformer.cu:487-513), here with the device's
+// powf / cosf / sinf (within a few ulp of the host's).
+__global__ void rope_tables_kernel(float* cos_tab, float* sin_tab, int npos, int head_dim) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= npos * 32) return;
+  const int p = idx / 32, i = idx % 32;
+  const float freq = 1.0f / powf(10000.0f, (float)(2 * i) / (float)head_dim);
+  const float ang = (float)p * freq;
+  cos_tab[idx] = cosf(ang);
+  sin_tab[idx] = sinf(ang);
+}
+
 }  // namespace
 
 void Model::transformer_noalloc(int d, int axis, float* x, int B, int T, cudaStream_t s) {
@@ -93,19 +110,12 @@ void Model::transformer_noalloc(int d, int axis, float* x, int B, int T, cudaStr
   unsigned char* big = xn + xn_bytes + gates_bytes;
   unsigned char* ao = big + big_bytes;
 
-  // rotary tables for this axis, computed like Model::rope_table (host fp32) and copied in
+  // rotary tables for this axis, filled on the device (no host table, no copy,
+  // no stream synchronisation)
   {
-    std::vector<float> c((size_t)npos * 32), sn((size_t)npos * 32);
-    for (int p = 0; p < npos; ++p)
-      for (int i = 0; i < 32; ++i) {
-        const float freq = 1.0f / std::pow(10000.0f, (float)(2 * i) / (float)I.dim_head);
-        const float ang = (float)p * freq;
-        c[(size_t)p * 32 + i] = std::cos(ang);
-        sn[(size_t)p * 32 + i] = std::sin(ang);
-      }
-    MSST_CUDA(cudaMemcpyAsync(cos_tab, c.data(), c.size() * 4, cudaMemcpyHostToDevice, s));
-    MSST_CUDA(cudaMemcpyAsync(sin_tab, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice, s));
-    MSST_CUDA(cudaStreamSynchronize(s));  // host vectors go out of scope
+    const int n = npos * 32;
+    rope_tables_kernel<<<(n + 255) / 256, 256, 0, s>>>(cos_tab, sin_tab, npos, I.dim_head);
+    MSST_CUDA(cudaGetLastError());
   }
 
   // tensor maps over the scratch regions (host-side encoding only)
@@ -167,7 +177,7 @@ void Model::transformer_noalloc(int d, int axis, float* x, int B, int T, cudaStr
       p.pos_mod = npos;
       p.rope_cos = cos_tab;
       p.rope_sin = sin_tab;
-      gemm(m_xn, L.m_wqkv, mo_qkv, p, kEpiQkvRope, 3 * inner_ % 256 == 0 ? 256 : 192, s);
+      gemm(m_xn, L.m_wqkv, mo_qkv, p, kEpiQkvRope, L.bn_qkv, s);
     }
     {
       AttnParams a{};
@@ -190,12 +200,11 @@ void Model::transformer_noalloc(int d, int axis, float* x, int B, int T, cudaStr
       }
       MSST_CUDA(launch_attention(m_qkv, a, bf16_, num_sms_, s));
     }
-    const int bn_d = D % 256 == 0 ? 256 : (D % 192 == 0 ? 192 : 128);
     {
       GemmParams p{};
       p.num_groups = 1;
       p.groups[0] = one((int)M, D, inner_, x, D, nullptr);
-      gemm(m_ao, L.m_wout, mo_x, p, kEpiResid32, bn_d, s);
+      gemm(m_ao, L.m_wout, mo_x, p, kEpiResid32, L.bn_out, s);
     }
     RmsNormArgs rf{};
     rf.x = x;
@@ -210,13 +219,13 @@ void Model::transformer_noalloc(int d, int axis, float* x, int B, int T, cudaStr
       p.num_groups = 1;
       p.act = kActGelu;
       p.groups[0] = one((int)M, ff_, D, big, ff_, L.b1.get<float>());
-      gemm(m_xn, L.m_w1, mo_ffh, p, kEpiStore16, ff_ % 256 == 0 ? 256 : 192, s);
+      gemm(m_xn, L.m_w1, mo_ffh, p, kEpiStore16, L.bn_w1, s);
     }
     {
       GemmParams p{};
       p.num_groups = 1;
       p.groups[0] = one((int)M, D, ff_, x, D, L.b2.get<float>());
-      gemm(m_ffh, L.m_w2, mo_x, p, kEpiResid32, bn_d, s);
+      gemm(m_ffh, L.m_w2, mo_x, p, kEpiResid32, L.bn_w2, s);
     }
   }
   if (mel_) {

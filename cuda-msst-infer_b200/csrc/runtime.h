@@ -148,6 +148,14 @@ inline CUtensorMap map_gemm_b(const void* base, uint64_t rows, uint64_t cols, ui
   return map_2d(base, rows, cols, ld, (uint32_t)(bn / 2));
 }
 
+// Column tile of the GEMM for an output width n (a weight's B map is encoded
+// for it: map_gemm_b(..., gemm_pick_bn(n))).
+inline int gemm_pick_bn(int n) {
+  if (n % 256 == 0) return 256;
+  if (n % 192 == 0) return 192;
+  return n <= 128 ? 128 : 256;
+}
+
 inline int device_sm_count() {
   int dev = 0, n = 0;
   MSST_CUDA(cudaGetDevice(&dev));

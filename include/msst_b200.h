@@ -11,7 +11,7 @@
  *     message of the calling thread's last failure.  The reference throws
  *     std::runtime_error for the same conditions (src/tensor.h:28-34); its C++
  *     call sites get that behaviour back from a thin wrapper that throws on a
- *     non-zero status (see INTEGRATION.md).
+ *     non-zero status.
  *   - 16-bit operands are fp16 (MSST_F16) or bf16 (MSST_BF16); accumulation is
  *     fp32; the residual stream and all model inputs/outputs are fp32.
  *   - K (the reduction length) of every GEMM is a multiple of 64; hidden sizes
@@ -261,8 +261,11 @@ int msst_roformer_ffn_block(msst_model* m, int depth_index, int axis, int layer,
  * needs about dim*2 + heads*4 + 2*max(3*heads*64, 4*dim) + heads*128 bytes per
  * token (about 10,000 tokens at dim 384) and larger calls fail with
  * MSST_ERR_INVALID.  Calls on one device share the array: calls that overlap on
- * the GPU race.  The first call on a device looks up the array's device address;
- * make it before any stream capture. */
+ * the GPU race.  The first call on a device looks up the array's device address,
+ * and under CUDA's lazy module loading it is also when the driver loads the
+ * library's module and backs the array with device memory: make one warm-up
+ * call per device at start-up, off the real-time thread and before any stream
+ * capture.  Later calls allocate nothing and do not synchronise the stream. */
 int msst_model_transformer_noalloc(msst_model* m, int depth_index, int axis, float* x, int batch, int T,
                                    void* stream);
 
