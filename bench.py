@@ -76,10 +76,11 @@ def model_file(cfg, which: int, rank: int, world: int, dist):
 
     d = os.environ.get("MSST_BENCH_DIR", "/tmp/msst_bench")
     os.makedirs(d, exist_ok=True)
-    path = os.path.join(d, f"config{which}_seed0.csm")
+    path = os.path.join(d, f"config{which}_seed0{'_bf16w' if which == 2 else ''}.csm")
     if rank == 0 and not os.path.exists(path):
         tmp = path + f".tmp{os.getpid()}"
-        synth.write_csm(tmp, cfg, synth.make_weights(cfg, 0))
+        # config 2 is a bf16 model: its N(0, 0.02) weights are bf16 values
+        synth.write_csm(tmp, cfg, synth.make_weights(cfg, 0, weight_dtype="bf16" if which == 2 else "fp32"))
         os.replace(tmp, path)
     if world > 1:
         dist.barrier()

@@ -454,6 +454,7 @@ int msst_band_gather(const float* spec, int B, int T, const msst_band_tables* t,
     use_device_of(spec);
     msst::BandInArgs bi{};
     bi.spec = reinterpret_cast<const float2*>(spec);
+    bi.spec_scale = 1.0f;
     bi.Bc = B;
     bi.C = t->channels;
     bi.T = T;
@@ -480,6 +481,8 @@ int msst_mask_apply(const float* spec, const float* masks, int B, int S, int T, 
     use_device_of(spec);
     msst::MaskApplyArgs ma{};
     ma.spec = reinterpret_cast<const float2*>(spec);
+    ma.spec_scale = 1.0f;
+    ma.out_scale = 1.0f;
     ma.mask = masks;
     ma.mask_stem_stride = (long long)B * T * t->sum_dims;
     ma.mask_ld = t->sum_dims;

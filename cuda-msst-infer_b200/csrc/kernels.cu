@@ -456,7 +456,7 @@ __global__ void __launch_bounds__(256) band_input_kernel(BandInArgs a) {
       const int rem = j - fl * per_bin;
       const int ch = rem >> 1, ri = rem & 1;
       const float2 z = a.spec[((long long)(b * a.C + ch) * a.T + t) * a.nbins + bins[fl]];
-      return ri ? z.y : z.x;
+      return (ri ? z.y : z.x) * a.spec_scale;
     };
     float ss = 0.f;
     for (int j = lane; j < dims; j += 32) {
@@ -501,8 +501,10 @@ __global__ void __launch_bounds__(256) mask_apply_kernel(MaskApplyArgs a) {
       }
       mr = mr / den;
       mi = mi / den;
-      const float2 z = a.spec[((long long)(b * a.C + c) * a.T + t) * a.nbins + f];
-      float2 o = make_float2(z.x * mr - z.y * mi, z.x * mi + z.y * mr);
+      float2 z = a.spec[((long long)(b * a.C + c) * a.T + t) * a.nbins + f];
+      z.x *= a.spec_scale;
+      z.y *= a.spec_scale;
+      float2 o = make_float2((z.x * mr - z.y * mi) * a.out_scale, (z.x * mi + z.y * mr) * a.out_scale);
       if (a.zero_dc && f == 0) o = make_float2(0.f, 0.f);
       a.out[((((long long)b * a.S + st) * a.C + c) * a.T + t) * a.nbins + f] = o;
     }
@@ -528,14 +530,19 @@ __global__ void __launch_bounds__(256)
 
 __global__ void __launch_bounds__(256)
     istft_ola_kernel(const float* __restrict__ frames, int BSC, int T, int n_fft, int hop,
-                     const float* __restrict__ win, const float* __restrict__ wsum, float* __restrict__ out) {
-  const long long Lout = (long long)(T - 1) * hop;
+                     const float* __restrict__ win, const float* __restrict__ wsum, float* __restrict__ out,
+                     long long Lout) {
+  const long long Lrec = (long long)(T - 1) * hop;  // reconstructed samples; the rest of a row is zero
   const long long total = (long long)BSC * Lout;
   const int pad = n_fft / 2;
   const float inv_n = 1.0f / (float)n_fft;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
     const long long bsc = i / Lout;
+    if (i - bsc * Lout >= Lrec) {
+      out[i] = 0.f;
+      continue;
+    }
     const long long p = i - bsc * Lout + pad;
     long long t_lo = (p - n_fft + hop) / hop;  // ceil((p - n_fft + 1) / hop) for p >= n_fft - 1
     if (p - n_fft + 1 <= 0) t_lo = 0;
@@ -652,6 +659,22 @@ __global__ void __launch_bounds__(256) chunk_finish_kernel(ChunkArgs a, const fl
   }
 }
 
+__global__ void __launch_bounds__(256) skip_add_kernel(float4* x, const float4* __restrict__ skips, int count,
+                                                       long long n4) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
+       i += (long long)gridDim.x * blockDim.x) {
+    float4 v = x[i];
+    for (int j = 0; j < count; ++j) {
+      const float4 s = __ldg(skips + (long long)j * n4 + i);
+      v.x += s.x;
+      v.y += s.y;
+      v.z += s.z;
+      v.w += s.w;
+    }
+    x[i] = v;
+  }
+}
+
 inline unsigned grid_for(long long n) {
   long long b = (n + 255) / 256;
   if (b > 148LL * 32) b = 148LL * 32;
@@ -709,11 +732,20 @@ cudaError_t launch_stft_frames(const float* audio, long long L, int BC, int T, i
 }
 
 cudaError_t launch_istft_ola(const float* frames, int BSC, int T, int n_fft, int hop, const float* win,
-                             const float* wsum, float* out, cudaStream_t s) {
-  LaunchScope scope("istft_ola", 0.0,
-                    (double)BSC * T * n_fft * 4.0 + (double)BSC * (T - 1) * (double)hop * 4.0, s);
-  istft_ola_kernel<<<grid_for((long long)BSC * (T - 1) * hop), 256, 0, s>>>(frames, BSC, T, n_fft, hop, win, wsum,
-                                                                           out);
+                             const float* wsum, float* out, long long out_len, cudaStream_t s) {
+  LaunchScope scope("istft_ola", 0.0, (double)BSC * T * n_fft * 4.0 + (double)BSC * (double)out_len * 4.0, s);
+  istft_ola_kernel<<<grid_for((long long)BSC * out_len), 256, 0, s>>>(frames, BSC, T, n_fft, hop, win, wsum, out,
+                                                                      out_len);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_skip_add(float* x, const float* skips, int count, long long n, cudaStream_t s) {
+  if (count <= 0 || n <= 0) return cudaSuccess;
+  if (n % 4 != 0 || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(skips) & 15))
+    return cudaErrorInvalidValue;
+  LaunchScope scope("skip_add", 0.0, (double)n * 4.0 * (count + 2), s);
+  skip_add_kernel<<<grid_for(n / 4), 256, 0, s>>>(reinterpret_cast<float4*>(x),
+                                                  reinterpret_cast<const float4*>(skips), count, n / 4);
   return cudaGetLastError();
 }
 

@@ -70,6 +70,8 @@ struct BandInArgs {
   const float* gamma;     // concatenated band gammas
   void* out;              // [Bc*T, ld] 16-bit
   long long ld;
+  float spec_scale;       // the STFT values are multiplied by this first (1, or
+                          // 1/sqrt(n_fft) for stft_normalized models, src/ops_stft.cu:358-365)
 };
 cudaError_t launch_band_input(const BandInArgs& a, int bf16, cudaStream_t s);
 
@@ -89,6 +91,9 @@ struct MaskApplyArgs {
   float2* out;             // [Bc*S*C*T, nbins]
   int Bc, S, C, T, nbins;
   int zero_dc;
+  float spec_scale;        // out = ((spec * spec_scale) x mask) * out_scale: the normalized
+  float out_scale;         // STFT of stft_normalized models and the iSTFT's undoing of it
+                           // (src/ops_stft.cu:358-365,380-389); 1 and 1 otherwise
 };
 cudaError_t launch_mask_apply(const MaskApplyArgs& a, cudaStream_t s);
 
@@ -100,9 +105,17 @@ cudaError_t launch_stft_frames(const float* audio, long long L, int BC, int T, i
 // iSTFT tail (src/ops_stft.cu:411-482): frames are the raw C2R outputs; each
 // output sample gathers its <= ceil(n_fft/hop) windowed frames, scales by
 // 1/n_fft, divides by the summed squared window where > 1e-8 and drops n_fft/2
-// samples of centre padding.  out [BSC, (T-1)*hop].
+// samples of centre padding.  out [BSC, out_len]: the (T-1)*hop reconstructed
+// samples, zero-padded or truncated to out_len (the `length` argument of
+// ops::istft, src/ops_stft.cu:484-493; out_len = (T-1)*hop is the default).
 cudaError_t launch_istft_ola(const float* frames, int BSC, int T, int n_fft, int hop, const float* win,
-                             const float* wsum, float* out, cudaStream_t s);
+                             const float* wsum, float* out, long long out_len, cudaStream_t s);
+
+// Skip connections of the Roformer depth loop (src/model_mel_band_roformer.cu:846-852):
+// x += skips[0] + skips[1] + ... + skips[count-1], added one at a time in that order
+// (the same fp32 sums as the reference's sequence of tensor adds); skips[j] lives
+// at skips + j * n.  x and skips 16-byte aligned, n % 4 == 0.
+cudaError_t launch_skip_add(float* x, const float* skips, int count, long long n, cudaStream_t s);
 
 // Chunked inference helpers (src/inference_app.cpp:100-324).
 // Gather `count` chunks starting at chunk index `first` of the reflect-padded

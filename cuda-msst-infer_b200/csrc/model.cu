@@ -6,6 +6,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstring>
 #include <fstream>
@@ -331,6 +332,7 @@ struct Model::Work {
   int B = 0, T = 0;
   long long M = 0, BT = 0;
   DeviceBuffer frames, spec, ispec, abs, x, xn, gates, big1, big2, ao, mask, chunk_in, chunk_out;
+  DeviceBuffer skips;  // skip_connection models: the outputs of depth blocks 0..depth-2
   CUtensorMap m_abs, m_xn, m_ao, m_big1_ffh, m_big2_ffh, m_qkv_time, m_qkv_band, m_h1, m_h2;
   // GEMM output maps (TMA stores)
   CUtensorMap mo_qkv, mo_ffh, mo_bs, mo_h1, mo_h2;
@@ -347,6 +349,7 @@ Model::~Model() {
 // load
 // ===========================================================================
 void Model::load(const std::string& path, int device, int precision) {
+  const auto t_load0 = std::chrono::steady_clock::now();
   MSST_REQUIRE(precision == MSST_F16 || precision == MSST_BF16, "precision must be MSST_F16 or MSST_BF16");
   device_ = device;
   bf16_ = precision;
@@ -389,10 +392,12 @@ void Model::load(const std::string& path, int device, int precision) {
   I.chunk_size = j.get_int("chunk_size", I.n_fft * 256);
   I.num_overlap = j.has("num_overlap") ? std::max(1, j.get_int("num_overlap", 2)) : 2;
   I.precision = precision;
-  if (j.get_bool("stft_normalized", false)) fail(MSST_ERR_UNSUPPORTED, "stft_normalized models are not supported");
-  if (j.get_bool("skip_connection", false)) fail(MSST_ERR_UNSUPPORTED, "skip_connection models are not supported");
-  if (j.get_bool("match_input_audio_length", false))
-    fail(MSST_ERR_UNSUPPORTED, "match_input_audio_length models are not supported");
+  stft_norm_ = j.get_bool("stft_normalized", false);
+  skip_ = j.get_bool("skip_connection", false);
+  match_len_ = j.get_bool("match_input_audio_length", false);
+  I.stft_normalized = stft_norm_;
+  I.skip_connection = skip_;
+  I.match_input_audio_length = match_len_;
   if (I.dim_head != 64) fail(MSST_ERR_UNSUPPORTED, "dim_head must be 64");
   if (win_len != I.n_fft) fail(MSST_ERR_UNSUPPORTED, "stft_win_length must equal stft_n_fft");
   if (I.n_fft & (I.n_fft - 1)) fail(MSST_ERR_UNSUPPORTED, "stft_n_fft must be a power of two");
@@ -410,13 +415,12 @@ void Model::load(const std::string& path, int device, int precision) {
   nfreq_.clear();
   bin_list_.clear();
   std::vector<float> denom(nbins_, 1.0f);
-  if (mel_) {
-    if (!csm.has("__precomputed__.freq_indices"))
-      fail(MSST_ERR_UNSUPPORTED, "MelBandRoformer .csm without __precomputed__ band tables");
+  if (mel_ && csm.has("__precomputed__.freq_indices")) {
     const std::vector<int64_t> fi = csm.get("__precomputed__.freq_indices").i64();
     const std::vector<int64_t> nf = csm.get("__precomputed__.num_freqs_per_band").i64();
     const std::vector<int64_t> nb = csm.get("__precomputed__.num_bands_per_freq").i64();
     I.num_bands = j.get_int("num_bands", (int)nf.size());
+    I.bands_from_file = 1;
     MSST_REQUIRE((int)nf.size() == I.num_bands, "num_freqs_per_band length != num_bands");
     size_t k = 0;
     for (int b = 0; b < I.num_bands; ++b) {
@@ -430,9 +434,15 @@ void Model::load(const std::string& path, int device, int precision) {
     }
     MSST_REQUIRE((int)nb.size() == nbins_, "num_bands_per_freq length != n_fft/2+1");
     for (int f = 0; f < nbins_; ++f) denom[f] = std::max((float)nb[f], 1e-8f);
+  } else if (mel_) {
+    // no precomputed tables in the file: derive them at load, as the reference does
+    I.num_bands = j.get_int("num_bands", 60);
+    I.bands_from_file = 0;
+    mel_bands_from_filterbank(denom);
   } else {
     const Json* fpb = j.find("freqs_per_bands");
     MSST_REQUIRE(fpb && fpb->kind == Json::Arr, "BSRoformer config lacks freqs_per_bands");
+    I.bands_from_file = 1;
     int start = 0;
     for (auto& v : fpb->arr) {
       nfreq_.push_back((int)v.num);
@@ -593,6 +603,53 @@ void Model::load(const std::string& path, int device, int precision) {
     }
   }
   MSST_CUDA(cudaDeviceSynchronize());
+  info_.load_ms =
+      (float)std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t_load0).count();
+}
+
+// MelBandRoformer band tables for a .csm without __precomputed__ tensors.  The
+// reference then builds them itself (src/model_mel_band_roformer.cu:214-313,
+// taken at :377) from its HTK-scale triangular filterbank (ops::mel_filterbank,
+// src/ops_misc.cu:469-525): num_bands + 2 points evenly spaced on the mel scale
+// m(f) = 2595 log10(1 + f / 700) between 0 Hz and sr / 2, FFT bin i at
+// sr * i / n_fft Hz, band b's triangle rising from point b to point b + 1 and
+// falling to point b + 2; filter [0][0] and [last][last] forced to 1; bin i
+// belongs to band b where the filter value is > 0.  The arithmetic is fp32 in the
+// same order as the reference's, since band membership is decided by exact
+// comparisons.
+void Model::mel_bands_from_filterbank(std::vector<float>& denom) {
+  const msst_model_info& I = info_;
+  const int nb = I.num_bands;
+  MSST_REQUIRE(nb >= 1, "num_bands must be >= 1");
+  const float f_hi = (float)I.sample_rate / 2.0f;
+  const auto to_mel = [](float f) { return 2595.0f * std::log10(1.0f + f / 700.0f); };
+  const auto to_hz = [](float m) { return 700.0f * (std::pow(10.0f, m / 2595.0f) - 1.0f); };
+  const float m_lo = to_mel(0.0f), m_hi = to_mel(f_hi);
+  std::vector<float> edge(nb + 2);
+  for (int i = 0; i < nb + 2; ++i) edge[i] = to_hz(m_lo + (m_hi - m_lo) * (float)i / (float)(nb + 1));
+  std::vector<int> count(nbins_, 0);
+  for (int b = 0; b < nb; ++b) {
+    const float lo = edge[b], mid = edge[b + 1], hi = edge[b + 2];
+    int n = 0;
+    for (int f = 0; f < nbins_; ++f) {
+      const float hz = (float)I.sample_rate * (float)f / (float)I.n_fft;
+      float v = 0.0f;
+      if (hz >= lo && hz <= mid) {
+        if (mid - lo > 0.0f) v = (hz - lo) / (mid - lo);
+      } else if (hz > mid && hz <= hi) {
+        if (hi - mid > 0.0f) v = (hi - hz) / (hi - mid);
+      }
+      if ((b == 0 && f == 0) || (b == nb - 1 && f == nbins_ - 1)) v = 1.0f;
+      if (v > 0.0f) {
+        bin_list_.push_back(f);
+        ++count[f];
+        ++n;
+      }
+    }
+    MSST_REQUIRE(n > 0, "mel band " + std::to_string(b) + " covers no FFT bin");
+    nfreq_.push_back(n);
+  }
+  for (int f = 0; f < nbins_; ++f) denom[f] = std::max((float)count[f], 1e-8f);
 }
 
 // ===========================================================================
@@ -700,6 +757,7 @@ Model::Work& Model::work(int B, int T) {
   w->big2.reset(2 * big);
   w->ao.reset(2 * (size_t)M * inner_);
   w->mask.reset(4 * (size_t)S * w->BT * sum_dims_);
+  if (skip_ && I.depth > 1) w->skips.reset(4 * (size_t)(I.depth - 1) * M * D);
   w->m_abs = map_2d(w->abs.get(), w->BT, ktot_, ktot_, kGemmBM);
   w->m_xn = map_2d(w->xn.get(), M, D, D, kGemmBM);
   w->m_ao = map_2d(w->ao.get(), M, inner_, inner_, kGemmBM);
@@ -757,6 +815,7 @@ void Model::run_front(const float* audio, int B, long long L, int T, cudaStream_
   bi.gamma = g_bs_.get<float>();
   bi.out = w.abs.get();
   bi.ld = ktot_;
+  bi.spec_scale = stft_norm_ ? 1.0f / std::sqrt((float)I.n_fft) : 1.0f;
   MSST_CUDA(launch_band_input(bi, bf16_, s));
   // band split: one group per band, output rows (bt*nb + band) of the residual stream
   GemmParams p{};
@@ -914,11 +973,30 @@ void Model::run_ffn_block(int d, int axis, int l, float* x, int B, int T, cudaSt
 void Model::run_trunk(int B, int T, cudaStream_t s, Work& w) {
   const msst_model_info& I = info_;
   const float* pending = nullptr;
+  const long long xn_elems = w.M * I.dim;
   for (int d = 0; d < I.depth; ++d) {
+    // skip connections (src/model_mel_band_roformer.cu:846-852,898-901): x += the
+    // outputs of every earlier depth block, which therefore carry their final norm
+    if (skip_ && d > 0)
+      MSST_CUDA(launch_skip_add(w.x.get<float>(), w.skips.get<float>(), d, xn_elems, s));
     for (int axis = 0; axis < 2; ++axis) {
       run_transformer(d, axis, w.x.get<float>(), B, T, pending, s, w);
       const TransformerWeights& tw = axis == 0 ? blocks_[d].first : blocks_[d].second;
       pending = mel_ ? tw.g_final.get<float>() : nullptr;
+    }
+    if (skip_ && d + 1 < I.depth) {
+      if (pending) {
+        RmsNormArgs rn{};
+        rn.x = w.x.get<float>();
+        rn.rows = w.M;
+        rn.D = I.dim;
+        rn.gamma_pre = pending;
+        rn.scale_pre = std::sqrt((float)I.dim);
+        MSST_CUDA(launch_rmsnorm(rn, bf16_, s));
+        pending = nullptr;
+      }
+      MSST_CUDA(cudaMemcpyAsync(w.skips.get<float>() + (size_t)d * xn_elems, w.x.get(), 4 * (size_t)xn_elems,
+                                cudaMemcpyDeviceToDevice, s));
     }
   }
   // final norm (MelBandRoformer: last transformer's norm_output; BSRoformer:
@@ -999,14 +1077,22 @@ void Model::forward(const float* audio, int B, int C, long long L, float* out, c
   ma.T = T;
   ma.nbins = nbins_;
   ma.zero_dc = zero_dc_ ? 1 : 0;
+  ma.spec_scale = stft_norm_ ? 1.0f / std::sqrt((float)I.n_fft) : 1.0f;
+  ma.out_scale = stft_norm_ ? std::sqrt((float)I.n_fft) : 1.0f;
   MSST_CUDA(launch_mask_apply(ma, s));
   // iSTFT (src/ops_stft.cu:371-489)
   const int BSC = B * I.num_stems * C_;
   if (cufftExecC2R(fft_plan(CUFFT_C2R, BSC * T, s), w.ispec.get<cufftComplex>(), w.frames.get<cufftReal>()) !=
       CUFFT_SUCCESS)
     fail(MSST_ERR_CUDA, "cufftExecC2R failed");
+  // output length: (T-1)*hop, or the input's length for match_input_audio_length models
+  // (src/model_mel_band_roformer.cu:764,1021; src/model_bs_roformer.cu:436,595)
   MSST_CUDA(launch_istft_ola(w.frames.get<float>(), BSC, T, I.n_fft, I.hop_length, window_.get<float>(),
-                             istft_wsum(T), out, s));
+                             istft_wsum(T), out, out_length(L), s));
+}
+
+long long Model::out_length(long long L) const {
+  return match_len_ ? L : (L / info_.hop_length) * info_.hop_length;
 }
 
 void Model::masks(const float* audio, int B, int C, long long L, float* masks_out, cudaStream_t s) {
@@ -1101,7 +1187,8 @@ void Model::separate(const float* track, int C, long long L, float overlap, int 
   const int S = I.num_stems;
   if (I.chunk_size <= 0 || L <= I.chunk_size) {
     // short input: one forward over the whole track (src/inference_app.cpp:463-472)
-    MSST_REQUIRE(L % I.hop_length == 0, "whole-track forward needs length % hop_length == 0");
+    MSST_REQUIRE(match_len_ || L % I.hop_length == 0,
+                 "whole-track forward needs length % hop_length == 0 (or a match_input_audio_length model)");
     forward(track, 1, C, L, out, s);
     return;
   }

@@ -46,6 +46,8 @@ class Model {
   int device() const { return device_; }
 
   void forward(const float* audio, int B, int C, long long L, float* out, cudaStream_t s);
+  // Samples per channel that forward() writes for an input of L samples.
+  long long out_length(long long L) const;
   void masks(const float* audio, int B, int C, long long L, float* masks_out, cudaStream_t s);
   void transformer(int depth_index, int axis, float* x, int B, int T, cudaStream_t s);
   // One layer's attention block (RMSNorm + gates, QKV + RoPE, attention, out
@@ -78,6 +80,7 @@ class Model {
   struct Work;  // per-(B, T) workspace
   Work& work(int B, int T);
   void run_trunk(int B, int T, cudaStream_t s, Work& w);
+  void mel_bands_from_filterbank(std::vector<float>& denom);
   void run_front(const float* audio, int B, long long L, int T, cudaStream_t s, Work& w);
   void run_masks(int B, int T, cudaStream_t s, Work& w, float* masks_out);
   void run_transformer(int d, int axis, float* x, int B, int T, const float* pending_gamma, cudaStream_t s, Work& w);
@@ -97,6 +100,7 @@ class Model {
   bool mel_ = true;
   int C_ = 2, nbins_ = 1025, hid_ = 1536, n_lin_ = 3, inner_ = 512, ff_ = 1536;
   bool zero_dc_ = true;
+  bool stft_norm_ = false, skip_ = false, match_len_ = false;
   int num_sms_ = 148;
 
   std::vector<int> nfreq_, bin_start_, bin_list_, dims_, kpad_, kcol_, dim_off_, out3_off_;

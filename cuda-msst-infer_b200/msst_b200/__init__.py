@@ -58,7 +58,9 @@ class BandTables(ctypes.Structure):
 class ModelInfo(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int) for n in (
         "model_type", "dim", "depth", "heads", "dim_head", "num_bands", "num_stems", "channels", "n_fft",
-        "hop_length", "sample_rate", "chunk_size", "num_overlap", "sum_band_dims", "precision")]
+        "hop_length", "sample_rate", "chunk_size", "num_overlap", "sum_band_dims", "precision",
+        "stft_normalized", "skip_connection", "match_input_audio_length", "bands_from_file")] + [
+        ("load_ms", ctypes.c_float)]
 
     def as_dict(self):
         return {n: getattr(self, n) for n, _ in self._fields_}
@@ -323,6 +325,8 @@ class Model:
             pass
 
     def out_length(self, length: int) -> int:
+        if self.info["match_input_audio_length"]:
+            return length
         return (length // self.info["hop_length"]) * self.info["hop_length"]
 
     def forward(self, audio, stream=None):

@@ -86,6 +86,26 @@ def mel_bands(sr: int, n_fft: int, num_bands: int, stereo: bool) -> MelBands:
     return MelBands(idx.astype(np.int64), fpb.sum(axis=1).astype(np.int64), fpb.sum(axis=0).astype(np.int64))
 
 
+def htk_band_sizes(sr: int, n_fft: int, num_bands: int) -> np.ndarray:
+    """Bins per band of the band tables the reference derives at load when a .csm
+    has no __precomputed__ tensors (its HTK-scale filterbank, thresholded at > 0,
+    first and last corners forced on; src/ops_misc.cu:469-525,
+    src/model_mel_band_roformer.cu:214-313), in fp32 as the reference computes them.
+    Only the sizes are needed here, to shape the band-split and mask weights."""
+    f32 = np.float32
+    to_mel = lambda f: f32(2595.0) * np.log10(f32(1.0) + f / f32(700.0))
+    to_hz = lambda m: f32(700.0) * (np.power(f32(10.0), m / f32(2595.0)) - f32(1.0))
+    m0, m1 = to_mel(f32(0.0)), to_mel(f32(sr) / f32(2.0))
+    i = np.arange(num_bands + 2, dtype=np.float32)
+    pts = to_hz(m0 + (m1 - m0) * i / f32(num_bands + 1)).astype(np.float32)
+    fr = (f32(sr) * np.arange(n_fft // 2 + 1, dtype=np.float32) / f32(n_fft)).astype(np.float32)
+    lo, mid, hi = pts[:-2, None], pts[1:-1, None], pts[2:, None]
+    on = ((fr >= lo) & (fr <= mid) & (mid - lo > 0) & (fr > lo)) | ((fr > mid) & (fr < hi) & (hi - mid > 0))
+    on[0, 0] = True
+    on[-1, -1] = True
+    return on.sum(axis=1).astype(np.int64)
+
+
 # ---------------------------------------------------------------------------
 # Model configs (BASELINE configs 0-2)
 # ---------------------------------------------------------------------------
@@ -113,26 +133,44 @@ def bsr_config(depth: int = 12, dim: int = 512, num_stems: int = 1, freqs_per_ba
     return cfg
 
 
-def band_dims(cfg: dict) -> list[int]:
+def band_dims(cfg: dict, precomputed_bands: bool = True) -> list[int]:
     ch = 2 if cfg.get("stereo", True) else 1
     if cfg["model_type"] == "mel_band_roformer":
+        if not precomputed_bands:
+            return [int(2 * n * ch) for n in htk_band_sizes(cfg["sample_rate"], cfg["stft_n_fft"], cfg["num_bands"])]
         mb = mel_bands(cfg["sample_rate"], cfg["stft_n_fft"], cfg["num_bands"], cfg.get("stereo", True))
         return mb.band_freq_dims(ch)
     return [2 * f * ch for f in cfg["freqs_per_bands"]]
 
 
-def make_weights(cfg: dict, seed: int = 0, std: float = 0.02) -> dict[str, np.ndarray]:
-    """Random-init state dict with the reference's tensor names (fp32; gammas = 1)."""
+def round_bf16(x: np.ndarray) -> np.ndarray:
+    """fp32 -> nearest bf16 value (ties to even), kept as fp32."""
+    u = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32)
+
+
+def make_weights(cfg: dict, seed: int = 0, std: float = 0.02, precomputed_bands: bool = True,
+                 weight_dtype: str = "fp32") -> dict[str, np.ndarray]:
+    """Random-init state dict with the reference's tensor names (fp32 arrays; gammas = 1).
+
+    precomputed_bands=False leaves out the MelBandRoformer's __precomputed__ band
+    tables (a checkpoint converted without librosa), so the band weights take the
+    shapes of the tables the reference then derives itself.  weight_dtype="bf16"
+    draws the same N(0, std) matrices and rounds them to bf16 values (a bf16
+    checkpoint; the .csm container still stores them as fp32).
+    """
     rng = np.random.default_rng(seed)
     mel = cfg["model_type"] == "mel_band_roformer"
     dim, heads, dh = cfg["dim"], cfg["heads"], cfg["dim_head"]
     inner = heads * dh
     ff = dim * cfg["mlp_expansion_factor"]
-    dims = band_dims(cfg)
+    dims = band_dims(cfg, precomputed_bands)
     sd: dict[str, np.ndarray] = {}
+    wcast = round_bf16 if weight_dtype == "bf16" else (lambda a: a)
 
     def lin(name, out_f, in_f, bias=True):
-        sd[name + ".weight"] = (rng.standard_normal((out_f, in_f)) * std).astype(np.float32)
+        sd[name + ".weight"] = wcast((rng.standard_normal((out_f, in_f)) * std).astype(np.float32))
         if bias:
             sd[name + ".bias"] = (rng.standard_normal(out_f) * std).astype(np.float32)
 
@@ -163,7 +201,7 @@ def make_weights(cfg: dict, seed: int = 0, std: float = 0.02) -> dict[str, np.nd
             sizes = [dim] + [ff] * (n_lin - 1) + [2 * d]
             for i in range(n_lin):
                 lin(f"mask_estimators.{s}.to_freqs.{b}.0.{2 * i}", sizes[i + 1], sizes[i])
-    if mel:
+    if mel and precomputed_bands:
         mb = mel_bands(cfg["sample_rate"], cfg["stft_n_fft"], cfg["num_bands"], cfg.get("stereo", True))
         sd["__precomputed__.freq_indices"] = mb.freq_indices
         sd["__precomputed__.num_freqs_per_band"] = mb.num_freqs_per_band

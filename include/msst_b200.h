@@ -63,6 +63,11 @@ typedef struct msst_model_info {
   int n_fft, hop_length, sample_rate, chunk_size, num_overlap;
   int sum_band_dims; /* width of one mask row, sum over bands of 2*channels*freqs */
   int precision;     /* MSST_F16 or MSST_BF16 */
+  /* config switches of the reference drivers (MBRConfig / BSRConfig::from_json) */
+  int stft_normalized, skip_connection, match_input_audio_length;
+  int bands_from_file; /* MelBandRoformer: 1 = __precomputed__ band tables of the .csm,
+                          0 = computed at load (the reference's mel fallback) */
+  float load_ms;       /* wall time of msst_model_load (read, convert, upload) */
 } msst_model_info;
 
 const char* msst_last_error(void);

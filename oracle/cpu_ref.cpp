@@ -315,4 +315,47 @@ void msst_oracle_istft(const float* spec, int64_t B, int64_t T, int n_fft, int h
   }
 }
 
+// MelBandRoformer band tables when a .csm carries no __precomputed__ tensors:
+// the reference derives them from its HTK-scale triangular filterbank
+// (ops::mel_filterbank, src/ops_misc.cu:469-525, thresholded at > 0 with the
+// first and last corners forced to 1 in compute_mel_bands,
+// src/model_mel_band_roformer.cu:214-240).  fp32 arithmetic in the reference's
+// order, contraction into FMAs off (membership is decided by exact comparisons).
+// Writes nfreq[num_bands], the bins of every band in order into bins
+// (capacity num_bands * (n_fft/2+1)) and the number of bands per bin into count;
+// returns the total number of (band, bin) pairs, or -1 if a band is empty.
+__attribute__((optimize("fp-contract=off"))) int msst_oracle_mel_bands_htk(int sr, int n_fft, int num_bands,
+                                                                         int* nfreq, int* bins, int* count) {
+  const int nbins = n_fft / 2 + 1;
+  auto mel = [](float f) { return 2595.0f * std::log10(1.0f + f / 700.0f); };
+  auto hz = [](float m) { return 700.0f * (std::pow(10.0f, m / 2595.0f) - 1.0f); };
+  const float m0 = mel(0.0f), m1 = mel((float)sr / 2.0f);
+  std::vector<float> pt(num_bands + 2);
+  for (int i = 0; i <= num_bands + 1; ++i) pt[i] = hz(m0 + (m1 - m0) * (float)i / (float)(num_bands + 1));
+  for (int f = 0; f < nbins; ++f) count[f] = 0;
+  int total = 0;
+  for (int b = 0; b < num_bands; ++b) {
+    int n = 0;
+    for (int f = 0; f < nbins; ++f) {
+      const float fr = (float)sr * (float)f / (float)n_fft;
+      const float l = pt[b], c = pt[b + 1], r = pt[b + 2];
+      float v = 0.0f;
+      if (fr >= l && fr <= c) {
+        if (c - l > 0.0f) v = (fr - l) / (c - l);
+      } else if (fr > c && fr <= r) {
+        if (r - c > 0.0f) v = (r - fr) / (r - c);
+      }
+      if ((b == 0 && f == 0) || (b == num_bands - 1 && f == nbins - 1)) v = 1.0f;
+      if (v > 0.0f) {
+        bins[total++] = f;
+        ++count[f];
+        ++n;
+      }
+    }
+    if (n == 0) return -1;
+    nfreq[b] = n;
+  }
+  return total;
+}
+
 }  // extern "C"

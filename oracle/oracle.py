@@ -57,6 +57,8 @@ def lib():
         L.msst_oracle_hann.argtypes = [c_int, _f32p]
         L.msst_oracle_stft.argtypes = [_f32p, i64, i64, c_int, c_int, _f32p, _f32p]
         L.msst_oracle_istft.argtypes = [_f32p, i64, i64, c_int, c_int, _f32p, _f32p]
+        L.msst_oracle_mel_bands_htk.argtypes = [c_int, c_int, c_int, ctypes.POINTER(c_int), ctypes.POINTER(c_int),
+                                                ctypes.POINTER(c_int)]
         L.msst_oracle_threads.restype = c_int
         L.msst_oracle_set_threads.argtypes = [c_int]
         _lib = L
@@ -171,6 +173,22 @@ def istft(spec, n_fft, hop, win):
     return out
 
 
+def mel_bands_htk(sr: int, n_fft: int, num_bands: int):
+    """(num_freqs_per_band, bins of every band in order, bands per bin) of the reference's
+    fallback when a .csm has no __precomputed__ tables (src/model_mel_band_roformer.cu:214-313,
+    src/ops_misc.cu:469-525), from cpu_ref.cpp's fp32 restatement."""
+    nbins = n_fft // 2 + 1
+    nfreq = np.zeros(num_bands, np.int32)
+    bins = np.zeros(num_bands * nbins, np.int32)
+    count = np.zeros(nbins, np.int32)
+    ip = ctypes.POINTER(ctypes.c_int)
+    n = lib().msst_oracle_mel_bands_htk(sr, n_fft, num_bands, nfreq.ctypes.data_as(ip), bins.ctypes.data_as(ip),
+                                        count.ctypes.data_as(ip))
+    if n < 0:
+        raise ValueError("a mel band covers no FFT bin")
+    return nfreq.astype(np.int64), bins[:n].astype(np.int64), count.astype(np.int64)
+
+
 # --------------------------------------------------------------------------- model
 class Model:
     """fp32 CPU forward of a MelBandRoformer / BSRoformer from (config, state dict)."""
@@ -181,10 +199,15 @@ class Model:
         self.mel = "__precomputed__.freq_indices" in self.sd or cfg.get("model_type") == "mel_band_roformer"
         self.ch = 2 if cfg.get("stereo", True) else 1
         self.nbins = cfg["stft_n_fft"] // 2 + 1
-        if self.mel:
+        if self.mel and "__precomputed__.freq_indices" not in self.sd:
+            # the reference's fallback: HTK filterbank bands computed at load
+            nfpb, mono, nbpf = mel_bands_htk(cfg["sample_rate"], cfg["stft_n_fft"], cfg.get("num_bands", 60))
+            self.freq_indices = (mono[:, None] * self.ch + np.arange(self.ch)[None, :]).reshape(-1)
+        elif self.mel:
             self.freq_indices = self.sd["__precomputed__.freq_indices"].astype(np.int64)
             nfpb = self.sd["__precomputed__.num_freqs_per_band"].astype(np.int64)
             nbpf = self.sd["__precomputed__.num_bands_per_freq"].astype(np.int64)
+        if self.mel:
             self.dims = [int(2 * n * self.ch) for n in nfpb]
             self.nbpf = np.repeat(nbpf, self.ch).astype(np.float32)
             self.num_bands = cfg.get("num_bands", len(self.dims))
@@ -244,6 +267,9 @@ class Model:
         cfg = self.cfg
         B, C, L = audio.shape
         st = stft(audio.reshape(B * C, L), cfg["stft_n_fft"], cfg["stft_hop_length"], self.win)
+        if cfg.get("stft_normalized", False):
+            # src/ops_stft.cu:358-365
+            st = st * (np.float32(1.0) / np.sqrt(np.float32(cfg["stft_n_fft"])))
         F, T = st.shape[1], st.shape[2]
         st = st.reshape(B, C, F, T, 2).transpose(0, 2, 1, 3, 4)
         return np.ascontiguousarray(st).reshape(B, F * C, T, 2)
@@ -328,13 +354,24 @@ class Model:
         out = np.ascontiguousarray(out).reshape(B * S * C, F, T, 2)
         if cfg.get("zero_dc", True):
             out[:, 0] = 0.0
+        if cfg.get("stft_normalized", False):
+            # the iSTFT undoes the normalisation first (src/ops_stft.cu:380-389)
+            out = out * np.sqrt(np.float32(cfg["stft_n_fft"]))
         y = istft(out, cfg["stft_n_fft"], cfg["stft_hop_length"], self.win)
         y = y.reshape(B, S, C, -1)
         return y[:, 0] if S == 1 else y
 
     def forward(self, audio):
         masks, st = self.masks(audio)
-        return self.apply_masks(masks, st)
+        y = self.apply_masks(masks, st)
+        if self.cfg.get("match_input_audio_length", False):
+            # ops::istft's `length`: zero-pad or truncate to the input length
+            # (src/model_mel_band_roformer.cu:764, src/ops_stft.cu:484-493)
+            L = audio.shape[-1]
+            if y.shape[-1] < L:
+                y = np.concatenate([y, np.zeros(y.shape[:-1] + (L - y.shape[-1],), np.float32)], axis=-1)
+            y = np.ascontiguousarray(y[..., :L])
+        return y
 
 
 # --------------------------------------------------------------------------- chunking

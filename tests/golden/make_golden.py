@@ -113,23 +113,164 @@ def htdemucs_ops(L, out_dir):
     return summary
 
 
+# Models with the reference drivers' optional config switches, small enough for
+# whole-array fixtures: band tables computed at load (no __precomputed__ tensors),
+# skip connections across depth blocks, a normalised STFT and the output cut or
+# padded to the input length (an input that is not a multiple of hop_length).
+OPTION_MODELS = {
+    "mbr_opts": dict(kind="mbr", cfg=dict(depth=2, dim=128, skip_connection=True, stft_normalized=True,
+                                          match_input_audio_length=True), seed=31, precomputed_bands=False),
+    "bsr_opts": dict(kind="bsr", cfg=dict(depth=2, dim=128, skip_connection=True, stft_normalized=True,
+                                          match_input_audio_length=True), seed=32),
+}
+OPTION_AUDIO = dict(n_samples=22050 + 123, seed=7)
+
+
+def _load(L, path, fp16):
+    h = L.refh_load(path.encode(), 0, fp16)
+    if not h:
+        raise RuntimeError(L.refh_last_error().decode())
+    return h
+
+
+def _run(L, fn, h, audio, shape):
+    ll = ctypes.c_longlong
+    buf = np.zeros(int(np.prod(shape)) + 16, np.float32)
+    n = ll(0)
+    B, C, Ls = audio.shape
+    check(fn(h, P(np.ascontiguousarray(audio)), B, C, Ls, P(buf), buf.size, ctypes.byref(n)), L)
+    assert n.value == int(np.prod(shape)), (n.value, shape)
+    return buf[: n.value].reshape(shape).copy()
+
+
+def option_models(L, out_dir):
+    """<name>_fp32.npz / _fp16.npz for OPTION_MODELS: whole masks and outputs."""
+    tmp = tempfile.mkdtemp()
+    summary = {}
+    audio = synth.make_audio(OPTION_AUDIO["n_samples"], 2, OPTION_AUDIO["seed"])[None]
+    for name, spec in OPTION_MODELS.items():
+        cfg = model_cfg(spec)
+        sd = synth.make_weights(cfg, spec["seed"], precomputed_bands=spec.get("precomputed_bands", True))
+        path = os.path.join(tmp, name + ".csm")
+        synth.write_csm(path, cfg, sd)
+        om = oracle.Model(cfg, sd)
+        o_masks, _ = om.masks(audio)
+        o_out = om.forward(audio)
+        for fp16 in (0, 1):
+            h = _load(L, path, fp16)
+            masks = _run(L, L.refh_masks, h, audio, o_masks.shape)
+            out = _run(L, L.refh_forward, h, audio, o_out.shape)
+            L.refh_free(h)
+            tag = f"{name}_{'fp16' if fp16 else 'fp32'}"
+            np.savez_compressed(os.path.join(out_dir, tag + ".npz"), masks=masks, out=out,
+                                meta=json.dumps(dict(model=name, spec=spec, fp16=fp16, **OPTION_AUDIO)))
+            summary[tag] = dict(mask_rel_l2_oracle=rel_l2(o_masks, masks), out_snr_db_oracle=snr_db(o_out, out))
+            print(tag, summary[tag], flush=True)
+    return summary
+
+
+# The benchmarked shapes (BASELINE configs 1 and 2) at full size; the arrays are
+# far too large to commit, so the fixtures keep seeded samples of them: windows
+# of the output waveforms and rows of the fp32 masks.
+BENCH_SHAPES = {
+    # config 1: MelBandRoformer D384 x 6, the bench's weights (seed 0) and 68.5 s track
+    # (seed 1234), separated with overlap 0.25 and 4 chunks per forward; masks of the
+    # track's first forward batch (its first 4 chunks)
+    "cfg1": dict(kind="mbr", cfg=dict(depth=6, dim=384), seed=0, weight_dtype="fp32", track_seconds=68.5,
+                 track_seed=1234, overlap=0.25, chunk_batch=4),
+    # config 2: BS-Roformer D512 x 12 with bf16 weights (seed 0), one forward of 8
+    # consecutive 352800-sample chunks of a seeded track
+    "cfg2": dict(kind="bsr", cfg=dict(depth=12, dim=512), seed=0, weight_dtype="bf16", chunks=8,
+                 audio_seed=2024),
+}
+N_WINDOWS, WINDOW, N_MASK_ROWS = 16, 4096, 32
+
+
+def sample_windows(n_rows, length, seed):
+    rng = np.random.default_rng(seed)
+    return np.sort(rng.integers(0, length - WINDOW, N_WINDOWS)), rng.choice(n_rows, N_MASK_ROWS, replace=False)
+
+
+def bench_shapes(L, out_dir):
+    """cfg1_ref.npz and cfg2_ref.npz: seeded samples of the reference's fp32 and fp16 outputs."""
+    tmp = tempfile.mkdtemp()
+    summary = {}
+    for name, spec in BENCH_SHAPES.items():
+        cfg = model_cfg(spec)
+        sd = synth.make_weights(cfg, spec["seed"], weight_dtype=spec["weight_dtype"])
+        path = os.path.join(tmp, name + ".csm")
+        synth.write_csm(path, cfg, sd)
+        arrays = {}
+        if name == "cfg1":
+            n = int(round(spec["track_seconds"] * 44100))
+            track = synth.make_audio(n, 2, spec["track_seed"])
+            step = oracle.resolve_step(cfg["chunk_size"], spec["overlap"], cfg["num_overlap"])
+            first = np.stack(oracle.chunk_inputs(track, cfg["chunk_size"], step)[: spec["chunk_batch"]])
+            T = cfg["chunk_size"] // cfg["stft_hop_length"] + 1
+            mshape = (spec["chunk_batch"], 1, T, sum(synth.band_dims(cfg)))
+            win, rows = sample_windows(spec["chunk_batch"] * T, n, 5)
+            for fp16 in (0, 1):
+                h = _load(L, path, fp16)
+                buf = np.zeros(track.size + 16, np.float32)
+                cnt, ms = ctypes.c_longlong(0), ctypes.c_double(0)
+                check(L.refh_separate(h, P(track), 2, n, spec["overlap"], spec["chunk_batch"], P(buf), buf.size,
+                                      ctypes.byref(cnt), ctypes.byref(ms)), L)
+                sep = buf[: cnt.value].reshape(2, n)
+                masks = _run(L, L.refh_masks, h, first, mshape).reshape(-1, mshape[-1])
+                L.refh_free(h)
+                tag = "fp16" if fp16 else "fp32"
+                arrays[f"out_{tag}"] = np.stack([sep[:, w:w + WINDOW] for w in win], axis=1)
+                arrays[f"mask_rows_{tag}"] = masks[rows]
+                print(name, tag, f"separate {ms.value:.1f} ms", flush=True)
+        else:
+            B = spec["chunks"]
+            audio = synth.make_audio(B * cfg["chunk_size"], 2, spec["audio_seed"])
+            audio = np.ascontiguousarray(audio.reshape(2, B, cfg["chunk_size"]).transpose(1, 0, 2))
+            T = cfg["chunk_size"] // cfg["stft_hop_length"] + 1
+            mshape = (B, 1, T, sum(synth.band_dims(cfg)))
+            win, rows = sample_windows(B * T, cfg["chunk_size"], 6)
+            for fp16 in (0, 1):
+                h = _load(L, path, fp16)
+                out = _run(L, L.refh_forward, h, audio, (B, 2, cfg["chunk_size"]))
+                masks = _run(L, L.refh_masks, h, audio, mshape).reshape(-1, mshape[-1])
+                L.refh_free(h)
+                tag = "fp16" if fp16 else "fp32"
+                arrays[f"out_{tag}"] = np.stack([out[:, :, w:w + WINDOW] for w in win], axis=2)
+                arrays[f"mask_rows_{tag}"] = masks[rows]
+                print(name, tag, flush=True)
+        arrays["windows"], arrays["mask_rows"] = win, rows
+        np.savez_compressed(os.path.join(out_dir, f"{name}_ref.npz"), meta=json.dumps(dict(spec=spec,
+                            window=WINDOW)), **arrays)
+        summary[name] = dict(out_snr_db_fp16_vs_fp32=snr_db(arrays["out_fp16"], arrays["out_fp32"]),
+                             mask_rel_l2_fp16_vs_fp32=rel_l2(arrays["mask_rows_fp16"], arrays["mask_rows_fp32"]))
+        print(name, summary[name], flush=True)
+    return summary
+
+
+def _merge_summary(out_dir, key, value):
+    path = os.path.join(out_dir, "pin_summary.json")
+    summary = json.load(open(path)) if os.path.exists(path) else {}
+    summary[key] = value
+    with open(path, "w") as f:
+        json.dump(summary, f, indent=1)
+    print(json.dumps(value, indent=1))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", required=True)
     ap.add_argument("--full", action="store_true", help="also pin config 0 at full size (summary only)")
-    ap.add_argument("--only", choices=["all", "htdemucs-ops"], default="all",
-                    help="htdemucs-ops: write ops_htdemucs.npz only and merge its pin summary")
+    ap.add_argument("--only", choices=["all", "htdemucs-ops", "options", "bench-shapes"], default="all",
+                    help="write only that group of fixtures and merge its pin summary")
     args = ap.parse_args()
     os.makedirs(args.out, exist_ok=True)
     L = ref_lib()
     if args.only == "htdemucs-ops":
-        path = os.path.join(args.out, "pin_summary.json")
-        summary = json.load(open(path)) if os.path.exists(path) else {}
-        summary["htdemucs_ops"] = htdemucs_ops(L, args.out)
-        with open(path, "w") as f:
-            json.dump(summary, f, indent=1)
-        print(json.dumps(summary["htdemucs_ops"], indent=1))
-        return
+        return _merge_summary(args.out, "htdemucs_ops", htdemucs_ops(L, args.out))
+    if args.only == "options":
+        return _merge_summary(args.out, "options", option_models(L, args.out))
+    if args.only == "bench-shapes":
+        return _merge_summary(args.out, "bench_shapes", bench_shapes(L, args.out))
     tmp = tempfile.mkdtemp()
     summary = {}
     ll = ctypes.c_longlong

@@ -133,3 +133,16 @@ def test_kernel_timing_api_without_gpu():
     kernel_timing(False)
     assert kernel_timing_report() == {}
     assert kernel_launches(reset=True) >= 0
+
+
+def test_htk_band_sizes_match_oracle():
+    """synth's band sizes for checkpoints without precomputed tables (used to shape
+    their weights) equal the oracle's C restatement of the reference's fallback."""
+    import oracle
+    from msst_b200 import synth
+
+    for nb in (32, 48, 60, 64):
+        sizes = synth.htk_band_sizes(44100, 2048, nb)
+        nfreq, bins, count = oracle.mel_bands_htk(44100, 2048, nb)
+        np.testing.assert_array_equal(sizes, nfreq)
+        assert count.min() >= 1 and bins.size == nfreq.sum()
