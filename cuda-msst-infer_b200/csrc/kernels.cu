@@ -531,19 +531,26 @@ __global__ void __launch_bounds__(256)
 __global__ void __launch_bounds__(256)
     istft_ola_kernel(const float* __restrict__ frames, int BSC, int T, int n_fft, int hop,
                      const float* __restrict__ win, const float* __restrict__ wsum, float* __restrict__ out,
-                     long long Lout) {
+                     long long Lout, int ref_compat) {
   const long long Lrec = (long long)(T - 1) * hop;  // reconstructed samples; the rest of a row is zero
+  const long long full = Lrec + n_fft;                // untrimmed reconstruction per row
   const long long total = (long long)BSC * Lout;
   const int pad = n_fft / 2;
   const float inv_n = 1.0f / (float)n_fft;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
-    const long long bsc = i / Lout;
-    if (i - bsc * Lout >= Lrec) {
+    long long bsc = i / Lout;
+    const long long j = i - bsc * Lout;
+    if (j >= Lrec) {
       out[i] = 0.f;
       continue;
     }
-    const long long p = i - bsc * Lout + pad;
+    long long p = j + pad;
+    if (ref_compat) {
+      const long long flat = pad + bsc * Lrec + j;
+      bsc = flat / full;
+      p = flat - bsc * full;
+    }
     long long t_lo = (p - n_fft + hop) / hop;  // ceil((p - n_fft + 1) / hop) for p >= n_fft - 1
     if (p - n_fft + 1 <= 0) t_lo = 0;
     long long t_hi = p / hop;
@@ -732,10 +739,12 @@ cudaError_t launch_stft_frames(const float* audio, long long L, int BC, int T, i
 }
 
 cudaError_t launch_istft_ola(const float* frames, int BSC, int T, int n_fft, int hop, const float* win,
-                             const float* wsum, float* out, long long out_len, cudaStream_t s) {
+                             const float* wsum, float* out, long long out_len, int ref_compat, cudaStream_t s) {
+  if (out_len < (long long)(T - 1) * hop) return cudaErrorInvalidValue;
+  if (out_len == (long long)(T - 1) * hop) ref_compat = 0;  // nothing padded: the rows are plain
   LaunchScope scope("istft_ola", 0.0, (double)BSC * T * n_fft * 4.0 + (double)BSC * (double)out_len * 4.0, s);
   istft_ola_kernel<<<grid_for((long long)BSC * out_len), 256, 0, s>>>(frames, BSC, T, n_fft, hop, win, wsum, out,
-                                                                      out_len);
+                                                                      out_len, ref_compat);
   return cudaGetLastError();
 }
 

@@ -106,10 +106,16 @@ cudaError_t launch_stft_frames(const float* audio, long long L, int BC, int T, i
 // output sample gathers its <= ceil(n_fft/hop) windowed frames, scales by
 // 1/n_fft, divides by the summed squared window where > 1e-8 and drops n_fft/2
 // samples of centre padding.  out [BSC, out_len]: the (T-1)*hop reconstructed
-// samples, zero-padded or truncated to out_len (the `length` argument of
+// samples, zero-padded to out_len >= (T-1)*hop (the `length` argument of
 // ops::istft, src/ops_stft.cu:484-493; out_len = (T-1)*hop is the default).
+// ref_compat (only meaningful when out_len > (T-1)*hop): reproduce the
+// reference's zero padding of the centre-trimmed slice, whose kernel reads its
+// strided source as if it were contiguous (src/tensor.cu:1184-1216 on the view
+// of src/ops_stft.cu:476-480): output row r, sample i < (T-1)*hop is the full
+// reconstruction (n_fft + (T-1)*hop samples per row) at flat position
+// n_fft/2 + r*(T-1)*hop + i.  Row 0 is unaffected; later rows are shifted.
 cudaError_t launch_istft_ola(const float* frames, int BSC, int T, int n_fft, int hop, const float* win,
-                             const float* wsum, float* out, long long out_len, cudaStream_t s);
+                             const float* wsum, float* out, long long out_len, int ref_compat, cudaStream_t s);
 
 // Skip connections of the Roformer depth loop (src/model_mel_band_roformer.cu:846-852):
 // x += skips[0] + skips[1] + ... + skips[count-1], added one at a time in that order

@@ -1053,6 +1053,11 @@ void Model::run_masks(int B, int T, cudaStream_t s, Work& w, float* masks_out) {
 }
 
 void Model::forward(const float* audio, int B, int C, long long L, float* out, cudaStream_t s) {
+  forward_impl(audio, B, C, L, out, false, s);
+}
+
+void Model::forward_impl(const float* audio, int B, int C, long long L, float* out, bool fix_padding,
+                         cudaStream_t s) {
   const msst_model_info& I = info_;
   MSST_REQUIRE(C == C_, "channel count does not match the model (stereo=" + std::to_string(C_ == 2) + ")");
   MSST_REQUIRE(B >= 1 && L > I.n_fft / 2, "audio too short");
@@ -1086,9 +1091,10 @@ void Model::forward(const float* audio, int B, int C, long long L, float* out, c
       CUFFT_SUCCESS)
     fail(MSST_ERR_CUDA, "cufftExecC2R failed");
   // output length: (T-1)*hop, or the input's length for match_input_audio_length models
-  // (src/model_mel_band_roformer.cu:764,1021; src/model_bs_roformer.cu:436,595)
+  // (src/model_mel_band_roformer.cu:764,1021; src/model_bs_roformer.cu:436,595), whose
+  // zero padding reproduces the reference's unless fix_padding
   MSST_CUDA(launch_istft_ola(w.frames.get<float>(), BSC, T, I.n_fft, I.hop_length, window_.get<float>(),
-                             istft_wsum(T), out, out_length(L), s));
+                             istft_wsum(T), out, out_length(L), fix_padding ? 0 : 1, s));
 }
 
 long long Model::out_length(long long L) const {
@@ -1189,7 +1195,7 @@ void Model::separate(const float* track, int C, long long L, float overlap, int 
     // short input: one forward over the whole track (src/inference_app.cpp:463-472)
     MSST_REQUIRE(match_len_ || L % I.hop_length == 0,
                  "whole-track forward needs length % hop_length == 0 (or a match_input_audio_length model)");
-    forward(track, 1, C, L, out, s);
+    forward_impl(track, 1, C, L, out, (flags & MSST_SEPARATE_FIX_TAIL_PADDING) != 0, s);
     return;
   }
   int chunk, step, nchunks;

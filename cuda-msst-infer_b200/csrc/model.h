@@ -80,6 +80,7 @@ class Model {
   struct Work;  // per-(B, T) workspace
   Work& work(int B, int T);
   void run_trunk(int B, int T, cudaStream_t s, Work& w);
+  void forward_impl(const float* audio, int B, int C, long long L, float* out, bool fix_padding, cudaStream_t s);
   void mel_bands_from_filterbank(std::vector<float>& denom);
   void run_front(const float* audio, int B, long long L, int T, cudaStream_t s, Work& w);
   void run_masks(int B, int T, cudaStream_t s, Work& w, float* masks_out);

@@ -279,11 +279,12 @@ void msst_oracle_stft(const float* sig, int64_t B, int64_t L, int n_fft, int hop
 // torch.istft(center=True) as src/ops_stft.cu:371-489: C2R inverse (imaginary parts of
 // the DC and Nyquist bins ignored, as cuFFT's C2R does), 1/n_fft, window, overlap-add,
 // divide by the summed squared window where it exceeds 1e-8, trim n_fft/2 each side.
-// spec [B, F, T, 2] -> out [B, (T-1)*hop] (length = n_fft + (T-1)*hop - n_fft).
+// spec [B, F, T, 2] -> out [B, (T-1)*hop] (length = n_fft + (T-1)*hop - n_fft); with
+// trim = 0 the whole n_fft + (T-1)*hop samples per row.
 void msst_oracle_istft(const float* spec, int64_t B, int64_t T, int n_fft, int hop, const float* win,
-                       float* out) {
+                       float* out, int trim) {
   const int64_t F = n_fft / 2 + 1;
-  const int64_t full = n_fft + (T - 1) * hop, pad = n_fft / 2, Lout = full - 2 * pad;
+  const int64_t full = n_fft + (T - 1) * hop, pad = trim ? n_fft / 2 : 0, Lout = full - 2 * pad;
   std::vector<float> wsum(full, 0.f);
   for (int64_t t = 0; t < T; ++t)
     for (int n = 0; n < n_fft; ++n) wsum[t * hop + n] += win[n] * win[n];

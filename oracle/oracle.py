@@ -56,7 +56,7 @@ def lib():
         L.msst_oracle_layernorm.argtypes = [_f32p, _f32p, _f32p, _f32p, i64, i64, c_float]
         L.msst_oracle_hann.argtypes = [c_int, _f32p]
         L.msst_oracle_stft.argtypes = [_f32p, i64, i64, c_int, c_int, _f32p, _f32p]
-        L.msst_oracle_istft.argtypes = [_f32p, i64, i64, c_int, c_int, _f32p, _f32p]
+        L.msst_oracle_istft.argtypes = [_f32p, i64, i64, c_int, c_int, _f32p, _f32p, c_int]
         L.msst_oracle_mel_bands_htk.argtypes = [c_int, c_int, c_int, ctypes.POINTER(c_int), ctypes.POINTER(c_int),
                                                 ctypes.POINTER(c_int)]
         L.msst_oracle_threads.restype = c_int
@@ -165,11 +165,14 @@ def stft(sig, n_fft, hop, win):
     return out
 
 
-def istft(spec, n_fft, hop, win):
+def istft(spec, n_fft, hop, win, trim: bool = True):
+    """[B, F, T, 2] -> [B, (T-1)*hop] (centre padding trimmed) or, trim=False, the
+    whole [B, n_fft + (T-1)*hop] window-normalised overlap-add."""
     spec = _c(spec)
     B, F, T, _ = spec.shape
-    out = np.empty((B, (T - 1) * hop), np.float32)
-    lib().msst_oracle_istft(_p(spec), B, T, n_fft, hop, _p(_c(win)), _p(out))
+    n = (T - 1) * hop if trim else (T - 1) * hop + n_fft
+    out = np.empty((B, n), np.float32)
+    lib().msst_oracle_istft(_p(spec), B, T, n_fft, hop, _p(_c(win)), _p(out), 1 if trim else 0)
     return out
 
 
@@ -357,21 +360,40 @@ class Model:
         if cfg.get("stft_normalized", False):
             # the iSTFT undoes the normalisation first (src/ops_stft.cu:380-389)
             out = out * np.sqrt(np.float32(cfg["stft_n_fft"]))
+        if cfg.get("match_input_audio_length", False):
+            self._untrimmed = istft(out, cfg["stft_n_fft"], cfg["stft_hop_length"], self.win, trim=False)
         y = istft(out, cfg["stft_n_fft"], cfg["stft_hop_length"], self.win)
         y = y.reshape(B, S, C, -1)
         return y[:, 0] if S == 1 else y
 
-    def forward(self, audio):
+    def forward(self, audio, ref_compat: bool = True):
         masks, st = self.masks(audio)
         y = self.apply_masks(masks, st)
         if self.cfg.get("match_input_audio_length", False):
-            # ops::istft's `length`: zero-pad or truncate to the input length
-            # (src/model_mel_band_roformer.cu:764, src/ops_stft.cu:484-493)
-            L = audio.shape[-1]
-            if y.shape[-1] < L:
-                y = np.concatenate([y, np.zeros(y.shape[:-1] + (L - y.shape[-1],), np.float32)], axis=-1)
-            y = np.ascontiguousarray(y[..., :L])
+            y = self._match_length(y, masks.shape[2], audio.shape[-1], ref_compat)
         return y
+
+    def _match_length(self, y, T, L, ref_compat):
+        """ops::istft's `length` (src/model_mel_band_roformer.cu:764, src/ops_stft.cu:476-493):
+        the (T-1)*hop reconstructed samples zero-padded to L.  The reference pads the
+        centre-trimmed view with Tensor::pad, whose kernel reads its strided source as
+        if it were contiguous (src/tensor.cu:1184-1216): with ref_compat=True row r,
+        sample i is taken from flat position n_fft/2 + r*(T-1)*hop + i of the untrimmed
+        [rows, n_fft + (T-1)*hop] reconstruction (row 0 is unaffected)."""
+        n = y.shape[-1]
+        if L <= n:
+            return np.ascontiguousarray(y[..., :L])
+        shape = y.shape
+        rows = y.reshape(-1, n)
+        if ref_compat and rows.shape[0] > 1:
+            full = self._untrimmed
+            pad = self.cfg["stft_n_fft"] // 2
+            flat = full.reshape(-1)
+            idx = pad + np.arange(rows.shape[0])[:, None] * n + np.arange(n)[None, :]
+            rows = flat[idx]
+        out = np.zeros((rows.shape[0], L), np.float32)
+        out[:, :n] = rows
+        return out.reshape(shape[:-1] + (L,))
 
 
 # --------------------------------------------------------------------------- chunking

@@ -189,7 +189,9 @@ def test_config0_full_size_vs_oracle(cuda, tmp_path_factory):
     y = m.forward(x).cpu().numpy()
     err, snr = rel_l2(masks, om_masks), snr_db(y, ref)
     print(f"config0 fp16: masks rel-L2 {err:.3e} vs the fp32 oracle, output {snr:.1f} dB")
-    assert err < MASK_TOL["fp16"]
+    # the north-star bar for config 0's fp32 masks (fp16 operands carry the same
+    # 11-bit significand as the reference's TF32 GEMMs)
+    assert err < 2e-3
     assert snr >= 45.0
     m.close()
 

@@ -92,3 +92,23 @@ def test_computed_mel_bands_match_oracle(cuda, option_models):
     np.testing.assert_array_equal(_device_ints(t.nfreq, t.num_bands), nfreq_ref)
     np.testing.assert_array_equal(_device_ints(t.bin_list, int(nfreq_ref.sum())), bins_ref)
     m.close()
+
+
+@pytest.mark.parametrize("name", ["mbr_opts", "bsr_opts"])
+def test_fixed_length_padding_vs_oracle(cuda, option_models, name):
+    """msst_model_separate on a short track (one whole-track forward) with
+    MSST_SEPARATE_FIX_TAIL_PADDING pads every output row with its own samples; the
+    oracle's ref_compat=False gives the same semantics."""
+    torch = cuda
+    import oracle
+    from msst_b200 import Model, synth
+
+    path, cfg, meta = option_models[name]
+    audio = synth.make_audio(meta["n_samples"], 2, meta["seed"])
+    m = Model(path, 0, "fp16")
+    y = m.separate(torch.from_numpy(audio).cuda(), fix_tail_padding=True).cpu().numpy()
+    m.close()
+    sd = synth.make_weights(cfg, meta["spec"]["seed"], precomputed_bands=meta["spec"].get("precomputed_bands", True))
+    ref = oracle.Model(cfg, sd).forward(audio[None], ref_compat=False)[0]
+    assert y.shape == ref.shape
+    assert snr_db(y, ref) >= 45.0

@@ -123,3 +123,22 @@ def test_layernorm_pin(name):
     z, _ = golden("ops_htdemucs.npz")
     x, g, b = op_cases.ln_inputs(name)
     assert rel_l2(o.layernorm(x, g, b, op_cases.LN_EPS), z[f"ln_{name}"]) < 1e-6
+
+
+@pytest.mark.parametrize("name", ["mbr_opts", "bsr_opts"])
+def test_options_pin(name):
+    """The oracle against the reference engine on models with its optional switches:
+    band tables derived at load, skip connections, a normalised STFT and the output
+    padded to the input length (including the reference's padding layout)."""
+    import oracle
+    from msst_b200 import synth
+
+    z, meta = golden(f"{name}_fp32.npz")
+    spec = meta["spec"]
+    cfg = (synth.mbr_config if spec["kind"] == "mbr" else synth.bsr_config)(**spec["cfg"])
+    sd = synth.make_weights(cfg, spec["seed"], precomputed_bands=spec.get("precomputed_bands", True))
+    audio = synth.make_audio(meta["n_samples"], 2, meta["seed"])[None]
+    om = oracle.Model(cfg, sd)
+    masks, _ = om.masks(audio)
+    assert rel_l2(masks, z["masks"]) < 2e-3
+    assert snr_db(om.forward(audio), z["out"]) >= 60.0
