@@ -1,34 +1,37 @@
 #!/usr/bin/env python
 """bench.py — audio-seconds separated per second for the Roformer path on B200.
 
-Workload: MelBandRoformer dim 384 x depth 6, 8 heads x 64,
-60 mel bands, n_fft 2048 / hop 441, one stem, fp16 operands; a 68.5 s stereo
-44.1 kHz track (3,020,850 samples, seeded 8 sines + pink noise, peak 0.5) cut
-into 352800-sample chunks with 2 s overlap (--overlap 0.25: step 264600,
-13 chunks) and run 4 chunks per forward.  Random N(0, 0.02) weights (no
-checkpoints are reachable), written as a .csm file.  One step = one separation
-of the track (chunking, 4 forwards, overlap-add stitch).
+Workload (the north star's scaling run): MelBandRoformer
+dim 384 x depth 6, 8 heads x 64, 60 mel bands, n_fft 2048 / hop 441, one stem,
+fp16 operands, on a 10-minute stereo 44.1 kHz track (26,460,000 samples per
+channel, seeded 8 sines + pink noise, peak 0.5) cut into 352800-sample chunks
+with 2 s overlap (--overlap 0.25: step 264600, 101 chunks), 4 chunks per
+forward.  Random N(0, 0.02) weights (no checkpoints are reachable), written as
+a .csm file.  One step = one separation of the whole track; at N GPUs the same
+track is separated by N ranks (strong scaling): chunks dealt round-robin, each
+round's outputs sent to rank 0, stitched there as they become final
+(msst_b200.dist).  At N = 1 a second line item, `config1`, times BASELINE
+config 1 (the same model on a 68.5 s track, 13 chunks).
 
   python bench.py [--gpus N --steps K --warmup W] [--impl reference] [--config 1|2]
 
 Arms:
   ours (default)   value: device-resident track, CUDA-event time of K steps
-                   (max over ranks); e2e: the same through the host-buffer public
-                   API (pinned host memory, H2D + D2H inside the timed region).
-                   At N > 1 the track is N x 68.5 s, its chunk plan is split into
-                   contiguous balanced ranges, one per rank, and the per-chunk
-                   stems are gathered to rank 0 over NCCL for the stitch (weak
-                   scaling).
-  roofline         every launch of the library inside the timed region is
-                   bracketed by CUDA events on its stream (msst_kernel_timing);
-                   the kernel with the largest total time is the dominant one and
-                   its achieved rate is its algorithmic FLOPs (or bytes) over its
-                   summed event time, against the sustained GEMM peak (or the
-                   copy bandwidth) of MEASURED_PEAKS.json.
+                   (max over ranks), no instrumentation.  e2e: the same through
+                   the host-buffer public API (pinned host memory; every rank
+                   copies up only the samples its chunks read, rank 0 copies each
+                   stitched range down as soon as it is final; all inside the
+                   timed region).
+  roofline         one more step with every launch bracketed by CUDA events
+                   (msst_kernel_timing): the kernel with the largest total time
+                   is the dominant one; its achieved rate is its algorithmic FLOPs
+                   (or bytes) over its summed event time, against the sustained
+                   GEMM peak (or the copy bandwidth) of MEASURED_PEAKS.json.
   reference        the reference has no CPU path; its CPU arm is the fp32 oracle
-                   port (oracle/) on the host cores, timed on a bounded sample
-                   (one depth block of one chunk per step, the band-split/mask
-                   ends once) and extrapolated to the whole track.
+                   port (oracle/) on all host cores; each step is one bounded
+                   sample (one depth block of one chunk), the band split and mask
+                   estimator ends are timed once, and the track's time is
+                   extrapolated from them (stated in the line).
 """
 from __future__ import annotations
 
@@ -45,7 +48,8 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "cuda-msst-infer_b200"))
 
-TRACK_SECONDS = 68.5
+TRACK_SAMPLES = 26_460_000   # 10 minutes at 44.1 kHz
+CONFIG1_SECONDS = 68.5
 SR = 44100
 CHUNK = 352800
 OVERLAP = 0.25
@@ -206,7 +210,9 @@ def cpu_sample(cfg, which):
     import oracle
     from msst_b200 import synth
 
-    om = oracle.Model(cfg, synth.make_weights(cfg, 0))
+    # torchrun sets OMP_NUM_THREADS=1; the baseline uses every host thread
+    oracle.set_threads(host_threads())
+    om = oracle.Model(cfg, synth.make_weights(cfg, 0, weight_dtype="bf16" if which == 2 else "fp32"))
     a = synth.make_audio(CHUNK, 2, 0)[None]
     t0 = time.perf_counter()
     st = om.stft_repr(a)
@@ -241,6 +247,13 @@ def emit(out, result):
     out.flush()
 
 
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def main():
     out = claim_stdout()
     ap = argparse.ArgumentParser()
@@ -248,10 +261,11 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", type=int, choices=[1, 2], default=1)
+    ap.add_argument("--config", type=int, choices=[1, 2], default=1,
+                    help="model: 1 = MelBandRoformer D384x6 fp16 (configs 1 and 4), 2 = BS-Roformer D512x12 bf16")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--seconds", type=float, default=TRACK_SECONDS,
-                    help="track length per rank (smaller values make a profiling case)")
+    ap.add_argument("--samples", type=int, default=TRACK_SAMPLES,
+                    help="track length in samples per channel (smaller values make a profiling case)")
     ap.add_argument("--chunk-batch", type=int, default=CHUNK_BATCH, help="chunks per forward")
     ap.add_argument("--micro", choices=["attention", "gemm", "sdpa"], default=None,
                     help="attention: BASELINE config 3; gemm: the transformer GEMMs at config 1's "
@@ -279,126 +293,166 @@ def main():
     if world > 1:
         from datetime import timedelta
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
     from msst_b200 import Model, kernel_launches, kernel_timing, kernel_timing_report, synth
+    from msst_b200.dist import ShardedSeparator
 
     cfg, prec, desc = model_config(args.config)
     path = model_file(cfg, args.config, rank, world, dist)
     model = Model(path, local, prec)
-    n_samples = int(round(args.seconds * SR)) * world
+    n_samples = args.samples
     track = synth.make_audio(n_samples, 2, 1234)
     plan = model.chunk_plan(n_samples, OVERLAP)
     audio_seconds = n_samples / SR
-
+    S = cfg["num_stems"]
+    sharded = ShardedSeparator(model, dist if world > 1 else None, rank, world)
+    track_dev = torch.from_numpy(track).cuda()
+    out_dev = torch.empty((S, 2, n_samples), dtype=torch.float32, device="cuda")
     if world == 1:
-        track_dev = torch.from_numpy(track).cuda()
-        out_dev = torch.empty((cfg["num_stems"], 2, n_samples), dtype=torch.float32, device="cuda")
         step = lambda: model.separate(track_dev, OVERLAP, args.chunk_batch, out=out_dev)
     else:
-        from msst_b200.dist import ShardedSeparator
-
-        sharded = ShardedSeparator(model, dist, rank, world)
-        track_dev = torch.from_numpy(track).cuda()
         step = lambda: sharded.separate(track_dev, OVERLAP, args.chunk_batch)
+
+    def timed(fn, steps):
+        """CUDA-event time per step of `steps` calls on the current stream, max over ranks."""
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(steps):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(e) / steps
+        if world > 1:
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
 
     for _ in range(args.warmup):
         step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
     kernel_launches(reset=True)
-    kernel_timing(True)
     with ClockSampler(local) as clk:
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        s.record()
-        for _ in range(args.steps):
-            step()
-        e.record()
-        torch.cuda.synchronize()
-    kernel_timing(False)
+        ms = timed(step, args.steps)
     launches = kernel_launches(reset=True)
-    stats = kernel_timing_report()
-    ms = s.elapsed_time(e) / args.steps
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-        dist.barrier()
     value = audio_seconds / (ms / 1e3)
     clocks = clk.summary()
 
-    # ---- e2e through the host-buffer public API (pinned memory, copies inside the timed region)
-    e2e = None
+    # ---- per-kernel table and roofline: one more step, every launch bracketed by events
+    kernel_timing(True)
+    sharded.profile = world > 1
+    ms_instrumented = timed(step, 1)
+    sharded.profile = False
+    kernel_timing(False)
+    stats = kernel_timing_report()
+    phases = None
+    if world > 1:
+        # every rank's own forward time and its tail (rank 0: the last round's
+        # receives, the final stitch); names the limiter of the scaling curve
+        t = torch.tensor([sharded.last_profile["forward_ms"], sharded.last_profile["tail_ms"]], device="cuda")
+        allp = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(allp, t)
+        allp = [x.tolist() for x in allp]
+        phases = {"forward_ms_per_rank": [round(a, 3) for a, _ in allp],
+                  "rank0_tail_ms": round(allp[0][1], 3),
+                  "note": "instrumented step: forward_ms = a rank's own chunk forwards (start to its last "
+                          "forward queued); rank0_tail_ms = after that, waiting for the last round's NCCL "
+                          "receives plus the final stitch"}
+
+    # ---- e2e through the host-buffer public API
+    pin_in = torch.from_numpy(track).pin_memory()
+    pin_out = torch.empty((S, 2, n_samples), dtype=torch.float32).pin_memory() if rank == 0 else None
     if world == 1:
-        pin_in = torch.from_numpy(track).pin_memory()
-        pin_out = torch.empty((cfg["num_stems"], 2, n_samples), dtype=torch.float32).pin_memory()
         hin, hout = pin_in.numpy(), pin_out.numpy()
-        model.separate_host(hin, OVERLAP, args.chunk_batch, out=hout)
-        t0 = time.perf_counter()
-        for _ in range(args.steps):
-            model.separate_host(hin, OVERLAP, args.chunk_batch, out=hout)
-        e2e_s = (time.perf_counter() - t0) / args.steps
-        e2e = {"value": audio_seconds / e2e_s, "unit": "audio-s/s", "h2d_bytes_per_step": int(track.nbytes),
-               "d2h_bytes_per_step": int(hout.nbytes), "ms_per_step": e2e_s * 1e3}
+        e2e_step = lambda: model.separate_host(hin, OVERLAP, args.chunk_batch, out=hout)
+        h2d = int(track.nbytes)
     else:
-        # every rank copies the host track in (pinned once, outside the timed
-        # region); rank 0 copies the stitched stems out
-        pin_in = torch.from_numpy(track).pin_memory()
-        tdev = torch.empty(pin_in.shape, dtype=torch.float32, device="cuda")
-        pin_out = torch.empty((cfg["num_stems"], 2, n_samples), dtype=torch.float32).pin_memory()
+        tdev = torch.empty_like(track_dev)
+        e2e_step = lambda: sharded.separate(tdev, OVERLAP, args.chunk_batch, track_host=pin_in,
+                                            out_host=pin_out)
+    e2e_step()
+    if world > 1:
+        t = torch.tensor([sharded.last_h2d_bytes], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t)
+        h2d = int(t.item())
+    e2e_ms = timed(e2e_step, args.steps)
+    e2e = {"value": audio_seconds / (e2e_ms / 1e3), "unit": "audio-s/s", "h2d_bytes_per_step": h2d,
+           "d2h_bytes_per_step": int(S * 2 * n_samples * 4), "ms_per_step": e2e_ms,
+           "path": "msst_model_separate_host" if world == 1 else
+                   "ShardedSeparator.separate(track_host=..., out_host=...) over msst_model_forward_chunks_strided / "
+                   "msst_model_stitch_range"}
+    if world == 1:
+        # every sample's stems must be finite after the timed host round trip
+        assert np.isfinite(pin_out.numpy()).all()
 
-        def e2e_step():
-            tdev.copy_(pin_in, non_blocking=True)
-            y = sharded.separate(tdev, OVERLAP, args.chunk_batch)
-            if rank == 0:
-                pin_out.view(y.shape).copy_(y, non_blocking=True)
-            torch.cuda.synchronize()
-
-        e2e_step()
-        dist.barrier()
-        t0 = time.perf_counter()
-        for _ in range(args.steps):
-            e2e_step()
-        dt = torch.tensor([(time.perf_counter() - t0) / args.steps], device="cuda")
-        dist.all_reduce(dt, op=dist.ReduceOp.MAX)
-        e2e = {"value": audio_seconds / float(dt.item()), "unit": "audio-s/s",
-               "h2d_bytes_per_step": int(track.nbytes) * world,
-               "d2h_bytes_per_step": int(track.nbytes) * cfg["num_stems"], "ms_per_step": float(dt.item()) * 1e3}
+    # ---- BASELINE config 1 on one GPU: the same model on the 68.5 s track
+    config1 = None
+    if world == 1 and args.samples == TRACK_SAMPLES:
+        n1 = int(round(CONFIG1_SECONDS * SR))
+        tr1 = synth.make_audio(n1, 2, 1234)
+        t1 = torch.from_numpy(tr1).cuda()
+        o1 = torch.empty((S, 2, n1), dtype=torch.float32, device="cuda")
+        st1 = lambda: model.separate(t1, OVERLAP, args.chunk_batch, out=o1)
+        for _ in range(2):
+            st1()
+        ms1 = timed(st1, args.steps)
+        p1i, p1o = torch.from_numpy(tr1).pin_memory(), torch.empty((S, 2, n1)).pin_memory()
+        e1 = lambda: model.separate_host(p1i.numpy(), OVERLAP, args.chunk_batch, out=p1o.numpy())
+        e1()
+        ms1e = timed(e1, args.steps)
+        config1 = {"workload": f"BASELINE config 1: {desc}; {n1 / SR:.1f} s stereo track, "
+                               f"{model.chunk_plan(n1, OVERLAP)['num_chunks']} chunks, {args.chunk_batch} per forward",
+                   "value": (n1 / SR) / (ms1 / 1e3), "ms_per_step": ms1,
+                   "e2e": {"value": (n1 / SR) / (ms1e / 1e3), "unit": "audio-s/s", "ms_per_step": ms1e,
+                           "h2d_bytes_per_step": int(tr1.nbytes), "d2h_bytes_per_step": int(S * tr1.nbytes)}}
 
     result = None
     if rank == 0:
         pk = peaks()
         T = CHUNK // cfg["stft_hop_length"] + 1
         roofline = dominant_roofline(stats, pk)
-        kern = kernel_table(stats, args.steps, pk[1], pk[2])
-        flop_step = sum(k["flop"] for k in stats.values()) / args.steps
-        kernel_ms = sum(k["total_ms"] for k in stats.values()) / args.steps
+        kern = kernel_table(stats, 1, pk[1], pk[2])
+        flop_step = sum(k["flop"] for k in stats.values())
+        kernel_ms = sum(k["total_ms"] for k in stats.values())
         result = {
             "metric": "audio-sec separated/sec", "value": value, "unit": "audio-s/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": prec, "data": "synthetic",
-            "config": {"workload": f"{desc}; {audio_seconds:.1f} s stereo track, {plan['num_chunks']} chunks of "
-                                   f"{CHUNK} (overlap {OVERLAP}), {args.chunk_batch} chunks per forward",
-                       "model": desc, "global_batch": args.chunk_batch, "seq_len": T, "parallelism": f"chunks x{world}",
+            "scaling": "strong", "vs_baseline": None, "dtype": prec, "data": "synthetic",
+            "config": {"workload": f"BASELINE config 4: {desc}; {audio_seconds:.1f} s stereo track "
+                                   f"({n_samples} samples per channel), {plan['num_chunks']} chunks of {CHUNK} "
+                                   f"(overlap {OVERLAP}), {args.chunk_batch} chunks per forward, dealt round-robin "
+                                   f"over {world} GPU(s)",
+                       "model": desc, "global_batch": args.chunk_batch * world, "seq_len": T,
+                       "parallelism": f"chunks round-robin x{world}",
                        "l2": "working set (weights + activations, GBs) far larger than the 126 MB L2",
-                       "baseline_config": args.config},
+                       "baseline_config": 4 if args.config == 1 else 2},
             "e2e": e2e, "gpu_launches": launches, "gpu_launches_per_step": launches / args.steps,
             "roofline": roofline, "clocks": clocks,
+            "model_load_ms": model.info["load_ms"],
+            "instrumented_step": {"ms": ms_instrumented, "library_kernel_ms": kernel_ms,
+                                  "note": "one extra step with every launch bracketed by CUDA events; the kernel "
+                                          "table and roofline come from it, value and e2e from the plain steps"},
             "kernels": {k: {kk: (round(vv, 5) if isinstance(vv, float) else vv) for kk, vv in v.items()}
                         for k, v in sorted(kern.items(), key=lambda kv: -kv[1]["ms_per_step"])},
-            "library_kernel_ms_per_step": kernel_ms,
             "contraction_tflop_per_step": flop_step / 1e12,
+            "stitch_ms_per_step": stats.get("stitch", {}).get("total_ms"),
         }
+        if phases:
+            result["phases"] = phases
+        if config1:
+            result["config1"] = config1
         if not args.no_cpu_baseline and world == 1:
             c = cpu_sample(cfg, args.config)
             per_chunk = c["front_s"] + cfg["depth"] * c["block_s"] + c["back_s"]
             result["cpu_baseline"] = {
                 "value": audio_seconds / (per_chunk * plan["num_chunks"]), "unit": "audio-s/s",
                 "cores": c["threads"], "kind": "port",
-                "sample": f"fp32 oracle: one {CHUNK}-sample chunk through band split ({c['front_s']:.2f} s), one "
-                          f"depth block ({c['block_s']:.2f} s) and the mask estimator + iSTFT ({c['back_s']:.2f} s); "
-                          f"extrapolated to {cfg['depth']} blocks and {plan['num_chunks']} chunks"}
+                "sample": f"fp32 oracle on {c['threads']} host threads: one {CHUNK}-sample chunk through band split "
+                          f"({c['front_s']:.2f} s), one depth block ({c['block_s']:.2f} s) and the mask estimator + "
+                          f"iSTFT ({c['back_s']:.2f} s); extrapolated to {cfg['depth']} blocks and "
+                          f"{plan['num_chunks']} chunks"}
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -638,28 +692,32 @@ def reference_sdpa(res):
 
 
 def run_reference(args):
-    """CPU arm: the fp32 oracle port of the reference's graph on the host cores."""
+    """CPU arm: the fp32 oracle port of the reference's graph on all host cores.
+
+    One step = one depth block (time + band transformer) of one 352800-sample chunk,
+    the bulk of the graph's work; the band split and the mask estimator + iSTFT of a
+    chunk are timed once during warm-up.  The track's time is extrapolated from these
+    (depth blocks x chunks), and the line says so; steps / ms_per_step describe the
+    samples actually timed."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
 
     cfg, prec, desc = model_config(args.config)
-    from msst_b200 import synth
-
-    n_samples = int(round(args.seconds * SR)) * args.gpus
+    n_samples = args.samples
     audio_seconds = n_samples / SR
     step_sz = oracle.resolve_step(CHUNK, OVERLAP, 2)
     _, _, starts = oracle.chunk_plan(n_samples, CHUNK, step_sz)
-    c = cpu_sample(cfg, args.config)  # also the warm-up of the port
+    c = cpu_sample(cfg, args.config)  # also the first warm-up of the port
     om, x = c["om"], c["x"]
     B, T, nb, D = x.shape
     blocks = []
-    for i in range(args.warmup + args.steps):
+    for i in range(max(0, args.warmup - 1) + args.steps):
         t0 = time.perf_counter()
         xt = np.ascontiguousarray(x.transpose(0, 2, 1, 3)).reshape(B * nb, T, D)
         xt = om.transformer(xt, "layers.0.0", cfg["time_transformer_depth"])
         xx = np.ascontiguousarray(xt.reshape(B, nb, T, D).transpose(0, 2, 1, 3))
         om.transformer(xx.reshape(B * T, nb, D), "layers.0.1", cfg["freq_transformer_depth"])
-        if i >= args.warmup:
+        if i >= max(0, args.warmup - 1):
             blocks.append(time.perf_counter() - t0)
     block = float(np.mean(blocks))
     per_chunk = c["front_s"] + cfg["depth"] * block + c["back_s"]
@@ -667,14 +725,17 @@ def run_reference(args):
     value = audio_seconds / track_s
     out = {
         "metric": "audio-sec separated/sec", "value": value, "unit": "audio-s/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": track_s * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic", "impl": "reference",
-        "config": {"workload": f"{desc}; {audio_seconds:.1f} s stereo track, {len(starts)} chunks of {CHUNK}",
-                   "model": desc, "baseline_config": args.config},
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": block * 1e3,
+        "step_definition": "one depth block (time + band transformer) of one chunk, fp32, all host threads",
+        "extrapolated_ms_per_track": track_s * 1e3, "higher_is_better": True,
+        "scaling": "none (host cores; the same at every --gpus)", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": f"BASELINE config 4: {desc}; {audio_seconds:.1f} s stereo track, {len(starts)} chunks "
+                               f"of {CHUNK}", "model": desc, "baseline_config": 4 if args.config == 1 else 2},
         "cpu_baseline": {"value": value, "unit": "audio-s/s", "cores": c["threads"], "kind": "port",
-                         "sample": f"per step one depth block of one chunk ({block:.2f} s mean); band split "
-                                   f"{c['front_s']:.2f} s and mask estimator + iSTFT {c['back_s']:.2f} s once; "
-                                   f"extrapolated to {cfg['depth']} blocks x {len(starts)} chunks"},
+                         "sample": f"per step one depth block of one chunk ({block:.2f} s mean over {len(blocks)}); "
+                                   f"band split {c['front_s']:.2f} s and mask estimator + iSTFT {c['back_s']:.2f} s "
+                                   f"once; extrapolated to {cfg['depth']} blocks x {len(starts)} chunks"},
         "e2e": {"value": value, "unit": "audio-s/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     ref = reference_gpu(cfg, args, prec)
@@ -707,22 +768,30 @@ def _reference_gpu(cfg, args, prec, lib_path):
         h = L.refh_load(path.encode(), 0, 1 if prec == "fp16" else 0)
         if not h:
             return {"unavailable": L.refh_last_error().decode()}
-        n = int(round(args.seconds * SR))
-        track = synth.make_audio(n, 2, 1234)
-        buf = np.zeros(track.size, np.float32)
-        cnt, ms = ctypes.c_longlong(0), ctypes.c_double(0)
-        times = []
-        for i in range(2 + max(1, min(args.steps, 3))):
-            rc = L.refh_separate(h, mg.P(track), 2, n, OVERLAP, args.chunk_batch, mg.P(buf), buf.size, ctypes.byref(cnt),
-                                 ctypes.byref(ms))
-            if rc != 0:
-                return {"unavailable": L.refh_last_error().decode()}
-            if i >= 2:
-                times.append(ms.value)
+        res = {"mode": "reference CUDA engine (oracle/_ref, sm_100a build), --fp16, app::run_inference wall time"}
+        cases = [("track", args.samples)]
+        if args.samples == TRACK_SAMPLES:
+            cases.append(("config1", int(round(CONFIG1_SECONDS * SR))))
+        for name, n in cases:
+            track = synth.make_audio(n, 2, 1234)
+            buf = np.zeros(track.size, np.float32)
+            cnt, ms = ctypes.c_longlong(0), ctypes.c_double(0)
+            times = []
+            for i in range(1 + max(1, min(args.steps, 3))):
+                rc = L.refh_separate(h, mg.P(track), 2, n, OVERLAP, args.chunk_batch, mg.P(buf), buf.size,
+                                     ctypes.byref(cnt), ctypes.byref(ms))
+                if rc != 0:
+                    return {"unavailable": L.refh_last_error().decode()}
+                if i >= 1:
+                    times.append(ms.value)
+            t = float(np.mean(times))
+            entry = {"value": (n / SR) / (t / 1e3), "unit": "audio-s/s", "ms_per_step": t, "samples": n}
+            if name == "track":
+                res.update(entry)
+            else:
+                res[name] = entry
         L.refh_free(h)
-        t = float(np.mean(times))
-        return {"value": (n / SR) / (t / 1e3), "unit": "audio-s/s", "ms_per_step": t,
-                "mode": "reference CUDA engine (oracle/_ref, sm_100a build), --fp16, app::run_inference wall time"}
+        return res
     except Exception as e:  # informative leg only
         return {"unavailable": str(e)}
 

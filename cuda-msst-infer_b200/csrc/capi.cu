@@ -615,9 +615,41 @@ int msst_model_forward_chunks(msst_model* m, const float* track, int channels, l
   return guarded([&] {
     MSST_REQUIRE(m && track && (out || count == 0), "null argument");
     serialized(m, as_stream(stream), [&] {
-      m->impl.forward_chunks(track, channels, length, overlap, first_chunk, count, chunk_batch, flags, out,
+      m->impl.forward_chunks(track, channels, length, overlap, first_chunk, 1, count, chunk_batch, flags, out,
                              as_stream(stream));
     });
+  });
+}
+
+int msst_model_forward_chunks_strided(msst_model* m, const float* track, int channels, long long length,
+                                      float overlap, int first_chunk, int chunk_stride, int count, int chunk_batch,
+                                      int flags, float* out, void* stream) {
+  return guarded([&] {
+    MSST_REQUIRE(m && track && (out || count == 0), "null argument");
+    serialized(m, as_stream(stream), [&] {
+      m->impl.forward_chunks(track, channels, length, overlap, first_chunk, chunk_stride, count, chunk_batch, flags,
+                             out, as_stream(stream));
+    });
+  });
+}
+
+int msst_model_stitch_range(msst_model* m, const float* chunks, int slot_ranks, int slot_cap, int channels,
+                            long long length, float overlap, long long begin, long long end, float* out,
+                            void* stream) {
+  return guarded([&] {
+    MSST_REQUIRE(m && chunks && out, "null argument");
+    serialized(m, as_stream(stream), [&] {
+      m->impl.stitch_range(chunks, slot_ranks, slot_cap, channels, length, overlap, begin, end, out,
+                           as_stream(stream));
+    });
+  });
+}
+
+int msst_model_chunk_span(const msst_model* m, long long length, float overlap, int chunk_index, int flags,
+                          long long* in_begin, long long* in_end, long long* out_begin, long long* out_end) {
+  return guarded([&] {
+    MSST_REQUIRE(m && in_begin && in_end && out_begin && out_end, "null argument");
+    m->impl.chunk_span(length, overlap, chunk_index, flags, in_begin, in_end, out_begin, out_end);
   });
 }
 

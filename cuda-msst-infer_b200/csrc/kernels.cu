@@ -438,25 +438,38 @@ cudaError_t rmsnorm_dispatch(const RmsNormArgs& a, cudaStream_t s) {
 }
 
 // ------------------------------------------------------------------ band input
+// One block per (chunk b, frame t): the frame's STFT row of every channel is
+// staged in shared memory by coalesced loads (C * nbins complex), then each warp
+// takes a band, reduces its sum of squares and writes the band's normalised,
+// K-padded 16-bit values as packed pairs (the band's region starts on a
+// 128-byte boundary).
 template <typename T>
 __global__ void __launch_bounds__(256) band_input_kernel(BandInArgs a) {
-  const int lane = threadIdx.x & 31;
-  const long long items = (long long)a.Bc * a.T * a.num_bands;
-  const long long warps_total = (long long)gridDim.x * (blockDim.x >> 5);
+  extern __shared__ float2 s_row[];  // [C][nbins]
+  const int bt = blockIdx.x;
+  const int b = bt / a.T, t = bt - b * a.T;
+  for (int c = 0; c < a.C; ++c) {
+    const float2* src = a.spec + ((long long)(b * a.C + c) * a.T + t) * a.nbins;
+    for (int f = threadIdx.x; f < a.nbins; f += blockDim.x) {
+      float2 z = __ldg(src + f);
+      z.x *= a.spec_scale;
+      z.y *= a.spec_scale;
+      s_row[c * a.nbins + f] = z;
+    }
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
   const int per_bin = 2 * a.C;
-  for (long long it = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); it < items; it += warps_total) {
-    const int band = (int)(it % a.num_bands);
-    const long long bt = it / a.num_bands;
-    const int b = (int)(bt / a.T), t = (int)(bt - (long long)b * a.T);
-    const int nf = a.nfreq[band];
+  T* orow = reinterpret_cast<T*>(a.out) + (long long)bt * a.ld;
+  for (int band = warp; band < a.num_bands; band += nwarps) {
+    const int nf = __ldg(a.nfreq + band);
     const int dims = nf * per_bin;
-    const int* bins = a.bin_list + a.bin_start[band];
+    const int* bins = a.bin_list + __ldg(a.bin_start + band);
     auto load = [&](int j) -> float {
       const int fl = j / per_bin;
       const int rem = j - fl * per_bin;
-      const int ch = rem >> 1, ri = rem & 1;
-      const float2 z = a.spec[((long long)(b * a.C + ch) * a.T + t) * a.nbins + bins[fl]];
-      return (ri ? z.y : z.x) * a.spec_scale;
+      const float2 z = s_row[(rem >> 1) * a.nbins + __ldg(bins + fl)];
+      return (rem & 1) ? z.y : z.x;
     };
     float ss = 0.f;
     for (int j = lane; j < dims; j += 32) {
@@ -466,42 +479,42 @@ __global__ void __launch_bounds__(256) band_input_kernel(BandInArgs a) {
     ss = warp_sum(ss);
     const float inv = rsqrtf(ss + 1e-12f);
     const float scale = sqrtf((float)dims);
-    const float* g = a.gamma + a.gcol[band];
-    T* o = reinterpret_cast<T*>(a.out) + bt * a.ld + a.kcol[band];
-    const int kp = a.kpad[band];
-    for (int j = lane; j < kp; j += 32) {
-      float y = 0.f;
-      if (j < dims) y = load(j) * inv * __ldg(g + j) * scale;
-      uint32_t pk = pack2<T>(y, 0.f);
-      o[j] = *reinterpret_cast<T*>(&pk);
+    const float* g = a.gamma + __ldg(a.gcol + band);
+    T* o = orow + __ldg(a.kcol + band);
+    const int kp = __ldg(a.kpad + band);
+    for (int j = 2 * lane; j < kp; j += 64) {
+      const float y0 = j < dims ? load(j) * inv * __ldg(g + j) * scale : 0.f;
+      const float y1 = j + 1 < dims ? load(j + 1) * inv * __ldg(g + j + 1) * scale : 0.f;
+      *reinterpret_cast<uint32_t*>(o + j) = pack2<T>(y0, y1);
     }
   }
 }
 
 // ------------------------------------------------------------------ mask apply
+// One block per (chunk b, stem, frame t): the frame's mask row is staged in shared
+// memory by coalesced loads, then threads walk the bins (coalesced STFT reads and
+// output writes), summing each bin's <= 2 band contributions from shared memory.
 __global__ void __launch_bounds__(256) mask_apply_kernel(MaskApplyArgs a) {
-  const long long total = (long long)a.Bc * a.S * a.T * a.nbins;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int f = (int)(i % a.nbins);
-    long long r = i / a.nbins;
-    const int t = (int)(r % a.T);
-    r /= a.T;
-    const int st = (int)(r % a.S);
-    const int b = (int)(r / a.S);
-    const float* mrow = a.mask + st * a.mask_stem_stride + ((long long)b * a.T + t) * a.mask_ld;
-    const int k0 = a.contrib_off[f], k1 = a.contrib_off[f + 1];
-    const float den = a.denom[f];
+  extern __shared__ float s_mask[];  // [mask_ld]
+  const int t = blockIdx.x % a.T;
+  const int rest = blockIdx.x / a.T;
+  const int st = rest % a.S, b = rest / a.S;
+  const float* mrow = a.mask + st * a.mask_stem_stride + ((long long)b * a.T + t) * a.mask_ld;
+  for (int i = threadIdx.x; i < a.mask_ld; i += blockDim.x) s_mask[i] = __ldg(mrow + i);
+  __syncthreads();
+  for (int f = threadIdx.x; f < a.nbins; f += blockDim.x) {
+    const int k0 = __ldg(a.contrib_off + f), k1 = __ldg(a.contrib_off + f + 1);
+    const float den = __ldg(a.denom + f);
     for (int c = 0; c < a.C; ++c) {
       float mr = 0.f, mi = 0.f;
       for (int k = k0; k < k1; ++k) {
-        const float2 m = *reinterpret_cast<const float2*>(mrow + a.contrib_col[k] + 2 * c);
-        mr += m.x;
-        mi += m.y;
+        const int col = __ldg(a.contrib_col + k) + 2 * c;
+        mr += s_mask[col];
+        mi += s_mask[col + 1];
       }
       mr = mr / den;
       mi = mi / den;
-      float2 z = a.spec[((long long)(b * a.C + c) * a.T + t) * a.nbins + f];
+      float2 z = __ldg(a.spec + ((long long)(b * a.C + c) * a.T + t) * a.nbins + f);
       z.x *= a.spec_scale;
       z.y *= a.spec_scale;
       float2 o = make_float2((z.x * mr - z.y * mi) * a.out_scale, (z.x * mi + z.y * mr) * a.out_scale);
@@ -512,96 +525,115 @@ __global__ void __launch_bounds__(256) mask_apply_kernel(MaskApplyArgs a) {
 }
 
 // ------------------------------------------------------------------ STFT / iSTFT
+// One block per frame (bc, t): 4 consecutive samples per thread, window and
+// frame written as float4 (n_fft % 4 == 0); the reflect padding only at the
+// track's two ends.
 __global__ void __launch_bounds__(256)
-    stft_frames_kernel(const float* __restrict__ audio, long long L, int BC, int T, int n_fft, int hop,
+    stft_frames_kernel(const float* __restrict__ audio, long long L, int T, int n_fft, int hop,
                        const float* __restrict__ win, float* __restrict__ frames) {
-  const long long total = (long long)BC * T * n_fft;
-  const int pad = n_fft / 2;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int n = (int)(i % n_fft);
-    const long long ft = i / n_fft;
-    const int t = (int)(ft % T);
-    const long long bc = ft / T;
-    const long long src = reflect_idx((long long)t * hop + n - pad, L);
-    frames[i] = audio[bc * L + src] * win[n];
+  const long long row = blockIdx.x;  // bc * T + t
+  const int t = (int)(row % T);
+  const float* src = audio + (row / T) * L;
+  float4* dst = reinterpret_cast<float4*>(frames + row * n_fft);
+  const long long base = (long long)t * hop - n_fft / 2;
+  const bool inside = base >= 0 && base + n_fft <= L;
+  for (int n = 4 * threadIdx.x; n < n_fft; n += 4 * blockDim.x) {
+    const float4 w = __ldg(reinterpret_cast<const float4*>(win + n));
+    float v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const long long i = base + n + u;
+      v[u] = __ldg(src + (inside ? i : reflect_idx(i, L)));
+    }
+    dst[n >> 2] = make_float4(v[0] * w.x, v[1] * w.y, v[2] * w.z, v[3] * w.w);
   }
 }
 
+// One block per (row, 1024 output samples); thread t handles samples t + 256u.
 __global__ void __launch_bounds__(256)
-    istft_ola_kernel(const float* __restrict__ frames, int BSC, int T, int n_fft, int hop,
-                     const float* __restrict__ win, const float* __restrict__ wsum, float* __restrict__ out,
-                     long long Lout, int ref_compat) {
-  const long long Lrec = (long long)(T - 1) * hop;  // reconstructed samples; the rest of a row is zero
-  const long long full = Lrec + n_fft;                // untrimmed reconstruction per row
-  const long long total = (long long)BSC * Lout;
+    istft_ola_kernel(const float* __restrict__ frames, int T, int n_fft, int hop, const float* __restrict__ win,
+                     const float* __restrict__ wsum, float* __restrict__ out, int Lout, int ref_compat) {
+  const int Lrec = (T - 1) * hop;  // reconstructed samples; the rest of a row is zero
+  const int full = Lrec + n_fft;   // untrimmed reconstruction per row
   const int pad = n_fft / 2;
   const float inv_n = 1.0f / (float)n_fft;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    long long bsc = i / Lout;
-    const long long j = i - bsc * Lout;
+  const int row0 = blockIdx.y;
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int j = blockIdx.x * 1024 + u * 256 + threadIdx.x;
+    if (j >= Lout) break;
+    float* o = out + (long long)row0 * Lout + j;
     if (j >= Lrec) {
-      out[i] = 0.f;
+      *o = 0.f;
       continue;
     }
-    long long p = j + pad;
+    long long row = row0;
+    int p = j + pad;
     if (ref_compat) {
-      const long long flat = pad + bsc * Lrec + j;
-      bsc = flat / full;
-      p = flat - bsc * full;
+      const long long flat = pad + (long long)row0 * Lrec + j;
+      row = flat / full;
+      p = (int)(flat - row * full);
     }
-    long long t_lo = (p - n_fft + hop) / hop;  // ceil((p - n_fft + 1) / hop) for p >= n_fft - 1
-    if (p - n_fft + 1 <= 0) t_lo = 0;
-    long long t_hi = p / hop;
-    if (t_hi > T - 1) t_hi = T - 1;
+    const int t_lo = p >= n_fft ? (p - n_fft) / hop + 1 : 0;
+    const int t_hi = min(T - 1, p / hop);
+    const float* fr = frames + row * T * (long long)n_fft;
     float acc = 0.f;
-    for (long long t = t_lo; t <= t_hi; ++t) {
-      const int n = (int)(p - t * hop);
-      if (n < 0 || n >= n_fft) continue;
-      acc += (frames[((bsc * T) + t) * n_fft + n] * inv_n) * win[n];
+    for (int t = t_lo; t <= t_hi; ++t) {
+      const int n = p - t * hop;
+      acc += (__ldg(fr + (long long)t * n_fft + n) * inv_n) * __ldg(win + n);
     }
-    const float ws = wsum[p];
-    out[i] = ws > 1e-8f ? acc / ws : acc;
+    const float ws = __ldg(wsum + p);
+    *o = ws > 1e-8f ? acc / ws : acc;
   }
 }
 
 // ------------------------------------------------------------------ chunking
-__device__ __forceinline__ float padded_track(const ChunkArgs& a, int c, long long p) {
-  // value of the reflect-padded track at channel c, padded index p (0 <= p < total)
-  const long long src = a.border ? reflect_idx(p - a.border, a.L) : p;
-  return a.track[(long long)c * a.L + src];
+// Both kernels map a block to 1024 consecutive samples of one row; thread t handles
+// samples t, t + 256, t + 512 and t + 768, so every warp access is 32 consecutive
+// floats.  Sample positions fit in 32 bits (the launchers check).
+__device__ __forceinline__ int reflect32(int i, int n) {
+  if (i < 0)
+    i = -i;
+  else if (i >= n)
+    i = 2 * (n - 1) - i;
+  return i < 0 ? 0 : (i >= n ? n - 1 : i);
 }
 
-__global__ void __launch_bounds__(256) chunk_gather_kernel(ChunkArgs a, int first, int count, float* batch) {
-  const long long total = (long long)count * a.C * a.chunk;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int j = (int)(i % a.chunk);
-    const long long kc = i / a.chunk;
-    const int c = (int)(kc % a.C);
-    const int k = first + (int)(kc / a.C);
-    const long long start = (long long)k * a.step;
-    const long long end = min(start + (long long)a.chunk, a.total);
-    const long long n = end - start;
+__device__ __forceinline__ float padded_track(const ChunkArgs& a, int c, int p) {
+  // value of the reflect-padded track at channel c, padded index p (0 <= p < total)
+  const int src = a.border ? reflect32(p - (int)a.border, (int)a.L) : p;
+  return __ldg(a.track + (long long)c * a.L + src);
+}
+
+__global__ void __launch_bounds__(256) chunk_gather_kernel(ChunkArgs a, int first, int stride, float* batch) {
+  const int kc = blockIdx.y;  // (chunk in batch) * C + channel
+  const int c = kc % a.C;
+  const int k = first + (kc / a.C) * stride;
+  const int start = k * a.step;
+  const int n = min(start + a.chunk, (int)a.total) - start;
+  float* row = batch + (long long)kc * a.chunk;
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int j = blockIdx.x * 1024 + u * 256 + threadIdx.x;
+    if (j >= a.chunk) break;
     float v;
     if (n >= a.chunk) {
       v = padded_track(a, c, start + j);
     } else {
       // src/inference_app.cpp:144-150: reflect if more than half a chunk remains, else zeros
       const bool reflect = n > a.chunk / 2;
-      long long sj = j < n ? j : 2 * (n - 1) - j;
+      int sj = j < n ? j : 2 * (n - 1) - j;
       sj = sj < 0 ? 0 : (sj >= n ? n - 1 : sj);
       if (!reflect && j >= n) {
         v = 0.f;
       } else if (a.ref_compat) {
-        const long long flat = start + (long long)c * n + sj;  // contiguous view of a strided slice
-        v = padded_track(a, (int)(flat / a.total), flat % a.total);
+        const long long flat = (long long)start + (long long)c * n + sj;  // contiguous view of a strided slice
+        v = padded_track(a, (int)(flat / a.total), (int)(flat % a.total));
       } else {
         v = padded_track(a, c, start + sj);
       }
     }
-    batch[i] = v;
+    row[j] = v;
   }
 }
 
@@ -622,47 +654,27 @@ __device__ __forceinline__ float fade_weight(int j, int chunk, bool first_chunk,
   return 1.f;
 }
 
-__global__ void __launch_bounds__(256) chunk_ola_kernel(ChunkArgs a, int first, int count, int num_chunks,
-                                                        const float* y, float* acc, float* wsum) {
-  const long long g0 = (long long)first * a.step;
-  const long long g1 = min((long long)(first + count - 1) * a.step + a.chunk, a.total);
-  const long long span = g1 - g0;
-  const long long total = (long long)(a.C + 1) * span;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int c = (int)(i / span);  // c == C: weight row
-    const long long p = g0 + i % span;
-    float s = c < a.C ? acc[(long long)c * a.total + p] : wsum[p];
-    for (int kk = 0; kk < count; ++kk) {
-      const int k = first + kk;
-      const long long start = (long long)k * a.step;
-      const long long end = min(start + (long long)a.chunk, a.total);
-      if (p < start || p >= end) continue;
-      const int j = (int)(p - start);
-      const float w = fade_weight(j, a.chunk, k == 0, end >= a.total);
-      if (c < a.C)
-        s += y[((long long)kk * a.C + c) * a.chunk + j] * w;
-      else
-        s += w;
+__global__ void __launch_bounds__(256) stitch_kernel(StitchArgs a) {
+  const int r = blockIdx.y;
+  const int total = (int)a.total, border = (int)a.border;
+  const long long per_slot = (long long)a.rows * a.chunk;
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const long long p = a.begin + (long long)blockIdx.x * 1024 + u * 256 + threadIdx.x;
+    if (p >= a.end) break;
+    const int q = (int)p + border;
+    const int k_hi = min(a.num_chunks - 1, q / a.step);
+    const int k_lo = q >= a.chunk ? (q - a.chunk) / a.step + 1 : 0;
+    float acc = 0.f, wsum = 0.f;
+    for (int k = k_lo; k <= k_hi; ++k) {
+      const int start = k * a.step;
+      const int j = q - start;
+      const float w = fade_weight(j, a.chunk, k == 0, start + a.chunk >= total);
+      const long long slot = (long long)(k % a.slot_ranks) * a.slot_cap + k / a.slot_ranks;
+      acc += __ldg(a.y + slot * per_slot + (long long)r * a.chunk + j) * w;
+      wsum += w;
     }
-    if (c < a.C)
-      acc[(long long)c * a.total + p] = s;
-    else
-      wsum[p] = s;
-  }
-  (void)num_chunks;
-}
-
-__global__ void __launch_bounds__(256) chunk_finish_kernel(ChunkArgs a, const float* acc, const float* wsum,
-                                                           float* out) {
-  const long long total = (long long)a.C * a.L;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int c = (int)(i / a.L);
-    const long long p = i % a.L + a.border;
-    const float w = wsum[p];
-    const float v = acc[(long long)c * a.total + p];
-    out[i] = w > 1e-8f ? v / w : v;
+    a.out[(long long)r * a.L + p] = wsum > 1e-8f ? acc / wsum : acc;
   }
 }
 
@@ -709,42 +721,53 @@ cudaError_t launch_layernorm(const LayerNormArgs& a, cudaStream_t s) {
 }
 
 cudaError_t launch_band_input(const BandInArgs& a, int bf16, cudaStream_t s) {
-  const long long warps = (long long)a.Bc * a.T * a.num_bands;
-  long long blocks = (warps + 7) / 8;
-  if (blocks > 148LL * 32) blocks = 148LL * 32;
-  if (blocks < 1) return cudaSuccess;
+  const long long rows = (long long)a.Bc * a.T;
+  if (rows < 1) return cudaSuccess;
+  if (rows > 0x7fffffffLL || (a.ld & 1)) return cudaErrorInvalidValue;
+  const size_t smem = sizeof(float2) * (size_t)a.C * a.nbins;
   // the STFT read once, the packed A operand written once
-  LaunchScope scope("band_input", 0.0,
-                    (double)a.Bc * a.C * a.T * a.nbins * 8.0 + (double)a.Bc * a.T * a.ld * 2.0, s);
-  if (bf16)
-    band_input_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, s>>>(a);
-  else
-    band_input_kernel<__half><<<(unsigned)blocks, 256, 0, s>>>(a);
+  LaunchScope scope("band_input", 0.0, (double)a.Bc * a.C * a.T * a.nbins * 8.0 + (double)rows * a.ld * 2.0, s);
+  if (bf16) {
+    if (smem > 48 * 1024)
+      cudaFuncSetAttribute(band_input_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    band_input_kernel<__nv_bfloat16><<<(unsigned)rows, 256, smem, s>>>(a);
+  } else {
+    if (smem > 48 * 1024)
+      cudaFuncSetAttribute(band_input_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    band_input_kernel<__half><<<(unsigned)rows, 256, smem, s>>>(a);
+  }
   return cudaGetLastError();
 }
 
 cudaError_t launch_mask_apply(const MaskApplyArgs& a, cudaStream_t s) {
+  const long long blocks = (long long)a.Bc * a.S * a.T;
+  if (blocks < 1) return cudaSuccess;
+  const size_t smem = sizeof(float) * (size_t)a.mask_ld;
+  if (blocks > 0x7fffffffLL || smem > 227 * 1024) return cudaErrorInvalidValue;
   const double tb = (double)a.Bc * a.T * a.nbins;
   LaunchScope scope("mask_apply", 0.0,
                     tb * a.C * 8.0 + (double)a.S * a.Bc * a.T * a.mask_ld * 4.0 + tb * a.S * a.C * 8.0, s);
-  mask_apply_kernel<<<grid_for((long long)a.Bc * a.S * a.T * a.nbins), 256, 0, s>>>(a);
+  if (smem > 48 * 1024) cudaFuncSetAttribute(mask_apply_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  mask_apply_kernel<<<(unsigned)blocks, 256, smem, s>>>(a);
   return cudaGetLastError();
 }
 
 cudaError_t launch_stft_frames(const float* audio, long long L, int BC, int T, int n_fft, int hop, const float* win,
                                float* frames, cudaStream_t s) {
+  if (n_fft % 4 != 0 || (long long)BC * T > 0x7fffffffLL) return cudaErrorInvalidValue;
   LaunchScope scope("stft_frames", 0.0, (double)BC * L * 4.0 + (double)BC * T * n_fft * 4.0, s);
-  stft_frames_kernel<<<grid_for((long long)BC * T * n_fft), 256, 0, s>>>(audio, L, BC, T, n_fft, hop, win, frames);
+  stft_frames_kernel<<<(unsigned)((long long)BC * T), 256, 0, s>>>(audio, L, T, n_fft, hop, win, frames);
   return cudaGetLastError();
 }
 
 cudaError_t launch_istft_ola(const float* frames, int BSC, int T, int n_fft, int hop, const float* win,
                              const float* wsum, float* out, long long out_len, int ref_compat, cudaStream_t s) {
   if (out_len < (long long)(T - 1) * hop) return cudaErrorInvalidValue;
+  if (out_len + n_fft >= (1LL << 31) || BSC > 65535) return cudaErrorInvalidValue;
   if (out_len == (long long)(T - 1) * hop) ref_compat = 0;  // nothing padded: the rows are plain
   LaunchScope scope("istft_ola", 0.0, (double)BSC * T * n_fft * 4.0 + (double)BSC * (double)out_len * 4.0, s);
-  istft_ola_kernel<<<grid_for((long long)BSC * out_len), 256, 0, s>>>(frames, BSC, T, n_fft, hop, win, wsum, out,
-                                                                      out_len, ref_compat);
+  istft_ola_kernel<<<dim3((unsigned)((out_len + 1023) / 1024), (unsigned)BSC), 256, 0, s>>>(
+      frames, T, n_fft, hop, win, wsum, out, (int)out_len, ref_compat);
   return cudaGetLastError();
 }
 
@@ -758,26 +781,23 @@ cudaError_t launch_skip_add(float* x, const float* skips, int count, long long n
   return cudaGetLastError();
 }
 
-cudaError_t launch_chunk_gather(const ChunkArgs& a, int first, int count, float* batch, cudaStream_t s) {
+cudaError_t launch_chunk_gather(const ChunkArgs& a, int first, int stride, int count, float* batch, cudaStream_t s) {
+  if (count <= 0) return cudaSuccess;
+  if (a.total + a.chunk >= (1LL << 31) || (long long)count * a.C > 65535 || stride < 1) return cudaErrorInvalidValue;
   LaunchScope scope("chunk_gather", 0.0, 2.0 * count * a.C * (double)a.chunk * 4.0, s);
-  chunk_gather_kernel<<<grid_for((long long)count * a.C * a.chunk), 256, 0, s>>>(a, first, count, batch);
+  chunk_gather_kernel<<<dim3((unsigned)((a.chunk + 1023) / 1024), (unsigned)(count * a.C)), 256, 0, s>>>(a, first,
+                                                                                                      stride, batch);
   return cudaGetLastError();
 }
 
-cudaError_t launch_chunk_ola(const ChunkArgs& a, int first, int count, int num_chunks, const float* y, float* acc,
-                             float* wsum, cudaStream_t s) {
-  const long long g0 = (long long)first * a.step;
-  const long long g1 = std::min((long long)(first + count - 1) * a.step + a.chunk, a.total);
-  LaunchScope scope("chunk_ola", 0.0,
-                    (double)count * a.C * a.chunk * 4.0 + 2.0 * (a.C + 1) * (double)(g1 - g0) * 4.0, s);
-  chunk_ola_kernel<<<grid_for((long long)(a.C + 1) * (g1 - g0)), 256, 0, s>>>(a, first, count, num_chunks, y, acc,
-                                                                              wsum);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_chunk_finish(const ChunkArgs& a, const float* acc, const float* wsum, float* out, cudaStream_t s) {
-  LaunchScope scope("chunk_finish", 0.0, (double)a.L * (2.0 * a.C + 1.0) * 4.0, s);
-  chunk_finish_kernel<<<grid_for((long long)a.C * a.L), 256, 0, s>>>(a, acc, wsum, out);
+cudaError_t launch_stitch(const StitchArgs& a, cudaStream_t s) {
+  if (a.end <= a.begin) return cudaSuccess;
+  if (a.total + a.chunk >= (1LL << 31) || a.rows > 65535 || a.slot_ranks < 1 || a.begin < 0 || a.end > a.L)
+    return cudaErrorInvalidValue;
+  const long long n = a.end - a.begin;
+  // every output sample written once; each chunk sample it covers read once (overlaps twice)
+  LaunchScope scope("stitch", 0.0, (double)a.rows * n * 4.0 * 2.0, s);
+  stitch_kernel<<<dim3((unsigned)((n + 1023) / 1024), (unsigned)a.rows), 256, 0, s>>>(a);
   return cudaGetLastError();
 }
 

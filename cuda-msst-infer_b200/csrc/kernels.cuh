@@ -124,7 +124,7 @@ cudaError_t launch_istft_ola(const float* frames, int BSC, int T, int n_fft, int
 cudaError_t launch_skip_add(float* x, const float* skips, int count, long long n, cudaStream_t s);
 
 // Chunked inference helpers (src/inference_app.cpp:100-324).
-// Gather `count` chunks starting at chunk index `first` of the reflect-padded
+// Gather `count` chunks, indices first, first + stride, ..., of the reflect-padded
 // track into batch [count, C, chunk].  The padded track is never materialised:
 // padded index p maps to track index reflect(p - border).  The final, short
 // chunk is padded to `chunk` samples; ref_compat reproduces the reference's
@@ -139,17 +139,28 @@ struct ChunkArgs {
   int step;
   int ref_compat;
 };
-cudaError_t launch_chunk_gather(const ChunkArgs& a, int first, int count, float* batch, cudaStream_t s);
+cudaError_t launch_chunk_gather(const ChunkArgs& a, int first, int stride, int count, float* batch, cudaStream_t s);
 
-// Windowed overlap-add of `count` chunk outputs y [count, C, chunk] (chunk
-// indices first..first+count-1) into acc [C, total] and wsum [total], chunks in
-// order (deterministic, no atomics).  Linear fade of chunk/10 samples, dropped at
-// the track's first and last chunk.
-cudaError_t launch_chunk_ola(const ChunkArgs& a, int first, int count, int num_chunks, const float* y, float* acc,
-                             float* wsum, cudaStream_t s);
-
-// out[c, i] = acc[c, border + i] / wsum[border + i] (where wsum > 1e-8), i < L.
-cudaError_t launch_chunk_finish(const ChunkArgs& a, const float* acc, const float* wsum, float* out,
-                                cudaStream_t s);
+// Windowed overlap-add stitch of chunk outputs, as a gather over the output
+// (src/inference_app.cpp:252-306, src/ops_fused.cu:138-188): for every output
+// row r < rows and track sample p in [begin, end), with q = p + border,
+//   acc  = sum over the chunks k covering q, in increasing k, of y_k[r, q - k*step] * w_k
+//   wsum = sum of the same w_k,   out[r, p] = wsum > 1e-8 ? acc / wsum : acc
+// where w_k is the linear fade of chunk/10 samples (dropped at the track's first
+// and last chunk).  The sums run in chunk order from zero, as the reference's
+// accumulation buffer does, so the result does not depend on how the output is
+// split into ranges.  Chunk k's output [rows, chunk] sits at y + slot(k)*rows*chunk,
+// slot(k) = (k % slot_ranks) * slot_cap + k / slot_ranks (chunk order when
+// slot_ranks = 1; round-robin shards gathered rank after rank otherwise).
+struct StitchArgs {
+  const float* y;
+  int rows;
+  int chunk, step, num_chunks;
+  long long border, total, L;
+  int slot_ranks, slot_cap;
+  float* out;              // [rows, L]
+  long long begin, end;
+};
+cudaError_t launch_stitch(const StitchArgs& a, cudaStream_t s);
 
 }  // namespace msst

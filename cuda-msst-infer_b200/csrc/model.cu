@@ -331,7 +331,7 @@ static DeviceBuffer upload_16(const std::vector<float>& v, int bf16) {
 struct Model::Work {
   int B = 0, T = 0;
   long long M = 0, BT = 0;
-  DeviceBuffer frames, spec, ispec, abs, x, xn, gates, big1, big2, ao, mask, chunk_in, chunk_out;
+  DeviceBuffer frames, spec, ispec, abs, x, xn, gates, big1, big2, ao, mask, chunk_in;
   DeviceBuffer skips;  // skip_connection models: the outputs of depth blocks 0..depth-2
   CUtensorMap m_abs, m_xn, m_ao, m_big1_ffh, m_big2_ffh, m_qkv_time, m_qkv_band, m_h1, m_h2;
   // GEMM output maps (TMA stores)
@@ -343,6 +343,9 @@ Model::Model() = default;
 Model::~Model() {
   for (auto& kv : plans_) cufftDestroy(kv.second);
   if (host_stream_) cudaStreamDestroy(host_stream_);
+  for (cudaStream_t st : copy_streams_)
+    if (st) cudaStreamDestroy(st);
+  for (cudaEvent_t e : events_) cudaEventDestroy(e);
 }
 
 // ===========================================================================
@@ -1186,16 +1189,101 @@ void Model::chunk_plan(long long L, float overlap, int* chunk, int* step, long l
   *num_chunks = (int)((tot + st - 1) / st);
 }
 
-void Model::separate(const float* track, int C, long long L, float overlap, int chunk_batch, int flags, float* out,
-                     cudaStream_t s) {
+// Sample ranges of chunk k of a track's plan: [*in_lo, *in_hi) of the track that
+// its gather reads (the reflect padding and, for a short final chunk, the
+// reference's contiguous-source padding included) and [*out_lo, *out_hi) of the
+// output that its overlap-add touches.
+void Model::chunk_span(long long L, float overlap, int k, int flags, long long* in_lo, long long* in_hi,
+                       long long* out_lo, long long* out_hi) const {
+  int chunk, step, n;
+  long long border, total;
+  chunk_plan(L, overlap, &chunk, &step, &border, &total, &n);
+  MSST_REQUIRE(k >= 0 && k < n, "chunk index outside the track's plan");
+  const long long s0 = (long long)k * step, e0 = std::min(s0 + chunk, total);
+  long long lo = L, hi = -1;
+  // padded positions [a, b) -> track samples: reflect is monotone between its
+  // breakpoints, so the extremes are at the range ends and the breakpoints
+  auto cover = [&](long long a, long long b) {
+    if (b <= a) return;
+    const long long pts[6] = {a, b - 1, border - 1, border, border + L - 1, border + L};
+    for (long long q : pts) {
+      if (q < a || q >= b) continue;
+      long long i = border ? q - border : q;
+      if (i < 0) i = -i;
+      else if (i >= L) i = 2 * (L - 1) - i;
+      i = std::min(std::max(i, 0LL), L - 1);
+      lo = std::min(lo, i);
+      hi = std::max(hi, i + 1);
+    }
+  };
+  cover(s0, e0);
+  const bool ref_compat = !(flags & MSST_SEPARATE_FIX_TAIL_PADDING);
+  if (e0 - s0 < chunk && ref_compat && C_ > 1) cover(0, std::min(total, (long long)(C_ - 1) * (e0 - s0)));
+  *in_lo = lo;
+  *in_hi = hi;
+  *out_lo = std::min(std::max(s0 - border, 0LL), L);
+  *out_hi = std::min(std::max(e0 - border, 0LL), L);
+}
+
+cudaEvent_t Model::pipeline_event(size_t i) {
+  while (events_.size() <= i) {
+    cudaEvent_t e;
+    MSST_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    events_.push_back(e);
+  }
+  return events_[i];
+}
+
+cudaStream_t Model::copy_stream(int which) {
+  cudaStream_t& st = copy_streams_[which];
+  if (!st) MSST_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+  return st;
+}
+
+void Model::stitch_range(const float* chunks, int slot_ranks, int slot_cap, int C, long long L, float overlap,
+                         long long begin, long long end, float* out, cudaStream_t s) {
+  int chunk, step, n;
+  long long border, total;
+  chunk_plan(L, overlap, &chunk, &step, &border, &total, &n);
+  MSST_REQUIRE(slot_ranks >= 1 && slot_cap >= (n + slot_ranks - 1) / slot_ranks, "chunk slot layout too small");
+  MSST_REQUIRE(begin >= 0 && begin <= end && end <= L, "stitch range outside the track");
+  StitchArgs a{};
+  a.y = chunks;
+  a.rows = info_.num_stems * C;
+  a.chunk = chunk;
+  a.step = step;
+  a.num_chunks = n;
+  a.border = border;
+  a.total = total;
+  a.L = L;
+  a.slot_ranks = slot_ranks;
+  a.slot_cap = slot_cap;
+  a.out = out;
+  a.begin = begin;
+  a.end = end;
+  MSST_CUDA(launch_stitch(a, s));
+}
+
+// Chunked separation (src/inference_app.cpp:100-324): the chunk outputs of the
+// whole plan are kept ([num_chunks, stems*C, chunk]), and after every forward
+// batch the output samples no later chunk touches are stitched.  With host
+// buffers the track goes up in per-batch pieces on one copy stream (all issued
+// first, each batch waits only for its own piece) and every stitched range goes
+// down on another as soon as it is final, so the copies overlap the compute.
+void Model::separate_pipeline(const float* track, const float* track_host, int C, long long L, float overlap,
+                              int chunk_batch, int flags, float* out, float* out_host, cudaStream_t s) {
   const msst_model_info& I = info_;
   MSST_REQUIRE(C == C_, "channel count does not match the model");
   const int S = I.num_stems;
+  const size_t row_bytes = sizeof(float) * (size_t)L;
   if (I.chunk_size <= 0 || L <= I.chunk_size) {
     // short input: one forward over the whole track (src/inference_app.cpp:463-472)
     MSST_REQUIRE(match_len_ || L % I.hop_length == 0,
                  "whole-track forward needs length % hop_length == 0 (or a match_input_audio_length model)");
+    if (track_host) MSST_CUDA(cudaMemcpyAsync(const_cast<float*>(track), track_host, row_bytes * C,
+                                              cudaMemcpyHostToDevice, s));
     forward_impl(track, 1, C, L, out, (flags & MSST_SEPARATE_FIX_TAIL_PADDING) != 0, s);
+    if (out_host) MSST_CUDA(cudaMemcpyAsync(out_host, out, row_bytes * S * C, cudaMemcpyDeviceToHost, s));
     return;
   }
   int chunk, step, nchunks;
@@ -1212,28 +1300,73 @@ void Model::separate(const float* track, int C, long long L, float overlap, int 
   ci.chunk = chunk;
   ci.step = step;
   ci.ref_compat = (flags & MSST_SEPARATE_FIX_TAIL_PADDING) ? 0 : 1;
-  ChunkArgs co = ci;
-  co.C = S * C;
   const int T = chunk / I.hop_length + 1;
   Work& w = work(eb, T);
   w.chunk_in.ensure(sizeof(float) * (size_t)eb * C * chunk);
-  w.chunk_out.ensure(sizeof(float) * (size_t)eb * S * C * chunk);
-  const size_t acc_bytes = sizeof(float) * (size_t)(S * C + 1) * total;
-  sep_acc_.ensure(acc_bytes);
-  float* d_acc = sep_acc_.get<float>();
-  float* d_wsum = d_acc + (size_t)S * C * total;
-  MSST_CUDA(cudaMemsetAsync(d_acc, 0, acc_bytes, s));
-  for (int g0 = 0; g0 < nchunks; g0 += eb) {
-    const int cnt = std::min(eb, nchunks - g0);
-    MSST_CUDA(launch_chunk_gather(ci, g0, cnt, w.chunk_in.get<float>(), s));
-    forward(w.chunk_in.get<float>(), cnt, C, chunk, w.chunk_out.get<float>(), s);
-    MSST_CUDA(launch_chunk_ola(co, g0, cnt, nchunks, w.chunk_out.get<float>(), d_acc, d_wsum, s));
+  const size_t per_chunk = (size_t)S * C * chunk;
+  sep_chunks_.ensure(sizeof(float) * per_chunk * nchunks);
+  float* ys = sep_chunks_.get<float>();
+  const int nbatch = (nchunks + eb - 1) / eb;
+  if (track_host) {
+    // the track goes up as a growing prefix: each batch's piece ends where its chunks stop reading
+    cudaStream_t up = copy_stream(0);
+    MSST_CUDA(cudaEventRecord(pipeline_event(0), s));  // the buffer may still be read by earlier work
+    MSST_CUDA(cudaStreamWaitEvent(up, pipeline_event(0), 0));
+    long long copied = 0;
+    for (int b = 0; b < nbatch; ++b) {
+      long long need = copied;
+      for (int k = b * eb; k < std::min(nchunks, (b + 1) * eb); ++k) {
+        long long lo, hi, olo, ohi;
+        chunk_span(L, overlap, k, flags, &lo, &hi, &olo, &ohi);
+        need = std::max(need, hi);
+      }
+      if (need > copied)
+        MSST_CUDA(cudaMemcpy2DAsync(const_cast<float*>(track) + copied, row_bytes, track_host + copied, row_bytes,
+                                    sizeof(float) * (size_t)(need - copied), (size_t)C, cudaMemcpyHostToDevice, up));
+      copied = need;
+      MSST_CUDA(cudaEventRecord(pipeline_event(1 + b), up));
+    }
   }
-  MSST_CUDA(launch_chunk_finish(co, d_acc, d_wsum, out, s));
-  MSST_CUDA(cudaStreamSynchronize(s));
+  long long done = 0;
+  for (int b = 0; b < nbatch; ++b) {
+    const int g0 = b * eb, cnt = std::min(eb, nchunks - g0);
+    if (track_host) MSST_CUDA(cudaStreamWaitEvent(s, pipeline_event(1 + b), 0));
+    MSST_CUDA(launch_chunk_gather(ci, g0, 1, cnt, w.chunk_in.get<float>(), s));
+    forward(w.chunk_in.get<float>(), cnt, C, chunk, ys + (size_t)g0 * per_chunk, s);
+    long long upto = L;
+    if (g0 + cnt < nchunks) {
+      long long lo, hi, olo, ohi;
+      chunk_span(L, overlap, g0 + cnt, flags, &lo, &hi, &olo, &ohi);
+      upto = olo;
+    }
+    if (upto > done) {
+      stitch_range(ys, 1, nchunks, C, L, overlap, done, upto, out, s);
+      if (out_host) {
+        cudaStream_t down = copy_stream(1);
+        cudaEvent_t ev = pipeline_event(1 + nbatch + b);
+        MSST_CUDA(cudaEventRecord(ev, s));
+        MSST_CUDA(cudaStreamWaitEvent(down, ev, 0));
+        MSST_CUDA(cudaMemcpy2DAsync(out_host + done, row_bytes, out + done, row_bytes,
+                                    sizeof(float) * (size_t)(upto - done), (size_t)S * C, cudaMemcpyDeviceToHost,
+                                    down));
+      }
+      done = upto;
+    }
+  }
+  if (out_host) {
+    // the call's stream covers the copies, so the caller's sync (and the next call) sees them
+    cudaEvent_t ev = pipeline_event(1 + 2 * nbatch);
+    MSST_CUDA(cudaEventRecord(ev, copy_stream(1)));
+    MSST_CUDA(cudaStreamWaitEvent(s, ev, 0));
+  }
 }
 
-void Model::forward_chunks(const float* track, int C, long long L, float overlap, int first, int count,
+void Model::separate(const float* track, int C, long long L, float overlap, int chunk_batch, int flags, float* out,
+                     cudaStream_t s) {
+  separate_pipeline(track, nullptr, C, L, overlap, chunk_batch, flags, out, nullptr, s);
+}
+
+void Model::forward_chunks(const float* track, int C, long long L, float overlap, int first, int stride, int count,
                            int chunk_batch, int flags, float* out, cudaStream_t s) {
   const msst_model_info& I = info_;
   MSST_REQUIRE(C == C_, "channel count does not match the model");
@@ -1241,7 +1374,9 @@ void Model::forward_chunks(const float* track, int C, long long L, float overlap
   long long border, total;
   chunk_plan(L, overlap, &chunk, &step, &border, &total, &nchunks);
   MSST_REQUIRE(chunk % I.hop_length == 0, "chunk_size must be a multiple of hop_length");
-  MSST_REQUIRE(first >= 0 && count >= 0 && first + count <= nchunks, "chunk range outside the track's plan");
+  MSST_REQUIRE(stride >= 1, "chunk stride must be >= 1");
+  MSST_REQUIRE(first >= 0 && count >= 0 && (count == 0 || first + (long long)(count - 1) * stride < nchunks),
+               "chunk range outside the track's plan");
   if (count == 0) return;
   const int S = I.num_stems;
   const int eb = std::max(1, std::min(chunk_batch > 0 ? chunk_batch : 2, count));
@@ -1258,38 +1393,18 @@ void Model::forward_chunks(const float* track, int C, long long L, float overlap
   Work& w = work(eb, T);
   w.chunk_in.ensure(sizeof(float) * (size_t)eb * C * chunk);
   const size_t per_chunk = (size_t)S * C * chunk;
-  for (int g0 = first; g0 < first + count; g0 += eb) {
-    const int cnt = std::min(eb, first + count - g0);
-    MSST_CUDA(launch_chunk_gather(ci, g0, cnt, w.chunk_in.get<float>(), s));
-    forward(w.chunk_in.get<float>(), cnt, C, chunk, out + (size_t)(g0 - first) * per_chunk, s);
+  for (int i0 = 0; i0 < count; i0 += eb) {
+    const int cnt = std::min(eb, count - i0);
+    MSST_CUDA(launch_chunk_gather(ci, first + i0 * stride, stride, cnt, w.chunk_in.get<float>(), s));
+    forward(w.chunk_in.get<float>(), cnt, C, chunk, out + (size_t)i0 * per_chunk, s);
   }
 }
 
 void Model::stitch(const float* chunks, int C, long long L, float overlap, float* out, cudaStream_t s) {
-  const msst_model_info& I = info_;
-  int chunk, step, nchunks;
+  int chunk, step, n;
   long long border, total;
-  chunk_plan(L, overlap, &chunk, &step, &border, &total, &nchunks);
-  const int S = I.num_stems;
-  ChunkArgs co{};
-  co.C = S * C;
-  co.L = L;
-  co.border = border;
-  co.total = total;
-  co.chunk = chunk;
-  co.step = step;
-  const size_t acc_bytes = sizeof(float) * (size_t)(S * C + 1) * total;
-  sep_acc_.ensure(acc_bytes);
-  float* d_acc = sep_acc_.get<float>();
-  float* d_wsum = d_acc + (size_t)S * C * total;
-  MSST_CUDA(cudaMemsetAsync(d_acc, 0, acc_bytes, s));
-  const size_t per_chunk = (size_t)S * C * chunk;
-  constexpr int kGroup = 4;  // chunks folded per launch, in chunk order
-  for (int g0 = 0; g0 < nchunks; g0 += kGroup) {
-    const int cnt = std::min(kGroup, nchunks - g0);
-    MSST_CUDA(launch_chunk_ola(co, g0, cnt, nchunks, chunks + (size_t)g0 * per_chunk, d_acc, d_wsum, s));
-  }
-  MSST_CUDA(launch_chunk_finish(co, d_acc, d_wsum, out, s));
+  chunk_plan(L, overlap, &chunk, &step, &border, &total, &n);
+  stitch_range(chunks, 1, n, C, L, overlap, 0, L, out, s);
 }
 
 cudaStream_t Model::host_stream() {
@@ -1304,9 +1419,8 @@ void Model::separate_host(const float* track_host, int C, long long L, float ove
   const size_t out_bytes = in_bytes * (size_t)info_.num_stems;
   host_in_.ensure(in_bytes);
   host_out_.ensure(out_bytes);
-  MSST_CUDA(cudaMemcpyAsync(host_in_.get(), track_host, in_bytes, cudaMemcpyHostToDevice, host_stream_));
-  separate(host_in_.get<float>(), C, L, overlap, chunk_batch, flags, host_out_.get<float>(), host_stream_);
-  MSST_CUDA(cudaMemcpyAsync(out_host, host_out_.get(), out_bytes, cudaMemcpyDeviceToHost, host_stream_));
+  separate_pipeline(host_in_.get<float>(), track_host, C, L, overlap, chunk_batch, flags, host_out_.get<float>(),
+                    out_host, host_stream_);
   MSST_CUDA(cudaStreamSynchronize(host_stream_));
 }
 

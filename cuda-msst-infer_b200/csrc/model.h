@@ -72,9 +72,16 @@ class Model {
                   int* num_chunks) const;
   // Sharded separation: forward chunks [first, first + count) of the track's plan
   // into out [count, stems*C, chunk], and stitch all chunk outputs of a track.
-  void forward_chunks(const float* track, int C, long long L, float overlap, int first, int count, int chunk_batch,
-                      int flags, float* out, cudaStream_t s);
+  // Chunks first, first + stride, ... (count of them), chunk_batch per forward.
+  void forward_chunks(const float* track, int C, long long L, float overlap, int first, int stride, int count,
+                      int chunk_batch, int flags, float* out, cudaStream_t s);
   void stitch(const float* chunks, int C, long long L, float overlap, float* out, cudaStream_t s);
+  // Stitch output samples [begin, end) from chunk outputs laid out in slots
+  // (k % slot_ranks) * slot_cap + k / slot_ranks (StitchArgs).
+  void stitch_range(const float* chunks, int slot_ranks, int slot_cap, int C, long long L, float overlap,
+                    long long begin, long long end, float* out, cudaStream_t s);
+  void chunk_span(long long L, float overlap, int k, int flags, long long* in_lo, long long* in_hi, long long* out_lo,
+                  long long* out_hi) const;
 
  private:
   struct Work;  // per-(B, T) workspace
@@ -94,6 +101,10 @@ class Model {
   const float* rope_table(int n, bool sine);
   const float* istft_wsum(int T);
   cufftHandle fft_plan(cufftType type, int batch, cudaStream_t s);
+  void separate_pipeline(const float* track, const float* track_host, int C, long long L, float overlap,
+                         int chunk_batch, int flags, float* out, float* out_host, cudaStream_t s);
+  cudaEvent_t pipeline_event(size_t i);
+  cudaStream_t copy_stream(int which);
 
   msst_model_info info_{};
   int device_ = 0;
@@ -119,9 +130,11 @@ class Model {
   std::map<int, DeviceBuffer> rope_cos_, rope_sin_, wsum_;
   std::map<std::pair<int, int>, cufftHandle> plans_;
   std::map<std::pair<int, int>, std::unique_ptr<Work>> work_;
-  DeviceBuffer sep_acc_;                 // overlap-add accumulator of separate(), grown on demand
+  DeviceBuffer sep_chunks_;              // chunk outputs of separate(), grown on demand
   DeviceBuffer host_in_, host_out_;      // staging of separate_host()
   cudaStream_t host_stream_ = nullptr;   // stream of separate_host()
+  cudaStream_t copy_streams_[2] = {nullptr, nullptr};  // separate_host(): track up, stems down
+  std::vector<cudaEvent_t> events_;      // separate_host() pipeline events, grown on demand
 
  public:
   Model();

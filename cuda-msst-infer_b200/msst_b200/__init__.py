@@ -32,6 +32,7 @@ EXPORTS = [
     "msst_roformer_attn_block", "msst_roformer_ffn_block", "msst_model_load", "msst_model_free", "msst_model_get_info", "msst_model_forward",
     "msst_model_masks", "msst_model_transformer", "msst_model_transformer_noalloc", "msst_model_separate", "msst_model_separate_host",
     "msst_model_chunk_plan", "msst_model_forward_chunks", "msst_model_stitch",
+    "msst_model_forward_chunks_strided", "msst_model_stitch_range", "msst_model_chunk_span",
 ]
 
 
@@ -113,6 +114,11 @@ def lib():
                                         ctypes.POINTER(i64), ctypes.POINTER(i64), ctypes.POINTER(c_int)]
     L.msst_model_forward_chunks.argtypes = [vp, vp, c_int, i64, c_float, c_int, c_int, c_int, c_int, vp, vp]
     L.msst_model_stitch.argtypes = [vp, vp, c_int, i64, c_float, vp, vp]
+    L.msst_model_forward_chunks_strided.argtypes = [vp, vp, c_int, i64, c_float, c_int, c_int, c_int, c_int, c_int,
+                                                    vp, vp]
+    L.msst_model_stitch_range.argtypes = [vp, vp, c_int, c_int, c_int, i64, c_float, i64, i64, vp, vp]
+    pi64 = ctypes.POINTER(i64)
+    L.msst_model_chunk_span.argtypes = [vp, i64, c_float, c_int, c_int, pi64, pi64, pi64, pi64]
     _lib = L
     return L
 
@@ -410,6 +416,34 @@ class Model:
                                               SEPARATE_FIX_TAIL_PADDING if fix_tail_padding else 0,
                                               _ptr(out) if count else None, _stream(stream)))
         return out
+
+    def forward_chunks_strided(self, track, overlap: float, first: int, stride: int, count: int,
+                               chunk_batch: int = 0, fix_tail_padding: bool = False, out=None, stream=None):
+        """Forward chunks first, first+stride, ... (count) of a CUDA fp32 [C, L] track -> [count, S*C, chunk]."""
+        torch = _torch()
+        C, L = track.shape
+        chunk = self.chunk_plan(L, overlap)["chunk_size"]
+        if out is None:
+            out = torch.empty((count, self.info["num_stems"] * C, chunk), dtype=torch.float32, device=track.device)
+        check(lib().msst_model_forward_chunks_strided(self._h, _ptr(track), C, L, overlap, first, stride, count,
+                                                      chunk_batch, SEPARATE_FIX_TAIL_PADDING if fix_tail_padding
+                                                      else 0, _ptr(out) if count else None, _stream(stream)))
+        return out
+
+    def stitch_range(self, chunks, slot_ranks: int, slot_cap: int, channels: int, length: int, overlap: float,
+                     begin: int, end: int, out, stream=None):
+        """Stitch output samples [begin, end) into out [S, C, L] from chunk outputs in round-robin slots."""
+        check(lib().msst_model_stitch_range(self._h, _ptr(chunks), slot_ranks, slot_cap, channels, length, overlap,
+                                            begin, end, _ptr(out), _stream(stream)))
+        return out
+
+    def chunk_span(self, length: int, overlap: float, k: int, fix_tail_padding: bool = False):
+        """((in_begin, in_end), (out_begin, out_end)) sample ranges of chunk k of the track's plan."""
+        v = [ctypes.c_longlong() for _ in range(4)]
+        check(lib().msst_model_chunk_span(self._h, length, overlap, k,
+                                          SEPARATE_FIX_TAIL_PADDING if fix_tail_padding else 0,
+                                          *[ctypes.byref(x) for x in v]))
+        return (v[0].value, v[1].value), (v[2].value, v[3].value)
 
     def stitch(self, chunks, channels: int, length: int, overlap: float, out=None, stream=None):
         """Overlap-add all chunk outputs [num_chunks, S*C, chunk] of a track -> [S, C, L] (S squeezed when 1)."""

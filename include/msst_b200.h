@@ -297,6 +297,33 @@ int msst_model_forward_chunks(msst_model* m, const float* track, int channels, l
 int msst_model_stitch(msst_model* m, const float* chunks, int channels, long long length, float overlap, float* out,
                       void* stream);
 
+/* Round-robin sharding (chunk i on rank i % world, the reference's chunk list of
+ * src/inference_app.cpp:131-137 dealt out): msst_model_forward_chunks over chunks
+ * first_chunk, first_chunk + chunk_stride, ... (count of them). */
+int msst_model_forward_chunks_strided(msst_model* m, const float* track, int channels, long long length,
+                                      float overlap, int first_chunk, int chunk_stride, int count, int chunk_batch,
+                                      int flags, float* out, void* stream);
+
+/* The overlap-add of msst_model_stitch (src/inference_app.cpp:252-306,
+ * src/ops_fused.cu:138-188) for output samples [begin, end) only, written into
+ * out [num_stems, channels, length] (other samples untouched).  Chunk k's output
+ * [num_stems*channels, chunk_size] is read from slot (k % slot_ranks) * slot_cap +
+ * k / slot_ranks of `chunks` (slot_ranks = 1, slot_cap = num_chunks: chunk order;
+ * slot_ranks = world: each rank's round-robin shard after the previous rank's).
+ * Each sample is summed over its chunks in chunk order, so stitching a track in
+ * ranges gives the same result as one msst_model_stitch. */
+int msst_model_stitch_range(msst_model* m, const float* chunks, int slot_ranks, int slot_cap, int channels,
+                            long long length, float overlap, long long begin, long long end, float* out,
+                            void* stream);
+
+/* Sample ranges of chunk `chunk_index` of a track's plan: [*in_begin, *in_end) of
+ * the track its gather reads (reflect padding, and the reference's padding of a
+ * short final chunk unless flags has MSST_SEPARATE_FIX_TAIL_PADDING), and
+ * [*out_begin, *out_end) of the output its overlap-add touches.  Output samples
+ * before chunk k's out_begin are final once chunks 0..k-1 are stitched. */
+int msst_model_chunk_span(const msst_model* m, long long length, float overlap, int chunk_index, int flags,
+                          long long* in_begin, long long* in_end, long long* out_begin, long long* out_end);
+
 /* Chunk plan of msst_model_separate for a track length (src/inference_app.cpp:119-138). */
 int msst_model_chunk_plan(const msst_model* m, long long length, float overlap, int* chunk_size, int* step,
                           long long* border, long long* padded_length, int* num_chunks);

@@ -1,9 +1,11 @@
 """CPU: chunk-sharded separation (msst_b200.dist.ShardedSeparator) over gloo ranks.
 
-The compute is the fp32 oracle on CPU tensors; what is tested is the sharding,
-the padded gather to rank 0 and the in-order stitch: the sharded result must be
-bit-identical to single-process separation.  A second test kills a rank before
-the collective and checks that the survivor fails with an error within the
+The compute is the fp32 oracle on CPU tensors; what is tested is the round-robin
+dealing, the per-round sends to rank 0, the round-robin slot layout and the
+progressive in-order stitch (range by range, copied into a host output as each
+range becomes final): the sharded result must be bit-identical to
+single-process separation.  A second test kills a rank before the first round's
+transfer and checks that the survivor fails with an error within the
 process-group timeout instead of hanging.
 """
 from __future__ import annotations
@@ -54,26 +56,38 @@ def _worker(rank, world, port, out_path, fail_rank):
                             timeout=timedelta(seconds=10))
     step = oracle.resolve_step(CHUNK, 0.25, 2)
     inputs = oracle.chunk_inputs(track, CHUNK, step)
+    border, total, starts = oracle.chunk_plan(track.shape[1], CHUNK, step)
 
     def plan(L, overlap):
-        return dict(num_chunks=len(oracle.chunk_plan(L, CHUNK, step)[2]), chunk_size=CHUNK)
+        return dict(num_chunks=len(starts), chunk_size=CHUNK)
 
-    def fwd(trk, overlap, first, count, cb, fix, out):
-        for k in range(first, first + count):
-            out[k - first] = torch.from_numpy(om.forward(inputs[k][None])[0])
+    def span(L, overlap, k, fix):
+        s0, e0 = starts[k], min(starts[k] + CHUNK, total)
+        return (0, L), (min(max(s0 - border, 0), L), min(max(e0 - border, 0), L))
+
+    def fwd(trk, overlap, first, stride, count, cb, fix, out):
+        for i in range(count):
+            out[i] = torch.from_numpy(om.forward(inputs[first + i * stride][None])[0])
         return out
 
-    def stitch(chunks, C, L, overlap):
-        return torch.from_numpy(oracle.stitch(list(chunks.numpy()), L, CHUNK, step))
+    def stitch_range(chunks, sr, sc, C, L, overlap, b, e, out):
+        ys = [chunks[(k % sr) * sc + k // sr].numpy() for k in range(len(starts))]
+        full = oracle.stitch(ys, L, CHUNK, step)
+        out[0, :, b:e] = torch.from_numpy(full[:, b:e])
+        return out
 
-    sep = ShardedSeparator(None, dist, rank, world, fwd, stitch, plan, stems=1)
+    sep = ShardedSeparator(None, dist, rank, world, fwd, stitch_range, plan, span, stems=1)
+    sep._bufs["all"] = torch.zeros((world * -(-len(starts) // world), 2, CHUNK))
     try:
         if rank == fail_rank:
-            raise SystemExit(3)  # this rank dies before the collective
-        y = sep.separate(torch.from_numpy(track), overlap=0.25)
+            raise SystemExit(3)  # this rank dies before the first round's transfer
+        host_out = np.full((1, 2, track.shape[1]), np.nan, np.float32) if rank == 0 else None
+        y = sep.separate(torch.zeros(track.shape), overlap=0.25, chunk_batch=1, track_host=track,
+                         out_host=host_out)
         if rank == 0:
             ref = oracle.separate(lambda a: om.forward(a), track, CHUNK, step, batch=4)
-            np.save(out_path, np.array([float(np.abs(y.numpy() - ref).max()), float(y.shape[1])]))
+            diff = max(float(np.abs(y.numpy() - ref).max()), float(np.abs(host_out[0] - ref).max()))
+            np.save(out_path, np.array([diff, float(y.shape[1])]))
         dist.destroy_process_group()
     except RuntimeError as e:  # collective failed because a peer is gone
         if rank == 0:
@@ -112,12 +126,17 @@ def test_rank_failure_is_reported_not_hung(tmp_path):
 
 
 def test_shard_ranges():
-    from msst_b200.dist import max_shard, shard
+    from msst_b200.dist import max_shard, round_chunks, shard
 
     for n in (1, 5, 13, 92, 101):
         for w in (1, 2, 3, 8):
             spans = [shard(n, w, r) for r in range(w)]
             assert sum(c for _, c in spans) == n
-            assert all(spans[r][0] + spans[r][1] == spans[r + 1][0] for r in range(w - 1))
             assert max(c for _, c in spans) - min(c for _, c in spans) <= 1
             assert max(c for _, c in spans) == max_shard(n, w)
+            for cb in (1, 4):
+                # round j of all ranks together covers the chunk prefix [j*cb*w, (j+1)*cb*w)
+                rounds = -(-max_shard(n, w) // cb)
+                for j in range(rounds):
+                    got = sorted(k for r in range(w) for k in round_chunks(n, w, r, cb, j))
+                    assert got == list(range(j * cb * w, min(n, (j + 1) * cb * w)))
