@@ -646,10 +646,10 @@ int msst_model_stitch_range(msst_model* m, const float* chunks, int slot_ranks, 
 }
 
 int msst_model_chunk_span(const msst_model* m, long long length, float overlap, int chunk_index, int flags,
-                          long long* in_begin, long long* in_end, long long* out_begin, long long* out_end) {
+                          long long* in_ranges, long long* out_begin, long long* out_end) {
   return guarded([&] {
-    MSST_REQUIRE(m && in_begin && in_end && out_begin && out_end, "null argument");
-    m->impl.chunk_span(length, overlap, chunk_index, flags, in_begin, in_end, out_begin, out_end);
+    MSST_REQUIRE(m && in_ranges && out_begin && out_end, "null argument");
+    m->impl.chunk_span(length, overlap, chunk_index, flags, in_ranges, out_begin, out_end);
   });
 }
 

@@ -450,6 +450,7 @@ __global__ void __launch_bounds__(256) band_input_kernel(BandInArgs a) {
   const int b = bt / a.T, t = bt - b * a.T;
   for (int c = 0; c < a.C; ++c) {
     const float2* src = a.spec + ((long long)(b * a.C + c) * a.T + t) * a.nbins;
+#pragma unroll 4
     for (int f = threadIdx.x; f < a.nbins; f += blockDim.x) {
       float2 z = __ldg(src + f);
       z.x *= a.spec_scale;
@@ -459,16 +460,15 @@ __global__ void __launch_bounds__(256) band_input_kernel(BandInArgs a) {
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-  const int per_bin = 2 * a.C;
+  const int shift = a.C == 2 ? 2 : 1;  // values per bin: 2 * C (re, im per channel)
   T* orow = reinterpret_cast<T*>(a.out) + (long long)bt * a.ld;
   for (int band = warp; band < a.num_bands; band += nwarps) {
     const int nf = __ldg(a.nfreq + band);
-    const int dims = nf * per_bin;
+    const int dims = nf << shift;
     const int* bins = a.bin_list + __ldg(a.bin_start + band);
     auto load = [&](int j) -> float {
-      const int fl = j / per_bin;
-      const int rem = j - fl * per_bin;
-      const float2 z = s_row[(rem >> 1) * a.nbins + __ldg(bins + fl)];
+      const int rem = j & ((1 << shift) - 1);
+      const float2 z = s_row[(rem >> 1) * a.nbins + __ldg(bins + (j >> shift))];
       return (rem & 1) ? z.y : z.x;
     };
     float ss = 0.f;
@@ -500,7 +500,14 @@ __global__ void __launch_bounds__(256) mask_apply_kernel(MaskApplyArgs a) {
   const int rest = blockIdx.x / a.T;
   const int st = rest % a.S, b = rest / a.S;
   const float* mrow = a.mask + st * a.mask_stem_stride + ((long long)b * a.T + t) * a.mask_ld;
-  for (int i = threadIdx.x; i < a.mask_ld; i += blockDim.x) s_mask[i] = __ldg(mrow + i);
+  if (((a.mask_ld | (int)a.mask_stem_stride) & 3) == 0 && (reinterpret_cast<uintptr_t>(a.mask) & 15) == 0) {
+    const float4* m4 = reinterpret_cast<const float4*>(mrow);
+    float4* s4 = reinterpret_cast<float4*>(s_mask);
+#pragma unroll 4
+    for (int i = threadIdx.x; i < (a.mask_ld >> 2); i += blockDim.x) s4[i] = __ldg(m4 + i);
+  } else {
+    for (int i = threadIdx.x; i < a.mask_ld; i += blockDim.x) s_mask[i] = __ldg(mrow + i);
+  }
   __syncthreads();
   for (int f = threadIdx.x; f < a.nbins; f += blockDim.x) {
     const int k0 = __ldg(a.contrib_off + f), k1 = __ldg(a.contrib_off + f + 1);
@@ -723,7 +730,7 @@ cudaError_t launch_layernorm(const LayerNormArgs& a, cudaStream_t s) {
 cudaError_t launch_band_input(const BandInArgs& a, int bf16, cudaStream_t s) {
   const long long rows = (long long)a.Bc * a.T;
   if (rows < 1) return cudaSuccess;
-  if (rows > 0x7fffffffLL || (a.ld & 1)) return cudaErrorInvalidValue;
+  if (rows > 0x7fffffffLL || (a.ld & 1) || a.C < 1 || a.C > 2) return cudaErrorInvalidValue;
   const size_t smem = sizeof(float2) * (size_t)a.C * a.nbins;
   // the STFT read once, the packed A operand written once
   LaunchScope scope("band_input", 0.0, (double)a.Bc * a.C * a.T * a.nbins * 8.0 + (double)rows * a.ld * 2.0, s);

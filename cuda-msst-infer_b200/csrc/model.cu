@@ -1189,38 +1189,43 @@ void Model::chunk_plan(long long L, float overlap, int* chunk, int* step, long l
   *num_chunks = (int)((tot + st - 1) / st);
 }
 
-// Sample ranges of chunk k of a track's plan: [*in_lo, *in_hi) of the track that
-// its gather reads (the reflect padding and, for a short final chunk, the
-// reference's contiguous-source padding included) and [*out_lo, *out_hi) of the
-// output that its overlap-add touches.
-void Model::chunk_span(long long L, float overlap, int k, int flags, long long* in_lo, long long* in_hi,
-                       long long* out_lo, long long* out_hi) const {
+// Sample ranges of chunk k of a track's plan: in[0..1] and in[2..3] are the two
+// ranges [begin, end) of the track that its gather reads (its own reflect-padded
+// window; for a short final chunk with the reference's contiguous-source padding
+// also the track's first samples, else an empty second range), and
+// [*out_lo, *out_hi) the output samples its overlap-add touches.
+void Model::chunk_span(long long L, float overlap, int k, int flags, long long* in, long long* out_lo,
+                       long long* out_hi) const {
   int chunk, step, n;
   long long border, total;
   chunk_plan(L, overlap, &chunk, &step, &border, &total, &n);
   MSST_REQUIRE(k >= 0 && k < n, "chunk index outside the track's plan");
   const long long s0 = (long long)k * step, e0 = std::min(s0 + chunk, total);
-  long long lo = L, hi = -1;
   // padded positions [a, b) -> track samples: reflect is monotone between its
   // breakpoints, so the extremes are at the range ends and the breakpoints
-  auto cover = [&](long long a, long long b) {
-    if (b <= a) return;
-    const long long pts[6] = {a, b - 1, border - 1, border, border + L - 1, border + L};
-    for (long long q : pts) {
-      if (q < a || q >= b) continue;
-      long long i = border ? q - border : q;
-      if (i < 0) i = -i;
-      else if (i >= L) i = 2 * (L - 1) - i;
-      i = std::min(std::max(i, 0LL), L - 1);
-      lo = std::min(lo, i);
-      hi = std::max(hi, i + 1);
+  auto cover = [&](long long a, long long b, long long* r) {
+    long long lo = L, hi = 0;
+    if (b > a) {
+      const long long pts[6] = {a, b - 1, border - 1, border, border + L - 1, border + L};
+      for (long long q : pts) {
+        if (q < a || q >= b) continue;
+        long long i = border ? q - border : q;
+        if (i < 0) i = -i;
+        else if (i >= L) i = 2 * (L - 1) - i;
+        i = std::min(std::max(i, 0LL), L - 1);
+        lo = std::min(lo, i);
+        hi = std::max(hi, i + 1);
+      }
     }
+    r[0] = std::min(lo, hi);
+    r[1] = hi;
   };
-  cover(s0, e0);
+  cover(s0, e0, in);
   const bool ref_compat = !(flags & MSST_SEPARATE_FIX_TAIL_PADDING);
-  if (e0 - s0 < chunk && ref_compat && C_ > 1) cover(0, std::min(total, (long long)(C_ - 1) * (e0 - s0)));
-  *in_lo = lo;
-  *in_hi = hi;
+  if (e0 - s0 < chunk && ref_compat && C_ > 1)
+    cover(0, std::min(total, (long long)(C_ - 1) * (e0 - s0)), in + 2);
+  else
+    in[2] = in[3] = 0;
   *out_lo = std::min(std::max(s0 - border, 0LL), L);
   *out_hi = std::min(std::max(e0 - border, 0LL), L);
 }
@@ -1316,9 +1321,9 @@ void Model::separate_pipeline(const float* track, const float* track_host, int C
     for (int b = 0; b < nbatch; ++b) {
       long long need = copied;
       for (int k = b * eb; k < std::min(nchunks, (b + 1) * eb); ++k) {
-        long long lo, hi, olo, ohi;
-        chunk_span(L, overlap, k, flags, &lo, &hi, &olo, &ohi);
-        need = std::max(need, hi);
+        long long in[4], olo, ohi;
+        chunk_span(L, overlap, k, flags, in, &olo, &ohi);
+        need = std::max(need, std::max(in[1], in[3]));
       }
       if (need > copied)
         MSST_CUDA(cudaMemcpy2DAsync(const_cast<float*>(track) + copied, row_bytes, track_host + copied, row_bytes,
@@ -1335,8 +1340,8 @@ void Model::separate_pipeline(const float* track, const float* track_host, int C
     forward(w.chunk_in.get<float>(), cnt, C, chunk, ys + (size_t)g0 * per_chunk, s);
     long long upto = L;
     if (g0 + cnt < nchunks) {
-      long long lo, hi, olo, ohi;
-      chunk_span(L, overlap, g0 + cnt, flags, &lo, &hi, &olo, &ohi);
+      long long in[4], olo, ohi;
+      chunk_span(L, overlap, g0 + cnt, flags, in, &olo, &ohi);
       upto = olo;
     }
     if (upto > done) {

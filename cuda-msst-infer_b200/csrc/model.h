@@ -80,7 +80,7 @@ class Model {
   // (k % slot_ranks) * slot_cap + k / slot_ranks (StitchArgs).
   void stitch_range(const float* chunks, int slot_ranks, int slot_cap, int C, long long L, float overlap,
                     long long begin, long long end, float* out, cudaStream_t s);
-  void chunk_span(long long L, float overlap, int k, int flags, long long* in_lo, long long* in_hi, long long* out_lo,
+  void chunk_span(long long L, float overlap, int k, int flags, long long* in, long long* out_lo,
                   long long* out_hi) const;
 
  private:

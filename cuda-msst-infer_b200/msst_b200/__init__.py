@@ -118,7 +118,7 @@ def lib():
                                                     vp, vp]
     L.msst_model_stitch_range.argtypes = [vp, vp, c_int, c_int, c_int, i64, c_float, i64, i64, vp, vp]
     pi64 = ctypes.POINTER(i64)
-    L.msst_model_chunk_span.argtypes = [vp, i64, c_float, c_int, c_int, pi64, pi64, pi64, pi64]
+    L.msst_model_chunk_span.argtypes = [vp, i64, c_float, c_int, c_int, pi64, pi64, pi64]
     _lib = L
     return L
 
@@ -438,12 +438,15 @@ class Model:
         return out
 
     def chunk_span(self, length: int, overlap: float, k: int, fix_tail_padding: bool = False):
-        """((in_begin, in_end), (out_begin, out_end)) sample ranges of chunk k of the track's plan."""
-        v = [ctypes.c_longlong() for _ in range(4)]
+        """([(in_begin, in_end), ...], (out_begin, out_end)): the track ranges chunk k of the
+        track's plan reads (one, or two for a short final chunk) and the output it touches."""
+        rng = (ctypes.c_longlong * 4)()
+        ob, oe = ctypes.c_longlong(), ctypes.c_longlong()
         check(lib().msst_model_chunk_span(self._h, length, overlap, k,
-                                          SEPARATE_FIX_TAIL_PADDING if fix_tail_padding else 0,
-                                          *[ctypes.byref(x) for x in v]))
-        return (v[0].value, v[1].value), (v[2].value, v[3].value)
+                                          SEPARATE_FIX_TAIL_PADDING if fix_tail_padding else 0, rng,
+                                          ctypes.byref(ob), ctypes.byref(oe)))
+        ins = [(rng[0], rng[1])] + ([(rng[2], rng[3])] if rng[3] > rng[2] else [])
+        return ins, (ob.value, oe.value)
 
     def stitch(self, chunks, channels: int, length: int, overlap: float, out=None, stream=None):
         """Overlap-add all chunk outputs [num_chunks, S*C, chunk] of a track -> [S, C, L] (S squeezed when 1)."""

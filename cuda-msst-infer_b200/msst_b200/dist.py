@@ -47,7 +47,7 @@ class ShardedSeparator:
     forward:        fn(track, overlap, first, stride, count, chunk_batch, fix_tail_padding, out) -> out
     stitch_range:   fn(chunks, slot_ranks, slot_cap, C, L, overlap, begin, end, out) -> out
     plan:           fn(L, overlap) -> dict(num_chunks=..., chunk_size=...)
-    span:           fn(L, overlap, k, fix_tail_padding) -> ((in_begin, in_end), (out_begin, out_end))
+    span:           fn(L, overlap, k, fix_tail_padding) -> ([(in_begin, in_end), ...], (out_begin, out_end))
     stems:          number of stems (from the model by default)
     """
 
@@ -129,7 +129,8 @@ class ShardedSeparator:
                 up.wait_stream(torch.cuda.current_stream(track.device))
             host = torch.from_numpy(track_host) if not torch.is_tensor(track_host) else track_host
             for j in range(rounds):
-                spans = [self._span(L, overlap, k, fix_tail_padding)[0] for k in round_chunks(n, W, r, cb, j)]
+                spans = [sp for k in round_chunks(n, W, r, cb, j) for sp in self._span(L, overlap, k,
+                                                                                        fix_tail_padding)[0]]
                 with torch.cuda.stream(up) if is_cuda else _nullctx():
                     for lo, hi in _merge(spans):
                         for c in range(C):

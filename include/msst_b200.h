@@ -316,13 +316,15 @@ int msst_model_stitch_range(msst_model* m, const float* chunks, int slot_ranks, 
                             long long length, float overlap, long long begin, long long end, float* out,
                             void* stream);
 
-/* Sample ranges of chunk `chunk_index` of a track's plan: [*in_begin, *in_end) of
- * the track its gather reads (reflect padding, and the reference's padding of a
- * short final chunk unless flags has MSST_SEPARATE_FIX_TAIL_PADDING), and
- * [*out_begin, *out_end) of the output its overlap-add touches.  Output samples
- * before chunk k's out_begin are final once chunks 0..k-1 are stitched. */
+/* Sample ranges of chunk `chunk_index` of a track's plan.  in_ranges[4] receives
+ * two ranges [begin, end) of the track its gather reads: its own reflect-padded
+ * window, and (only for a short final chunk with the reference's padding, i.e.
+ * without MSST_SEPARATE_FIX_TAIL_PADDING) the first samples of the track that
+ * padding reads, else an empty range.  [*out_begin, *out_end) is the output its
+ * overlap-add touches: output samples before chunk k's out_begin are final once
+ * chunks 0..k-1 are stitched. */
 int msst_model_chunk_span(const msst_model* m, long long length, float overlap, int chunk_index, int flags,
-                          long long* in_begin, long long* in_end, long long* out_begin, long long* out_end);
+                          long long* in_ranges, long long* out_begin, long long* out_end);
 
 /* Chunk plan of msst_model_separate for a track length (src/inference_app.cpp:119-138). */
 int msst_model_chunk_plan(const msst_model* m, long long length, float overlap, int* chunk_size, int* step,

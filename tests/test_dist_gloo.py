@@ -63,7 +63,7 @@ def _worker(rank, world, port, out_path, fail_rank):
 
     def span(L, overlap, k, fix):
         s0, e0 = starts[k], min(starts[k] + CHUNK, total)
-        return (0, L), (min(max(s0 - border, 0), L), min(max(e0 - border, 0), L))
+        return [(0, L)], (min(max(s0 - border, 0), L), min(max(e0 - border, 0), L))
 
     def fwd(trk, overlap, first, stride, count, cb, fix, out):
         for i in range(count):

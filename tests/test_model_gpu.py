@@ -135,10 +135,12 @@ def test_chunked_separation_vs_reference(cuda, tmp_path_factory):
 
 
 def test_forward_chunks_and_stitch_equal_separate(cuda, tmp_path_factory):
-    """The sharded building blocks (any split of the chunk range) reproduce msst_model_separate."""
+    """The sharded building blocks reproduce msst_model_separate: chunks dealt
+    round-robin over 1-3 ranks (msst_model_forward_chunks_strided), gathered rank
+    after rank and stitched in one piece or in ranges (msst_model_stitch_range)."""
     torch = cuda
     from msst_b200 import Model, synth
-    from msst_b200.dist import shard
+    from msst_b200.dist import max_shard, shard
 
     z, meta = golden("mbr_chunked_fp32.npz")
     path, _, _ = _model_file(tmp_path_factory, "mbr", meta["cfg"], meta["weights_seed"], "mbr_shard")
@@ -147,10 +149,22 @@ def test_forward_chunks_and_stitch_equal_separate(cuda, tmp_path_factory):
     ov = meta["overlap"]
     ref = m.separate(track, overlap=ov, chunk_batch=2).cpu().numpy()
     n = m.chunk_plan(track.shape[1], ov)["num_chunks"]
+    L = track.shape[1]
+    ordered = m.forward_chunks(track, ov, 0, n, chunk_batch=2)
+    assert snr_db(m.stitch(ordered, 2, L, ov).cpu().numpy(), ref) >= 70.0
     for world in (1, 2, 3):
-        parts = [m.forward_chunks(track, ov, *shard(n, world, r), chunk_batch=2) for r in range(world)]
-        y = m.stitch(torch.cat(parts), 2, track.shape[1], ov).cpu().numpy()
-        assert snr_db(y, ref) >= 70.0
+        cap = max_shard(n, world)
+        allbuf = torch.zeros((world * cap, 2, ordered.shape[-1]), device="cuda")
+        for r in range(world):
+            first, count = shard(n, world, r)
+            if count:
+                m.forward_chunks_strided(track, ov, first, world, count, chunk_batch=2,
+                                         out=allbuf[r * cap:r * cap + count])
+        out = torch.zeros((1, 2, L), device="cuda")
+        cuts = [0, L // 3, L // 3 + 1, L // 2, L]
+        for b, e in zip(cuts[:-1], cuts[1:]):
+            m.stitch_range(allbuf, world, cap, 2, L, ov, b, e, out)
+        assert snr_db(out[0].cpu().numpy(), ref) >= 70.0
     m.close()
 
 
@@ -284,3 +298,40 @@ def test_device_error_flag_clear(cuda):
     from msst_b200 import device_error
 
     assert device_error(True) == 0
+
+
+@pytest.mark.parametrize("fix", [False, True])
+def test_chunk_span_covers_every_read(cuda, tmp_path_factory, fix):
+    """msst_model_chunk_span names every track sample a chunk reads: a rank whose
+    track buffer holds only its own chunks' ranges (NaN elsewhere) reproduces the
+    full-track result, with and without the reference's tail padding."""
+    torch = cuda
+    from msst_b200 import Model, synth
+    from msst_b200.dist import max_shard, shard
+
+    z, meta = golden("mbr_chunked_fp32.npz")
+    path, _, _ = _model_file(tmp_path_factory, "mbr", meta["cfg"], meta["weights_seed"], "mbr_span")
+    host = torch.from_numpy(synth.make_audio(meta["track_len"], 2, meta["track_seed"]))
+    track = host.cuda()
+    m = Model(path, 0, "fp16")
+    ov = meta["overlap"]
+    L = track.shape[1]
+    ref = m.separate(track, overlap=ov, chunk_batch=2, fix_tail_padding=fix).cpu().numpy()
+    n = m.chunk_plan(L, ov)["num_chunks"]
+    for world in (2, 3):
+        cap = max_shard(n, world)
+        allbuf = torch.zeros((world * cap, 2, m.chunk_plan(L, ov)["chunk_size"]), device="cuda")
+        for r in range(world):
+            first, count = shard(n, world, r)
+            part = torch.full_like(track, float("nan"))
+            for k in range(first, n, world):
+                for lo, hi in m.chunk_span(L, ov, k, fix)[0]:
+                    part[:, lo:hi] = track[:, lo:hi]
+            m.forward_chunks_strided(part, ov, first, world, count, chunk_batch=2, fix_tail_padding=fix,
+                                     out=allbuf[r * cap:r * cap + count])
+        out = torch.zeros((1, 2, L), device="cuda")
+        m.stitch_range(allbuf, world, cap, 2, L, ov, 0, L, out)
+        y = out[0].cpu().numpy()
+        assert np.isfinite(y).all()
+        assert snr_db(y, ref) >= 70.0
+    m.close()
