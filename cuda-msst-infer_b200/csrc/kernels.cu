@@ -438,54 +438,80 @@ cudaError_t rmsnorm_dispatch(const RmsNormArgs& a, cudaStream_t s) {
 }
 
 // ------------------------------------------------------------------ band input
-// One block per (chunk b, frame t): the frame's STFT row of every channel is
-// staged in shared memory by coalesced loads (C * nbins complex), then each warp
-// takes a band, reduces its sum of squares and writes the band's normalised,
-// K-padded 16-bit values as packed pairs (the band's region starts on a
-// 128-byte boundary).
+// One block per (chunk b, frame t).  The frame's STFT values of every channel are
+// staged bin-major, [bin][channel][re, im], by coalesced loads: in that order a band
+// whose bins form an ascending run (every MelBandRoformer and BS-Roformer table)
+// is one contiguous span of the staged row, already in the reference's
+// (bin, channel, re/im) folding, so each warp normalises a band with float2
+// reads and packed 16-bit stores.  Other tables take an indexed path.
 template <typename T>
 __global__ void __launch_bounds__(256) band_input_kernel(BandInArgs a) {
-  extern __shared__ float2 s_row[];  // [C][nbins]
+  extern __shared__ float s_row[];  // [nbins][C][2]
   const int bt = blockIdx.x;
   const int b = bt / a.T, t = bt - b * a.T;
-  for (int c = 0; c < a.C; ++c) {
-    const float2* src = a.spec + ((long long)(b * a.C + c) * a.T + t) * a.nbins;
+  const int C = a.C;
+  for (int c = 0; c < C; ++c) {
+    const float2* src = a.spec + ((long long)(b * C + c) * a.T + t) * a.nbins;
 #pragma unroll 4
     for (int f = threadIdx.x; f < a.nbins; f += blockDim.x) {
       float2 z = __ldg(src + f);
       z.x *= a.spec_scale;
       z.y *= a.spec_scale;
-      s_row[c * a.nbins + f] = z;
+      *reinterpret_cast<float2*>(s_row + 2 * (f * C + c)) = z;
     }
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-  const int shift = a.C == 2 ? 2 : 1;  // values per bin: 2 * C (re, im per channel)
   T* orow = reinterpret_cast<T*>(a.out) + (long long)bt * a.ld;
   for (int band = warp; band < a.num_bands; band += nwarps) {
     const int nf = __ldg(a.nfreq + band);
-    const int dims = nf << shift;
+    const int dims = 2 * C * nf;
     const int* bins = a.bin_list + __ldg(a.bin_start + band);
-    auto load = [&](int j) -> float {
-      const int rem = j & ((1 << shift) - 1);
-      const float2 z = s_row[(rem >> 1) * a.nbins + __ldg(bins + (j >> shift))];
-      return (rem & 1) ? z.y : z.x;
-    };
-    float ss = 0.f;
-    for (int j = lane; j < dims; j += 32) {
-      const float v = load(j);
-      ss += v * v;
-    }
-    ss = warp_sum(ss);
-    const float inv = rsqrtf(ss + 1e-12f);
-    const float scale = sqrtf((float)dims);
+    const int first = __ldg(bins);
+    bool run = true;
+    for (int q = lane; q < nf; q += 32) run = run && __ldg(bins + q) == first + q;
+    run = __all_sync(0xffffffffu, run);
     const float* g = a.gamma + __ldg(a.gcol + band);
     T* o = orow + __ldg(a.kcol + band);
     const int kp = __ldg(a.kpad + band);
-    for (int j = 2 * lane; j < kp; j += 64) {
-      const float y0 = j < dims ? load(j) * inv * __ldg(g + j) * scale : 0.f;
-      const float y1 = j + 1 < dims ? load(j + 1) * inv * __ldg(g + j + 1) * scale : 0.f;
-      *reinterpret_cast<uint32_t*>(o + j) = pack2<T>(y0, y1);
+    if (run) {
+      const float2* v2 = reinterpret_cast<const float2*>(s_row + 2 * C * first);
+      float ss = 0.f;
+      for (int i = lane; 2 * i < dims; i += 32) {
+        const float2 v = v2[i];
+        ss = fmaf(v.x, v.x, fmaf(v.y, v.y, ss));
+      }
+      ss = warp_sum(ss);
+      const float inv = rsqrtf(ss + 1e-12f);
+      const float scale = sqrtf((float)dims);
+      for (int i = lane; 2 * i < kp; i += 32) {
+        float2 y = make_float2(0.f, 0.f);
+        if (2 * i < dims) {
+          const float2 v = v2[i];
+          const float2 gg = __ldg(reinterpret_cast<const float2*>(g) + i);
+          y = make_float2(v.x * inv * gg.x * scale, v.y * inv * gg.y * scale);
+        }
+        reinterpret_cast<uint32_t*>(o)[i] = pack2<T>(y.x, y.y);
+      }
+    } else {
+      auto load = [&](int j) -> float {
+        const int per_bin = 2 * C;
+        const int fl = j / per_bin, rem = j - fl * per_bin;
+        return s_row[2 * (__ldg(bins + fl) * C + (rem >> 1)) + (rem & 1)];
+      };
+      float ss = 0.f;
+      for (int j = lane; j < dims; j += 32) {
+        const float v = load(j);
+        ss += v * v;
+      }
+      ss = warp_sum(ss);
+      const float inv = rsqrtf(ss + 1e-12f);
+      const float scale = sqrtf((float)dims);
+      for (int j = 2 * lane; j < kp; j += 64) {
+        const float y0 = j < dims ? load(j) * inv * __ldg(g + j) * scale : 0.f;
+        const float y1 = j + 1 < dims ? load(j + 1) * inv * __ldg(g + j + 1) * scale : 0.f;
+        *reinterpret_cast<uint32_t*>(o + j) = pack2<T>(y0, y1);
+      }
     }
   }
 }
@@ -493,7 +519,8 @@ __global__ void __launch_bounds__(256) band_input_kernel(BandInArgs a) {
 // ------------------------------------------------------------------ mask apply
 // One block per (chunk b, stem, frame t): the frame's mask row is staged in shared
 // memory by coalesced loads, then threads walk the bins (coalesced STFT reads and
-// output writes), summing each bin's <= 2 band contributions from shared memory.
+// output writes), summing each bin's band contributions from shared memory, in
+// table order; with bin_pack a bin's two contributions and count come in one load.
 __global__ void __launch_bounds__(256) mask_apply_kernel(MaskApplyArgs a) {
   extern __shared__ float s_mask[];  // [mask_ld]
   const int t = blockIdx.x % a.T;
@@ -510,21 +537,41 @@ __global__ void __launch_bounds__(256) mask_apply_kernel(MaskApplyArgs a) {
   }
   __syncthreads();
   for (int f = threadIdx.x; f < a.nbins; f += blockDim.x) {
-    const int k0 = __ldg(a.contrib_off + f), k1 = __ldg(a.contrib_off + f + 1);
-    const float den = __ldg(a.denom + f);
+    int4 pk = make_int4(-2, -1, 0, 0);
+    if (a.bin_pack) pk = __ldg(a.bin_pack + f);
+    int k0 = 0, k1 = 0;
+    float den;
+    if (pk.x == -2) {
+      k0 = __ldg(a.contrib_off + f);
+      k1 = __ldg(a.contrib_off + f + 1);
+      den = __ldg(a.denom + f);
+    } else {
+      den = __int_as_float(pk.w);
+    }
     for (int c = 0; c < a.C; ++c) {
+      float2 zz = __ldg(a.spec + ((long long)(b * a.C + c) * a.T + t) * a.nbins + f);
       float mr = 0.f, mi = 0.f;
-      for (int k = k0; k < k1; ++k) {
-        const int col = __ldg(a.contrib_col + k) + 2 * c;
-        mr += s_mask[col];
-        mi += s_mask[col + 1];
+      if (pk.x == -2) {
+        for (int k = k0; k < k1; ++k) {
+          const int col = __ldg(a.contrib_col + k) + 2 * c;
+          mr += s_mask[col];
+          mi += s_mask[col + 1];
+        }
+      } else {
+        if (pk.x >= 0) {
+          mr += s_mask[pk.x + 2 * c];
+          mi += s_mask[pk.x + 2 * c + 1];
+        }
+        if (pk.y >= 0) {
+          mr += s_mask[pk.y + 2 * c];
+          mi += s_mask[pk.y + 2 * c + 1];
+        }
       }
       mr = mr / den;
       mi = mi / den;
-      float2 z = __ldg(a.spec + ((long long)(b * a.C + c) * a.T + t) * a.nbins + f);
-      z.x *= a.spec_scale;
-      z.y *= a.spec_scale;
-      float2 o = make_float2((z.x * mr - z.y * mi) * a.out_scale, (z.x * mi + z.y * mr) * a.out_scale);
+      zz.x *= a.spec_scale;
+      zz.y *= a.spec_scale;
+      float2 o = make_float2((zz.x * mr - zz.y * mi) * a.out_scale, (zz.x * mi + zz.y * mr) * a.out_scale);
       if (a.zero_dc && f == 0) o = make_float2(0.f, 0.f);
       a.out[((((long long)b * a.S + st) * a.C + c) * a.T + t) * a.nbins + f] = o;
     }
@@ -532,31 +579,28 @@ __global__ void __launch_bounds__(256) mask_apply_kernel(MaskApplyArgs a) {
 }
 
 // ------------------------------------------------------------------ STFT / iSTFT
-// One block per frame (bc, t): 4 consecutive samples per thread, window and
-// frame written as float4 (n_fft % 4 == 0); the reflect padding only at the
-// track's two ends.
+// One block per frame (bc, t); thread i handles samples i + 256u (every warp access
+// is 32 consecutive floats); the reflect padding only at the track's two ends.
 __global__ void __launch_bounds__(256)
     stft_frames_kernel(const float* __restrict__ audio, long long L, int T, int n_fft, int hop,
                        const float* __restrict__ win, float* __restrict__ frames) {
   const long long row = blockIdx.x;  // bc * T + t
   const int t = (int)(row % T);
   const float* src = audio + (row / T) * L;
-  float4* dst = reinterpret_cast<float4*>(frames + row * n_fft);
+  float* dst = frames + row * n_fft;
   const long long base = (long long)t * hop - n_fft / 2;
-  const bool inside = base >= 0 && base + n_fft <= L;
-  for (int n = 4 * threadIdx.x; n < n_fft; n += 4 * blockDim.x) {
-    const float4 w = __ldg(reinterpret_cast<const float4*>(win + n));
-    float v[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const long long i = base + n + u;
-      v[u] = __ldg(src + (inside ? i : reflect_idx(i, L)));
-    }
-    dst[n >> 2] = make_float4(v[0] * w.x, v[1] * w.y, v[2] * w.z, v[3] * w.w);
+  if (base >= 0 && base + n_fft <= L) {
+    const float* s0 = src + base;
+#pragma unroll 8
+    for (int n = threadIdx.x; n < n_fft; n += blockDim.x) dst[n] = __ldg(s0 + n) * __ldg(win + n);
+  } else {
+    for (int n = threadIdx.x; n < n_fft; n += blockDim.x) dst[n] = __ldg(src + reflect_idx(base + n, L)) * __ldg(win + n);
   }
 }
 
-// One block per (row, 1024 output samples); thread t handles samples t + 256u.
+// One block per (row, 1024 output samples); thread t handles samples t + 256u.  A
+// sample gathers at most kMaxFrames frames; their loads are issued together.
+constexpr int kIstftMaxFrames = 8;  // ceil(n_fft / hop) <= 8 (checked by the launcher)
 __global__ void __launch_bounds__(256)
     istft_ola_kernel(const float* __restrict__ frames, int T, int n_fft, int hop, const float* __restrict__ win,
                      const float* __restrict__ wsum, float* __restrict__ out, int Lout, int ref_compat) {
@@ -565,7 +609,7 @@ __global__ void __launch_bounds__(256)
   const int pad = n_fft / 2;
   const float inv_n = 1.0f / (float)n_fft;
   const int row0 = blockIdx.y;
-#pragma unroll
+#pragma unroll 1
   for (int u = 0; u < 4; ++u) {
     const int j = blockIdx.x * 1024 + u * 256 + threadIdx.x;
     if (j >= Lout) break;
@@ -584,11 +628,18 @@ __global__ void __launch_bounds__(256)
     const int t_lo = p >= n_fft ? (p - n_fft) / hop + 1 : 0;
     const int t_hi = min(T - 1, p / hop);
     const float* fr = frames + row * T * (long long)n_fft;
-    float acc = 0.f;
-    for (int t = t_lo; t <= t_hi; ++t) {
-      const int n = p - t * hop;
-      acc += (__ldg(fr + (long long)t * n_fft + n) * inv_n) * __ldg(win + n);
+    float v[kIstftMaxFrames], w[kIstftMaxFrames];
+#pragma unroll
+    for (int i = 0; i < kIstftMaxFrames; ++i) {
+      const int tt = t_lo + i, n = p - tt * hop;
+      const bool on = tt <= t_hi;
+      v[i] = on ? __ldg(fr + (long long)tt * n_fft + n) : 0.f;
+      w[i] = on ? __ldg(win + n) : 0.f;
     }
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < kIstftMaxFrames; ++i)
+      if (t_lo + i <= t_hi) acc += (v[i] * inv_n) * w[i];
     const float ws = __ldg(wsum + p);
     *o = ws > 1e-8f ? acc / ws : acc;
   }
@@ -619,6 +670,15 @@ __global__ void __launch_bounds__(256) chunk_gather_kernel(ChunkArgs a, int firs
   const int start = k * a.step;
   const int n = min(start + a.chunk, (int)a.total) - start;
   float* row = batch + (long long)kc * a.chunk;
+  const int j0 = blockIdx.x * 1024;
+  const int src0 = start + j0 - (int)a.border;
+  if (n >= a.chunk && j0 + 1024 <= a.chunk && src0 >= 0 && src0 + 1024 <= (int)a.L) {
+    // interior block: a plain copy of 1024 track samples
+    const float* s = a.track + (long long)c * a.L + src0;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) row[j0 + u * 256 + threadIdx.x] = __ldg(s + u * 256 + threadIdx.x);
+    return;
+  }
 #pragma unroll
   for (int u = 0; u < 4; ++u) {
     const int j = blockIdx.x * 1024 + u * 256 + threadIdx.x;
@@ -673,6 +733,7 @@ __global__ void __launch_bounds__(256) stitch_kernel(StitchArgs a) {
     const int k_hi = min(a.num_chunks - 1, q / a.step);
     const int k_lo = q >= a.chunk ? (q - a.chunk) / a.step + 1 : 0;
     float acc = 0.f, wsum = 0.f;
+#pragma unroll 2
     for (int k = k_lo; k <= k_hi; ++k) {
       const int start = k * a.step;
       const int j = q - start;
@@ -730,7 +791,7 @@ cudaError_t launch_layernorm(const LayerNormArgs& a, cudaStream_t s) {
 cudaError_t launch_band_input(const BandInArgs& a, int bf16, cudaStream_t s) {
   const long long rows = (long long)a.Bc * a.T;
   if (rows < 1) return cudaSuccess;
-  if (rows > 0x7fffffffLL || (a.ld & 1) || a.C < 1 || a.C > 2) return cudaErrorInvalidValue;
+  if (rows > 0x7fffffffLL || (a.ld & 1) || a.C < 1) return cudaErrorInvalidValue;
   const size_t smem = sizeof(float2) * (size_t)a.C * a.nbins;
   // the STFT read once, the packed A operand written once
   LaunchScope scope("band_input", 0.0, (double)a.Bc * a.C * a.T * a.nbins * 8.0 + (double)rows * a.ld * 2.0, s);
@@ -769,7 +830,7 @@ cudaError_t launch_stft_frames(const float* audio, long long L, int BC, int T, i
 
 cudaError_t launch_istft_ola(const float* frames, int BSC, int T, int n_fft, int hop, const float* win,
                              const float* wsum, float* out, long long out_len, int ref_compat, cudaStream_t s) {
-  if (out_len < (long long)(T - 1) * hop) return cudaErrorInvalidValue;
+  if (out_len < (long long)(T - 1) * hop || (n_fft + hop - 1) / hop > kIstftMaxFrames) return cudaErrorInvalidValue;
   if (out_len + n_fft >= (1LL << 31) || BSC > 65535) return cudaErrorInvalidValue;
   if (out_len == (long long)(T - 1) * hop) ref_compat = 0;  // nothing padded: the rows are plain
   LaunchScope scope("istft_ola", 0.0, (double)BSC * T * n_fft * 4.0 + (double)BSC * (double)out_len * 4.0, s);

@@ -94,6 +94,10 @@ struct MaskApplyArgs {
   float spec_scale;        // out = ((spec * spec_scale) x mask) * out_scale: the normalized
   float out_scale;         // STFT of stft_normalized models and the iSTFT's undoing of it
                            // (src/ops_stft.cu:358-365,380-389); 1 and 1 otherwise
+  // optional [nbins] per-bin summary of the tables above, for bins with at most
+  // two contributions: {col0, col1 or -1, 0, denom bits}; x = -2 marks a bin that
+  // takes the general path.  nullptr: the general path everywhere.
+  const int4* bin_pack;
 };
 cudaError_t launch_mask_apply(const MaskApplyArgs& a, cudaStream_t s);
 

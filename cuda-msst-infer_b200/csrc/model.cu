@@ -496,6 +496,19 @@ void Model::load(const std::string& path, int device, int precision) {
   d_contrib_off_ = upload_i32(coff);
   d_contrib_col_ = upload_i32(ccol);
   d_denom_ = upload_f32(denom);
+  {
+    // per-bin summary for the mask merge: the (at most two) contributions and the count
+    std::vector<int> pack(4 * (size_t)nbins_);
+    for (int f = 0; f < nbins_; ++f) {
+      const int n = coff[f + 1] - coff[f];
+      int* e = pack.data() + 4 * (size_t)f;
+      e[0] = n <= 2 ? (n >= 1 ? ccol[coff[f]] : -1) : -2;
+      e[1] = n == 2 ? ccol[coff[f] + 1] : -1;
+      e[2] = 0;
+      std::memcpy(&e[3], &denom[f], 4);
+    }
+    d_bin_pack_ = upload_i32(pack);
+  }
 
   // ---- window (periodic Hann, src/ops_stft.cu:253-259)
   {
@@ -1078,6 +1091,7 @@ void Model::forward_impl(const float* audio, int B, int C, long long L, float* o
   ma.contrib_off = d_contrib_off_.get<int>();
   ma.contrib_col = d_contrib_col_.get<int>();
   ma.denom = d_denom_.get<float>();
+  ma.bin_pack = d_bin_pack_.get<int4>();
   ma.out = w.ispec.get<float2>();
   ma.Bc = B;
   ma.S = I.num_stems;

@@ -118,7 +118,7 @@ class Model {
   std::vector<int> nfreq_, bin_start_, bin_list_, dims_, kpad_, kcol_, dim_off_, out3_off_;
   int ktot_ = 0, sum_dims_ = 0, sum_out3_ = 0;
   DeviceBuffer d_nfreq_, d_bin_start_, d_bin_list_, d_kpad_, d_kcol_, d_gcol_;
-  DeviceBuffer d_contrib_off_, d_contrib_col_, d_denom_;
+  DeviceBuffer d_contrib_off_, d_contrib_col_, d_denom_, d_bin_pack_;
 
   DeviceBuffer w_bs_, b_bs_, g_bs_;
   CUtensorMap m_wbs_;
