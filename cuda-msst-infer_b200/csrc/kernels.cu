@@ -467,14 +467,40 @@ __global__ void __launch_bounds__(256) band_input_kernel(BandInArgs a) {
     const int nf = __ldg(a.nfreq + band);
     const int dims = 2 * C * nf;
     const int* bins = a.bin_list + __ldg(a.bin_start + band);
-    const int first = __ldg(bins);
-    bool run = true;
-    for (int q = lane; q < nf; q += 32) run = run && __ldg(bins + q) == first + q;
-    run = __all_sync(0xffffffffu, run);
+    int first;
+    if (a.run_first) {
+      first = __ldg(a.run_first + band);
+    } else {
+      first = __ldg(bins);
+      bool run = true;
+      for (int q = lane; q < nf; q += 32) run = run && __ldg(bins + q) == first + q;
+      if (!__all_sync(0xffffffffu, run)) first = -1;
+    }
     const float* g = a.gamma + __ldg(a.gcol + band);
     T* o = orow + __ldg(a.kcol + band);
     const int kp = __ldg(a.kpad + band);
-    if (run) {
+    if (first >= 0 && C == 2 && (reinterpret_cast<uintptr_t>(g) & 15) == 0) {
+      // stereo: 4 values per bin, so the band's span and gamma are float4-aligned
+      const float4* v4 = reinterpret_cast<const float4*>(s_row + 4 * first);
+      const float4* g4 = reinterpret_cast<const float4*>(g);
+      float ss = 0.f;
+      for (int i = lane; 4 * i < dims; i += 32) {
+        const float4 v = v4[i];
+        ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+      }
+      ss = warp_sum(ss);
+      const float inv = rsqrtf(ss + 1e-12f);
+      const float scale = sqrtf((float)dims);
+      for (int i = lane; 4 * i < kp; i += 32) {
+        uint2 pk = make_uint2(0u, 0u);
+        if (4 * i < dims) {
+          const float4 v = v4[i], gg = __ldg(g4 + i);
+          pk = make_uint2(pack2<T>(v.x * inv * gg.x * scale, v.y * inv * gg.y * scale),
+                          pack2<T>(v.z * inv * gg.z * scale, v.w * inv * gg.w * scale));
+        }
+        reinterpret_cast<uint2*>(o)[i] = pk;
+      }
+    } else if (first >= 0) {
       const float2* v2 = reinterpret_cast<const float2*>(s_row + 2 * C * first);
       float ss = 0.f;
       for (int i = lane; 2 * i < dims; i += 32) {
@@ -599,8 +625,9 @@ __global__ void __launch_bounds__(256)
 }
 
 // One block per (row, 1024 output samples); thread t handles samples t + 256u.  A
-// sample gathers at most kMaxFrames frames; their loads are issued together.
-constexpr int kIstftMaxFrames = 8;  // ceil(n_fft / hop) <= 8 (checked by the launcher)
+// sample gathers at most kMaxF = ceil(n_fft / hop) frames; their loads are issued
+// together.
+template <int kMaxF>
 __global__ void __launch_bounds__(256)
     istft_ola_kernel(const float* __restrict__ frames, int T, int n_fft, int hop, const float* __restrict__ win,
                      const float* __restrict__ wsum, float* __restrict__ out, int Lout, int ref_compat) {
@@ -627,18 +654,18 @@ __global__ void __launch_bounds__(256)
     }
     const int t_lo = p >= n_fft ? (p - n_fft) / hop + 1 : 0;
     const int t_hi = min(T - 1, p / hop);
-    const float* fr = frames + row * T * (long long)n_fft;
-    float v[kIstftMaxFrames], w[kIstftMaxFrames];
+    const float* fr = frames + row * T * (long long)n_fft + (long long)t_lo * n_fft + (p - t_lo * hop);
+    float v[kMaxF], w[kMaxF];
 #pragma unroll
-    for (int i = 0; i < kIstftMaxFrames; ++i) {
-      const int tt = t_lo + i, n = p - tt * hop;
-      const bool on = tt <= t_hi;
-      v[i] = on ? __ldg(fr + (long long)tt * n_fft + n) : 0.f;
+    for (int i = 0; i < kMaxF; ++i) {
+      const bool on = t_lo + i <= t_hi;
+      const int n = p - (t_lo + i) * hop;
+      v[i] = on ? __ldg(fr + i * (n_fft - hop)) : 0.f;
       w[i] = on ? __ldg(win + n) : 0.f;
     }
     float acc = 0.f;
 #pragma unroll
-    for (int i = 0; i < kIstftMaxFrames; ++i)
+    for (int i = 0; i < kMaxF; ++i)
       if (t_lo + i <= t_hi) acc += (v[i] * inv_n) * w[i];
     const float ws = __ldg(wsum + p);
     *o = ws > 1e-8f ? acc / ws : acc;
@@ -646,7 +673,7 @@ __global__ void __launch_bounds__(256)
 }
 
 // ------------------------------------------------------------------ chunking
-// Both kernels map a block to 1024 consecutive samples of one row; thread t handles
+// The stitch maps a block to 1024 consecutive samples of one row; thread t handles
 // samples t, t + 256, t + 512 and t + 768, so every warp access is 32 consecutive
 // floats.  Sample positions fit in 32 bits (the launchers check).
 __device__ __forceinline__ int reflect32(int i, int n) {
@@ -663,44 +690,49 @@ __device__ __forceinline__ float padded_track(const ChunkArgs& a, int c, int p) 
   return __ldg(a.track + (long long)c * a.L + src);
 }
 
-__global__ void __launch_bounds__(256) chunk_gather_kernel(ChunkArgs a, int first, int stride, float* batch) {
-  const int kc = blockIdx.y;  // (chunk in batch) * C + channel
-  const int c = kc % a.C;
-  const int k = first + (kc / a.C) * stride;
+// Sample j of chunk k, channel c (j < chunk): the padded track, or for the final
+// short chunk its reflect / zero padding (src/inference_app.cpp:144-150).
+__device__ __forceinline__ float chunk_sample(const ChunkArgs& a, int k, int c, int j) {
   const int start = k * a.step;
   const int n = min(start + a.chunk, (int)a.total) - start;
-  float* row = batch + (long long)kc * a.chunk;
-  const int j0 = blockIdx.x * 1024;
-  const int src0 = start + j0 - (int)a.border;
-  if (n >= a.chunk && j0 + 1024 <= a.chunk && src0 >= 0 && src0 + 1024 <= (int)a.L) {
-    // interior block: a plain copy of 1024 track samples
-    const float* s = a.track + (long long)c * a.L + src0;
-#pragma unroll
-    for (int u = 0; u < 4; ++u) row[j0 + u * 256 + threadIdx.x] = __ldg(s + u * 256 + threadIdx.x);
-    return;
+  if (n >= a.chunk) return padded_track(a, c, start + j);
+  const bool reflect = n > a.chunk / 2;
+  int sj = j < n ? j : 2 * (n - 1) - j;
+  sj = sj < 0 ? 0 : (sj >= n ? n - 1 : sj);
+  if (!reflect && j >= n) return 0.f;
+  if (a.ref_compat) {
+    const long long flat = (long long)start + (long long)c * n + sj;  // contiguous view of a strided slice
+    return padded_track(a, (int)(flat / a.total), (int)(flat % a.total));
   }
-#pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    const int j = blockIdx.x * 1024 + u * 256 + threadIdx.x;
-    if (j >= a.chunk) break;
-    float v;
-    if (n >= a.chunk) {
-      v = padded_track(a, c, start + j);
-    } else {
-      // src/inference_app.cpp:144-150: reflect if more than half a chunk remains, else zeros
-      const bool reflect = n > a.chunk / 2;
-      int sj = j < n ? j : 2 * (n - 1) - j;
-      sj = sj < 0 ? 0 : (sj >= n ? n - 1 : sj);
-      if (!reflect && j >= n) {
-        v = 0.f;
-      } else if (a.ref_compat) {
-        const long long flat = (long long)start + (long long)c * n + sj;  // contiguous view of a strided slice
-        v = padded_track(a, (int)(flat / a.total), (int)(flat % a.total));
-      } else {
-        v = padded_track(a, c, start + sj);
-      }
+  return padded_track(a, c, start + sj);
+}
+
+// Frames of chunk first + (row / (C*T)) * stride, channel (row / T) % C, frame row % T
+// (torch.stft center=True reflect padding inside the chunk), read straight from the
+// track; interior frames of interior chunks are plain copies of track samples.
+__global__ void __launch_bounds__(256)
+    stft_frames_chunk_kernel(ChunkArgs a, int first, int stride, int T, int n_fft, int hop,
+                             const float* __restrict__ win, float* __restrict__ frames) {
+  const int row = blockIdx.x;  // (kk * C + c) * T + t
+  const int t = row % T;
+  const int c = (row / T) % a.C;
+  const int k = first + (row / (T * a.C)) * stride;
+  float* dst = frames + (long long)row * n_fft;
+  const int base = t * hop - n_fft / 2;  // chunk sample of frame sample 0
+  const int start = k * a.step;
+  const bool whole = start + a.chunk <= (int)a.total;
+  const int src0 = start + base - (int)a.border;
+  if (whole && base >= 0 && base + n_fft <= a.chunk && src0 >= 0 && src0 + n_fft <= (int)a.L) {
+    const float* s0 = a.track + (long long)c * a.L + src0;
+#pragma unroll 8
+    for (int n = threadIdx.x; n < n_fft; n += blockDim.x) dst[n] = __ldg(s0 + n) * __ldg(win + n);
+  } else {
+    for (int n = threadIdx.x; n < n_fft; n += blockDim.x) {
+      int i = base + n;
+      i = i < 0 ? -i : (i >= a.chunk ? 2 * (a.chunk - 1) - i : i);
+      i = i < 0 ? 0 : (i >= a.chunk ? a.chunk - 1 : i);
+      dst[n] = chunk_sample(a, k, c, i) * __ldg(win + n);
     }
-    row[j] = v;
   }
 }
 
@@ -830,12 +862,41 @@ cudaError_t launch_stft_frames(const float* audio, long long L, int BC, int T, i
 
 cudaError_t launch_istft_ola(const float* frames, int BSC, int T, int n_fft, int hop, const float* win,
                              const float* wsum, float* out, long long out_len, int ref_compat, cudaStream_t s) {
-  if (out_len < (long long)(T - 1) * hop || (n_fft + hop - 1) / hop > kIstftMaxFrames) return cudaErrorInvalidValue;
+  const int maxf = (n_fft + hop - 1) / hop;
+  if (out_len < (long long)(T - 1) * hop || maxf > 8) return cudaErrorInvalidValue;
   if (out_len + n_fft >= (1LL << 31) || BSC > 65535) return cudaErrorInvalidValue;
   if (out_len == (long long)(T - 1) * hop) ref_compat = 0;  // nothing padded: the rows are plain
   LaunchScope scope("istft_ola", 0.0, (double)BSC * T * n_fft * 4.0 + (double)BSC * (double)out_len * 4.0, s);
-  istft_ola_kernel<<<dim3((unsigned)((out_len + 1023) / 1024), (unsigned)BSC), 256, 0, s>>>(
-      frames, T, n_fft, hop, win, wsum, out, (int)out_len, ref_compat);
+  const dim3 grid((unsigned)((out_len + 1023) / 1024), (unsigned)BSC);
+  switch (maxf) {
+#define MSST_ISTFT_CASE(f)                                                                             \
+  case f:                                                                                              \
+    istft_ola_kernel<f><<<grid, 256, 0, s>>>(frames, T, n_fft, hop, win, wsum, out, (int)out_len, ref_compat); \
+    break;
+    MSST_ISTFT_CASE(1)
+    MSST_ISTFT_CASE(2)
+    MSST_ISTFT_CASE(3)
+    MSST_ISTFT_CASE(4)
+    MSST_ISTFT_CASE(5)
+    MSST_ISTFT_CASE(6)
+    MSST_ISTFT_CASE(7)
+    MSST_ISTFT_CASE(8)
+#undef MSST_ISTFT_CASE
+    default:
+      return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_stft_frames_chunks(const ChunkArgs& a, int first, int stride, int count, int T, int n_fft,
+                                      int hop, const float* win, float* frames, cudaStream_t s) {
+  if (count <= 0) return cudaSuccess;
+  if (a.total + a.chunk >= (1LL << 31) || (long long)count * a.C * T > 0x7fffffffLL || stride < 1)
+    return cudaErrorInvalidValue;
+  // the chunk samples read once (frames overlap in L1/L2), the frames written once
+  LaunchScope scope("stft_frames", 0.0,
+                    (double)count * a.C * a.chunk * 4.0 + (double)count * a.C * T * n_fft * 4.0, s);
+  stft_frames_chunk_kernel<<<(unsigned)(count * a.C * T), 256, 0, s>>>(a, first, stride, T, n_fft, hop, win, frames);
   return cudaGetLastError();
 }
 
@@ -846,15 +907,6 @@ cudaError_t launch_skip_add(float* x, const float* skips, int count, long long n
   LaunchScope scope("skip_add", 0.0, (double)n * 4.0 * (count + 2), s);
   skip_add_kernel<<<grid_for(n / 4), 256, 0, s>>>(reinterpret_cast<float4*>(x),
                                                   reinterpret_cast<const float4*>(skips), count, n / 4);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_chunk_gather(const ChunkArgs& a, int first, int stride, int count, float* batch, cudaStream_t s) {
-  if (count <= 0) return cudaSuccess;
-  if (a.total + a.chunk >= (1LL << 31) || (long long)count * a.C > 65535 || stride < 1) return cudaErrorInvalidValue;
-  LaunchScope scope("chunk_gather", 0.0, 2.0 * count * a.C * (double)a.chunk * 4.0, s);
-  chunk_gather_kernel<<<dim3((unsigned)((a.chunk + 1023) / 1024), (unsigned)(count * a.C)), 256, 0, s>>>(a, first,
-                                                                                                      stride, batch);
   return cudaGetLastError();
 }
 

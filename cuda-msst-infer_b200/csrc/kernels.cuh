@@ -70,6 +70,8 @@ struct BandInArgs {
   const float* gamma;     // concatenated band gammas
   void* out;              // [Bc*T, ld] 16-bit
   long long ld;
+  const int* run_first;   // optional [num_bands]: the band's first bin when its bins are an
+                          // ascending run (first, first+1, ...), else -1; nullptr: checked here
   float spec_scale;       // the STFT values are multiplied by this first (1, or
                           // 1/sqrt(n_fft) for stft_normalized models, src/ops_stft.cu:358-365)
 };
@@ -128,11 +130,11 @@ cudaError_t launch_istft_ola(const float* frames, int BSC, int T, int n_fft, int
 cudaError_t launch_skip_add(float* x, const float* skips, int count, long long n, cudaStream_t s);
 
 // Chunked inference helpers (src/inference_app.cpp:100-324).
-// Gather `count` chunks, indices first, first + stride, ..., of the reflect-padded
-// track into batch [count, C, chunk].  The padded track is never materialised:
-// padded index p maps to track index reflect(p - border).  The final, short
-// chunk is padded to `chunk` samples; ref_compat reproduces the reference's
-// contiguous-source indexing of that strided slice.
+// Chunks k of the reflect-padded track: chunk k is padded samples [k*step, k*step +
+// chunk).  The padded track is never materialised: padded index p maps to track
+// index reflect(p - border).  The final, short chunk is padded to `chunk` samples;
+// ref_compat reproduces the reference's contiguous-source indexing of that
+// strided slice.
 struct ChunkArgs {
   const float* track;      // [C, L] on device
   int C;
@@ -143,7 +145,12 @@ struct ChunkArgs {
   int step;
   int ref_compat;
 };
-cudaError_t launch_chunk_gather(const ChunkArgs& a, int first, int stride, int count, float* batch, cudaStream_t s);
+
+// STFT framing of chunks first, first + stride, ... (count of them) straight from
+// the track: launch_stft_frames over the batch [count, C, chunk] of those chunks,
+// without building it (frames [count*C*T, n_fft]).
+cudaError_t launch_stft_frames_chunks(const ChunkArgs& a, int first, int stride, int count, int T, int n_fft,
+                                      int hop, const float* win, float* frames, cudaStream_t s);
 
 // Windowed overlap-add stitch of chunk outputs, as a gather over the output
 // (src/inference_app.cpp:252-306, src/ops_fused.cu:138-188): for every output

@@ -331,7 +331,7 @@ static DeviceBuffer upload_16(const std::vector<float>& v, int bf16) {
 struct Model::Work {
   int B = 0, T = 0;
   long long M = 0, BT = 0;
-  DeviceBuffer frames, spec, ispec, abs, x, xn, gates, big1, big2, ao, mask, chunk_in;
+  DeviceBuffer frames, spec, ispec, abs, x, xn, gates, big1, big2, ao, mask;
   DeviceBuffer skips;  // skip_connection models: the outputs of depth blocks 0..depth-2
   CUtensorMap m_abs, m_xn, m_ao, m_big1_ffh, m_big2_ffh, m_qkv_time, m_qkv_band, m_h1, m_h2;
   // GEMM output maps (TMA stores)
@@ -493,6 +493,17 @@ void Model::load(const std::string& path, int device, int precision) {
   d_kpad_ = upload_i32(kpad_);
   d_kcol_ = upload_i32(kcol_);
   d_gcol_ = upload_i32(dim_off_);
+  {
+    // bands whose bins are an ascending run are contiguous spans of a staged STFT row
+    std::vector<int> rf(nb, -1);
+    for (int b = 0; b < nb; ++b) {
+      const int* bl = bin_list_.data() + bin_start_[b];
+      bool run = true;
+      for (int q = 1; q < nfreq_[b]; ++q) run = run && bl[q] == bl[0] + q;
+      if (run && nfreq_[b] > 0) rf[b] = bl[0];
+    }
+    d_run_first_ = upload_i32(rf);
+  }
   d_contrib_off_ = upload_i32(coff);
   d_contrib_col_ = upload_i32(ccol);
   d_denom_ = upload_f32(denom);
@@ -806,11 +817,17 @@ Model::Work& Model::work(int B, int T) {
 // ===========================================================================
 // forward pieces
 // ===========================================================================
-void Model::run_front(const float* audio, int B, long long L, int T, cudaStream_t s, Work& w) {
+void Model::run_front(const float* audio, const ChunkSource& src, int B, long long L, int T, cudaStream_t s,
+                      Work& w) {
   const msst_model_info& I = info_;
-  // STFT (src/ops_stft.cu:286-365) -> [B*C*T, nbins] complex
-  MSST_CUDA(launch_stft_frames(audio, L, B * C_, T, I.n_fft, I.hop_length, window_.get<float>(), w.frames.get<float>(),
-                               s));
+  // STFT (src/ops_stft.cu:286-365) -> [B*C*T, nbins] complex; chunks are framed straight
+  // from the track (the gathered chunk batch is never written)
+  if (src.chunks)
+    MSST_CUDA(launch_stft_frames_chunks(*src.chunks, src.first, src.stride, B, T, I.n_fft, I.hop_length,
+                                        window_.get<float>(), w.frames.get<float>(), s));
+  else
+    MSST_CUDA(launch_stft_frames(audio, L, B * C_, T, I.n_fft, I.hop_length, window_.get<float>(),
+                                 w.frames.get<float>(), s));
   if (cufftExecR2C(fft_plan(CUFFT_R2C, B * C_ * T, s), w.frames.get<cufftReal>(), w.spec.get<cufftComplex>()) !=
       CUFFT_SUCCESS)
     fail(MSST_ERR_CUDA, "cufftExecR2C failed");
@@ -832,6 +849,7 @@ void Model::run_front(const float* audio, int B, long long L, int T, cudaStream_
   bi.out = w.abs.get();
   bi.ld = ktot_;
   bi.spec_scale = stft_norm_ ? 1.0f / std::sqrt((float)I.n_fft) : 1.0f;
+  bi.run_first = d_run_first_.get<int>();
   MSST_CUDA(launch_band_input(bi, bf16_, s));
   // band split: one group per band, output rows (bt*nb + band) of the residual stream
   GemmParams p{};
@@ -1073,13 +1091,13 @@ void Model::forward(const float* audio, int B, int C, long long L, float* out, c
 }
 
 void Model::forward_impl(const float* audio, int B, int C, long long L, float* out, bool fix_padding,
-                         cudaStream_t s) {
+                         cudaStream_t s, const ChunkSource& src) {
   const msst_model_info& I = info_;
   MSST_REQUIRE(C == C_, "channel count does not match the model (stereo=" + std::to_string(C_ == 2) + ")");
   MSST_REQUIRE(B >= 1 && L > I.n_fft / 2, "audio too short");
   const int T = (int)(L / I.hop_length + 1);
   Work& w = work(B, T);
-  run_front(audio, B, L, T, s, w);
+  run_front(audio, src, B, L, T, s, w);
   run_trunk(B, T, s, w);
   run_masks(B, T, s, w, w.mask.get<float>());
   // mask merge + complex multiply + zero DC -> C2R input
@@ -1123,7 +1141,7 @@ void Model::masks(const float* audio, int B, int C, long long L, float* masks_ou
   MSST_REQUIRE(C == C_, "channel count does not match the model");
   const int T = (int)(L / I.hop_length + 1);
   Work& w = work(B, T);
-  run_front(audio, B, L, T, s, w);
+  run_front(audio, ChunkSource(), B, L, T, s, w);
   run_trunk(B, T, s, w);
   run_masks(B, T, s, w, masks_out);
 }
@@ -1319,9 +1337,6 @@ void Model::separate_pipeline(const float* track, const float* track_host, int C
   ci.chunk = chunk;
   ci.step = step;
   ci.ref_compat = (flags & MSST_SEPARATE_FIX_TAIL_PADDING) ? 0 : 1;
-  const int T = chunk / I.hop_length + 1;
-  Work& w = work(eb, T);
-  w.chunk_in.ensure(sizeof(float) * (size_t)eb * C * chunk);
   const size_t per_chunk = (size_t)S * C * chunk;
   sep_chunks_.ensure(sizeof(float) * per_chunk * nchunks);
   float* ys = sep_chunks_.get<float>();
@@ -1350,8 +1365,12 @@ void Model::separate_pipeline(const float* track, const float* track_host, int C
   for (int b = 0; b < nbatch; ++b) {
     const int g0 = b * eb, cnt = std::min(eb, nchunks - g0);
     if (track_host) MSST_CUDA(cudaStreamWaitEvent(s, pipeline_event(1 + b), 0));
-    MSST_CUDA(launch_chunk_gather(ci, g0, 1, cnt, w.chunk_in.get<float>(), s));
-    forward(w.chunk_in.get<float>(), cnt, C, chunk, ys + (size_t)g0 * per_chunk, s);
+    ChunkSource src;
+    src.chunks = &ci;
+    src.first = g0;
+    forward_impl(nullptr, cnt, C, chunk, ys + (size_t)g0 * per_chunk, false, s, src);
+    // without host output, one stitch at the end (a single large launch)
+    if (!out_host && g0 + cnt < nchunks) continue;
     long long upto = L;
     if (g0 + cnt < nchunks) {
       long long in[4], olo, ohi;
@@ -1408,14 +1427,14 @@ void Model::forward_chunks(const float* track, int C, long long L, float overlap
   ci.chunk = chunk;
   ci.step = step;
   ci.ref_compat = (flags & MSST_SEPARATE_FIX_TAIL_PADDING) ? 0 : 1;
-  const int T = chunk / I.hop_length + 1;
-  Work& w = work(eb, T);
-  w.chunk_in.ensure(sizeof(float) * (size_t)eb * C * chunk);
   const size_t per_chunk = (size_t)S * C * chunk;
   for (int i0 = 0; i0 < count; i0 += eb) {
     const int cnt = std::min(eb, count - i0);
-    MSST_CUDA(launch_chunk_gather(ci, first + i0 * stride, stride, cnt, w.chunk_in.get<float>(), s));
-    forward(w.chunk_in.get<float>(), cnt, C, chunk, out + (size_t)i0 * per_chunk, s);
+    ChunkSource src;
+    src.chunks = &ci;
+    src.first = first + i0 * stride;
+    src.stride = stride;
+    forward_impl(nullptr, cnt, C, chunk, out + (size_t)i0 * per_chunk, false, s, src);
   }
 }
 

@@ -15,6 +15,7 @@
 #include <vector>
 
 #include "gemm.cuh"
+#include "kernels.cuh"
 #include "runtime.h"
 
 namespace msst {
@@ -37,6 +38,13 @@ struct TransformerWeights {
 struct StemWeights {
   std::vector<DeviceBuffer> w, b;  // per MLP layer, all bands concatenated along rows
   std::vector<CUtensorMap> m;
+};
+
+// The forward's input: audio [B, C, L], or (chunks != nullptr) chunks first,
+// first + stride, ... of a track read in place (L = chunk size).
+struct ChunkSource {
+  const ChunkArgs* chunks = nullptr;
+  int first = 0, stride = 1;
 };
 
 class Model {
@@ -87,9 +95,10 @@ class Model {
   struct Work;  // per-(B, T) workspace
   Work& work(int B, int T);
   void run_trunk(int B, int T, cudaStream_t s, Work& w);
-  void forward_impl(const float* audio, int B, int C, long long L, float* out, bool fix_padding, cudaStream_t s);
+  void forward_impl(const float* audio, int B, int C, long long L, float* out, bool fix_padding, cudaStream_t s,
+                    const ChunkSource& src = ChunkSource());
   void mel_bands_from_filterbank(std::vector<float>& denom);
-  void run_front(const float* audio, int B, long long L, int T, cudaStream_t s, Work& w);
+  void run_front(const float* audio, const ChunkSource& src, int B, long long L, int T, cudaStream_t s, Work& w);
   void run_masks(int B, int T, cudaStream_t s, Work& w, float* masks_out);
   void run_transformer(int d, int axis, float* x, int B, int T, const float* pending_gamma, cudaStream_t s, Work& w);
   void run_attn_block(int d, int axis, int l, float* x, int B, int T, const float* pending_gamma, cudaStream_t s,
@@ -117,7 +126,7 @@ class Model {
 
   std::vector<int> nfreq_, bin_start_, bin_list_, dims_, kpad_, kcol_, dim_off_, out3_off_;
   int ktot_ = 0, sum_dims_ = 0, sum_out3_ = 0;
-  DeviceBuffer d_nfreq_, d_bin_start_, d_bin_list_, d_kpad_, d_kcol_, d_gcol_;
+  DeviceBuffer d_nfreq_, d_bin_start_, d_bin_list_, d_kpad_, d_kcol_, d_gcol_, d_run_first_;
   DeviceBuffer d_contrib_off_, d_contrib_col_, d_denom_, d_bin_pack_;
 
   DeviceBuffer w_bs_, b_bs_, g_bs_;
