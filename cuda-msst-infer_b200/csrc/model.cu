@@ -8,6 +8,7 @@
 #include <algorithm>
 #include <chrono>
 #include <cmath>
+#include <thread>
 #include <cstring>
 #include <fstream>
 
@@ -291,20 +292,14 @@ static Csm read_csm(const std::string& path) {
 }
 
 // ===========================================================================
-// Upload helpers
+// Upload helpers.  During Model::load an Uploader stages every tensor through
+// two pinned host buffers: the values are converted (to the 16-bit operand type
+// where the kernels read 16-bit) by all host threads straight into one buffer
+// while the other is copied to the device with cudaMemcpyAsync, so conversion
+// and DMA overlap (the reference converts and uploads tensor by tensor from
+// pageable memory, src/weights.cu:412-524).  Outside load (tables built on first
+// use) the helpers copy synchronously.
 // ===========================================================================
-static DeviceBuffer upload_f32(const std::vector<float>& v) {
-  DeviceBuffer b(v.size() * 4);
-  if (!v.empty()) MSST_CUDA(cudaMemcpy(b.get(), v.data(), v.size() * 4, cudaMemcpyHostToDevice));
-  return b;
-}
-
-static DeviceBuffer upload_i32(const std::vector<int>& v) {
-  DeviceBuffer b(std::max<size_t>(v.size(), 1) * 4);
-  if (!v.empty()) MSST_CUDA(cudaMemcpy(b.get(), v.data(), v.size() * 4, cudaMemcpyHostToDevice));
-  return b;
-}
-
 static void to16(const float* src, size_t n, uint16_t* dst, int bf16) {
   for (size_t i = 0; i < n; ++i) {
     if (bf16) {
@@ -317,11 +312,102 @@ static void to16(const float* src, size_t n, uint16_t* dst, int bf16) {
   }
 }
 
+// fn(begin, end) over [0, n) on up to `threads` host threads (inline when small)
+template <typename F>
+static void parallel_range(size_t n, unsigned threads, F&& fn) {
+  if (n < (1u << 18) || threads <= 1) {
+    fn((size_t)0, n);
+    return;
+  }
+  std::vector<std::thread> pool;
+  const size_t per = (n + threads - 1) / threads;
+  for (unsigned t = 0; t < threads; ++t) {
+    const size_t b = t * per, e = std::min(n, b + per);
+    if (b >= e) break;
+    pool.emplace_back([&fn, b, e] { fn(b, e); });
+  }
+  for (auto& th : pool) th.join();
+}
+
+class Uploader {
+ public:
+  Uploader() {
+    threads_ = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+    MSST_CUDA(cudaStreamCreateWithFlags(&st_, cudaStreamNonBlocking));
+    for (int i = 0; i < 2; ++i) {
+      MSST_CUDA(cudaMallocHost(&buf_[i], kStage));
+      MSST_CUDA(cudaEventCreateWithFlags(&ev_[i], cudaEventDisableTiming));
+    }
+  }
+  ~Uploader() {
+    cudaStreamSynchronize(st_);
+    for (int i = 0; i < 2; ++i) {
+      if (buf_[i]) cudaFreeHost(buf_[i]);
+      if (ev_[i]) cudaEventDestroy(ev_[i]);
+    }
+    if (st_) cudaStreamDestroy(st_);
+  }
+  Uploader(const Uploader&) = delete;
+  Uploader& operator=(const Uploader&) = delete;
+
+  // copy `bytes` to dst; fill(staging, first element, element count) writes the
+  // values of elements [first, first + count) (esize bytes each) into staging
+  template <typename Fill>
+  void put(void* dst, size_t count, size_t esize, Fill&& fill) {
+    const size_t per = kStage / esize;
+    for (size_t off = 0; off < count; off += per) {
+      const size_t n = std::min(per, count - off);
+      MSST_CUDA(cudaEventSynchronize(ev_[cur_]));  // the DMA that last read this buffer is done
+      uint8_t* stg = buf_[cur_];
+      parallel_range(n, threads_, [&](size_t b, size_t e) { fill(stg + b * esize, off + b, e - b); });
+      MSST_CUDA(cudaMemcpyAsync(static_cast<uint8_t*>(dst) + off * esize, stg, n * esize, cudaMemcpyHostToDevice,
+                                st_));
+      MSST_CUDA(cudaEventRecord(ev_[cur_], st_));
+      cur_ ^= 1;
+    }
+  }
+  void finish() { MSST_CUDA(cudaStreamSynchronize(st_)); }
+
+ private:
+  static constexpr size_t kStage = 32ull << 20;
+  cudaStream_t st_ = nullptr;
+  uint8_t* buf_[2] = {nullptr, nullptr};
+  cudaEvent_t ev_[2] = {nullptr, nullptr};
+  int cur_ = 0;
+  unsigned threads_ = 1;
+};
+
+thread_local Uploader* t_uploader = nullptr;  // set while Model::load runs on this thread
+
+static DeviceBuffer upload_raw(const void* src, size_t count, size_t esize) {
+  DeviceBuffer b(std::max<size_t>(count, 1) * esize);
+  if (count == 0) return b;
+  if (t_uploader) {
+    const uint8_t* s8 = static_cast<const uint8_t*>(src);
+    t_uploader->put(b.get(), count, esize,
+                    [&](uint8_t* d, size_t first, size_t n) { std::memcpy(d, s8 + first * esize, n * esize); });
+  } else {
+    MSST_CUDA(cudaMemcpy(b.get(), src, count * esize, cudaMemcpyHostToDevice));
+  }
+  return b;
+}
+
+static DeviceBuffer upload_f32(const std::vector<float>& v) { return upload_raw(v.data(), v.size(), 4); }
+
+static DeviceBuffer upload_i32(const std::vector<int>& v) { return upload_raw(v.data(), v.size(), 4); }
+
 static DeviceBuffer upload_16(const std::vector<float>& v, int bf16) {
-  std::vector<uint16_t> h(v.size());
-  to16(v.data(), v.size(), h.data(), bf16);
-  DeviceBuffer b(h.size() * 2);
-  MSST_CUDA(cudaMemcpy(b.get(), h.data(), h.size() * 2, cudaMemcpyHostToDevice));
+  DeviceBuffer b(std::max<size_t>(v.size(), 1) * 2);
+  if (v.empty()) return b;
+  if (t_uploader) {
+    t_uploader->put(b.get(), v.size(), 2, [&](uint8_t* d, size_t first, size_t n) {
+      to16(v.data() + first, n, reinterpret_cast<uint16_t*>(d), bf16);
+    });
+  } else {
+    std::vector<uint16_t> h(v.size());
+    to16(v.data(), v.size(), h.data(), bf16);
+    MSST_CUDA(cudaMemcpy(b.get(), h.data(), h.size() * 2, cudaMemcpyHostToDevice));
+  }
   return b;
 }
 
@@ -358,6 +444,12 @@ void Model::load(const std::string& path, int device, int precision) {
   bf16_ = precision;
   Csm csm = read_csm(path);
   MSST_CUDA(cudaSetDevice(device));
+  Uploader uploader;
+  struct Scope {
+    Uploader* prev;
+    explicit Scope(Uploader* u) : prev(t_uploader) { t_uploader = u; }
+    ~Scope() { t_uploader = prev; }
+  } scope(&uploader);
   num_sms_ = device_sm_count();
   const Json& j = csm.config;
 
@@ -629,6 +721,7 @@ void Model::load(const std::string& path, int device, int precision) {
       sw.m.push_back(map_gemm_b(sw.w.back().get(), rows_total, K, K, 256));
     }
   }
+  uploader.finish();
   MSST_CUDA(cudaDeviceSynchronize());
   info_.load_ms =
       (float)std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t_load0).count();
