@@ -60,4 +60,28 @@ cudaError_t launch_attention(const CUtensorMap& qkv_map, const AttnParams& p, in
 cudaError_t launch_sdpa(const CUtensorMap& q_map, const CUtensorMap& k_map, const CUtensorMap& v_map,
                         const AttnParams& p, int bf16, int num_sms, cudaStream_t stream);
 
+// Band-axis attention block fused with its QKV projection (band_attn.cu):
+//   out[token, h*64 .. +64) = gate[token, h] * softmax_F(Q_h K_h^T / 8) V_h
+// with [Q_h K_h V_h] = xn . [Wq_h; Wk_h; Wv_h]^T and rotary (interleaved pairs,
+// position = the token's band index) on Q_h and K_h, for sequences of F <= 64
+// consecutive tokens (one per frame).  map_xn: xn [tokens, D] 16-bit, box {64,
+// attn_band_slot(F)}; map_w: W_qkv [3*inner, D] 16-bit, box {64, 64}; both 128B
+// swizzle.  D % 64 == 0, D <= 512, head_dim 64.
+struct BandAttnParams {
+  int num_seqs;            // B*T sequences
+  int F;                   // tokens per sequence (num_bands)
+  int slot;                // attn_band_slot(F)
+  int D;                   // model width (K of the projection)
+  int heads;               // H; inner = H*64
+  int inner;
+  float scale_log2;        // softmax scale * log2(e)
+  const float* rope_cos;   // [F, 32]
+  const float* rope_sin;   // [F, 32]
+  const float* gates;      // [tokens, H] (sigmoid applied) or nullptr
+  void* out;               // [tokens, out_ld] 16-bit
+  long long out_ld;
+};
+cudaError_t launch_band_attention_fused(const CUtensorMap& map_xn, const CUtensorMap& map_w, const BandAttnParams& p,
+                                        int bf16, int num_sms, cudaStream_t stream);
+
 }  // namespace msst

@@ -420,6 +420,7 @@ struct Model::Work {
   DeviceBuffer frames, spec, ispec, abs, x, xn, gates, big1, big2, ao, mask;
   DeviceBuffer skips;  // skip_connection models: the outputs of depth blocks 0..depth-2
   CUtensorMap m_abs, m_xn, m_ao, m_big1_ffh, m_big2_ffh, m_qkv_time, m_qkv_band, m_h1, m_h2;
+  CUtensorMap m_xn_slot;  // xn in boxes of one band sequence's slot (band_attn.cu)
   // GEMM output maps (TMA stores)
   CUtensorMap mo_qkv, mo_ffh, mo_bs, mo_h1, mo_h2;
 };
@@ -684,6 +685,7 @@ void Model::load(const std::string& path, int device, int precision) {
         L.m_w1 = map_gemm_b(L.w1.get(), ff_, D, D, L.bn_w1);
         L.m_w2 = map_gemm_b(L.w2.get(), D, ff_, ff_, L.bn_w2);
         L.m_w1_f = map_2d(L.w1.get(), ff_, D, D, 128);
+        L.m_wqkv64 = map_2d(L.wqkv.get(), 3 * inner_, D, D, 64);
         L.m_w2_f = map_2d(L.w2.get(), D, ff_, ff_, 128);
       }
       if (mel_) tw.g_final = upload_f32(vec(tp + ".norm.gamma", D));
@@ -880,6 +882,7 @@ Model::Work& Model::work(int B, int T) {
   if (skip_ && I.depth > 1) w->skips.reset(4 * (size_t)(I.depth - 1) * M * D);
   w->m_abs = map_2d(w->abs.get(), w->BT, ktot_, ktot_, kGemmBM);
   w->m_xn = map_2d(w->xn.get(), M, D, D, kGemmBM);
+  w->m_xn_slot = map_2d(w->xn.get(), M, D, D, (uint32_t)attn_band_slot(nb));
   w->m_ao = map_2d(w->ao.get(), M, inner_, inner_, kGemmBM);
   w->m_big2_ffh = map_2d(w->big2.get(), M, ff_, ff_, kGemmBM);
   w->m_h1 = map_2d(w->big1.get(), M, hid_, hid_, kGemmBM);
@@ -993,6 +996,23 @@ void Model::run_attn_block(int d, int axis, int l, float* x, int B, int T, const
   rn.gates = w.gates.get<float>();
   rn.heads = I.heads;
   MSST_CUDA(launch_rmsnorm(rn, bf16_, s));
+  if (axis == 1 && band_fused_ok()) {
+    // band axis: QKV projection, rotary, attention, gates and head merge in one kernel
+    BandAttnParams bp{};
+    bp.num_seqs = (int)w.BT;
+    bp.F = nb;
+    bp.slot = attn_band_slot(nb);
+    bp.D = D;
+    bp.heads = I.heads;
+    bp.inner = inner_;
+    bp.scale_log2 = (1.0f / std::sqrt((float)I.dim_head)) * 1.4426950408889634f;
+    bp.rope_cos = rope_table(nb, false);
+    bp.rope_sin = rope_table(nb, true);
+    bp.gates = w.gates.get<float>();
+    bp.out = w.ao.get();
+    bp.out_ld = inner_;
+    MSST_CUDA(launch_band_attention_fused(w.m_xn_slot, L.m_wqkv64, bp, bf16_, num_sms_, s));
+  } else {
   // QKV + RoPE
   {
     GemmParams p{};
@@ -1035,6 +1055,7 @@ void Model::run_attn_block(int d, int axis, int l, float* x, int B, int T, const
     }
     MSST_CUDA(launch_attention(axis == 0 ? w.m_qkv_time : w.m_qkv_band, a, bf16_, num_sms_, s));
   }
+  }
   // out projection + residual
   {
     GemmParams p{};
@@ -1053,6 +1074,16 @@ bool Model::ffn_fused_ok() const {
     return e ? atoi(e) : 1;
   }();
   return env != 0 && info_.dim % 128 == 0 && info_.dim <= 384 && ff_ % 128 == 0;
+}
+
+// Band-axis attention fused with its QKV projection (band_attn.cu) for sequences of
+// up to 64 bands; MSST_BAND_FUSED=0 selects the QKV GEMM + attention kernel path.
+bool Model::band_fused_ok() const {
+  static const int env = [] {
+    const char* e = getenv("MSST_BAND_FUSED");
+    return e ? atoi(e) : 1;
+  }();
+  return env != 0 && info_.num_bands <= 64 && info_.dim <= 512 && info_.dim % 64 == 0 && info_.dim_head == 64;
 }
 
 void Model::run_ffn_block(int d, int axis, int l, float* x, int B, int T, cudaStream_t s, Work& w) {

@@ -28,6 +28,7 @@ struct LayerWeights {
   // every launch that reads a map must pass the same bn
   int bn_qkv = 0, bn_out = 0, bn_w1 = 0, bn_w2 = 0;
   CUtensorMap m_w1_f, m_w2_f;                // 128-row boxes for the fused feed-forward kernel
+  CUtensorMap m_wqkv64;                      // 64-row boxes: one head's Q, K or V rows (band_attn.cu)
 };
 
 struct TransformerWeights {
@@ -104,6 +105,7 @@ class Model {
   void run_attn_block(int d, int axis, int l, float* x, int B, int T, const float* pending_gamma, cudaStream_t s,
                       Work& w);
   bool ffn_fused_ok() const;
+  bool band_fused_ok() const;
   void run_ffn_block(int d, int axis, int l, float* x, int B, int T, cudaStream_t s, Work& w);
   void gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, GemmParams& p, int epi, int bn,
             cudaStream_t s);

@@ -120,6 +120,7 @@ void Model::transformer_noalloc(int d, int axis, float* x, int B, int T, cudaStr
 
   // tensor maps over the scratch regions (host-side encoding only)
   const CUtensorMap m_xn = map_2d(xn, M, D, D, kGemmBM);
+  const CUtensorMap m_xn_slot = map_2d(xn, M, D, D, (uint32_t)attn_band_slot(nb));
   const CUtensorMap m_ao = map_2d(ao, M, inner_, inner_, kGemmBM);
   const CUtensorMap m_ffh = map_2d(big, M, ff_, ff_, kGemmBM);
   const CUtensorMap mo_qkv = map_out_2d(big, false, M, 3 * inner_, 3 * inner_);
@@ -167,38 +168,56 @@ void Model::transformer_noalloc(int d, int axis, float* x, int B, int T, cudaStr
     rn.gates = gates;
     rn.heads = H;
     MSST_CUDA(launch_rmsnorm(rn, bf16_, s));
-    {
-      GemmParams p{};
-      p.num_groups = 1;
-      p.groups[0] = one((int)M, 3 * inner_, D, big, 3 * inner_, nullptr);
-      p.rope_cols = 2 * inner_;
-      p.head_dim = I.dim_head;
-      p.pos_div = axis == 0 ? nb : 1;
-      p.pos_mod = npos;
-      p.rope_cos = cos_tab;
-      p.rope_sin = sin_tab;
-      gemm(m_xn, L.m_wqkv, mo_qkv, p, kEpiQkvRope, L.bn_qkv, s);
-    }
-    {
-      AttnParams a{};
-      a.mode = axis;
-      a.B = B;
-      a.T = T;
-      a.F = nb;
-      a.heads = H;
-      a.num_tokens = (int)M;
-      a.scale_log2 = (1.0f / std::sqrt((float)I.dim_head)) * 1.4426950408889634f;
-      a.gates = gates;
-      a.out = ao;
-      if (axis == 0) {
-        a.seq_len = T;
-        a.q_tiles = (T + 127) / 128;
-      } else {
-        a.seq_len = nb;
-        a.seqs_per_tile = 128 / attn_band_slot(nb);
-        a.q_tiles = (int)(((long long)B * T + a.seqs_per_tile - 1) / a.seqs_per_tile);
+    if (axis == 1 && band_fused_ok()) {
+      // band axis: the QKV projection stays on chip (as the allocating path runs it)
+      BandAttnParams bp{};
+      bp.num_seqs = B * T;
+      bp.F = nb;
+      bp.slot = attn_band_slot(nb);
+      bp.D = D;
+      bp.heads = H;
+      bp.inner = inner_;
+      bp.scale_log2 = (1.0f / std::sqrt((float)I.dim_head)) * 1.4426950408889634f;
+      bp.rope_cos = cos_tab;
+      bp.rope_sin = sin_tab;
+      bp.gates = gates;
+      bp.out = ao;
+      bp.out_ld = inner_;
+      MSST_CUDA(launch_band_attention_fused(m_xn_slot, L.m_wqkv64, bp, bf16_, num_sms_, s));
+    } else {
+      {
+        GemmParams p{};
+        p.num_groups = 1;
+        p.groups[0] = one((int)M, 3 * inner_, D, big, 3 * inner_, nullptr);
+        p.rope_cols = 2 * inner_;
+        p.head_dim = I.dim_head;
+        p.pos_div = axis == 0 ? nb : 1;
+        p.pos_mod = npos;
+        p.rope_cos = cos_tab;
+        p.rope_sin = sin_tab;
+        gemm(m_xn, L.m_wqkv, mo_qkv, p, kEpiQkvRope, L.bn_qkv, s);
       }
-      MSST_CUDA(launch_attention(m_qkv, a, bf16_, num_sms_, s));
+      {
+        AttnParams a{};
+        a.mode = axis;
+        a.B = B;
+        a.T = T;
+        a.F = nb;
+        a.heads = H;
+        a.num_tokens = (int)M;
+        a.scale_log2 = (1.0f / std::sqrt((float)I.dim_head)) * 1.4426950408889634f;
+        a.gates = gates;
+        a.out = ao;
+        if (axis == 0) {
+          a.seq_len = T;
+          a.q_tiles = (T + 127) / 128;
+        } else {
+          a.seq_len = nb;
+          a.seqs_per_tile = 128 / attn_band_slot(nb);
+          a.q_tiles = (int)(((long long)B * T + a.seqs_per_tile - 1) / a.seqs_per_tile);
+        }
+        MSST_CUDA(launch_attention(m_qkv, a, bf16_, num_sms_, s));
+      }
     }
     {
       GemmParams p{};

@@ -167,9 +167,11 @@ inline int device_sm_count() {
 unsigned gemm_device_error(bool clear);
 unsigned attention_device_error(bool clear);
 unsigned kernels_device_error(bool clear);
+unsigned band_attention_device_error(bool clear);
 
 inline unsigned device_error(bool clear) {
-  return gemm_device_error(clear) | attention_device_error(clear) | kernels_device_error(clear);
+  return gemm_device_error(clear) | attention_device_error(clear) | kernels_device_error(clear) |
+         band_attention_device_error(clear);
 }
 
 // Launch accounting (launch_stats.cu; see LaunchScope in common.cuh).

@@ -258,3 +258,38 @@ def test_mask_apply_vs_oracle(cuda, tmp_path_factory, kind):
         ref[:, :, 0] = 0.0
     assert rel_l2(out, ref) < 1e-5
     m.close()
+
+
+# (kind, model kwargs, precision, T): band counts 60 / 62 (slot 64) and 32 (slot 32),
+# widths 128 / 384 / 512 (the last with the 2-stage weight ring), an odd number of
+# band sequences (a half-empty last tile) and T = 801 (many tiles per CTA)
+BAND_CASES = [
+    ("mbr", dict(depth=1, dim=128), "fp16", 41),
+    ("bsr", dict(depth=1, dim=384), "fp16", 801),
+    ("bsr", dict(depth=1, dim=512), "bf16", 57),
+    ("mbr", dict(depth=1, dim=256, num_bands=32), "fp16", 33),
+]
+
+
+@pytest.mark.parametrize("kind,kw,prec,T", BAND_CASES)
+def test_band_attention_block_vs_oracle(cuda, tmp_path_factory, kind, kw, prec, T):
+    """The band-axis attention block (QKV projection, rotary, attention, gates and
+    head merge in one kernel, band_attn.cu) against the fp32 oracle."""
+    torch = cuda
+    import oracle
+    from msst_b200 import Model, device_error
+
+    path, cfg, sd = _model(tmp_path_factory, kind, kw, 23 + kw["dim"])
+    om = oracle.Model(cfg, sd)
+    m = Model(path, 0, prec)
+    B, nb, D = 1, m.info["num_bands"], m.info["dim"]
+    rng = np.random.default_rng(T)
+    x = rng.standard_normal((B, T, nb, D)).astype(np.float32)
+    xt = torch.from_numpy(x.copy()).cuda()
+    m.attn_block(0, "band", 0, xt)
+    y = xt.cpu().numpy()
+    xb = x.reshape(B * T, nb, D)
+    r = (xb + om.attention_block(xb, "layers.0.1.layers.0.0", nb)).reshape(B, T, nb, D)
+    assert device_error(True) == 0
+    assert rel_l2(y, r) < {"fp16": 3e-3, "bf16": 1.5e-2}[prec]
+    m.close()
