@@ -11,18 +11,21 @@
 // tile and head h:
 //   1. QKV_h = xn . [Wq_h; Wk_h; Wv_h]^T        M128 N192 K=dim, into TMEM (two
 //                                                 buffers alternate between heads)
-//   2. drain (8 warps): QKV_h -> registers, rotary on Q and K, 16-bit Q, K, V tiles
-//      into shared memory (128B swizzle, as TMA would write them)
+//   2. drain (8 warps, each 32 columns of Q, K and V): QKV_h -> registers, rotary
+//      on Q and K, 16-bit Q, K, V tiles into shared memory (128B swizzle, as TMA
+//      would write them)
 //   3. S = Q K^T                                  M128 N128 K64, into TMEM
 //   4. softmax (warps 2-5, one row per thread): the row's own slot only; P (16-bit,
 //      zero outside the slot) written over the first 64 columns of S in TMEM
 //   5. O = P V                                    M128 N64 K128, A from TMEM, into
 //                                                 the drained QKV_h buffer
-//   6. output (warps 6-9): O / rowsum * gate -> 16-bit -> [token, h*64 ..)
+//   6. output (warps 6-9, after draining the next head, while its softmax runs):
+//      O / rowsum * gate -> 16-bit -> [token, h*64 ..)
 // The MMA warp issues QKV_{h+1} right after S_h, so the tensor pipe computes the
 // next head's projection while the softmax of this one runs.
 //
-// CTA = 320 threads: warp 0 TMA, warp 1 MMA issuer, warps 2-9 as above.
+// CTA = 320 threads: warp 0 TMA, warp 1 MMA issuer, warps 2-9 as above.  Every
+// wait sits on the head-to-head critical path, so none takes the suspend hint.
 // TMEM: QKV buffers [0, 192) and [192, 384), S [384, 512) (P over [384, 448)).
 // Shared memory: xn tile (dim/64 blocks of 128x64, resident per tile), a ring of
 // W stages (192 rows x 64, three 64-row TMA boxes), Q, K, V tiles, row sums.
@@ -41,7 +44,7 @@ constexpr uint32_t kColQB0 = 0, kColQB1 = 192, kColS = 384;
 // shared memory layout for a model dim D (xn tile D/64 blocks) and W ring depth
 __host__ __device__ constexpr int band_w_stages(int D) { return D <= 384 ? 3 : 2; }
 __host__ __device__ constexpr size_t band_smem_bytes(int D) {
-  return 1024 + (size_t)(D / 64) * kBlock + (size_t)band_w_stages(D) * kWStage + 3 * kBlock + 2 * 128 * 4 + 512;
+  return 1024 + (size_t)(D / 64) * kBlock + (size_t)band_w_stages(D) * kWStage + 3 * kBlock + 2 * 128 * 4 + 384;
 }
 
 template <typename T, int kNch>
@@ -60,21 +63,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sV = sK + kBlock;
   float* sL = reinterpret_cast<float*>(sV + kBlock);  // [2][128] row sums, by head parity
   uint64_t* bars = reinterpret_cast<uint64_t*>(sL + 256);
-  uint64_t* x_full = bars + 0;
-  uint64_t* x_empty = bars + 1;
-  uint64_t* w_full = bars + 2;      // [3]
-  uint64_t* w_empty = bars + 5;     // [3]
-  uint64_t* qkv_full = bars + 8;    // [2]
-  uint64_t* qb_free = bars + 10;    // [2]
-  uint64_t* q_ready = bars + 12;
-  uint64_t* smem_free = bars + 13;
-  uint64_t* s_full = bars + 14;
-  uint64_t* p_full = bars + 15;
+  // xn per k-block, so the next tile's k-block kb loads as soon as the last head's
+  // projection has read this tile's k-block kb
+  uint64_t* x_full = bars + 0;      // [8]
+  uint64_t* x_empty = bars + 8;     // [8]
+  uint64_t* w_full = bars + 16;     // [3]
+  uint64_t* w_empty = bars + 19;    // [3]
+  uint64_t* qkv_full = bars + 22;   // [2]
+  uint64_t* qb_free = bars + 24;    // [2]
+  uint64_t* q_ready = bars + 26;
+  uint64_t* smem_free = bars + 27;
+  uint64_t* s_full = bars + 28;
+  uint64_t* p_full = bars + 29;
   // by head parity: the output warps wait for head g while the softmax warps may
   // already have finished head g + 1, so these two alternate between two barriers
-  uint64_t* o_full = bars + 16;     // [2]
-  uint64_t* l_ready = bars + 18;    // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
+  uint64_t* o_full = bars + 30;     // [2]
+  uint64_t* l_ready = bars + 32;    // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 34);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -85,8 +90,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int total_g = my_tiles * H;  // (tile, head) steps of this CTA
 
   if (threadIdx.x == 0) {
-    mbar_init(x_full, 1);
-    mbar_init(x_empty, 1);
+    for (int kb = 0; kb < 8; ++kb) {
+      mbar_init(&x_full[kb], 1);
+      mbar_init(&x_empty[kb], 1);
+    }
     for (int s = 0; s < 3; ++s) {
       mbar_init(&w_full[s], 1);
       mbar_init(&w_empty[s], 1);
@@ -125,15 +132,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t slot_bytes = (uint32_t)p.slot * 128u;
       for (int lt = 0; ok && lt < my_tiles; ++lt) {
         const int t = (int)blockIdx.x + lt * (int)gridDim.x;
-        if (!mbar_wait(x_empty, (lt & 1) ^ 1u, kErrTimeoutSmemEmpty, abort_flag)) break;
-        mbar_arrive_expect_tx(x_full, nkb * kBlock);
         // one box of `slot` rows per sequence (rows past the tokens are zero-filled)
-        for (int k = 0; k < spt; ++k)
-          for (int kb = 0; kb < nkb; ++kb)
-            tma_load_2d(sX + kb * kBlock + k * slot_bytes, &map_xn, x_full, kb * 64, (t * spt + k) * p.F);
+        for (int kb = 0; ok && kb < nkb; ++kb) {
+          if (!mbar_wait<false>(&x_empty[kb], (lt & 1) ^ 1u, kErrTimeoutSmemEmpty, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&x_full[kb], kBlock);
+          for (int k = 0; k < spt; ++k)
+            tma_load_2d(sX + kb * kBlock + k * slot_bytes, &map_xn, &x_full[kb], kb * 64, (t * spt + k) * p.F);
+        }
         for (int h = 0; ok && h < H; ++h) {
           for (int kb = 0; kb < nkb; ++kb) {
-            if (!mbar_wait(&w_empty[st], ph ^ 1u, kErrTimeoutSmemEmpty, abort_flag)) {
+            if (!mbar_wait<false>(&w_empty[st], ph ^ 1u, kErrTimeoutSmemEmpty, abort_flag)) {
               ok = false;
               break;
             }
@@ -161,12 +172,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       auto issue_qkv = [&](int g) -> bool {
         const int b = g & 1, lt = g / H, h = g % H;
-        if (h == 0 && !mbar_wait(x_full, lt & 1, kErrTimeoutTmaFull, abort_flag)) return false;
-        if (!mbar_wait(&qb_free[b], ((g >> 1) & 1) ^ 1u, kErrTimeoutTmemEmpty, abort_flag)) return false;
+        if (!mbar_wait<false>(&qb_free[b], ((g >> 1) & 1) ^ 1u, kErrTimeoutTmemEmpty, abort_flag)) return false;
         tc_fence_after();
         const uint32_t d = tmem + (b ? kColQB1 : kColQB0);
         for (int kb = 0; kb < nkb; ++kb) {
-          if (!mbar_wait(&w_full[st], ph, kErrTimeoutTmaFull, abort_flag)) return false;
+          if (h == 0 && !mbar_wait<false>(&x_full[kb], lt & 1, kErrTimeoutTmaFull, abort_flag)) return false;
+          if (!mbar_wait<false>(&w_full[st], ph, kErrTimeoutTmaFull, abort_flag)) return false;
           tc_fence_after();
           const uint32_t a0 = smem_u32(sX + kb * kBlock);
           const uint32_t b0 = smem_u32(sW + st * kWStage);
@@ -175,19 +186,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             umma_f16_ss(d, sw128_desc(a0 + kk * 32, 16, 1024), sw128_desc(b0 + kk * 32, 16, 1024), idesc_qkv,
                         (kb | kk) != 0 ? 1u : 0u);
           umma_commit(&w_empty[st]);
+          if (h == H - 1) umma_commit(&x_empty[kb]);  // the tile's xn k-block is no longer read
           if (++st == nst) {
             st = 0;
             ph ^= 1u;
           }
         }
         umma_commit(&qkv_full[b]);
-        if (h == H - 1) umma_commit(x_empty);  // the tile's xn is no longer read
         return true;
       };
       if (total_g > 0) ok = issue_qkv(0);
       for (int g = 0; ok && g < total_g; ++g) {
         // S_g once the drain has written Q, K, V
-        if (!mbar_wait(q_ready, g & 1, kErrTimeoutAttnQ, abort_flag)) break;
+        if (!mbar_wait<false>(q_ready, g & 1, kErrTimeoutAttnQ, abort_flag)) break;
         tc_fence_after();
         {
           const uint32_t qa = smem_u32(sQ), ka = smem_u32(sK);
@@ -200,7 +211,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool next_same_tile = g + 1 < total_g && (g + 1) % H != 0;
         if (next_same_tile && !(ok = issue_qkv(g + 1))) break;
         // O_g = P_g V_g into the drained QKV_g buffer
-        if (!mbar_wait(p_full, g & 1, kErrTimeoutAttnP, abort_flag)) break;
+        if (!mbar_wait<false>(p_full, g & 1, kErrTimeoutAttnP, abort_flag)) break;
         tc_fence_after();
         {
           const uint32_t dO = tmem + ((g & 1) ? kColQB1 : kColQB0);
@@ -230,8 +241,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto output = [&](int g) -> bool {
       const int lt = g / H, h = g % H;
       const int t = (int)blockIdx.x + lt * (int)gridDim.x;
-      if (!mbar_wait(&o_full[g & 1], (g >> 1) & 1, kErrTimeoutAttnO, abort_flag)) return false;
-      if (!mbar_wait(&l_ready[g & 1], (g >> 1) & 1, kErrTimeoutAttnO, abort_flag)) return false;
+      if (!mbar_wait<false>(&o_full[g & 1], (g >> 1) & 1, kErrTimeoutAttnO, abort_flag)) return false;
+      if (!mbar_wait<false>(&l_ready[g & 1], (g >> 1) & 1, kErrTimeoutAttnO, abort_flag)) return false;
       tc_fence_after();
       const uint32_t oAddr = tmem + lane_off + ((g & 1) ? kColQB1 : kColQB0);
       uint32_t ra[32], rb[32];
@@ -260,38 +271,48 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       return true;
     };
+    // This thread's rotary factors, loaded once: its row's position never changes
+    // (sequences sit at fixed slots) and warp half hf rotates pairs [16 hf, 16 hf + 16)
+    // of Q and K (per-lane table loads inside the head loop hit one cache line per
+    // lane and throttled the whole kernel)
+    float rc[16], rs[16];
+    {
+      const float4* c4 = reinterpret_cast<const float4*>(p.rope_cos + (size_t)pos * 32 + 16 * hf);
+      const float4* s4 = reinterpret_cast<const float4*>(p.rope_sin + (size_t)pos * 32 + 16 * hf);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float4 a = __ldg(c4 + u), b = __ldg(s4 + u);
+        rc[4 * u] = a.x, rc[4 * u + 1] = a.y, rc[4 * u + 2] = a.z, rc[4 * u + 3] = a.w;
+        rs[4 * u] = b.x, rs[4 * u + 1] = b.y, rs[4 * u + 2] = b.z, rs[4 * u + 3] = b.w;
+      }
+    }
     for (int g = 0; ok && g < total_g; ++g) {
       const int b = g & 1;
-      // ---- drain QKV_g: this warp's 96 columns, rotary on Q and K, 16-bit into sQ/sK/sV
-      if (!mbar_wait(&qkv_full[b], (g >> 1) & 1, kErrTimeoutTmemFull, abort_flag)) break;
+      // ---- drain QKV_g: columns [32 hf, 32 hf + 32) of Q, K and V, rotary on Q and K,
+      // 16-bit into sQ / sK / sV
+      if (!mbar_wait<false>(&qkv_full[b], (g >> 1) & 1, kErrTimeoutTmemFull, abort_flag)) break;
       tc_fence_after();
       const uint32_t qb = tmem + lane_off + (b ? kColQB1 : kColQB0);
       uint32_t v0[32], v1[32], v2[32];
-      tmem_ld32(qb + hf * 96, v0);
-      tmem_ld32(qb + hf * 96 + 32, v1);
-      tmem_ld32(qb + hf * 96 + 64, v2);
+      tmem_ld32(qb + hf * 32, v0);
+      tmem_ld32(qb + 64 + hf * 32, v1);
+      tmem_ld32(qb + 128 + hf * 32, v2);
       tmem_ld_wait();
       // Q, K, V of the previous head consumed by its S and P.V MMAs
-      if (!mbar_wait(smem_free, (g & 1) ^ 1u, kErrTimeoutAttnKV, abort_flag)) break;
+      if (!mbar_wait<false>(smem_free, (g & 1) ^ 1u, kErrTimeoutAttnKV, abort_flag)) break;
 #pragma unroll
       for (int ch = 0; ch < 3; ++ch) {
         uint32_t(&v)[32] = ch == 0 ? v0 : (ch == 1 ? v1 : v2);
-        const int col = hf * 96 + ch * 32;  // column within QKV_h: [0,64) Q, [64,128) K, [128,192) V
-        if (col < 128) {
-          const int i0 = (col & 63) >> 1;
-          const float* cs = p.rope_cos + (size_t)pos * 32 + i0;
-          const float* sn = p.rope_sin + (size_t)pos * 32 + i0;
+        if (ch < 2) {
 #pragma unroll
           for (int k = 0; k < 16; ++k) {
             const float x0 = __uint_as_float(v[2 * k]), x1 = __uint_as_float(v[2 * k + 1]);
-            const float cc = __ldg(cs + k), ss = __ldg(sn + k);
-            v[2 * k] = __float_as_uint(x0 * cc - x1 * ss);
-            v[2 * k + 1] = __float_as_uint(x0 * ss + x1 * cc);
+            v[2 * k] = __float_as_uint(x0 * rc[k] - x1 * rs[k]);
+            v[2 * k + 1] = __float_as_uint(x0 * rs[k] + x1 * rc[k]);
           }
         }
-        uint8_t* tile = col < 64 ? sQ : (col < 128 ? sK : sV);
-        uint8_t* rowp = tile + r * 128;
-        const int chunk0 = (col & 63) >> 3;  // first 16-byte chunk of these 32 columns
+        uint8_t* rowp = (ch == 0 ? sQ : (ch == 1 ? sK : sV)) + r * 128;
+        const int chunk0 = hf * 4;  // first 16-byte chunk of these 32 columns
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const uint4 w = make_uint4(pack2<T>(__uint_as_float(v[8 * u]), __uint_as_float(v[8 * u + 1])),
@@ -307,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(q_ready);
       if (hf == 0) {
         // ---- softmax of S_g over the row's own slot; P over S's first 64 columns
-        if (!mbar_wait(s_full, g & 1, kErrTimeoutAttnS, abort_flag)) break;
+        if (!mbar_wait<false>(s_full, g & 1, kErrTimeoutAttnS, abort_flag)) break;
         tc_fence_after();
         const uint32_t sAddr = tmem + lane_off + kColS;
         const int c_lo = (slot_of_row * p.slot) >> 5;  // first chunk of the row's slot (kNch chunks)
