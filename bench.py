@@ -160,7 +160,9 @@ NCU_TRAFFIC: dict = {
     # the out-projection (K=512); at dim <= 384 the FFN2 residual GEMM is part of ffn_fused
     "gemm_resid32": {"dram_bytes": 123456512 + 11998464, "flop": 18897960960},
     # profiles/ffn_fused_mbr_cfg1_chunk1.md: the fused feed-forward block, one chunk
-    "ffn_fused": {"dram_bytes": 113154816 + 15404544, "flop": 113387765760},
+    "ffn_fused": {"dram_bytes": 113155584 + 15893504, "flop": 113387765760},
+    # profiles/band_attention_fused_mbr_cfg1_chunk1.md: band-axis QKV projection + attention, one chunk
+    "band_attention_fused": {"dram_bytes": 39705344 + 1760000, "flop": 56693882880 + 5905612800},
 }
 
 
