@@ -5,8 +5,10 @@
 #include <atomic>
 #include <cmath>
 #include <cstring>
+#include <initializer_list>
 #include <mutex>
 #include <string>
+#include <utility>
 
 #include "attention.cuh"
 #include "gemm.cuh"
@@ -47,15 +49,50 @@ int guarded(F&& f) {
 
 cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Makes `device` current for the scope of one entry point and restores the
+// caller's current device on the way out, so a call on a model of another GPU
+// leaves the host thread's device (which frameworks such as PyTorch read back
+// for their next allocation) as it found it.
+class DeviceScope {
+ public:
+  explicit DeviceScope(int device) {
+    MSST_CUDA(cudaGetDevice(&prev_));
+    if (prev_ != device) MSST_CUDA(cudaSetDevice(device));
+    cur_ = device;
+  }
+  ~DeviceScope() {
+    if (prev_ >= 0 && prev_ != cur_) cudaSetDevice(prev_);
+  }
+  DeviceScope(const DeviceScope&) = delete;
+  DeviceScope& operator=(const DeviceScope&) = delete;
+
+ private:
+  int prev_ = -1, cur_ = -1;
+};
+
+// A buffer handed to a model entry point must be device memory of the model's GPU
+// (or managed memory): a kernel reading a host pointer or another GPU's memory
+// without a peer mapping would fault, so such calls are refused up front.
+void require_on_device(const void* p, int device, const char* what) {
+  cudaPointerAttributes a{};
+  MSST_CUDA(cudaPointerGetAttributes(&a, p));
+  MSST_REQUIRE(a.type == cudaMemoryTypeManaged || (a.type == cudaMemoryTypeDevice && a.device == device),
+               std::string(what) + " must be device memory on the model's GPU (" + std::to_string(device) + ")");
+}
+
 // The model-level calls of one msst_model share its workspace, so they run one
 // host thread at a time, and a call on a different stream than the previous one
 // first makes its stream wait (on the device) for the previous call's work.  The
 // event is recorded even when the call fails part way, since some of its work may
-// already be queued.
+// already be queued.  `buffers` are the call's device operands (null entries are
+// skipped), checked against the model's device.
 template <typename F>
-void serialized(msst_model* m, cudaStream_t s, F&& f) {
+void serialized(msst_model* m, cudaStream_t s, std::initializer_list<std::pair<const void*, const char*>> buffers,
+                F&& f) {
   std::lock_guard<std::mutex> lock(m->mu);
-  MSST_CUDA(cudaSetDevice(m->impl.device()));
+  DeviceScope dev(m->impl.device());
+  for (const auto& b : buffers)
+    if (b.first) require_on_device(b.first, m->impl.device(), b.second);
   if (!m->done) MSST_CUDA(cudaEventCreateWithFlags(&m->done, cudaEventDisableTiming));
   if (m->used && s != m->last) MSST_CUDA(cudaStreamWaitEvent(s, m->done, 0));
   try {
@@ -108,14 +145,16 @@ void check_align(const void* p, const char* what) {
   MSST_REQUIRE((reinterpret_cast<uintptr_t>(p) & 15) == 0, std::string(what) + " must be 16-byte aligned");
 }
 
-// Op-level entry points run on the device that owns their first operand.
-void use_device_of(const void* p) {
+// Op-level entry points run on the device that owns their first operand (made
+// current for the call's scope).
+int device_of(const void* p) {
   cudaPointerAttributes a{};
   MSST_CUDA(cudaPointerGetAttributes(&a, p));
   MSST_REQUIRE(a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged, "operand is not device memory");
-  int cur = -1;
+  if (a.type == cudaMemoryTypeDevice) return a.device;
+  int cur = 0;
   MSST_CUDA(cudaGetDevice(&cur));
-  if (cur != a.device) MSST_CUDA(cudaSetDevice(a.device));
+  return cur;
 }
 
 }  // namespace
@@ -159,7 +198,7 @@ int msst_rmsnorm(const float* x, long long rows, int D, const float* gamma, floa
     MSST_REQUIRE(D % 128 == 0 && D <= 1024, "D must be a multiple of 128 and <= 1024");
     MSST_REQUIRE(!wg || (bg && gates && heads > 0 && heads <= 32), "gate projection needs bg, gates, 0<heads<=32");
     check_align(x, "x");
-    use_device_of(x);
+    DeviceScope dev_scope(device_of(x));
     msst::RmsNormArgs a{};
     a.x = const_cast<float*>(x);
     a.rows = rows;
@@ -192,7 +231,7 @@ int msst_gemm(const void* x, long long rows, int K, long long ldx, const void* w
     const bool out32 = epilogue != MSST_EPI_STORE16;
     MSST_REQUIRE(ldo >= (epilogue == MSST_EPI_GLU32 ? N / 2 : N) && (ldo * (out32 ? 4 : 2)) % 16 == 0,
                  "ldo must cover the output row and be a multiple of 16 bytes");
-    use_device_of(x);
+    DeviceScope dev_scope(device_of(x));
     const int bn = pick_bn(N);
     const CUtensorMap ma = msst::map_2d(x, (uint64_t)rows, (uint64_t)K, (uint64_t)ldx, msst::kGemmBM);
     const CUtensorMap mb = msst::map_gemm_b(w, (uint64_t)N, (uint64_t)K, (uint64_t)K, bn);
@@ -223,7 +262,7 @@ int msst_gemm_qkv_rope(const void* x, long long rows, int K, const void* w, int 
     MSST_REQUIRE(K > 0 && K % 64 == 0 && heads > 0 && pos_div > 0 && pos_mod > 0, "bad shape");
     check_align(x, "x");
     check_align(w, "w");
-    use_device_of(x);
+    DeviceScope dev_scope(device_of(x));
     const int N = 3 * heads * 64;
     const int bn = pick_bn(N);
     const CUtensorMap ma = msst::map_2d(x, (uint64_t)rows, (uint64_t)K, (uint64_t)K, msst::kGemmBM);
@@ -260,7 +299,7 @@ int msst_attention(const void* qkv16, int B, int T, int F, int heads, int axis, 
     MSST_REQUIRE(axis == MSST_AXIS_TIME || F <= 128, "band axis supports at most 128 bands");
     check_align(qkv16, "qkv16");
     check_align(out16, "out16");
-    use_device_of(qkv16);
+    DeviceScope dev_scope(device_of(qkv16));
     const long long M = (long long)B * T * F;
     MSST_REQUIRE(M < (1LL << 31), "too many tokens");
     const uint64_t C3 = 3ull * heads * 64;
@@ -310,7 +349,7 @@ int msst_layernorm(const float* x, long long rows, int D, const float* gamma, co
     check_align(beta, "beta");
     check_align(out, "out");
     if (rows == 0) return;
-    use_device_of(x);
+    DeviceScope dev_scope(device_of(x));
     msst::LayerNormArgs a{};
     a.x = x;
     a.rows = rows;
@@ -338,7 +377,7 @@ int msst_sdpa(const void* q, const void* k, const void* v, int B, int H, int Nq,
     check_align(k, "k");
     check_align(v, "v");
     check_align(out, "out");
-    use_device_of(q);
+    DeviceScope dev_scope(device_of(q));
     const float s = scale == 0.f ? 1.0f / std::sqrt((float)head_dim) : scale;
     msst::AttnParams a{};
     a.mode = 2;
@@ -389,7 +428,7 @@ int msst_grouped_gemm(int num_groups, const msst_gemm_group* groups, const void*
     check_align(x, "x");
     check_align(w, "w");
     check_align(out, "out");
-    use_device_of(x);
+    DeviceScope dev_scope(device_of(x));
     msst::GemmParams p{};
     p.num_groups = num_groups;
     p.act = act;
@@ -451,7 +490,7 @@ int msst_band_gather(const float* spec, int B, int T, const msst_band_tables* t,
     MSST_REQUIRE(B > 0 && T > 0 && t->num_bands > 0 && t->nbins > 0 && t->channels > 0, "bad shape");
     MSST_REQUIRE(ldo >= t->sum_kpad && ldo % 8 == 0, "ldo must cover sum_kpad and be a multiple of 8");
     check_align(out16, "out16");
-    use_device_of(spec);
+    DeviceScope dev_scope(device_of(spec));
     msst::BandInArgs bi{};
     bi.spec = reinterpret_cast<const float2*>(spec);
     bi.spec_scale = 1.0f;
@@ -478,7 +517,7 @@ int msst_mask_apply(const float* spec, const float* masks, int B, int S, int T, 
   return guarded([&] {
     MSST_REQUIRE(spec && masks && t && out && t->contrib_off && t->contrib_col && t->denom, "null argument");
     MSST_REQUIRE(B > 0 && S > 0 && T > 0 && t->nbins > 0 && t->channels > 0 && t->sum_dims > 0, "bad shape");
-    use_device_of(spec);
+    DeviceScope dev_scope(device_of(spec));
     msst::MaskApplyArgs ma{};
     ma.spec = reinterpret_cast<const float2*>(spec);
     ma.spec_scale = 1.0f;
@@ -504,22 +543,36 @@ int msst_model_load(const char* path, int device, int precision, msst_model** ou
   return guarded([&] {
     MSST_REQUIRE(path && out, "null argument");
     *out = nullptr;
+    // the caller's current device, restored after the load (which makes `device`
+    // current); a file error is reported as such even on a machine without a GPU
+    int prev = -1;
+    if (cudaGetDevice(&prev) != cudaSuccess) {
+      prev = -1;
+      cudaGetLastError();
+    }
     auto* m = new msst_model();
     try {
       m->impl.load(path, device, precision);
     } catch (...) {
       delete m;
+      if (prev >= 0) cudaSetDevice(prev);
       throw;
     }
+    if (prev >= 0) cudaSetDevice(prev);
     *out = m;
   });
 }
 
 void msst_model_free(msst_model* m) {
   if (!m) return;
-  cudaSetDevice(m->impl.device());
-  if (m->done) cudaEventDestroy(m->done);
-  delete m;
+  try {
+    DeviceScope dev(m->impl.device());
+    if (m->done) cudaEventDestroy(m->done);
+    delete m;
+  } catch (...) {
+    // the device could not be made current: release the host side only
+    delete m;
+  }
 }
 
 int msst_model_get_info(const msst_model* m, msst_model_info* info) {
@@ -533,7 +586,7 @@ int msst_model_forward(msst_model* m, const float* audio, int batch, int channel
                        void* stream) {
   return guarded([&] {
     MSST_REQUIRE(m && audio && out, "null argument");
-    serialized(m, as_stream(stream), [&] { m->impl.forward(audio, batch, channels, length, out, as_stream(stream)); });
+    serialized(m, as_stream(stream), {{audio, "audio"}, {out, "out"}}, [&] { m->impl.forward(audio, batch, channels, length, out, as_stream(stream)); });
   });
 }
 
@@ -541,14 +594,14 @@ int msst_model_masks(msst_model* m, const float* audio, int batch, int channels,
                      void* stream) {
   return guarded([&] {
     MSST_REQUIRE(m && audio && masks, "null argument");
-    serialized(m, as_stream(stream), [&] { m->impl.masks(audio, batch, channels, length, masks, as_stream(stream)); });
+    serialized(m, as_stream(stream), {{audio, "audio"}, {masks, "masks"}}, [&] { m->impl.masks(audio, batch, channels, length, masks, as_stream(stream)); });
   });
 }
 
 int msst_model_transformer(msst_model* m, int depth_index, int axis, float* x, int batch, int T, void* stream) {
   return guarded([&] {
     MSST_REQUIRE(m && x, "null argument");
-    serialized(m, as_stream(stream), [&] { m->impl.transformer(depth_index, axis, x, batch, T, as_stream(stream)); });
+    serialized(m, as_stream(stream), {{x, "x"}}, [&] { m->impl.transformer(depth_index, axis, x, batch, T, as_stream(stream)); });
   });
 }
 
@@ -556,7 +609,7 @@ int msst_roformer_attn_block(msst_model* m, int depth_index, int axis, int layer
                              void* stream) {
   return guarded([&] {
     MSST_REQUIRE(m && x, "null argument");
-    serialized(m, as_stream(stream), [&] {
+    serialized(m, as_stream(stream), {{x, "x"}}, [&] {
       m->impl.attn_block(depth_index, axis, layer, x, batch, T, as_stream(stream));
     });
   });
@@ -566,7 +619,7 @@ int msst_roformer_ffn_block(msst_model* m, int depth_index, int axis, int layer,
                             void* stream) {
   return guarded([&] {
     MSST_REQUIRE(m && x, "null argument");
-    serialized(m, as_stream(stream), [&] {
+    serialized(m, as_stream(stream), {{x, "x"}}, [&] {
       m->impl.ffn_block(depth_index, axis, layer, x, batch, T, as_stream(stream));
     });
   });
@@ -583,7 +636,7 @@ int msst_model_transformer_noalloc(msst_model* m, int depth_index, int axis, flo
                                    void* stream) {
   return guarded([&] {
     MSST_REQUIRE(m && x, "null argument");
-    serialized(m, as_stream(stream), [&] {
+    serialized(m, as_stream(stream), {{x, "x"}}, [&] {
       m->impl.transformer_noalloc(depth_index, axis, x, batch, T, as_stream(stream));
     });
   });
@@ -593,7 +646,7 @@ int msst_model_separate(msst_model* m, const float* track, int channels, long lo
                         int chunk_batch, int flags, float* out, void* stream) {
   return guarded([&] {
     MSST_REQUIRE(m && track && out, "null argument");
-    serialized(m, as_stream(stream), [&] {
+    serialized(m, as_stream(stream), {{track, "track"}, {out, "out"}}, [&] {
       m->impl.separate(track, channels, length, overlap, chunk_batch, flags, out, as_stream(stream));
     });
   });
@@ -603,8 +656,7 @@ int msst_model_separate_host(msst_model* m, const float* track_host, int channel
                              int chunk_batch, int flags, float* out_host) {
   return guarded([&] {
     MSST_REQUIRE(m && track_host && out_host && channels > 0 && length > 0, "null argument");
-    MSST_CUDA(cudaSetDevice(m->impl.device()));
-    serialized(m, m->impl.host_stream(), [&] {
+    serialized(m, m->impl.host_stream(), {}, [&] {
       m->impl.separate_host(track_host, channels, length, overlap, chunk_batch, flags, out_host);
     });
   });
@@ -614,7 +666,7 @@ int msst_model_forward_chunks(msst_model* m, const float* track, int channels, l
                               int first_chunk, int count, int chunk_batch, int flags, float* out, void* stream) {
   return guarded([&] {
     MSST_REQUIRE(m && track && (out || count == 0), "null argument");
-    serialized(m, as_stream(stream), [&] {
+    serialized(m, as_stream(stream), {{track, "track"}, {out, "out"}}, [&] {
       m->impl.forward_chunks(track, channels, length, overlap, first_chunk, 1, count, chunk_batch, flags, out,
                              as_stream(stream));
     });
@@ -626,7 +678,7 @@ int msst_model_forward_chunks_strided(msst_model* m, const float* track, int cha
                                       int flags, float* out, void* stream) {
   return guarded([&] {
     MSST_REQUIRE(m && track && (out || count == 0), "null argument");
-    serialized(m, as_stream(stream), [&] {
+    serialized(m, as_stream(stream), {{track, "track"}, {out, "out"}}, [&] {
       m->impl.forward_chunks(track, channels, length, overlap, first_chunk, chunk_stride, count, chunk_batch, flags,
                              out, as_stream(stream));
     });
@@ -638,7 +690,7 @@ int msst_model_stitch_range(msst_model* m, const float* chunks, int slot_ranks, 
                             void* stream) {
   return guarded([&] {
     MSST_REQUIRE(m && chunks && out, "null argument");
-    serialized(m, as_stream(stream), [&] {
+    serialized(m, as_stream(stream), {{chunks, "chunks"}, {out, "out"}}, [&] {
       m->impl.stitch_range(chunks, slot_ranks, slot_cap, channels, length, overlap, begin, end, out,
                            as_stream(stream));
     });
@@ -657,7 +709,7 @@ int msst_model_stitch(msst_model* m, const float* chunks, int channels, long lon
                       void* stream) {
   return guarded([&] {
     MSST_REQUIRE(m && chunks && out, "null argument");
-    serialized(m, as_stream(stream), [&] {
+    serialized(m, as_stream(stream), {{chunks, "chunks"}, {out, "out"}}, [&] {
       m->impl.stitch(chunks, channels, length, overlap, out, as_stream(stream));
     });
   });

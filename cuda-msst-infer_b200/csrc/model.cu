@@ -724,6 +724,7 @@ void Model::load(const std::string& path, int device, int precision) {
     }
   }
   uploader.finish();
+  if (!host_stream_) MSST_CUDA(cudaStreamCreateWithFlags(&host_stream_, cudaStreamNonBlocking));
   MSST_CUDA(cudaDeviceSynchronize());
   info_.load_ms =
       (float)std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t_load0).count();
@@ -1569,14 +1570,11 @@ void Model::stitch(const float* chunks, int C, long long L, float overlap, float
   stitch_range(chunks, 1, n, C, L, overlap, 0, L, out, s);
 }
 
-cudaStream_t Model::host_stream() {
-  if (!host_stream_) MSST_CUDA(cudaStreamCreateWithFlags(&host_stream_, cudaStreamNonBlocking));
-  return host_stream_;
-}
+// Created at load on the model's device.
+cudaStream_t Model::host_stream() { return host_stream_; }
 
 void Model::separate_host(const float* track_host, int C, long long L, float overlap, int chunk_batch, int flags,
                           float* out_host) {
-  host_stream();
   const size_t in_bytes = sizeof(float) * (size_t)C * L;
   const size_t out_bytes = in_bytes * (size_t)info_.num_stems;
   host_in_.ensure(in_bytes);

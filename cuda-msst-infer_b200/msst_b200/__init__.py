@@ -167,9 +167,10 @@ def _ptr(t):
     return ctypes.c_void_p(t.data_ptr()) if t is not None else None
 
 
-def _stream(stream=None):
+def _stream(stream=None, device=None):
+    """The given stream, else the current stream of `device` (the current device when None)."""
     torch = _torch()
-    s = stream if stream is not None else torch.cuda.current_stream()
+    s = stream if stream is not None else torch.cuda.current_stream(device)
     return ctypes.c_void_p(s.cuda_stream)
 
 
@@ -200,7 +201,7 @@ class ops:
             gates = torch.empty(x.shape[:-1] + (heads,), dtype=torch.float32, device=x.device)
         check(lib().msst_rmsnorm(_ptr(x), rows, D, _ptr(gamma.contiguous()), float(scale), _dtype_code(dtype),
                                  _ptr(out), _ptr(wg.contiguous()) if wg is not None else None,
-                                 _ptr(bg.contiguous()) if bg is not None else None, heads, _ptr(gates), _stream()))
+                                 _ptr(bg.contiguous()) if bg is not None else None, heads, _ptr(gates), _stream(None, x.device)))
         return out, gates
 
     @staticmethod
@@ -220,7 +221,7 @@ class ops:
         ldo = out.shape[-1]
         check(lib().msst_gemm(_ptr(x), rows, K, x.stride(-2) if x.dim() > 1 else K, _ptr(w.contiguous()), N,
                               _ptr(bias.contiguous()) if bias is not None else None, epi, ACT[act],
-                              _dtype_code(x.dtype), _ptr(out), ldo, _stream()))
+                              _dtype_code(x.dtype), _ptr(out), ldo, _stream(None, x.device)))
         return out
 
     @staticmethod
@@ -232,7 +233,7 @@ class ops:
             out = torch.empty((rows, 3 * heads * 64), dtype=x.dtype, device=x.device)
         check(lib().msst_gemm_qkv_rope(_ptr(x.contiguous()), rows, K, _ptr(w.contiguous()), heads,
                                        _ptr(cos.contiguous()), _ptr(sin.contiguous()), pos_div, pos_mod,
-                                       _dtype_code(x.dtype), _ptr(out), _stream()))
+                                       _dtype_code(x.dtype), _ptr(out), _stream(None, x.device)))
         return out
 
     @staticmethod
@@ -241,7 +242,7 @@ class ops:
         out = torch.empty((B * T * F, heads * 64), dtype=qkv.dtype, device=qkv.device)
         check(lib().msst_attention(_ptr(qkv.contiguous()), B, T, F, heads, AXIS[axis] if isinstance(axis, str) else axis,
                                    float(scale), _ptr(gates.contiguous()) if gates is not None else None,
-                                   _dtype_code(qkv.dtype), _ptr(out), _stream()))
+                                   _dtype_code(qkv.dtype), _ptr(out), _stream(None, qkv.device)))
         return out
 
     @staticmethod
@@ -255,7 +256,7 @@ class ops:
         out = torch.empty(x.shape, dtype=dtype, device=x.device)
         code = F32 if dtype == torch.float32 else _dtype_code(dtype)
         check(lib().msst_layernorm(_ptr(x), x.numel() // D, D, _ptr(gamma.contiguous()), _ptr(beta.contiguous()),
-                                   float(eps), code, _ptr(out), _stream()))
+                                   float(eps), code, _ptr(out), _stream(None, x.device)))
         return out
 
     @staticmethod
@@ -271,7 +272,7 @@ class ops:
             raise ValueError("q, k and v must share one 16-bit dtype")
         out = torch.empty((B, H, Nq, d), dtype=q.dtype, device=q.device)
         check(lib().msst_sdpa(_ptr(q.contiguous()), _ptr(k.contiguous()), _ptr(v.contiguous()), B, H, Nq, Nk, d,
-                              float(scale), _dtype_code(q.dtype), _ptr(out), _stream()))
+                              float(scale), _dtype_code(q.dtype), _ptr(out), _stream(None, q.device)))
         return out
 
     @staticmethod
@@ -286,7 +287,7 @@ class ops:
                                 g["bias"].data_ptr() if g.get("bias") is not None else None)
         check(lib().msst_grouped_gemm(len(groups), arr, _ptr(x), x.shape[0], x.shape[1], _ptr(w), w.shape[0],
                                       w.shape[1], EPI[epilogue], ACT[act], _dtype_code(x.dtype), _ptr(out),
-                                      out.shape[0], out.shape[1], _stream(stream)))
+                                      out.shape[0], out.shape[1], _stream(stream, x.device)))
         return out
 
     @staticmethod
@@ -295,7 +296,7 @@ class ops:
         torch = _torch()
         out = torch.empty((B * T, tables.sum_kpad), dtype=dtype, device=spec.device)
         check(lib().msst_band_gather(_ptr(spec.contiguous()), B, T, ctypes.byref(tables), _dtype_code(dtype),
-                                     _ptr(out), tables.sum_kpad, _stream(stream)))
+                                     _ptr(out), tables.sum_kpad, _stream(stream, spec.device)))
         return out
 
     @staticmethod
@@ -304,7 +305,7 @@ class ops:
         torch = _torch()
         out = torch.empty((B * S * tables.channels, T, tables.nbins, 2), dtype=torch.float32, device=spec.device)
         check(lib().msst_mask_apply(_ptr(spec.contiguous()), _ptr(masks.contiguous()), B, S, T, ctypes.byref(tables),
-                                    1 if zero_dc else 0, _ptr(out), _stream(stream)))
+                                    1 if zero_dc else 0, _ptr(out), _stream(stream, spec.device)))
         return out
 
 class Model:
@@ -342,7 +343,7 @@ class Model:
         B, C, L = audio.shape
         S = self.info["num_stems"]
         out = torch.empty((B, S, C, self.out_length(L)), dtype=torch.float32, device=audio.device)
-        check(lib().msst_model_forward(self._h, _ptr(audio), B, C, L, _ptr(out), _stream(stream)))
+        check(lib().msst_model_forward(self._h, _ptr(audio), B, C, L, _ptr(out), _stream(stream, self.device)))
         return out[:, 0] if S == 1 else out
 
     def masks(self, audio, stream=None):
@@ -352,21 +353,21 @@ class Model:
         T = L // self.info["hop_length"] + 1
         out = torch.empty((B, self.info["num_stems"], T, self.info["sum_band_dims"]), dtype=torch.float32,
                           device=audio.device)
-        check(lib().msst_model_masks(self._h, _ptr(audio), B, C, L, _ptr(out), _stream(stream)))
+        check(lib().msst_model_masks(self._h, _ptr(audio), B, C, L, _ptr(out), _stream(stream, self.device)))
         return out
 
     def attn_block(self, depth_index: int, axis, layer: int, x, stream=None):
         """Layer `layer`'s attention block, in place on x fp32 [B, T, bands, dim]."""
         B, T = x.shape[0], x.shape[1]
         check(lib().msst_roformer_attn_block(self._h, depth_index, AXIS[axis] if isinstance(axis, str) else axis,
-                                             layer, _ptr(x), B, T, _stream(stream)))
+                                             layer, _ptr(x), B, T, _stream(stream, self.device)))
         return x
 
     def ffn_block(self, depth_index: int, axis, layer: int, x, stream=None):
         """Layer `layer`'s feed-forward block, in place on x fp32 [B, T, bands, dim]."""
         B, T = x.shape[0], x.shape[1]
         check(lib().msst_roformer_ffn_block(self._h, depth_index, AXIS[axis] if isinstance(axis, str) else axis,
-                                            layer, _ptr(x), B, T, _stream(stream)))
+                                            layer, _ptr(x), B, T, _stream(stream, self.device)))
         return x
 
     def band_tables(self) -> "BandTables":
@@ -379,7 +380,7 @@ class Model:
         """Apply one axial transformer in place to x fp32 [B, T, bands, dim]."""
         B, T = x.shape[0], x.shape[1]
         check(lib().msst_model_transformer(self._h, depth_index, AXIS[axis] if isinstance(axis, str) else axis,
-                                           _ptr(x), B, T, _stream(stream)))
+                                           _ptr(x), B, T, _stream(stream, self.device)))
         return x
 
     def chunk_plan(self, length: int, overlap: float = 0.0):
@@ -400,7 +401,7 @@ class Model:
             out = torch.empty((S, C, L), dtype=torch.float32, device=track.device)
         check(lib().msst_model_separate(self._h, _ptr(track), C, L, overlap, chunk_batch,
                                         SEPARATE_FIX_TAIL_PADDING if fix_tail_padding else 0, _ptr(out),
-                                        _stream(stream)))
+                                        _stream(stream, self.device)))
         return out[0] if S == 1 else out
 
     def forward_chunks(self, track, overlap: float, first: int, count: int, chunk_batch: int = 0,
@@ -414,7 +415,7 @@ class Model:
             out = torch.empty((count, self.info["num_stems"] * C, chunk), dtype=torch.float32, device=track.device)
         check(lib().msst_model_forward_chunks(self._h, _ptr(track), C, L, overlap, first, count, chunk_batch,
                                               SEPARATE_FIX_TAIL_PADDING if fix_tail_padding else 0,
-                                              _ptr(out) if count else None, _stream(stream)))
+                                              _ptr(out) if count else None, _stream(stream, self.device)))
         return out
 
     def forward_chunks_strided(self, track, overlap: float, first: int, stride: int, count: int,
@@ -427,14 +428,14 @@ class Model:
             out = torch.empty((count, self.info["num_stems"] * C, chunk), dtype=torch.float32, device=track.device)
         check(lib().msst_model_forward_chunks_strided(self._h, _ptr(track), C, L, overlap, first, stride, count,
                                                       chunk_batch, SEPARATE_FIX_TAIL_PADDING if fix_tail_padding
-                                                      else 0, _ptr(out) if count else None, _stream(stream)))
+                                                      else 0, _ptr(out) if count else None, _stream(stream, self.device)))
         return out
 
     def stitch_range(self, chunks, slot_ranks: int, slot_cap: int, channels: int, length: int, overlap: float,
                      begin: int, end: int, out, stream=None):
         """Stitch output samples [begin, end) into out [S, C, L] from chunk outputs in round-robin slots."""
         check(lib().msst_model_stitch_range(self._h, _ptr(chunks), slot_ranks, slot_cap, channels, length, overlap,
-                                            begin, end, _ptr(out), _stream(stream)))
+                                            begin, end, _ptr(out), _stream(stream, self.device)))
         return out
 
     def chunk_span(self, length: int, overlap: float, k: int, fix_tail_padding: bool = False):
@@ -455,7 +456,7 @@ class Model:
         if out is None:
             out = torch.empty((S, channels, length), dtype=torch.float32, device=chunks.device)
         check(lib().msst_model_stitch(self._h, _ptr(chunks.contiguous()), channels, length, overlap, _ptr(out),
-                                      _stream(stream)))
+                                      _stream(stream, self.device)))
         return out[0] if S == 1 else out
 
     def separate_host(self, track: np.ndarray, overlap: float = 0.0, chunk_batch: int = 0,

@@ -17,6 +17,11 @@
  *   - K (the reduction length) of every GEMM is a multiple of 64; hidden sizes
  *     of the Roformer (dim, heads*64, 4*dim) satisfy this, band inputs are padded.
  *   - head_dim is 64 on the Roformer path; msst_sdpa takes head_dim <= 64.
+ *   - devices: a msst_model runs on the GPU it was loaded on; its device buffers
+ *     must live on that GPU (or be managed memory), anything else is refused with
+ *     MSST_ERR_INVALID before a kernel runs.  Op-level calls run on the GPU of
+ *     their first operand.  Every call leaves the calling thread's current device
+ *     as it found it.
  */
 #ifndef MSST_B200_H
 #define MSST_B200_H

@@ -294,6 +294,44 @@ def test_two_devices_one_process(cuda, small_models):
     np.testing.assert_array_equal(ys[0], ys[1])
 
 
+def test_calls_keep_the_callers_device(cuda, small_models):
+    """Loading, running and freeing a model of GPU 1 leave the host thread's current
+    device (which PyTorch reads for its next allocation) at GPU 0."""
+    torch = cuda
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from msst_b200 import Model, synth
+
+    path, _, _, _ = small_models["mbr_small"]
+    torch.cuda.set_device(0)
+    m = Model(path, 1, "fp16")
+    assert torch.cuda.current_device() == 0
+    m.forward(torch.from_numpy(synth.make_audio(22050, 2, 4)[None]).to("cuda:1"))
+    assert torch.cuda.current_device() == 0
+    m.close()
+    assert torch.cuda.current_device() == 0
+
+
+def test_buffers_off_the_models_device_are_refused(cuda, small_models):
+    """Host memory, or memory of another GPU, handed to a model entry point is an
+    error returned before any kernel runs; the model keeps working afterwards."""
+    torch = cuda
+    from msst_b200 import Model, MsstError, synth
+
+    path, _, _, _ = small_models["mbr_small"]
+    m = Model(path, 0, "fp16")
+    audio = torch.from_numpy(synth.make_audio(22050, 2, 5)[None])
+    with pytest.raises(MsstError, match="model's GPU"):
+        m.forward(audio)  # host tensor
+    if torch.cuda.device_count() >= 2:
+        with pytest.raises(MsstError, match="model's GPU"):
+            m.forward(audio.to("cuda:1"))
+    y = m.forward(audio.cuda())
+    torch.cuda.synchronize()
+    assert np.isfinite(y.cpu().numpy()).all()
+    m.close()
+
+
 def test_device_error_flag_clear(cuda):
     from msst_b200 import device_error
 
