@@ -14,8 +14,9 @@
 //              also guarantees PV_w(j) has finished reading P_w
 //   warps 2-5  softmax of tile a, warps 6-9 softmax of tile b: one query row per
 //              thread; steady-state tiles take one pass over S in TMEM (exponent
-//              against the running reference max, which moves lazily: O in TMEM
-//              is rescaled only when the max grows by more than 2^8), P
+//              against the running reference max, which moves lazily: only a row
+//              sum above 4096 sends a warp through the exact two passes, which
+//              move the max and rescale O in TMEM), P
 //              written as packed 16-bit pairs into TMEM (the MMA's A operand);
 //              fully masked 32-column chunks are skipped per warp.  The epilogue
 //              divides by the row sum, applies the head gate and writes the
@@ -34,12 +35,20 @@ constexpr uint32_t kTileBytes = 128 * 64 * 2;   // one 128x64 16-bit tile
 constexpr size_t kAttnSmem = 1024 + 2 * kTileBytes + kKvStages * 2 * kTileBytes + 256;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColO = 256, kColP = 384;
-constexpr float kRescaleLog2 = 8.0f;  // lazy rescale threshold (log2 units)
+// A steady-state step exponentiates against the reference max without tracking
+// the row's maximum; its row sum bounds every P entry, so a sum above this bound
+// (or not finite) sends the row's warp through the exact passes.  4096 leaves P
+// far inside fp16's range and is never reached by a row whose scores stay at or
+// below the reference max (at most 128 entries of 1 per step).
+constexpr float kSumLimit = 4096.0f;
 // Of every 4 column pairs of an unmasked 32-column chunk, this many take their
 // exponentials from the FMA-pipe polynomial (poly_exp2x2) and the rest from the
-// MUFU unit, which is the busiest pipe of the softmax.
+// MUFU unit.  With the steady state's per-element max tracking gone, all-MUFU is
+// the fastest mix on both axes (fp16 and bf16: 3-5 % ahead of one pair in four,
+// whose extra FMA-pipe instructions now cost more issue slots than the MUFU
+// work they take over).
 #ifndef MSST_ATTN_POLY_PAIRS
-#define MSST_ATTN_POLY_PAIRS 1
+#define MSST_ATTN_POLY_PAIRS 0
 #endif
 constexpr int kPolyPairsPerQuad = MSST_ATTN_POLY_PAIRS;
 
@@ -89,8 +98,7 @@ __device__ __forceinline__ bool uses(const AttnParams& p, int w, int j) { return
 // chunks below `c_full` need no per-column mask (warp-uniform), the others mask
 // columns outside [klo, khi).
 //   kPass 0: row max of the valid scores -> mx
-//   kPass 1: P = exp2(s*c - mc) into smem, row sum, max of the exponent -> mx
-//   kPass 2: P = exp2(s*c - mc) into smem, row sum
+//   kPass 1, 2: P = exp2(s*c - mc) into TMEM, row sum
 // ---------------------------------------------------------------------------
 template <typename T, int kPass>
 __device__ __forceinline__ void process_chunk(const uint32_t (&r)[32], int ch, bool in_range, bool unmasked, int klo,
@@ -120,14 +128,9 @@ __device__ __forceinline__ void process_chunk(const uint32_t (&r)[32], int ch, b
 #pragma unroll
       for (int i = 0; i < 16; ++i) pk[i] = 0u;
     } else if (unmasked) {
-      float a0 = -INFINITY, a1 = -INFINITY;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const float2 a = __ffma2_rn(make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), c2, nm2);
-        if constexpr (kPass == 1) {
-          a0 = fmaxf(a0, a.x);
-          a1 = fmaxf(a1, a.y);
-        }
         float2 e;
         if ((i & 3) < kPolyPairsPerQuad) {
           e = poly_exp2x2(a);
@@ -138,17 +141,12 @@ __device__ __forceinline__ void process_chunk(const uint32_t (&r)[32], int ch, b
         sum2 = __fadd2_rn(sum2, e);
         pk[i] = pack2<T>(e.x, e.y);
       }
-      if constexpr (kPass == 1) mx = fmaxf(mx, fmaxf(a0, a1));
     } else {
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const int col = ch * 32 + 2 * i;
         const bool v0 = col >= klo && col < khi, v1 = col + 1 >= klo && col + 1 < khi;
         const float2 a = __ffma2_rn(make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), c2, nm2);
-        if constexpr (kPass == 1) {
-          if (v0) mx = fmaxf(mx, a.x);
-          if (v1) mx = fmaxf(mx, a.y);
-        }
         const float e0 = v0 ? fast_exp2(a.x) : 0.f, e1 = v1 ? fast_exp2(a.y) : 0.f;
         sum2 = __fadd2_rn(sum2, make_float2(e0, e1));
         pk[i] = pack2<T>(e0, e1);
@@ -167,7 +165,7 @@ __device__ __forceinline__ void process_chunk(const uint32_t (&r)[32], int ch, b
 // kFirst (with kPass 1): the reference max is not known yet; it is taken from the
 // first loaded chunk's valid scores (returned in m0), and the pass proceeds as a
 // steady-state pass against it (the caller falls back to the exact two passes if
-// a later chunk exceeds it by more than 2^8).
+// the row sum shows that a later chunk went far above it).
 // kBand: the row's window may start past chunk 0 (band axis); the time axis always
 // starts at chunk 0, where the first-chunk max is taken unconditionally.
 template <typename T, int kPass, bool kFirst = false, bool kBand = false>
@@ -432,10 +430,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           float2 sum2 = make_float2(0.f, 0.f);
           bool exact = false;
           if (!exact) {
-            // steady state: exponentiate against the current reference max in one pass and
-            // track how far above it the row went; a tile's first step takes its
-            // reference max from the first 32 columns
-            float amax = -INFINITY;
+            // steady state: exponentiate against the current reference max in one pass; a
+            // tile's first step takes its reference max from the first 32 columns.  The
+            // row sum bounds how far above the reference the row went.
+            float amax = -INFINITY;  // unused by the steady-state passes
             if (used == 0) {
               float m0 = -INFINITY;
               if (p.mode != 1)
@@ -447,7 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const float mc = (m == -INFINITY) ? 0.f : m * c;
               row_pass<T, 1>(sAddr, c_lo, c_hi, c_full, klo, khi, c, mc, amax, sum2, pAddr);
             }
-            if (__any_sync(0xffffffffu, amax > kRescaleLog2)) {
+            if (__any_sync(0xffffffffu, !(sum2.x + sum2.y <= kSumLimit))) {
               exact = true;
               sum2 = make_float2(0.f, 0.f);
               if (used == 0) m = -INFINITY;
@@ -456,8 +454,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (exact) {
             float mx = -INFINITY;
             row_pass<T, 0>(sAddr, c_lo, c_hi, c_full, klo, khi, c, 0.f, mx, sum2, pAddr);
-            // lazy rescale: move the reference max only when it grows by > 2^8
-            const bool grow = (mx > m) && ((m == -INFINITY) || (mx - m) * c > kRescaleLog2);
+            // move the reference max to the row's true max (O and l rescaled), so the
+            // following steady-state steps stay below the sum bound
+            const bool grow = mx > m;
             if (__any_sync(0xffffffffu, grow)) {
               const float m_new = grow ? mx : m;
               const float alpha = (m == -INFINITY) ? 0.f : fast_exp2((m - m_new) * c);
