@@ -450,14 +450,37 @@ __global__ void __launch_bounds__(256) band_input_kernel(BandInArgs a) {
   const int bt = blockIdx.x;
   const int b = bt / a.T, t = bt - b * a.T;
   const int C = a.C;
-  for (int c = 0; c < C; ++c) {
-    const float2* src = a.spec + ((long long)(b * C + c) * a.T + t) * a.nbins;
+  if (C <= 2 && a.nbins <= 5 * 256 && blockDim.x == 256) {
+    // up to stereo x 1280 bins: every load of the frame issued before the first use
+    float2 z[2][5];
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const float2* src = a.spec + ((long long)(b * C + min(c, C - 1)) * a.T + t) * a.nbins;
+#pragma unroll
+      for (int i = 0; i < 5; ++i) {
+        const int f = threadIdx.x + 256 * i;
+        z[c][i] = (c < C && f < a.nbins) ? __ldg(src + f) : make_float2(0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < 2; ++c)
+#pragma unroll
+      for (int i = 0; i < 5; ++i) {
+        const int f = threadIdx.x + 256 * i;
+        if (c < C && f < a.nbins)
+          *reinterpret_cast<float2*>(s_row + 2 * (f * C + c)) =
+              make_float2(z[c][i].x * a.spec_scale, z[c][i].y * a.spec_scale);
+      }
+  } else {
+    for (int c = 0; c < C; ++c) {
+      const float2* src = a.spec + ((long long)(b * C + c) * a.T + t) * a.nbins;
 #pragma unroll 4
-    for (int f = threadIdx.x; f < a.nbins; f += blockDim.x) {
-      float2 z = __ldg(src + f);
-      z.x *= a.spec_scale;
-      z.y *= a.spec_scale;
-      *reinterpret_cast<float2*>(s_row + 2 * (f * C + c)) = z;
+      for (int f = threadIdx.x; f < a.nbins; f += blockDim.x) {
+        float2 z = __ldg(src + f);
+        z.x *= a.spec_scale;
+        z.y *= a.spec_scale;
+        *reinterpret_cast<float2*>(s_row + 2 * (f * C + c)) = z;
+      }
     }
   }
   __syncthreads();
@@ -724,8 +747,36 @@ __global__ void __launch_bounds__(256)
   const int src0 = start + base - (int)a.border;
   if (whole && base >= 0 && base + n_fft <= a.chunk && src0 >= 0 && src0 + n_fft <= (int)a.L) {
     const float* s0 = a.track + (long long)c * a.L + src0;
+    // (a 16-byte-aligned track keeps the aligned-down first load inside it)
+    if ((n_fft & 3) == 0 &&
+        ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(win) |
+          reinterpret_cast<uintptr_t>(a.track)) & 15) == 0) {
+      // four samples per thread: the source run starts m floats past a 16-byte boundary,
+      // so each group is taken from two aligned float4 loads of the track (the second
+      // only where m > 0 and it stays inside the frame's own samples)
+      const int m = (int)((reinterpret_cast<uintptr_t>(s0) >> 2) & 3);
+      const float4* a4 = reinterpret_cast<const float4*>(s0 - m);
+      const float4* w4 = reinterpret_cast<const float4*>(win);
+      float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll 2
+      for (int g = threadIdx.x; 4 * g < n_fft; g += blockDim.x) {
+        const float4 w = __ldg(w4 + g);
+        float4 x;
+        if (m == 0) {
+          x = __ldg(a4 + g);
+        } else if (4 * g + 7 - m < n_fft) {
+          const float4 lo = __ldg(a4 + g), hi = __ldg(a4 + g + 1);
+          x = m == 1 ? make_float4(lo.y, lo.z, lo.w, hi.x)
+                     : (m == 2 ? make_float4(lo.z, lo.w, hi.x, hi.y) : make_float4(lo.w, hi.x, hi.y, hi.z));
+        } else {
+          x = make_float4(__ldg(s0 + 4 * g), __ldg(s0 + 4 * g + 1), __ldg(s0 + 4 * g + 2), __ldg(s0 + 4 * g + 3));
+        }
+        d4[g] = make_float4(x.x * w.x, x.y * w.y, x.z * w.z, x.w * w.w);
+      }
+    } else {
 #pragma unroll 8
-    for (int n = threadIdx.x; n < n_fft; n += blockDim.x) dst[n] = __ldg(s0 + n) * __ldg(win + n);
+      for (int n = threadIdx.x; n < n_fft; n += blockDim.x) dst[n] = __ldg(s0 + n) * __ldg(win + n);
+    }
   } else {
     for (int n = threadIdx.x; n < n_fft; n += blockDim.x) {
       int i = base + n;
@@ -775,6 +826,52 @@ __global__ void __launch_bounds__(256) stitch_kernel(StitchArgs a) {
       wsum += w;
     }
     a.out[(long long)r * a.L + p] = wsum > 1e-8f ? acc / wsum : acc;
+  }
+}
+
+// Four consecutive output samples per thread (float4 loads and stores).  Taken when
+// the chunk length, step, border, row length and the range start are multiples of 4:
+// the chunk boundaries then fall between groups, so the group's four samples share
+// one chunk range and every chunk slice is a 16-byte-aligned float4.  Same
+// arithmetic, in the same order, per sample as stitch_kernel.
+__global__ void __launch_bounds__(256) stitch4_kernel(StitchArgs a) {
+  const int r = blockIdx.y;
+  const int total = (int)a.total, border = (int)a.border;
+  const long long per_slot = (long long)a.rows * a.chunk;
+  const long long p = a.begin + 4 * ((long long)blockIdx.x * 256 + threadIdx.x);
+  if (p >= a.end) return;
+  const int q = (int)p + border;
+  const int k_hi = min(a.num_chunks - 1, q / a.step);
+  const int k_lo = q >= a.chunk ? (q - a.chunk) / a.step + 1 : 0;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f), wsum = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 2
+  for (int k = k_lo; k <= k_hi; ++k) {
+    const int start = k * a.step;
+    const int j = q - start;
+    const bool first = k == 0, last = start + a.chunk >= total;
+    const float4 w = make_float4(fade_weight(j, a.chunk, first, last), fade_weight(j + 1, a.chunk, first, last),
+                                 fade_weight(j + 2, a.chunk, first, last), fade_weight(j + 3, a.chunk, first, last));
+    const long long slot = (long long)(k % a.slot_ranks) * a.slot_cap + k / a.slot_ranks;
+    const float4 y = __ldg(reinterpret_cast<const float4*>(a.y + slot * per_slot + (long long)r * a.chunk + j));
+    acc.x += y.x * w.x;
+    acc.y += y.y * w.y;
+    acc.z += y.z * w.z;
+    acc.w += y.w * w.w;
+    wsum.x += w.x;
+    wsum.y += w.y;
+    wsum.z += w.z;
+    wsum.w += w.w;
+  }
+  float4 o;
+  o.x = wsum.x > 1e-8f ? acc.x / wsum.x : acc.x;
+  o.y = wsum.y > 1e-8f ? acc.y / wsum.y : acc.y;
+  o.z = wsum.z > 1e-8f ? acc.z / wsum.z : acc.z;
+  o.w = wsum.w > 1e-8f ? acc.w / wsum.w : acc.w;
+  if (p + 4 <= a.end) {
+    *reinterpret_cast<float4*>(a.out + (long long)r * a.L + p) = o;
+  } else {
+    const float ov[4] = {o.x, o.y, o.z, o.w};
+    for (int i = 0; i < 4 && p + i < a.end; ++i) a.out[(long long)r * a.L + p + i] = ov[i];
   }
 }
 
@@ -917,7 +1014,12 @@ cudaError_t launch_stitch(const StitchArgs& a, cudaStream_t s) {
   const long long n = a.end - a.begin;
   // every output sample written once; each chunk sample it covers read once (overlaps twice)
   LaunchScope scope("stitch", 0.0, (double)a.rows * n * 4.0 * 2.0, s);
-  stitch_kernel<<<dim3((unsigned)((n + 1023) / 1024), (unsigned)a.rows), 256, 0, s>>>(a);
+  const bool vec = a.chunk % 4 == 0 && a.step % 4 == 0 && a.border % 4 == 0 && a.L % 4 == 0 && a.begin % 4 == 0 &&
+                   (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.out) & 15) == 0;
+  if (vec)
+    stitch4_kernel<<<dim3((unsigned)((n + 1023) / 1024), (unsigned)a.rows), 256, 0, s>>>(a);
+  else
+    stitch_kernel<<<dim3((unsigned)((n + 1023) / 1024), (unsigned)a.rows), 256, 0, s>>>(a);
   return cudaGetLastError();
 }
 
