@@ -10,8 +10,10 @@ forward.  Random N(0, 0.02) weights (no checkpoints are reachable), written as
 a .csm file.  One step = one separation of the whole track; at N GPUs the same
 track is separated by N ranks (strong scaling): chunks dealt round-robin, each
 round's outputs sent to rank 0, stitched there as they become final
-(msst_b200.dist).  At N = 1 a second line item, `config1`, times BASELINE
-config 1 (the same model on a 68.5 s track, 13 chunks).
+(msst_b200.dist).  At N = 1 three more line items: `config1` times BASELINE
+config 1 (the same model on a 68.5 s track, 13 chunks), `config2` BASELINE
+config 2 (BS-Roformer D512x12, bf16, one forward of 8 chunks) and `config3`
+BASELINE config 3 (the axial attention alone, both axes).
 
   python bench.py [--gpus N --steps K --warmup W] [--impl reference] [--config 1|2]
 
@@ -410,6 +412,18 @@ def main():
                    "e2e": {"value": (n1 / SR) / (ms1e / 1e3), "unit": "audio-s/s", "ms_per_step": ms1e,
                            "h2d_bytes_per_step": int(tr1.nbytes), "d2h_bytes_per_step": int(S * tr1.nbytes)}}
 
+    # ---- BASELINE configs 2 (BS-Roformer D512x12 bf16) and 3 (attention alone) on one GPU
+    config2 = config3 = None
+    if world == 1 and args.samples == TRACK_SAMPLES and args.config == 1:
+        del t1, o1
+        res3 = attention_tflops(args.steps, args.warmup)
+        burst = peaks()[0]
+        config3 = {"workload": "BASELINE config 3: axial attention alone, bf16, q/k/v ~ N(0, 1), scale 1/8; "
+                               "B = 4 chunks, T = 801, F = 62, 8 heads x 64",
+                   "time_axis": res3["time"], "band_axis": res3["band"],
+                   "frac_of_burst_peak": {k: v["tflops"] / burst for k, v in res3.items()}}
+        config2 = run_config2(args.steps, args.warmup, timed)
+
     result = None
     if rank == 0:
         pk = peaks()
@@ -445,6 +459,10 @@ def main():
             result["phases"] = phases
         if config1:
             result["config1"] = config1
+        if config2:
+            result["config2"] = config2
+        if config3:
+            result["config3"] = config3
         if not args.no_cpu_baseline and world == 1:
             c = cpu_sample(cfg, args.config)
             per_chunk = c["front_s"] + cfg["depth"] * c["block_s"] + c["back_s"]
@@ -462,16 +480,13 @@ def main():
         emit(out, result)
 
 
-def run_micro_attention(args):
-    """BASELINE config 3: axial attention alone, bf16, q/k/v ~ N(0, 1), scale 1/8, non-causal;
-    time axis B' = 4 x 62 sequences of 801, band axis B' = 4 x 801 sequences of 62 (8 heads x 64).
-    Ours: msst_attention on one fused QKV buffer (RoPE lives in the QKV GEMM epilogue, not in
-    this kernel).  Reference: its ops::scaled_dot_product_attention (oracle/_ref) on the same
-    shapes in fp32 (TF32 GEMMs) and fp16-value mode, device time per call."""
+def attention_tflops(steps, warmup):
+    """BASELINE config 3 through msst_attention: bf16 q/k/v ~ N(0, 1) in one fused QKV buffer
+    (B = 4 chunks, T = 801, F = 62, 8 heads x 64, scale 1/8); device time per call on the
+    current stream, both axes.  The QKV buffer (950 MB) is larger than L2."""
     import torch
     from msst_b200 import ops
 
-    torch.cuda.set_device(0)
     B, T, F, H = 4, 801, 62, 8
     M = B * T * F
     g = torch.Generator(device="cuda").manual_seed(0)
@@ -479,12 +494,12 @@ def run_micro_attention(args):
     res = {}
     for axis, nseq, n in (("time", B * F, T), ("band", B * T, F)):
         fn = lambda: ops.attention(qkv, B, T, F, H, axis, 0.125)
-        for _ in range(max(3, args.warmup)):
+        for _ in range(max(3, warmup)):
             fn()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
         s.record()
-        iters = max(5, args.steps)
+        iters = max(5, steps)
         for _ in range(iters):
             fn()
         e.record()
@@ -493,6 +508,56 @@ def run_micro_attention(args):
         flop = 4.0 * nseq * H * n * n * 64
         res[axis] = {"sequences": nseq, "seq_len": n, "gflop": flop / 1e9, "ms": ms,
                      "tflops": flop / (ms * 1e-3) / 1e12}
+    del qkv
+    return res
+
+
+def run_config2(steps, warmup, timed):
+    """BASELINE config 2 on one GPU: BS-Roformer D512x12, bf16 operands, one forward of 8
+    seeded 352800-sample stereo chunks (64 audio-seconds), device-resident and end to end
+    (pinned host chunks up, stems down, inside the timed region)."""
+    import torch
+    from msst_b200 import Model, synth
+
+    cfg2, prec2, desc2 = model_config(2)
+    m2 = Model(model_file(cfg2, 2, 0, 1, None), torch.cuda.current_device(), prec2)
+    nb = 8
+    host = np.stack([synth.make_audio(CHUNK, 2, 100 + i) for i in range(nb)])
+    audio = torch.from_numpy(host).cuda()
+    fwd = lambda: m2.forward(audio)
+    for _ in range(max(2, warmup)):
+        fwd()
+    ms = timed(fwd, steps)
+    pin_in = torch.from_numpy(host).pin_memory()
+    pin_out = torch.empty(tuple(fwd().shape), dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        y = m2.forward(pin_in.cuda(non_blocking=True))
+        pin_out.copy_(y, non_blocking=True)
+
+    e2e_step()
+    ms_e = timed(e2e_step, steps)
+    torch.cuda.synchronize()
+    assert np.isfinite(pin_out.numpy()).all()
+    m2.close()
+    sec = nb * CHUNK / SR
+    return {"workload": f"BASELINE config 2: {desc2}; one forward of {nb} stereo chunks of {CHUNK} samples "
+                        f"({sec:.0f} audio-s)",
+            "value": sec / (ms / 1e3), "unit": "audio-s/s", "ms_per_step": ms,
+            "e2e": {"value": sec / (ms_e / 1e3), "unit": "audio-s/s", "ms_per_step": ms_e,
+                    "h2d_bytes_per_step": int(host.nbytes), "d2h_bytes_per_step": int(pin_out.numel() * 4)}}
+
+
+def run_micro_attention(args):
+    """BASELINE config 3: axial attention alone, bf16, q/k/v ~ N(0, 1), scale 1/8, non-causal;
+    time axis B' = 4 x 62 sequences of 801, band axis B' = 4 x 801 sequences of 62 (8 heads x 64).
+    Ours: msst_attention on one fused QKV buffer (RoPE lives in the QKV GEMM epilogue, not in
+    this kernel).  Reference: its ops::scaled_dot_product_attention (oracle/_ref) on the same
+    shapes in fp32 (TF32 GEMMs) and fp16-value mode, device time per call."""
+    import torch
+
+    torch.cuda.set_device(0)
+    res = attention_tflops(args.steps, args.warmup)
     burst, sustained, hbm, src = peaks()
     out = {"metric": "attention TFLOP/s (BASELINE config 3)", "value": res["time"]["tflops"], "unit": "TFLOP/s",
            "higher_is_better": True, "n_gpus": 1, "dtype": "bf16", "data": "synthetic",
