@@ -108,18 +108,20 @@ def _model(tmp_path_factory, kind, cfg_kw, seed):
     return path, cfg, sd
 
 
+@pytest.mark.parametrize("dim,T", [(128, 40), (384, 801), (512, 801)])
 @pytest.mark.parametrize("axis", ["time", "band"])
-def test_blocks_compose_to_transformer(cuda, tmp_path_factory, axis):
+def test_blocks_compose_to_transformer(cuda, tmp_path_factory, axis, dim, T):
     """BS-Roformer (no per-transformer final norm): attention + feed-forward blocks
-    over all layers are bit-identical to msst_model_transformer."""
+    over all layers are bit-identical to msst_model_transformer, also at T = 801
+    (388 row tiles: several per CTA of the persistent kernels)."""
     torch = cuda
     from msst_b200 import Model
 
-    kw = dict(depth=1, dim=128, time_transformer_depth=2, freq_transformer_depth=2)
+    kw = dict(depth=1, dim=dim, time_transformer_depth=2, freq_transformer_depth=2)
     path, cfg, _ = _model(tmp_path_factory, "bsr", kw, 3)
     m = Model(path, 0, "bf16")
     g = torch.Generator(device="cuda").manual_seed(1)
-    x = torch.randn(1, 40, m.info["num_bands"], m.info["dim"], device="cuda", generator=g)
+    x = torch.randn(1, T, m.info["num_bands"], m.info["dim"], device="cuda", generator=g)
     ref = m.transformer(0, axis, x.clone())
     y = x.clone()
     layers = cfg["time_transformer_depth"] if axis == "time" else cfg["freq_transformer_depth"]
