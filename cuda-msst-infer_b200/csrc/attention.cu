@@ -305,14 +305,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       int pc = 0, kvc = 0;
       uint32_t pcnt[2] = {0, 0};  // P tiles consumed per query tile (phase of p_full)
       bool ok = true;
+      // Shared-memory descriptors are built once per operand tile; each 16-element
+      // k-step advances the start-address field (bytes >> 4) by a constant: 32 B along
+      // a K-major row (S), 16 rows of 128 B down the MN-major V tile (P.V).  The issuing
+      // thread is on the kernel's critical path, so its per-MMA work is kept minimal.
+      const uint64_t dq0 = sw128_desc(smem_u32(sQ), 16, 1024);
+      const uint64_t dkv0 = sw128_desc(smem_u32(sKV), 16, 1024);
+      const uint64_t dv0 = sw128_desc(smem_u32(sKV + kTileBytes), kTileBytes, 1024);
       auto issue_s = [&](int w, int st) {
-        const uint32_t qaddr = smem_u32(sQ + w * kTileBytes);
-        const uint32_t kaddr = smem_u32(sKV + st * 2 * kTileBytes);
+        const uint64_t dq = dq0 + (uint64_t)((w * kTileBytes) >> 4);
+        const uint64_t dk = dkv0 + (uint64_t)((st * 2 * kTileBytes) >> 4);
         const uint32_t dS = tmem + kColS + (uint32_t)(w * 128);
+        umma_f16_ss(dS, dq, dk, idesc_s, 0u);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          umma_f16_ss(dS, sw128_desc(qaddr + kk * 32, 16, 1024), sw128_desc(kaddr + kk * 32, 16, 1024), idesc_s,
-                      kk > 0 ? 1u : 0u);
+        for (int kk = 1; kk < 4; ++kk) umma_f16_ss(dS, dq + 2 * kk, dk + 2 * kk, idesc_s, 1u);
         umma_commit(&s_full[w]);
       };
       auto issue_pv = [&](int w, int st, bool first) -> bool {
@@ -320,12 +326,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++pcnt[w];
         tc_fence_after();
         const uint32_t paddr = tmem + kColP + (uint32_t)(w * 64);
-        const uint32_t vaddr = smem_u32(sKV + st * 2 * kTileBytes + kTileBytes);
+        const uint64_t dv = dv0 + (uint64_t)((st * 2 * kTileBytes) >> 4);
         const uint32_t dO = tmem + kColO + (uint32_t)(w * 64);
+        umma_f16_ts(dO, paddr, dv, idesc_o, first ? 0u : 1u);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_f16_ts(dO, paddr + (uint32_t)(kk * 8),
-                      sw128_desc(vaddr + kk * 2048, kTileBytes, 1024), idesc_o, (first && kk == 0) ? 0u : 1u);
+        for (int kk = 1; kk < 8; ++kk) umma_f16_ts(dO, paddr + (uint32_t)(kk * 8), dv + 128 * kk, idesc_o, 1u);
         return true;
       };
       for (int item = blockIdx.x; ok && item < p.total_items; item += gridDim.x, ++pc) {
