@@ -248,6 +248,31 @@ def bench_shapes(L, out_dir):
     return summary
 
 
+def config3(L, out_dir):
+    """config3_ref.npz: the reference's ops::scaled_dot_product_attention at BASELINE config 3's
+    shape (both axes, fp32 = TF32 QK^T mode and fp16-value mode) on the seeded bf16 inputs of
+    op_cases.config3_inputs, kept for the sampled (sequence, head) pairs as float16."""
+    c = op_cases.CONFIG3
+    arrays, summary = {}, {}
+    for axis in ("time", "band"):
+        q, k, v = op_cases.config3_inputs(axis)
+        S, H, N, D = q.shape
+        seq, head = op_cases.config3_samples(axis)
+        outs = {}
+        for fp16 in (0, 1):
+            out = np.zeros(q.size, np.float32)
+            check(L.refh_sdpa(P(q), P(k), P(v), S, H, N, D, c["scale"], fp16, P(out)), L)
+            out = out.reshape(S, H, N, D)
+            tag = "fp16" if fp16 else "fp32"
+            outs[tag] = out[seq, head]
+            arrays[f"{axis}_{tag}"] = outs[tag].astype(np.float16)
+            print("config3", axis, tag, flush=True)
+        summary[axis] = dict(sequences=S, seq_len=N, sampled=len(seq),
+                             fp16_vs_fp32_rel_l2=rel_l2(outs["fp16"], outs["fp32"]))
+    np.savez_compressed(os.path.join(out_dir, "config3_ref.npz"), meta=json.dumps(c), **arrays)
+    return summary
+
+
 def _merge_summary(out_dir, key, value):
     path = os.path.join(out_dir, "pin_summary.json")
     summary = json.load(open(path)) if os.path.exists(path) else {}
@@ -261,7 +286,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", required=True)
     ap.add_argument("--full", action="store_true", help="also pin config 0 at full size (summary only)")
-    ap.add_argument("--only", choices=["all", "htdemucs-ops", "options", "bench-shapes"], default="all",
+    ap.add_argument("--only", choices=["all", "htdemucs-ops", "options", "bench-shapes", "config3"], default="all",
                     help="write only that group of fixtures and merge its pin summary")
     args = ap.parse_args()
     os.makedirs(args.out, exist_ok=True)
@@ -272,6 +297,8 @@ def main():
         return _merge_summary(args.out, "options", option_models(L, args.out))
     if args.only == "bench-shapes":
         return _merge_summary(args.out, "bench_shapes", bench_shapes(L, args.out))
+    if args.only == "config3":
+        return _merge_summary(args.out, "config3", config3(L, args.out))
     tmp = tempfile.mkdtemp()
     summary = {}
     ll = ctypes.c_longlong
@@ -369,6 +396,7 @@ def main():
     summary["linear_gelu"] = rel_l2(oracle.linear(x, w, b, "gelu"), ops["lin_gelu_fp32"])
     np.savez_compressed(os.path.join(args.out, "ops.npz"), **ops)
     summary["htdemucs_ops"] = htdemucs_ops(L, args.out)
+    summary["config3"] = config3(L, args.out)
 
     # ---------------- full-size config 0 (summary only; arrays are too large) ----------------
     if args.full:

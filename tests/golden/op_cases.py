@@ -49,3 +49,36 @@ def ln_inputs(name: str):
     g = (1.0 + 0.1 * rng.standard_normal(D)).astype(np.float32)
     b = (0.1 * rng.standard_normal(D)).astype(np.float32)
     return x, g, b
+
+
+# the axial attention alone at the benchmarked shape, bf16 q/k/v ~ N(0, 1),
+# scale 1/8, B = 4 chunks, T = 801 frames, F = 62 bands, 8 heads x 64.  The time axis is B*F
+# sequences of T tokens, the band axis B*T sequences of F tokens.  The fixture
+# (config3_ref.npz) holds the reference's outputs for a seeded sample of (sequence, head)
+# pairs, stored as float16.
+CONFIG3 = dict(B=4, T=801, F=62, H=8, D=64, scale=0.125, seeds={"time": 61, "band": 62},
+               samples={"time": 8, "band": 64}, sample_seed=63)
+
+
+def bf16_values(a: np.ndarray) -> np.ndarray:
+    """fp32 array rounded to the nearest bf16 value (ties to even), kept in fp32."""
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32)
+    r = ((u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))) & np.uint32(0xFFFF0000)).astype(np.uint32)
+    return r.view(np.float32)
+
+
+def config3_inputs(axis: str):
+    """q, k, v [S, H, N, D] fp32 holding bf16 values, S sequences of N tokens on `axis`."""
+    c = CONFIG3
+    S, N = (c["B"] * c["F"], c["T"]) if axis == "time" else (c["B"] * c["T"], c["F"])
+    rng = np.random.default_rng(c["seeds"][axis])
+    return tuple(bf16_values(rng.standard_normal((S, c["H"], N, c["D"]), dtype=np.float32)) for _ in range(3))
+
+
+def config3_samples(axis: str):
+    """The sampled (sequence, head) pairs of the fixture, sorted."""
+    c = CONFIG3
+    S = c["B"] * c["F"] if axis == "time" else c["B"] * c["T"]
+    rng = np.random.default_rng(c["sample_seed"] + (0 if axis == "time" else 1))
+    flat = np.sort(rng.choice(S * c["H"], c["samples"][axis], replace=False))
+    return flat // c["H"], flat % c["H"]

@@ -1,7 +1,9 @@
 """GPU parity at the benchmarked shapes against the reference engine run on a B200
 (tests/golden/cfg{1,2}_ref.npz, written by tests/golden/make_golden.py
 --only bench-shapes from oracle/_ref; they hold seeded windows of the output
-waveforms and rows of the fp32 masks, the full arrays being hundreds of MB).
+waveforms and rows of the fp32 masks, the full arrays being hundreds of MB;
+tests/golden/config3_ref.npz, written by --only config3, the reference attention's
+output for sampled sequence-heads).
 
 * MelBandRoformer D384 x 6, fp16, the bench's own weights and
   68.5 s track, separated exactly as bench.py times it (overlap 0.25, 4 chunks per
@@ -12,8 +14,13 @@ waveforms and rows of the fp32 masks, the full arrays being hundreds of MB).
   forward of 8 chunks of 352800 samples.  Reference graph:
   src/model_bs_roformer.cu:420-609.
 
+* the axial attention alone at B = 4 chunks, T = 801, F = 62,
+  8 heads x 64, bf16 q/k/v ~ N(0, 1), both axes.  Reference op:
+  src/ops_attention.cu:522-599.
+
 Bars: output waveforms >= 45 dB SNR against the reference's fp32 and fp16 runs;
-masks within the stated relative L2 of the reference's fp32 masks.
+masks within the stated relative L2 of the reference's fp32 masks; attention
+outputs within 1e-2 relative L2.
 """
 from __future__ import annotations
 
@@ -94,3 +101,48 @@ def test_config2_forward_vs_reference(cuda, tmp_path_factory):
             ref_fp16_vs_ref_fp32_snr_db=snr_db(z["out_fp16"], z["out_fp32"]))
     assert s32 >= SNR_MIN and s16 >= SNR_MIN
     assert e32 < MASK_TOL["bf16"]
+
+
+@pytest.mark.parametrize("axis", ["time", "band"])
+def test_config3_attention_vs_reference(cuda, axis):
+    """BASELINE config 3 at its own shape (B = 4 chunks, T = 801, F = 62, 8 heads x 64, bf16
+    q/k/v ~ N(0, 1), scale 1/8): msst_attention against the reference's
+    ops::scaled_dot_product_attention (src/ops_attention.cu:522-599) on the same seeded inputs,
+    in its fp32 (TF32 QK^T) and fp16-value modes, on the fixture's sampled (sequence, head)
+    pairs.  The bar, 1e-2 relative L2, is bf16's output rounding with margin (the reference's
+    two modes differ by about 5e-4)."""
+    torch = cuda
+    import op_cases
+    from msst_b200 import ops
+
+    z, meta = golden("config3_ref.npz")
+    c = op_cases.CONFIG3
+    B, T, F, H, D = c["B"], c["T"], c["F"], c["H"], c["D"]
+    q, k, v = op_cases.config3_inputs(axis)
+
+    def token_major(a):
+        # [S, H, N, D] -> [B*T*F, H*D] on the token grid (sequence s = b*F + f on the time axis,
+        # b*T + t on the band axis)
+        t = torch.from_numpy(a).cuda()
+        if axis == "time":
+            t = t.view(B, F, H, T, D).permute(0, 3, 1, 2, 4)
+        else:
+            t = t.view(B, T, H, F, D).permute(0, 1, 3, 2, 4)
+        return t.reshape(B * T * F, H * D).to(torch.bfloat16)
+
+    qkv = torch.cat([token_major(a) for a in (q, k, v)], dim=1).contiguous()
+    del q, k, v
+    y = ops.attention(qkv, B, T, F, H, axis, c["scale"]).float()
+    torch.cuda.synchronize()
+    seq, head = op_cases.config3_samples(axis)
+    N = T if axis == "time" else F
+    if axis == "time":
+        y = y.view(B, T, F, H, D).permute(0, 2, 3, 1, 4).reshape(B * F, H, T, D)
+    else:
+        y = y.view(B, T, F, H, D).permute(0, 1, 3, 2, 4).reshape(B * T, H, F, D)
+    ours = y[torch.from_numpy(seq).cuda(), torch.from_numpy(head).cuda()].cpu().numpy()
+    assert ours.shape == (len(seq), N, D)
+    e32 = rel_l2(ours, z[f"{axis}_fp32"].astype(np.float32))
+    e16 = rel_l2(ours, z[f"{axis}_fp16"].astype(np.float32))
+    _report(f"config3 {axis}", rel_l2_vs_ref_fp32=e32, rel_l2_vs_ref_fp16=e16)
+    assert e32 < 1e-2 and e16 < 1e-2
