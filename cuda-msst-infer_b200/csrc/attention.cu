@@ -53,43 +53,95 @@ constexpr float kSumLimit = 4096.0f;
 constexpr int kPolyPairsPerQuad = MSST_ATTN_POLY_PAIRS;
 
 struct PairGeom {
-  int head;
   int steps;        // K/V tiles streamed for this pair
   bool has_b;       // second query tile present
-  // time axis
-  int b, f, t0a;    // t0 of tile a; tile b starts at t0a + 128
+  bool split;       // time axis: the two tiles belong to different (sequence, head) units,
+                    // each with its own K/V stream (tile w uses the steps j with j % 2 == w)
+  // time axis: unit of each tile (head, chunk b, band f) and its first query row
+  int head, b, f, t0a;
+  int head2, b2, f2, t0b;
   // band axis
   int r0a, rows;    // first sequence of tile a; sequences per packed tile
 };
 
+// Time axis (modes 0, 2): a unit is one (sequence, head), u = (b * F + f) * heads + head,
+// with q_tiles query tiles.  Its tiles go in pairs (2 qp, 2 qp + 1) sharing every K/V
+// tile.  When q_tiles is odd the last tile of each unit is a short tail (33 rows of an
+// 801-frame sequence); the tails of units 2g and 2g + 1 run as one pair, each with its
+// own K/V stream, so no query tile runs without a partner.  Items are ordered by unit
+// group g: the full pairs of unit 2g, those of unit 2g + 1, then their tail pair.
+__device__ __forceinline__ void time_unit(const AttnParams& p, int u, int& head, int& b, int& f) {
+  head = u % p.heads;
+  const int s = u / p.heads;
+  b = s / p.F;
+  f = s - b * p.F;
+}
+
+template <bool kBand>
 __device__ __forceinline__ PairGeom pair_geom(const AttnParams& p, int item) {
   PairGeom g;
-  if (p.mode != 1) {
-    const int pairs = (p.q_tiles + 1) >> 1;
-    const int qp = item % pairs;
-    const int sh = item / pairs;
-    g.head = sh % p.heads;
-    const int s = sh / p.heads;
-    g.b = s / p.F;
-    g.f = s - g.b * p.F;
-    g.t0a = qp * 256;
-    g.has_b = 2 * qp + 1 < p.q_tiles;
+  g.split = false;
+  if constexpr (!kBand) {
+    const int full = p.q_tiles >> 1;       // full pairs per unit
+    const int tail = p.q_tiles & 1;        // a tail tile per unit
+    const int per_group = 2 * full + tail;
+    const int units = p.units;
+    int u0, kind;                          // kind < full: full pair `kind` of unit u0; else the tail
+    const int pg = item / per_group, r = item - pg * per_group;
+    if (2 * pg + 1 < units || units % 2 == 0) {
+      u0 = 2 * pg + (r < 2 * full ? r / full : 0);
+      kind = r < 2 * full ? r % full : full;
+    } else {
+      // the last unit of an odd count, alone in its group: its full pairs, then its tail
+      u0 = 2 * pg;
+      kind = r;
+    }
+    time_unit(p, u0, g.head, g.b, g.f);
     g.steps = p.kv_tiles;
+    if (kind < full) {
+      g.t0a = kind * 256;
+      g.has_b = true;
+      g.head2 = g.head;
+      g.b2 = g.b;
+      g.f2 = g.f;
+      g.t0b = g.t0a + 128;
+    } else {
+      g.t0a = g.t0b = full * 256;
+      g.has_b = u0 + 1 < units && u0 % 2 == 0;
+      if (g.has_b) {
+        g.split = true;
+        g.steps = 2 * p.kv_tiles;
+        time_unit(p, u0 + 1, g.head2, g.b2, g.f2);
+      } else {
+        g.head2 = g.head;
+        g.b2 = g.b;
+        g.f2 = g.f;
+      }
+    }
     g.r0a = g.rows = 0;
   } else {
-    g.head = item % p.heads;
+    g.head = g.head2 = item % p.heads;
     const int pr = item / p.heads;
     g.rows = p.seqs_per_tile;
     g.r0a = 2 * pr * g.rows;
     g.has_b = 2 * pr + 1 < p.q_tiles;
     g.steps = g.has_b ? 2 : 1;
-    g.b = g.f = g.t0a = 0;
+    g.b = g.f = g.t0a = g.b2 = g.f2 = g.t0b = 0;
   }
   return g;
 }
 
 // Does query tile w (0 = a, 1 = b) consume K/V step j?
-__device__ __forceinline__ bool uses(const AttnParams& p, int w, int j) { return p.mode != 1 ? true : (j == w); }
+template <bool kBand>
+__device__ __forceinline__ bool uses(const PairGeom& g, int w, int j) {
+  if constexpr (kBand)
+    return j == w;
+  else
+    return g.split ? (j & 1) == w : true;
+}
+
+// K/V tile index of step j of a time-axis pair
+__device__ __forceinline__ int kv_block(const PairGeom& g, int j) { return g.split ? (j >> 1) : j; }
 
 // ---------------------------------------------------------------------------
 // One softmax pass over a 128-column S row held in TMEM (4 chunks of 32
@@ -204,7 +256,8 @@ __device__ __forceinline__ void row_pass(uint32_t sAddr, int c_lo, int c_hi, int
   process_chunk<T, kPass>(rb, 3, in3, c_lo <= 3 && 3 < c_full, klo, khi, c2, nm2, mx, sum2, pAddr);
 }
 
-template <typename T>
+// kBand: the band-axis schedule (mode 1); otherwise the time-axis one (modes 0, 2).
+template <typename T, bool kBand>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_kernel(const __grid_constant__ CUtensorMap qkv, const __grid_constant__ CUtensorMap kmap,
                      const __grid_constant__ CUtensorMap vmap, const __grid_constant__ AttnParams p) {
@@ -259,13 +312,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       int pc = 0, kvc = 0;
       bool ok = true;
       for (int item = blockIdx.x; ok && item < p.total_items; item += gridDim.x, ++pc) {
-        const PairGeom g = pair_geom(p, item);
+        const PairGeom g = pair_geom<kBand>(p, item);
         if (!mbar_wait<false>(q_empty, (pc & 1) ^ 1, kErrTimeoutAttnQ, abort_flag)) break;
         mbar_arrive_expect_tx(q_full, (g.has_b ? 2 : 1) * kTileBytes);
         const int xq = g.head * 64;
-        if (p.mode != 1) {
+        if constexpr (!kBand) {
           tma_load_4d(sQ, &qkv, q_full, xq, g.f, g.t0a, g.b);
-          if (g.has_b) tma_load_4d(sQ + kTileBytes, &qkv, q_full, xq, g.f, g.t0a + 128, g.b);
+          if (g.has_b) tma_load_4d(sQ + kTileBytes, &qkv, q_full, g.head2 * 64, g.f2, g.t0b, g.b2);
         } else {
           // one box of `slot` rows per sequence, at its aligned slot of the tile
           const uint32_t slot_bytes = (128u / (uint32_t)g.rows) * 128u;
@@ -275,6 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                           (g.r0a + w * g.rows + k) * p.seq_len, 0, 0);
         }
         const int xk = p.k_col + g.head * 64, xv = p.v_col + g.head * 64;
+        const int xk2 = p.k_col + g.head2 * 64, xv2 = p.v_col + g.head2 * 64;
         for (int j = 0; j < g.steps; ++j, ++kvc) {
           const int st = kvc % kKvStages;
           if (!mbar_wait<false>(&kv_empty[st], ((kvc / kKvStages) & 1) ^ 1, kErrTimeoutAttnKV, abort_flag)) {
@@ -283,9 +337,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           mbar_arrive_expect_tx(&kv_full[st], 2 * kTileBytes);
           uint8_t* dk = sKV + st * 2 * kTileBytes;
-          if (p.mode != 1) {
-            tma_load_4d(dk, &kmap, &kv_full[st], xk, g.f, j * 128, g.b);
-            tma_load_4d(dk + kTileBytes, &vmap, &kv_full[st], xv, g.f, j * 128, g.b);
+          if constexpr (!kBand) {
+            // a split pair's odd steps stream the second unit's K/V
+            const bool second = g.split && (j & 1);
+            const int kb = kv_block(g, j) * 128;
+            tma_load_4d(dk, &kmap, &kv_full[st], second ? xk2 : xk, second ? g.f2 : g.f, kb, second ? g.b2 : g.b);
+            tma_load_4d(dk + kTileBytes, &vmap, &kv_full[st], second ? xv2 : xv, second ? g.f2 : g.f, kb,
+                        second ? g.b2 : g.b);
           } else {
             const uint32_t slot_bytes = (128u / (uint32_t)g.rows) * 128u;
             for (int k = 0; k < g.rows; ++k) {
@@ -334,7 +392,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         return true;
       };
       for (int item = blockIdx.x; ok && item < p.total_items; item += gridDim.x, ++pc) {
-        const PairGeom g = pair_geom(p, item);
+        const PairGeom g = pair_geom<kBand>(p, item);
         const int nw = g.has_b ? 2 : 1;
         if (!mbar_wait<false>(q_full, pc & 1, kErrTimeoutAttnQ, abort_flag)) break;
         tc_fence_after();
@@ -348,14 +406,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           for (int w = 0; w < nw; ++w) {
-            if (!uses(p, w, j)) continue;
+            if (!uses<kBand>(g, w, j)) continue;
             if (last_used[w] >= 0) {
               if (!issue_pv(w, last_used[w], used_count[w] == 1)) {
                 ok = false;
                 break;
               }
               // the previous K/V stage is free once the last tile using it has issued its PV
-              if (w == nw - 1 || p.mode == 1) umma_commit(&kv_empty[last_used[w]]);
+              if (w == nw - 1 || kBand || g.split) umma_commit(&kv_empty[last_used[w]]);
             }
             issue_s(w, st);
             last_used[w] = st;
@@ -369,7 +427,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          if (w == nw - 1 || p.mode == 1) umma_commit(&kv_empty[last_used[w]]);
+          if (w == nw - 1 || kBand || g.split) umma_commit(&kv_empty[last_used[w]]);
           umma_commit(&o_done[w]);
         }
         kvc += g.steps;
@@ -388,16 +446,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t scnt = 0, ocnt = 0;
     bool ok = true;
     for (int item = blockIdx.x; ok && item < p.total_items; item += gridDim.x) {
-      const PairGeom g = pair_geom(p, item);
+      const PairGeom g = pair_geom<kBand>(p, item);
       if (w == 1 && !g.has_b) continue;
       // rows of this thread / warp
       bool valid;
       long long token;
       int lo = 0, hi_seq = 0;
-      if (p.mode != 1) {
-        const int t = g.t0a + w * 128 + row;
+      if constexpr (!kBand) {
+        const int t = (w == 0 ? g.t0a : g.t0b) + row;
         valid = t < p.T;
-        token = ((long long)g.b * p.T + t) * p.F + g.f;
+        token = ((long long)(w == 0 ? g.b : g.b2) * p.T + t) * p.F + (w == 0 ? g.f : g.f2);
       } else {
         const int slot = 128 / g.rows;
         const int k = row / slot, rr = row - k * slot;
@@ -411,7 +469,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float m = -INFINITY, l = 0.f;
       int used = 0;
       for (int j = 0; j < g.steps; ++j) {
-        if (!uses(p, w, j)) continue;
+        if (!uses<kBand>(g, w, j)) continue;
         if (!mbar_wait<false>(&s_full[w], scnt & 1, kErrTimeoutAttnS, abort_flag)) {
           ok = false;
           break;
@@ -420,9 +478,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         // valid key columns [klo, khi) of this tile for this row; warp-uniform chunk range
         int klo, khi;
-        if (p.mode != 1) {
+        if constexpr (!kBand) {
           klo = 0;
-          khi = min(128, p.kv_len - j * 128);
+          khi = min(128, p.kv_len - kv_block(g, j) * 128);
         } else {
           klo = lo;
           khi = hi_seq;
@@ -441,7 +499,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             float amax = -INFINITY;  // unused by the steady-state passes
             if (used == 0) {
               float m0 = -INFINITY;
-              if (p.mode != 1)
+              if constexpr (!kBand)
                 row_pass<T, 1, true>(sAddr, c_lo, c_hi, c_full, klo, khi, c, 0.f, amax, sum2, pAddr, &m0);
               else
                 row_pass<T, 1, true, true>(sAddr, c_lo, c_hi, c_full, klo, khi, c, 0.f, amax, sum2, pAddr, &m0);
@@ -499,8 +557,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       if (warp_active) {
         float scale = l > 0.f ? 1.f / l : 0.f;
-        if (valid && p.gates != nullptr) scale *= __ldg(p.gates + token * p.heads + g.head);
-        uint4* out = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.out) + token * p.out_ld + g.head * 64);
+        const int head = w == 0 ? g.head : g.head2;
+        if (valid && p.gates != nullptr) scale *= __ldg(p.gates + token * p.heads + head);
+        uint4* out = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.out) + token * p.out_ld + head * 64);
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           uint32_t r[32];
@@ -533,8 +592,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <typename T>
 cudaError_t launch_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const AttnParams& p,
                      int num_sms, cudaStream_t s) {
-  static std::atomic<unsigned long long> configured{0};
-  cudaError_t e = ensure_smem_limit(attention_kernel<T>, (int)kAttnSmem, configured);
+  static std::atomic<unsigned long long> configured[2];
+  const bool band = p.mode == 1;
+  cudaError_t e = ensure_smem_limit(band ? attention_kernel<T, true> : attention_kernel<T, false>, (int)kAttnSmem,
+                                    configured[band ? 1 : 0]);
   if (e != cudaSuccess) return e;
 
   const int grid = p.total_items < num_sms ? p.total_items : num_sms;
@@ -548,7 +609,10 @@ cudaError_t launch_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtenso
   const double bytes = (2.0 * qrows + 2.0 * krows) * d * sizeof(T) + (p.gates ? 4.0 * qrows : 0.0);
   LaunchScope scope(p.mode == 0 ? "attention_time" : (p.mode == 1 ? "attention_band" : "attention_sdpa"), flop,
                     bytes, s);
-  attention_kernel<T><<<grid, kThreads, kAttnSmem, s>>>(mq, mk, mv, p);
+  if (band)
+    attention_kernel<T, true><<<grid, kThreads, kAttnSmem, s>>>(mq, mk, mv, p);
+  else
+    attention_kernel<T, false><<<grid, kThreads, kAttnSmem, s>>>(mq, mk, mv, p);
   return cudaGetLastError();
 }
 
@@ -561,16 +625,24 @@ cudaError_t launch_checked(const CUtensorMap& mq, const CUtensorMap& mk, const C
 
 }  // namespace
 
+// Items of the time-axis schedule (see pair_geom): every unit's full pairs, plus one
+// item per two units' tail tiles when q_tiles is odd.
+static long long time_axis_items(long long units, int q_tiles) {
+  return units * (q_tiles / 2) + ((q_tiles & 1) ? (units + 1) / 2 : 0);
+}
+
 cudaError_t launch_attention(const CUtensorMap& qkv_map, const AttnParams& p, int bf16, int num_sms,
                              cudaStream_t stream) {
   if (p.mode != 0 && p.mode != 1) return cudaErrorInvalidValue;
   if (p.mode == 1 && (p.seq_len < 1 || p.seq_len > 128 || p.seqs_per_tile != 128 / attn_band_slot(p.seq_len)))
     return cudaErrorInvalidValue;
   AttnParams a = p;
-  const long long pairs = (p.q_tiles + 1) / 2;
-  const long long items = p.mode == 0 ? (long long)p.B * p.F * p.heads * pairs : pairs * p.heads;
-  if (items > 0x7fffffffLL) return cudaErrorInvalidValue;
+  const long long units = (long long)p.B * p.F * p.heads;
+  const long long items =
+      p.mode == 0 ? time_axis_items(units, p.q_tiles) : (long long)((p.q_tiles + 1) / 2) * p.heads;
+  if (items > 0x7fffffffLL || units > 0x7fffffffLL) return cudaErrorInvalidValue;
   a.total_items = (int)items;
+  a.units = (int)units;
   a.kv_len = p.seq_len;
   a.kv_tiles = p.q_tiles;
   a.k_col = p.heads * 64;
@@ -589,9 +661,10 @@ cudaError_t launch_sdpa(const CUtensorMap& q_map, const CUtensorMap& k_map, cons
   if (p.q_tiles != (p.T + 127) / 128 || p.kv_tiles != (p.kv_len + 127) / 128) return cudaErrorInvalidValue;
   if ((long long)p.B * p.T != p.num_tokens) return cudaErrorInvalidValue;
   AttnParams a = p;
-  const long long items = (long long)p.B * ((p.q_tiles + 1) / 2);
+  const long long items = time_axis_items(p.B, p.q_tiles);
   if (items > 0x7fffffffLL) return cudaErrorInvalidValue;
   a.total_items = (int)items;
+  a.units = p.B;
   a.k_col = a.v_col = 0;
   return launch_checked(q_map, k_map, v_map, a, bf16, num_sms, stream);
 }

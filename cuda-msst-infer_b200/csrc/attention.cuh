@@ -30,7 +30,8 @@ struct AttnParams {
   int seq_len;        // T (modes 0, 2) or F (mode 1): query rows per sequence
   int q_tiles;        // modes 0, 2: ceil(T/128); mode 1: number of 128-row packed tiles
   int seqs_per_tile;  // mode 1: 128 / attn_band_slot(F)
-  int total_items;    // set by launch_attention: pairs of q-tiles x heads (x sequences on the time axis)
+  int total_items;    // set by the launchers: work items (pairs of query tiles)
+  int units;          // set by the launchers, modes 0 and 2: (sequence, head) units
   int num_tokens;     // B*T*F
   int kv_len;         // key rows per sequence (= seq_len except in mode 2)
   int kv_tiles;       // modes 0, 2: ceil(kv_len/128)
