@@ -55,10 +55,12 @@ def test_sdpa_vs_reference(cuda, name, prec):
 
 
 # edge shapes: one query / one key, keys inside the first 32-column chunk, several
-# K/V tiles with a ragged tail, query tiles without a pair partner, d = 8 and 64
+# K/V tiles with a ragged tail, query tiles without a pair partner, d = 8 and 64; the
+# odd last tile of each (batch, head) runs paired with the next one's, or alone when
+# their count is odd ((3, 1, 64, 33, 8), (1, 3, 300, 300, 64))
 @pytest.mark.parametrize("B,H,Nq,Nk,D", [(1, 1, 1, 1, 64), (2, 3, 7, 5, 48), (1, 2, 300, 259, 64),
                                           (1, 1, 129, 385, 16), (3, 1, 64, 33, 8), (1, 8, 257, 128, 48),
-                                          (2, 2, 128, 1, 32)])
+                                          (2, 2, 128, 1, 32), (1, 3, 300, 300, 64)])
 @pytest.mark.parametrize("prec", ["fp16", "bf16"])
 def test_sdpa_shapes_vs_oracle(cuda, B, H, Nq, Nk, D, prec):
     torch = cuda

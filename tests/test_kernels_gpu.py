@@ -256,7 +256,10 @@ def _attn_ref(qkv, B, T, F, H, axis, scale, gates):
 
 
 @pytest.mark.parametrize("prec", ["fp16", "bf16"])
+# time axis: (2, 801, 3, 2) pairs the 33-row tail tiles of 12 units; (1, 801, 3, 1) and (1, 300, 1, 3) leave an odd
+# unit's tail alone; (1, 100, 2, 8) has only tail tiles
 @pytest.mark.parametrize("axis,B,T,F,H", [("time", 2, 801, 3, 2), ("time", 1, 100, 2, 8), ("time", 1, 256, 1, 1),
+                                           ("time", 1, 801, 3, 1), ("time", 1, 300, 1, 3),
                                            ("band", 2, 50, 60, 2), ("band", 1, 33, 62, 8), ("band", 3, 7, 5, 1),
                                            ("band", 1, 20, 100, 2), ("band", 2, 9, 32, 2), ("band", 1, 11, 33, 1),
                                            ("band", 1, 5, 128, 1), ("band", 1, 40, 1, 1)])
