@@ -9,7 +9,8 @@
 #   build as shipped: it needs a generated webui header with symbols that
 #   tools/embed_html.py never emits).  Links cuBLAS, cuBLASLt, cuFFT, cuDNN.
 #
-# Usage: oracle/build_ref.sh [REF_SRC_DIR]   (default /root/reference/src)
+# Usage: oracle/build_ref.sh [REF_SRC_DIR]   (default: $REF_SRC, else the reference
+# checkout's src/ directory of this build container)
 set -euo pipefail
 HERE="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
 SRC="${1:-${REF_SRC:-/root/reference/src}}"
