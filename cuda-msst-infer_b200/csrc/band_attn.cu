@@ -7,8 +7,10 @@
 //
 // A band sequence (F <= 64 tokens) sits in an aligned slot of 32 or 64 rows of a
 // 128-row tile (two sequences per tile for F = 60 or 62), so every query row finds
-// all of its keys inside the tile.  Persistent CTAs walk the tiles; per
-// tile and head h:
+// all of its keys inside the tile.  Persistent CTAs each take a contiguous range
+// of the launch's (tile, head) steps (UnitRange: every CTA the same number, give or
+// take one; a range may start or end inside a tile, whose xn the CTA then loads
+// itself); per tile and head h:
 //   1. QKV_h = xn . [Wq_h; Wk_h; Wv_h]^T        M128 N192 K=dim, into TMEM (two
 //                                                 buffers alternate between heads)
 //   2. drain (8 warps, each 32 columns of Q, K and V): QKV_h -> registers, rotary
@@ -86,8 +88,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int H = p.heads;
   const int spt = 128 / p.slot;  // sequences per tile
   const int ntiles = (p.num_seqs + spt - 1) / spt;
-  const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-  const int total_g = my_tiles * H;  // (tile, head) steps of this CTA
+  // this CTA's (tile, head) steps, in segments of one tile each; step g is the g-th
+  // (tile, head) in segment order and segment s loads its tile's xn (phase s & 1)
+  const UnitRange range(ntiles, H, (int)blockIdx.x, (int)gridDim.x);
+  const int total_g = range.count;
 
   if (threadIdx.x == 0) {
     for (int kb = 0; kb < 8; ++kb) {
@@ -130,8 +134,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t ph = 0;
       bool ok = true;
       const uint32_t slot_bytes = (uint32_t)p.slot * 128u;
-      for (int lt = 0; ok && lt < my_tiles; ++lt) {
-        const int t = (int)blockIdx.x + lt * (int)gridDim.x;
+      for (int lt = 0; ok && lt < range.nseg; ++lt) {
+        int t, h_begin, h_end;
+        range.seg(lt, t, h_begin, h_end);
         // one box of `slot` rows per sequence (rows past the tokens are zero-filled)
         for (int kb = 0; ok && kb < nkb; ++kb) {
           if (!mbar_wait<false>(&x_empty[kb], (lt & 1) ^ 1u, kErrTimeoutSmemEmpty, abort_flag)) {
@@ -142,7 +147,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k = 0; k < spt; ++k)
             tma_load_2d(sX + kb * kBlock + k * slot_bytes, &map_xn, &x_full[kb], kb * 64, (t * spt + k) * p.F);
         }
-        for (int h = 0; ok && h < H; ++h) {
+        for (int h = h_begin; ok && h < h_end; ++h) {
           for (int kb = 0; kb < nkb; ++kb) {
             if (!mbar_wait<false>(&w_empty[st], ph ^ 1u, kErrTimeoutSmemEmpty, abort_flag)) {
               ok = false;
@@ -170,13 +175,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       int st = 0;
       uint32_t ph = 0;
       bool ok = true;
+      // (segment, head) of the step issue_qkv takes next (steps go in order); heads
+      // [q_h0, q_h1) of the segment
+      int q_s = 0, q_t, q_h0 = 0, q_h1 = 0;
+      if (range.nseg > 0) range.seg(0, q_t, q_h0, q_h1);
+      int q_h = q_h0;
       auto issue_qkv = [&](int g) -> bool {
-        const int b = g & 1, lt = g / H, h = g % H;
+        const int b = g & 1, lt = q_s, h = q_h;
+        // the segment's first step waits for its xn; its last releases it
+        const bool first_in_tile = h == q_h0, last_in_tile = h == q_h1 - 1;
+        if (++q_h == q_h1 && ++q_s < range.nseg) {
+          range.seg(q_s, q_t, q_h0, q_h1);
+          q_h = q_h0;
+        }
         if (!mbar_wait<false>(&qb_free[b], ((g >> 1) & 1) ^ 1u, kErrTimeoutTmemEmpty, abort_flag)) return false;
         tc_fence_after();
         const uint32_t d = tmem + (b ? kColQB1 : kColQB0);
         for (int kb = 0; kb < nkb; ++kb) {
-          if (h == 0 && !mbar_wait<false>(&x_full[kb], lt & 1, kErrTimeoutTmaFull, abort_flag)) return false;
+          if (first_in_tile && !mbar_wait<false>(&x_full[kb], lt & 1, kErrTimeoutTmaFull, abort_flag)) return false;
           if (!mbar_wait<false>(&w_full[st], ph, kErrTimeoutTmaFull, abort_flag)) return false;
           tc_fence_after();
           const uint32_t a0 = smem_u32(sX + kb * kBlock);
@@ -186,7 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             umma_f16_ss(d, sw128_desc(a0 + kk * 32, 16, 1024), sw128_desc(b0 + kk * 32, 16, 1024), idesc_qkv,
                         (kb | kk) != 0 ? 1u : 0u);
           umma_commit(&w_empty[st]);
-          if (h == H - 1) umma_commit(&x_empty[kb]);  // the tile's xn k-block is no longer read
+          if (last_in_tile) umma_commit(&x_empty[kb]);  // the tile's xn k-block is no longer read
           if (++st == nst) {
             st = 0;
             ph ^= 1u;
@@ -208,7 +224,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         idesc_s, kk > 0 ? 1u : 0u);
           umma_commit(s_full);
         }
-        const bool next_same_tile = g + 1 < total_g && (g + 1) % H != 0;
+        // q_h: head of step g + 1, the first of a new segment when it equals q_h0
+        const bool next_same_tile = g + 1 < total_g && q_h != q_h0;
         if (next_same_tile && !(ok = issue_qkv(g + 1))) break;
         // O_g = P_g V_g into the drained QKV_g buffer
         if (!mbar_wait<false>(p_full, g & 1, kErrTimeoutAttnP, abort_flag)) break;
@@ -238,9 +255,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float c = p.scale_log2;
     bool ok = true;
     // output of head g (warps 6-9): O / l * gate -> out
+    // (segment, tile, head) of the step output() takes next (steps go in order)
+    int o_s = 0, o_t = 0, o_h = 0, o_h1 = 0;
+    if (range.nseg > 0) range.seg(0, o_t, o_h, o_h1);
     auto output = [&](int g) -> bool {
-      const int lt = g / H, h = g % H;
-      const int t = (int)blockIdx.x + lt * (int)gridDim.x;
+      const int t = o_t, h = o_h;
+      if (++o_h == o_h1 && ++o_s < range.nseg) range.seg(o_s, o_t, o_h, o_h1);
       if (!mbar_wait<false>(&o_full[g & 1], (g >> 1) & 1, kErrTimeoutAttnO, abort_flag)) return false;
       if (!mbar_wait<false>(&l_ready[g & 1], (g >> 1) & 1, kErrTimeoutAttnO, abort_flag)) return false;
       tc_fence_after();
@@ -407,7 +427,8 @@ cudaError_t launch_band_t(const CUtensorMap& mx, const CUtensorMap& mw, const Ba
   if (e != cudaSuccess) return e;
   const int spt = 128 / p.slot;
   const int ntiles = (p.num_seqs + spt - 1) / spt;
-  const int grid = ntiles < num_sms ? ntiles : num_sms;
+  const long long units = (long long)ntiles * p.heads;  // (tile, head) steps, split evenly over the CTAs
+  const int grid = units < num_sms ? (int)units : num_sms;
   if (grid <= 0) return cudaSuccess;
   // algorithmic cost: the QKV projection of every token and the attention of every
   // query row against its sequence's keys; xn and W read once, the output written once

@@ -33,6 +33,7 @@ enum DeviceError : unsigned {
   kErrTimeoutFfnS = 10,
   kErrTimeoutFfnP = 11,
   kErrTimeoutFfnO = 12,
+  kErrTimeoutFfnFlag = 13,
 };
 
 // One flag per translation unit; each .cu exposes a host accessor (see
@@ -213,6 +214,62 @@ __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.
 __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 // All committed bulk groups have completed (writes performed).
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// A persistent CTA's share of a launch's work units, unit u = tile * J + j (j a
+// hidden chunk, a head, ...): the contiguous range [U*c/G, U*(c+1)/G) for CTA c of
+// G, so every CTA gets the same number of units give or take one, instead of whole
+// tiles dealt in rounds of G (where the last round leaves most CTAs idle).  Walked
+// in order as segments of one tile each: the tail [j_first, J) of the first tile,
+// whole tiles, the head [0, j_last) of the last tile.
+struct UnitRange {
+  int J, count, nseg, t_first, t_last, j_first, j_last;
+  __device__ __forceinline__ UnitRange(int ntiles, int J_, int c, int G) : J(J_) {
+    const long long U = (long long)ntiles * J;
+    const long long u0 = U * c / G, u1 = U * (c + 1) / G;
+    count = (int)(u1 - u0);
+    t_first = (int)(u0 / J);
+    j_first = (int)(u0 % J);
+    t_last = u1 > u0 ? (int)((u1 - 1) / J) : t_first;
+    j_last = u1 > u0 ? (int)((u1 - 1) % J) + 1 : j_first;
+    nseg = u1 > u0 ? t_last - t_first + 1 : 0;
+  }
+  // segment s: tile t, units [j0, j1)
+  __device__ __forceinline__ void seg(int s, int& t, int& j0, int& j1) const {
+    t = t_first + s;
+    j0 = t == t_first ? j_first : 0;
+    j1 = t == t_last ? j_last : J;
+  }
+};
+
+// A flag word in global memory handed between CTAs of one grid (every CTA
+// resident): the writer's earlier global writes, bulk (async-proxy) ones included
+// once their groups have completed, are visible to a reader that saw the value.
+__device__ __forceinline__ void flag_release(unsigned* f, unsigned v) {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
+}
+
+// Bounded wait until *f == v (acquire); false after recording `code` when the
+// wall-clock limit passes or another thread of the CTA gave up.
+__device__ __forceinline__ bool flag_wait(const unsigned* f, unsigned v, unsigned code, volatile int* abort) {
+  const unsigned long long t0 = global_timer_ns();
+  for (uint32_t spins = 0;; ++spins) {
+    unsigned cur;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(cur) : "l"(f) : "memory");
+    if (cur == v) {
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      return true;
+    }
+    if ((spins & 15u) == 15u) {
+      if (*abort) return false;
+      if (global_timer_ns() - t0 > kWaitLimitNs) {
+        record_error(code);
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");

@@ -793,8 +793,16 @@ cudaError_t dispatch_epi(const CUtensorMap& ma, const CUtensorMap& mb, const CUt
 }
 
 // ---------------------------------------------------------------------------
-// Fused feed-forward block (see gemm.cuh).  CTA = 320 threads, persistent over
-// 128-row tiles:
+// Fused feed-forward block (see gemm.cuh).  CTA = 320 threads, persistent over a
+// contiguous range of the launch's (128-row tile, 128-wide hidden chunk) units
+// (UnitRange), so every CTA gets the same number of chunks (give or take one)
+// instead of whole tiles in rounds of the grid size.  A tile whose chunks are split
+// between CTA c (chunks [0, k), the last segment of its range) and CTA c + 1
+// (chunks [k, J), its first segment) gets two partial reduce-adds into x, ordered
+// by a flag: c + 1 adds its partial O (no b2) and then releases the flag of each
+// epilogue warp; the matching warp of c acquires it (long since released: c + 1 did
+// that part first) before adding O + b2, so the result does not depend on timing.
+// Roles:
 //   warp 0     TMA: the tile's xn (D/64 swizzled 128x64 atoms, resident for the
 //              tile), then W1 / W2 128x64 blocks through a 16 KB ring in the order
 //              the MMAs consume them
@@ -849,6 +857,9 @@ __global__ void __launch_bounds__(320, 1)
   const int nkb = p.D / kBK;      // k-blocks of S
   const int J = p.H / kBH;        // hidden chunks
   const int ntiles = (p.m + kBM - 1) / kBM;
+  // this CTA's (tile, hidden chunk) units; the grid is at most ntiles CTAs, so every
+  // range holds at least J units and a tile is split between at most two CTAs
+  const UnitRange range(ntiles, J, (int)blockIdx.x, (int)gridDim.x);
   if (threadIdx.x == 0) {
     mbar_init(x_full, 1);
     mbar_init(x_empty, 1);
@@ -897,17 +908,18 @@ __global__ void __launch_bounds__(320, 1)
         }
         return true;
       };
-      int lt = 0;
-      for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x, ++lt) {
+      for (int lt = 0; ok && lt < range.nseg; ++lt) {
+        int t, j0, j1;
+        range.seg(lt, t, j0, j1);
         if (!mbar_wait(x_empty, (lt & 1) ^ 1u, kErrTimeoutSmemEmpty, abort_flag)) break;
         mbar_arrive_expect_tx(x_full, nkb * kBlock);
         for (int kb = 0; kb < nkb; ++kb) tma_load_2d(sX + kb * kBlock, &map_xn, x_full, kb * kBK, t * kBM);
-        // consumption order: S_0, then (S_{j+1}, O_j) for j = 0..J-1; an S stage holds
+        // consumption order: S_j0, then (S_{j+1}, O_j) for j = j0..j1-1; an S stage holds
         // k-blocks kb, kb+1 of W1_j, an O stage the chunk's two 64-column halves of W2
         // rows n3*128..
-        for (int kb = 0; ok && kb < nkb; kb += 2) ok = load_w(&map_w1, kb * kBK, 0, kBK, 0);
-        for (int j = 0; ok && j < J; ++j) {
-          if (j + 1 < J)
+        for (int kb = 0; ok && kb < nkb; kb += 2) ok = load_w(&map_w1, kb * kBK, j0 * kBH, kBK, 0);
+        for (int j = j0; ok && j < j1; ++j) {
+          if (j + 1 < j1)
             for (int kb = 0; ok && kb < nkb; kb += 2) ok = load_w(&map_w1, kb * kBK, (j + 1) * kBH, kBK, 0);
           // O stages: each 256-row piece of W2 per 64-column hidden half (two 128-row
           // boxes), then a last 128-row piece with both hidden halves
@@ -999,20 +1011,21 @@ __global__ void __launch_bounds__(320, 1)
         ++pc;
         return true;
       };
-      int lt = 0;
-      for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x, ++lt) {
+      for (int lt = 0; ok && lt < range.nseg; ++lt) {
+        int t, j0, j1;
+        range.seg(lt, t, j0, j1);
         if (!mbar_wait(x_full, lt & 1, kErrTimeoutTmaFull, abort_flag)) break;
         tc_fence_after();
         ok = issue_s();
-        for (int j = 0; ok && j < J; ++j) {
-          if (j + 1 < J) {
+        for (int j = j0; ok && j < j1; ++j) {
+          if (j + 1 < j1) {
             ok = issue_s();
-            if (ok && j + 2 == J) umma_commit(x_empty);  // the tile's last S reads xn
-          } else if (J == 1) {
+            if (ok && j + 2 == j1) umma_commit(x_empty);  // the segment's last S reads xn
+          } else if (j1 - j0 == 1) {
             umma_commit(x_empty);
           }
           if (!ok) break;
-          if (j == 0) {
+          if (j == j0) {
             // O of the previous tile drained by the epilogue
             if (!mbar_wait(o_free, (lt & 1) ^ 1u, kErrTimeoutFfnO, abort_flag)) {
               ok = false;
@@ -1020,7 +1033,7 @@ __global__ void __launch_bounds__(320, 1)
             }
             tc_fence_after();
           }
-          ok = issue_o(j == 0);
+          ok = issue_o(j == j0);
         }
         if (!ok) break;
         umma_commit(o_full);
@@ -1036,10 +1049,11 @@ __global__ void __launch_bounds__(320, 1)
     // so waiting for its own bulk reads is enough before it writes P again
     uint8_t* stg = sEpi + (half * 4 + q) * kStgBytes;
     uint32_t sc = 0, pc = 0;
-    int lt = 0;
     bool ok = true;
-    for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x, ++lt) {
-      for (int j = 0; j < J; ++j) {
+    for (int lt = 0; ok && lt < range.nseg; ++lt) {
+      int t, j0, j1;
+      range.seg(lt, t, j0, j1);
+      for (int j = j0; j < j1; ++j) {
         if (!mbar_wait(s_full, sc & 1, kErrTimeoutFfnS, abort_flag)) {
           ok = false;
           break;
@@ -1094,6 +1108,17 @@ __global__ void __launch_bounds__(320, 1)
       // O epilogue: columns [half * D/2, (half + 1) * D/2) of rows t*128 + r
       if (!mbar_wait(o_full, lt & 1, kErrTimeoutFfnO, abort_flag)) break;
       tc_fence_after();
+      // a split tile: the later chunks' part (tail part, j0 > 0, this CTA's first
+      // segment) adds its partial first; the part holding chunk 0 (head part, the
+      // range's last segment) adds O + b2 once the matching warp of the next CTA has
+      // released its flag
+      const bool tail_part = j0 > 0, head_part = j1 < J;
+      unsigned* my_flag = p.flags + (size_t)blockIdx.x * 8 + (warp - 2);
+      if (head_part) {
+        if (lane == 0) ok = flag_wait(my_flag + 8, p.epoch, kErrTimeoutFfnFlag, abort_flag);
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (!ok) break;
+      }
       const int row0 = t * kBM + q * 32;
       for (int c0 = half * (p.D / 2); c0 < (half + 1) * (p.D / 2); c0 += 32) {
         uint32_t rr[32];
@@ -1102,7 +1127,7 @@ __global__ void __launch_bounds__(320, 1)
         float v[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(rr[i]);
-        if (p.b2 != nullptr) {
+        if (p.b2 != nullptr && !tail_part) {
           const float4* b4 = reinterpret_cast<const float4*>(p.b2 + c0);
 #pragma unroll
           for (int q4 = 0; q4 < 8; ++q4) {
@@ -1126,6 +1151,14 @@ __global__ void __launch_bounds__(320, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(o_free);
+      if (tail_part) {
+        // the partial's reduce-adds have been performed before the flag is released
+        if (lane == 0) {
+          bulk_wait0();
+          flag_release(my_flag, p.epoch);
+        }
+        __syncwarp();
+      }
     }
     if (lane == 0) bulk_wait0();
     __syncwarp();
@@ -1163,7 +1196,8 @@ cudaError_t launch_gemm(const CUtensorMap& map_a, const CUtensorMap& map_b, cons
 
 cudaError_t launch_ffn_fused(const CUtensorMap& map_xn, const CUtensorMap& map_w1, const CUtensorMap& map_w2,
                              const CUtensorMap& map_x, const FfnParams& p, int bf16, int num_sms, cudaStream_t stream) {
-  if (p.m < 0 || p.D % ffn::kBM != 0 || p.D > ffn::kMaxD || p.H % ffn::kBH != 0 || p.H <= 0 || p.b1 == nullptr)
+  if (p.m < 0 || p.D % ffn::kBM != 0 || p.D > ffn::kMaxD || p.H % ffn::kBH != 0 || p.H <= 0 || p.b1 == nullptr ||
+      p.flags == nullptr)
     return cudaErrorInvalidValue;
   if (p.m == 0) return cudaSuccess;
   auto kern = bf16 ? ffn_fused_kernel<__nv_bfloat16> : ffn_fused_kernel<__half>;

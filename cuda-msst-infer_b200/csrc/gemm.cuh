@@ -88,6 +88,12 @@ struct FfnParams {
   int m, D, H;
   const float* b1;  // [H]
   const float* b2;  // [D] or nullptr
+  // Eight words per CTA (>= 8 x the device's SM count, zero-initialised once) and a
+  // value that differs from every earlier launch on the same words: orders the two
+  // partial reduce-adds of a 128-row tile whose hidden chunks are split between two
+  // neighbouring CTAs.
+  unsigned* flags;
+  unsigned epoch;
 };
 cudaError_t launch_ffn_fused(const CUtensorMap& map_xn, const CUtensorMap& map_w1, const CUtensorMap& map_w2,
                              const CUtensorMap& map_x, const FfnParams& p, int bf16, int num_sms, cudaStream_t stream);

@@ -419,6 +419,10 @@ struct Model::Work {
   long long M = 0, BT = 0;
   DeviceBuffer frames, spec, ispec, abs, x, xn, gates, big1, big2, ao, mask;
   DeviceBuffer skips;  // skip_connection models: the outputs of depth blocks 0..depth-2
+  // fused feed-forward: split-tile flags (8 words per CTA) and the launch counter
+  // whose value marks them (launches on one workspace are stream-ordered)
+  DeviceBuffer ffn_flags;
+  unsigned ffn_epoch = 0;
   CUtensorMap m_abs, m_xn, m_ao, m_big1_ffh, m_big2_ffh, m_qkv_time, m_qkv_band, m_h1, m_h2;
   CUtensorMap m_xn_slot;  // xn in boxes of one band sequence's slot (band_attn.cu)
   // GEMM output maps (TMA stores)
@@ -881,6 +885,8 @@ Model::Work& Model::work(int B, int T) {
   w->ao.reset(2 * (size_t)M * inner_);
   w->mask.reset(4 * (size_t)S * w->BT * sum_dims_);
   if (skip_ && I.depth > 1) w->skips.reset(4 * (size_t)(I.depth - 1) * M * D);
+  w->ffn_flags.reset(4 * 8 * (size_t)num_sms_);
+  MSST_CUDA(cudaMemset(w->ffn_flags.get(), 0, 4 * 8 * (size_t)num_sms_));
   w->m_abs = map_2d(w->abs.get(), w->BT, ktot_, ktot_, kGemmBM);
   w->m_xn = map_2d(w->xn.get(), M, D, D, kGemmBM);
   w->m_xn_slot = map_2d(w->xn.get(), M, D, D, (uint32_t)attn_band_slot(nb));
@@ -1111,6 +1117,9 @@ void Model::run_ffn_block(int d, int axis, int l, float* x, int B, int T, cudaSt
     fp.H = ff_;
     fp.b1 = L.b1.get<float>();
     fp.b2 = L.b2.get<float>();
+    fp.flags = w.ffn_flags.get<unsigned>();
+    if (++w.ffn_epoch == 0) ++w.ffn_epoch;  // 0 is the buffer's initial value
+    fp.epoch = w.ffn_epoch;
     MSST_CUDA(launch_ffn_fused(w.m_xn, L.m_w1_f, L.m_w2_f, mo_x, fp, bf16_, num_sms_, s));
     return;
   }
