@@ -749,12 +749,16 @@ bool use_pair(const GemmParams& p, int bn, int epi) {
     return e ? atoi(e) : 1;
   }();
   if (env == 0) return false;
-  if (env == 1 && epi != kEpiResid32) return false;
+  // by default: the residual GEMMs at K >= 512 and the 16-bit / GLU outputs at K >= 1024
+  // (the mask estimator's hidden layers, where the main loop outweighs the output
+  // writes; at K = 384 those are write-bound and the pair's coupled hand-off costs)
+  const bool wide_out = epi == kEpiStore16 || epi == kEpiGlu32;
+  if (env == 1 && epi != kEpiResid32 && !wide_out) return false;
   long long pair_tiles = 0;
   for (int i = 0; i < p.num_groups; ++i) {
     const GemmGroup& g = p.groups[i];
     if (g.n % bn != 0) return false;
-    if (env == 1 && g.k < 512) return false;
+    if (env == 1 && g.k < (wide_out ? 1024 : 512)) return false;
     pair_tiles += (long long)((g.m + 2 * kGemmBM - 1) / (2 * kGemmBM)) * (g.n / bn);
   }
   return pair_tiles >= 2 * 74;
