@@ -154,15 +154,17 @@ class ClockSampler:
 # without FLOPs): the capture is scaled to the timed region's average launch by
 # the ratio of algorithmic work.  The captures and their commands are in profiles/.
 NCU_TRAFFIC: dict = {
-    # profiles/dram_traffic_mbr_cfg1_chunk1.md: one 352800-sample chunk (48060 tokens)
-    "attention_time": {"dram_bytes": 149286400 + 23763200, "flop": 78839930880},
+    # profiles/attention_time_axis_mbr_cfg1_chunk1.md: the split-key time-axis kernel, one
+    # 352800-sample chunk (48060 tokens)
+    "attention_time": {"dram_bytes": 149505024 + 27155968, "flop": 78839930880},
+    # profiles/dram_traffic_mbr_cfg1_chunk1.md: one chunk
     "attention_band": {"dram_bytes": 149328896 + 20584704, "flop": 5905612800},
     "gemm_qkv_rope": {"dram_bytes": 38387712 + 90150144, "flop": 56693882880},
     "gemm_store16_gelu": {"dram_bytes": 38210816 + 90500608, "flop": 56693882880},
     # the out-projection (K=512); at dim <= 384 the FFN2 residual GEMM is part of ffn_fused
     "gemm_resid32": {"dram_bytes": 123456512 + 11998464, "flop": 18897960960},
     # profiles/ffn_fused_mbr_cfg1_chunk1.md: the fused feed-forward block, one chunk
-    "ffn_fused": {"dram_bytes": 113155584 + 15893504, "flop": 113387765760},
+    "ffn_fused": {"dram_bytes": 116556288 + 38805504, "flop": 113387765760},
     # profiles/band_attention_fused_mbr_cfg1_chunk1.md: band-axis QKV projection + attention, one chunk
     "band_attention_fused": {"dram_bytes": 39705344 + 1760000, "flop": 56693882880 + 5905612800},
 }
