@@ -223,7 +223,7 @@ __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_
 // whole tiles, the head [0, j_last) of the last tile.
 struct UnitRange {
   int J, count, nseg, t_first, t_last, j_first, j_last;
-  __device__ __forceinline__ UnitRange(int ntiles, int J_, int c, int G) : J(J_) {
+  __host__ __device__ __forceinline__ UnitRange(int ntiles, int J_, int c, int G) : J(J_) {
     const long long U = (long long)ntiles * J;
     const long long u0 = U * c / G, u1 = U * (c + 1) / G;
     count = (int)(u1 - u0);
@@ -234,7 +234,7 @@ struct UnitRange {
     nseg = u1 > u0 ? t_last - t_first + 1 : 0;
   }
   // segment s: tile t, units [j0, j1)
-  __device__ __forceinline__ void seg(int s, int& t, int& j0, int& j1) const {
+  __host__ __device__ __forceinline__ void seg(int s, int& t, int& j0, int& j1) const {
     t = t_first + s;
     j0 = t == t_first ? j_first : 0;
     j1 = t == t_last ? j_last : J;
